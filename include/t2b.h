@@ -1,0 +1,211 @@
+/*
+ * libt2b -- B200 (sm_100a) W4A16 group-128 decode hot path of torch2iron.
+ *
+ * C ABI.  All tensor pointers are DEVICE pointers owned by the caller; every
+ * call is asynchronous on the given stream (cudaStream_t passed as void*) and
+ * returns a status code (T2B_OK = 0).  Shape / alignment errors are detected
+ * on the host before anything is enqueued.
+ *
+ * Workspaces: kernels that split a reduction across CTAs take a caller-owned
+ * workspace (size from the matching *_workspace_bytes query).  It must be
+ * zero-filled once before first use (t2b_workspace_init); the kernels leave
+ * its counters re-armed for the next call.  Calls that share one workspace
+ * must be ordered on one stream.
+ *
+ * Ordering: kernels are launched with programmatic dependent launch.  Each
+ * kernel may start reading its (constant) weights before the preceding kernel
+ * in the stream has finished, so weights written by a kernel (e.g. a repack)
+ * must be complete -- synchronize the stream -- before the first call that
+ * reads them.
+ *
+ * Weight layout "T2B" (T2B_WFMT_T2B) for an [N, K] linear, group 128:
+ *   qw   uint8  [N][K/2]  byte k/2 of row n: low nibble q[n,k even], high q[n,k odd]
+ *                          (unsigned AutoGPTQ nibbles, 0..15)
+ *   meta uint32 [N][K/128] bits 0-15 fp16 scale, bits 16-20 zero point (1..16)
+ *   W[n,k] = (q[n,k] - zero[n,k/128]) * scale[n,k/128]
+ * Weight layout "QPARAM" (T2B_WFMT_QPARAM) is the reference's runtime row
+ * format (src/models/quantized_qwen3/packed_format.py:195-205): row n is
+ * K/2 bytes of biased int4 (zero 8) followed by K/128 bf16 scales.
+ */
+#ifndef T2B_H
+#define T2B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define T2B_API __attribute__((visibility("default")))
+#else
+#define T2B_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define T2B_OK 0
+#define T2B_ERR_SHAPE 1
+#define T2B_ERR_ALIGN 2
+#define T2B_ERR_LAUNCH 3
+#define T2B_ERR_TIMEOUT 4
+#define T2B_ERR_WORKSPACE 5
+#define T2B_ERR_ARG 6
+
+#define T2B_DTYPE_BF16 0
+#define T2B_DTYPE_F16 1
+#define T2B_DTYPE_F32 2
+
+#define T2B_WFMT_T2B 0
+#define T2B_WFMT_QPARAM 1
+
+/* Library / ABI version and a short human-readable message for a status. */
+T2B_API int t2b_version(void);
+T2B_API const char* t2b_status_string(int status);
+
+/* Zero a workspace (cudaMemsetAsync) before its first use. */
+T2B_API int t2b_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/*
+ * Repack AutoGPTQ-v1 tensors (qweight int32 [K/8,N], qzeros int32 [G,N/8],
+ * scales fp16 [G,N]) into the T2B layout.  Source row n lands at destination
+ * row  dst_row0 + (n / block_rows) * block_stride + n % block_rows, which
+ * builds fused matrices ([q;k;v] rows, or gate/up interleaved in 64-row
+ * blocks).  Plain copy: block_rows = N, block_stride = 0.
+ * Replaces the offline unpack of packed_format.py:88-146 / the dequant of
+ * fast_packed_format.py:132-161 (done once at load, never per token).
+ */
+T2B_API int t2b_repack_autogptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales_f16, int K, int N,
+                        int group_size, uint8_t* qw, uint32_t* meta, int dst_row0, int block_rows,
+                        int block_stride, void* stream);
+
+/*
+ * y[M,N] = x[M,K] . W^T  (fp32 accumulate of the exact dequantized weights).
+ * x / y dtypes: T2B_DTYPE_*.  wfmt T2B (weight = qw, meta) or QPARAM (weight =
+ * qparam rows, meta = NULL).  Any M >= 1; M <= 8 per CTA row-block.
+ * Replaces W4A16GEMV (src/models/quantized_qwen3/operators/w4a16_gemv/op.py:22-126,
+ * kernel.cc:29-133) and the W4A16GEMM family (w4a16_gemm/op.py:22-399).
+ */
+T2B_API size_t t2b_w4a16_gemm_workspace_bytes(int M, int N, int K);
+T2B_API int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype, void* y,
+                   int y_dtype, int M, int N, int K, int group_size, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/*
+ * Fused attention input block for one decoder layer, one new token per row:
+ *   xn = RMSNorm(x_resid; ssq, ln_w, eps)              (model.py:172-181)
+ *   [q;k;v] = xn . Wqkv^T                              (model.py:248-250)
+ *   q,k = RMSNorm_head(q|k; q_norm_w|k_norm_w, eps)    (model.py:252-253; skipped if NULL)
+ *   q,k = interleaved RoPE(angles[pos[m]])             (model.py:184-196)
+ *   q_out[m] = q ; k_cache/v_cache[m][kv][pos[m]] = k, v   (model.py:256-264)
+ * x_resid fp32 [M,H]; ssq fp32 [M] (sum of squares of each x_resid row);
+ * angles fp32 [max_ctx, head_dim]; caches bf16 [M][n_kv][max_ctx][head_dim];
+ * q_out bf16 [M][n_heads*head_dim].  ssq_clear (may be NULL): fp32 [M] zeroed.
+ * Replaces RMSNorm + W4A16KGroupGEMM(q) + W4A16PairedKGroupGEMM(k,v) +
+ * 2x RMSNormRoPE + CopyPresentPacketKV (batch_decode_fused.py:426-474).
+ */
+T2B_API size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, int head_dim);
+T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const float* x_resid, const float* ssq,
+                              const uint16_t* ln_w, float eps, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                              const float* angles, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
+                              uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
+                              int head_dim, int max_ctx, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * GQA decode attention, one query token per row, over the bf16 cache:
+ *   out[m, h] = softmax(q[m,h] . K[m, h/qpg, 0..pos[m]]^T / sqrt(hd)) . V  (model.py:266-279)
+ * q bf16 [M][n_heads*hd]; caches bf16 [M][n_kv][max_ctx][hd]; out bf16 [M][n_heads*hd].
+ * Replaces LlamaChunkedAttention (src/torch2iron/operators/llama_chunked_attention/op.py:21-165).
+ */
+T2B_API size_t t2b_decode_attention_workspace_bytes(int M, int n_heads, int n_kv, int head_dim, int max_ctx);
+T2B_API int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
+                         uint16_t* out, int M, int n_heads, int n_kv, int head_dim, int max_ctx, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/*
+ * Attention over the reference's packet cache
+ * [group][chunk][K chunk*hd | V chunk*hd | mask chunk] (bf16), skipping slots
+ * whose mask <= 0.5, all packet_seq_len slots scanned.  q, out bf16 [G][qpg][hd].
+ * Replaces LlamaChunkedAttention with its own packet argument
+ * (llama_chunked_attention/op.py:156-165, attention_reference.py:110-171).
+ */
+T2B_API int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, uint16_t* out, int n_groups, int q_per_group,
+                         int head_dim, int packet_seq_len, int chunk, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/*
+ * x_resid[M,H] += attn[M,K] . Wo^T ; ssq_out[m] += sum_n x_resid[m,n]^2.
+ * ssq_out must be zero before the call (zeroed by the preceding block's ssq_clear).
+ * Replaces W4A16KGroupGEMM(o) + ResidualAddRMSNorm (batch_decode_fused.py:485-498).
+ */
+T2B_API size_t t2b_oproj_residual_workspace_bytes(int M, int H, int K);
+T2B_API int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* attn, float* x_resid,
+                       float* ssq_out, int M, int H, int K, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * h[M,I] = silu(xn . Wg^T) * (xn . Wu^T), xn = RMSNorm(x_resid; ssq, ln_w, eps).
+ * qw/meta hold gate/up interleaved in 64-row blocks (block b: gate rows
+ * 64b..64b+63, then up rows 64b..64b+63).  ssq_clear as above.
+ * Replaces RMSNorm + W4A16PairedKGroupGEMM(gate,up) + SiLUMul
+ * (batch_decode_fused.py:499-506, model.py:215-216).
+ */
+T2B_API size_t t2b_upgate_swiglu_workspace_bytes(int M, int H, int I);
+T2B_API int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const float* x_resid, const float* ssq,
+                      const uint16_t* ln_w, float eps, uint16_t* h_out, float* ssq_clear, int M, int H, int I,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * x_resid[M,H] += h[M,I] . Wd^T ; ssq_out as for t2b_oproj_residual.
+ * Replaces W4A16KGroupGEMM(down) + ResidualAddRMSNorm (batch_decode_fused.py:507-530).
+ */
+T2B_API size_t t2b_down_residual_workspace_bytes(int M, int H, int I);
+T2B_API int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* h, float* x_resid, float* ssq_out,
+                      int M, int H, int I, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * x_resid[m] = float(table[tokens[m]]) ; ssq_out[m] = sum x_resid[m]^2.
+ * Replaces the host-side embedding of qwen_npu.py:180-185 (model.py:469).
+ */
+T2B_API int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* x_resid, float* ssq_out, int M, int H,
+                   int vocab, void* stream);
+
+/*
+ * out[m] = bf16(RMSNorm(x_resid[m]; ssq, w, eps)) -- the final norm (model.py:409,477).
+ */
+T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out, int M,
+                      int H, void* stream);
+
+/*
+ * Greedy pick: idx[m] = argmax_v logits[m, v] (lowest index on ties), logits
+ * dtype T2B_DTYPE_*, row stride ld.  Replaces the host argmax of
+ * qwen_npu.py:321 / model.py:492.
+ */
+T2B_API size_t t2b_argmax_workspace_bytes(int M, int V);
+T2B_API int t2b_argmax_rows(const void* logits, int dtype, int M, int V, int ld, int32_t* idx, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/*
+ * Standalone reference operators (same argument meaning as the NPU ops):
+ *   RMSNormRoPE (src/torch2iron/operators/rms_norm_rope/op.py:19-90):
+ *     out[r] = rope(rmsnorm(in[r]; w, eps), angles[r / (rows/angle_rows)]),
+ *     rope_mode 0 = interleaved (model.py:184-196), 1 = two halves (kernel.cc:39-67).
+ *   ResidualAddRMSNorm (residual_add_rms_norm/op.py:19-85):
+ *     x_out = x + update ; norm_out = rmsnorm(x_out per tile_size row; w, eps)
+ *   SiLUMul (silu_mul/op.py:20-80): out = silu(a) * b
+ *   CopyPresentPacketKV (copy_present_packet_kv/op.py:19-80): present_k/v = k/v and
+ *     packet[key/value offset + g*per_group + d] = k/v[g, d], mask slot set to 1.
+ * All bf16.
+ */
+T2B_API int t2b_rms_norm_rope(const uint16_t* in, const uint16_t* w, const uint16_t* angles, uint16_t* out, int rows,
+                      int cols, int angle_rows, float eps, int rope_mode, void* stream);
+T2B_API int t2b_residual_add_rms_norm(const uint16_t* x, const uint16_t* update, const uint16_t* w, uint16_t* x_out,
+                              uint16_t* norm_out, int size, int tile_size, float eps, void* stream);
+T2B_API int t2b_silu_mul(const uint16_t* a, const uint16_t* b, uint16_t* out, int size, void* stream);
+T2B_API int t2b_copy_present_packet_kv(const uint16_t* k, const uint16_t* v, uint16_t* present_k, uint16_t* present_v,
+                               uint16_t* packet, int num_kv_groups, int head_dim, int packet_elements_per_group,
+                               int key_packet_offset, int value_packet_offset, int mask_offset, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* T2B_H */

@@ -1,0 +1,51 @@
+"""CPU checks of the C-ABI library: it loads and exports every symbol the header declares."""
+
+import re
+from pathlib import Path
+
+import pytest
+
+from torch2iron_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_symbols():
+    text = (ROOT / "include" / "t2b.h").read_text()
+    return sorted(set(re.findall(r"T2B_API\s+[\w\s\*]+?\b(t2b_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = header_symbols()
+    assert len(syms) >= 20
+    assert "t2b_w4a16_gemm" in syms and "t2b_decode_attention" in syms
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.load()
+    for s in header_symbols():
+        assert hasattr(lib, s), s
+
+
+def test_binding_covers_header():
+    assert set(header_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_host_side_errors():
+    lib = _lib.load()
+    assert lib.t2b_version() >= 1
+    assert b"shape" in lib.t2b_status_string(1)
+    # host-side validation happens before any launch: no device needed
+    assert lib.t2b_w4a16_gemm(None, None, 0, None, 0, None, 0, 1, 128, 256, 128, None, 0, None) == 6
+    assert lib.t2b_w4a16_gemm(1, 1, 0, 1, 0, 1, 0, 1, 128, 256, 64, None, 0, None) == 1   # group 64
+    assert lib.t2b_decode_attention(16, 16, 16, 16, 16, 1, 16, 8, 128, 100, None, 0, None) == 1  # ctx % 8
+    assert lib.t2b_qkv_norm_rope_kvwrite(*([16] * 5), 1e-6, *([16] * 8), 1, 1024, 16, 8, 96, 64, None, 0,
+                                         None) == 1   # head_dim 96
+
+
+def test_workspace_queries():
+    lib = _lib.load()
+    assert lib.t2b_w4a16_gemm_workspace_bytes(1, 128, 256) == 0
+    assert lib.t2b_w4a16_gemm_workspace_bytes(8, 1024, 3072) > 0
+    assert lib.t2b_decode_attention_workspace_bytes(64, 16, 8, 128, 256) == 0
+    assert lib.t2b_decode_attention_workspace_bytes(1, 16, 8, 128, 4096) > 0

@@ -1,0 +1,115 @@
+"""W4A16 GEMV/GEMM parity through the C-ABI against the oracle and reference goldens.
+
+Bar: each GEMV/GEMM within 1e-2 relative error
+(max-abs error / max |ref|) of fp32-accumulated dequantized math.  The
+kernel dequantizes exactly and accumulates in fp32, so fp32 outputs are held
+to 1e-4 and 16-bit outputs to 1e-2.
+"""
+
+import pytest
+import torch
+
+import oracle
+from tests import golden_io as gio
+from tests.gpu_util import rel_err
+from torch2iron_b200 import _lib, synth
+from torch2iron_b200 import weights as W
+from torch2iron_b200.operators import W4A16GEMM, W4A16GEMV
+
+pytestmark = pytest.mark.gpu
+
+
+def gemm(w: W.W4Weight, x: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
+    M, K = x.shape
+    N = w.out_features
+    y = torch.empty(M, N, dtype=out_dtype, device="cuda")
+    L = _lib.lib()
+    n = max(L.t2b_w4a16_gemm_workspace_bytes(M, N, K), 256)
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    _lib.call("t2b_w4a16_gemm", _lib.ptr(w.qw), _lib.ptr(w.meta), _lib.WFMT_T2B, _lib.ptr(x), _lib.DTYPE[x.dtype],
+              _lib.ptr(y), _lib.DTYPE[out_dtype], M, N, K, 128, _lib.ptr(ws), n, _lib.stream())
+    torch.cuda.synchronize()
+    return y
+
+
+def test_config0_gemv_fp16():
+    d = gio.load("config0.npz")
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(3072, 1024, generator=g) * 0.02
+    x = torch.randn(1, 1024, generator=g).to(torch.float16)
+    lin = synth.quantize_rtn_autogptq(w)
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    y = gemm(dw, x.cuda(), torch.float16)
+    assert rel_err(y, torch.from_numpy(d["y"])) <= 1e-2
+    y32 = gemm(dw, x.cuda(), torch.float32)
+    assert rel_err(y32, torch.from_numpy(d["y"])) <= 1e-5
+
+
+def test_repack_matches_reference_dequant():
+    d = gio.load("gemv_autogptq.npz")
+    lin = gio.linear(d, "p")
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    dense = oracle.autogptq_linear_to_dense(lin.qweight, lin.qzeros, lin.scales)
+    assert torch.equal(W.dequantize(dw).cpu(), dense)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8])
+def test_golden_gemv_batches(M):
+    d = gio.load("gemv_autogptq.npz")
+    lin = gio.linear(d, "p")
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    x = torch.from_numpy(d["x"])[:M].cuda()
+    y = gemm(dw, x, torch.float32)
+    assert rel_err(y, torch.from_numpy(d["y"])[:M]) <= 1e-5
+
+
+@pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 3072), (6144, 1024), (1024, 2048), (256, 512), (128, 256)])
+@pytest.mark.parametrize("M", [1, 4, 8, 13, 64])
+def test_gemm_shapes_vs_oracle(N, K, M):
+    g = torch.Generator().manual_seed(N * 7 + K + M)
+    lin = synth.random_linear(N, K, g)
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    ref = oracle.GroupedW4A16Linear(lin.qweight, lin.qzeros, lin.scales)(x.float())
+    y = gemm(dw, x.cuda(), torch.float32)
+    assert rel_err(y, ref) <= 1e-4
+    yb = gemm(dw, x.cuda(), torch.bfloat16)
+    assert rel_err(yb, ref) <= 1e-2
+
+
+def test_gemm_operator_and_repeat_calls_reuse_workspace():
+    """Counters re-arm: the same workspace serves consecutive calls."""
+    g = torch.Generator().manual_seed(11)
+    lin = synth.random_linear(1024, 3072, g)
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    x = torch.randn(4, 3072, generator=g).to(torch.bfloat16)
+    ref = oracle.GroupedW4A16Linear(lin.qweight, lin.qzeros, lin.scales)(x.float())
+    op = W4A16GEMM(M=4, K=3072, N=1024)
+    for _ in range(3):
+        c = torch.empty(4, 1024, dtype=torch.bfloat16, device="cuda")
+        op(x.cuda(), dw, c)
+        torch.cuda.synchronize()
+        assert rel_err(c, ref) <= 1e-2
+
+
+def test_qparam_gemv_operator_matches_reference_runtime():
+    d = gio.load("qparam_linear.npz")
+    qparam = torch.from_numpy(d["qparam"]).cuda()
+    x = gio.bf16(d["x"]).cuda()
+    op = W4A16GEMV(M=256, K=512, num_batches=3, shared_qparam=True)
+    y = torch.empty(3, 256, dtype=torch.bfloat16, device="cuda")
+    op(qparam, x, y)
+    torch.cuda.synchronize()
+    assert rel_err(y, torch.from_numpy(d["y"])) <= 1e-2
+
+
+def test_shape_errors_raise():
+    with pytest.raises(_lib.T2BError):
+        dw = W.W4Weight(torch.zeros(100, 128, dtype=torch.uint8, device="cuda"),
+                        torch.zeros(100, 2, dtype=torch.int32, device="cuda"), 100, 256)
+        gemm(dw, torch.zeros(1, 256, dtype=torch.bfloat16, device="cuda"))

@@ -1,0 +1,60 @@
+"""CPU-side host logic: operator validation (reference error behaviour), configs, synth."""
+
+import pytest
+import torch
+
+import oracle
+from torch2iron_b200 import synth
+from torch2iron_b200.config import LLAMA_3_2_1B, QWEN3_0_6B, QWEN3_8B
+from torch2iron_b200.operators import (LlamaChunkedAttention, RMSNormRoPE, ResidualAddRMSNorm, SiLUMul, W4A16GEMM,
+                                       W4A16GEMV, W4A16KGroupGEMM)
+from torch2iron_b200.rope import rope_angles
+
+
+def test_reference_validation_errors():
+    with pytest.raises(ValueError, match="K must be even"):
+        W4A16GEMV(M=128, K=255)
+    with pytest.raises(ValueError, match="multiple of group_size"):
+        W4A16GEMV(M=128, K=200)
+    with pytest.raises(ValueError, match="tile_k == group_size"):
+        W4A16GEMM(M=8, K=1024, N=1024, tile_k=64)
+    with pytest.raises(ValueError, match="k_tiles must be divisible"):
+        W4A16KGroupGEMM(M=8, K=384, N=128, k_group=2)
+    with pytest.raises(ValueError, match="cols must be divisible by 32"):
+        RMSNormRoPE(rows=8, cols=100, angle_rows=8)
+    with pytest.raises(ValueError, match="epsilon must be positive"):
+        RMSNormRoPE(rows=8, cols=128, angle_rows=8, epsilon=0)
+    with pytest.raises(ValueError, match="divisible by chunk_size"):
+        LlamaChunkedAttention(max_seq_len=100)
+    with pytest.raises(ValueError):
+        ResidualAddRMSNorm(size=1000, num_aie_columns=8, tile_size=1024)
+    with pytest.raises(ValueError):
+        SiLUMul(size=1000, tile_size=512)
+
+
+def test_arg_specs_follow_reference_shapes():
+    op = W4A16GEMV(M=3072, K=1024)
+    spec = op.get_arg_spec()
+    assert spec[0].shape == (3072, 1024 // 2 + 8 * 2) and spec[0].dtype == torch.uint8
+    assert spec[1].shape == (1024,) and spec[2].shape == (3072,)
+    a = LlamaChunkedAttention(max_seq_len=512, num_kv_groups=8, q_heads_per_group=2, head_dim=128)
+    assert a.get_arg_spec()[1].shape == (8 * 8 * (2 * 64 * 128 + 64),)
+
+
+def test_presets_validate():
+    for cfg in (QWEN3_0_6B, LLAMA_3_2_1B, QWEN3_8B):
+        cfg.validate()
+    assert QWEN3_0_6B.q_heads_per_group == 2 and LLAMA_3_2_1B.q_heads_per_group == 4
+
+
+def test_rope_table_is_the_reference_formula():
+    assert torch.equal(rope_angles(128, 300, 1e6), oracle.compute_rope_angles(128, 300, 1e6))
+
+
+def test_synth_recipe_properties():
+    g = torch.Generator().manual_seed(0)
+    lin = synth.random_linear(256, 512, g)
+    assert lin.qweight.shape == (64, 256) and lin.qweight.dtype == torch.int32
+    assert lin.qzeros.shape == (4, 32) and lin.scales.shape == (4, 256) and lin.scales.dtype == torch.float16
+    z = oracle.unpack_autogptq_qzeros(lin.qzeros, 256)
+    assert 1 <= int(z.min()) and int(z.max()) <= 15

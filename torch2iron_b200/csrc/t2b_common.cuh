@@ -1,0 +1,145 @@
+// Shared device helpers for the sm_100a W4A16 decode kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/t2b.h"
+
+#define T2B_DEV __device__ __forceinline__
+
+namespace t2b {
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL).  A kernel launched with the
+// programmatic-stream-serialization attribute may start while its predecessor
+// is still running; it must not touch anything the predecessor writes (or
+// reads) until grid_dep_wait() returns.  Weights are constant, so every
+// kernel here prefetches them before the wait.
+// ---------------------------------------------------------------------------
+T2B_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+T2B_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Number formats
+// ---------------------------------------------------------------------------
+T2B_DEV float bf16_bits_to_f32(uint32_t lo16) { return __uint_as_float(lo16 << 16); }
+T2B_DEV float bf16_to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+T2B_DEV float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+enum XDtype { X_BF16 = T2B_DTYPE_BF16, X_F16 = T2B_DTYPE_F16, X_F32 = T2B_DTYPE_F32 };
+
+T2B_DEV float load_act(const void* p, int dtype, size_t i) {
+  if (dtype == X_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dtype == X_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+T2B_DEV void store_act(void* p, int dtype, size_t i, float v) {
+  if (dtype == X_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dtype == X_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// ---------------------------------------------------------------------------
+// Reductions
+// ---------------------------------------------------------------------------
+T2B_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+T2B_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Split-K ticket.  Every CTA that contributes a partial to output tile `t`
+// stores it (plain global stores), then calls split_ticket(); exactly one CTA
+// -- the last to arrive -- gets `true`, re-arms the counter to zero for the
+// next launch and runs the epilogue.  Partials must then be read with
+// ld.global.cg (L1 bypass) -- see ldcg().
+// ---------------------------------------------------------------------------
+T2B_DEV bool split_ticket(int* counter, int arrivals) {
+  __shared__ int s_last;
+  __threadfence();  // make this thread's partial stores visible device-wide
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int prev = atomicAdd(counter, 1);
+    s_last = (prev == arrivals - 1);
+    if (s_last) atomicExch(counter, 0);
+  }
+  __syncthreads();
+  bool last = s_last != 0;
+  if (last) __threadfence();  // acquire side
+  return last;
+}
+
+T2B_DEV float ldcg(const float* p) { return __ldcg(p); }
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk async copy (TMA 1-D) with bounded waits.
+// ---------------------------------------------------------------------------
+T2B_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+T2B_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+T2B_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+T2B_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+T2B_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+T2B_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+T2B_DEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+T2B_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Spin on an mbarrier phase for at most `limit_ns` of wall time (each
+// try_wait already suspends for a hardware-chosen interval).  On timeout the
+// error word (if any) gets T2B_ERR_TIMEOUT and false is returned; the caller
+// must stop using the stage.
+T2B_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, int* err, uint64_t limit_ns = 500000000ull) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, phase)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) break;
+  }
+  if (err) atomicCAS(err, 0, T2B_ERR_TIMEOUT);
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
+// src, dst 16-byte aligned; bytes a multiple of 16.
+T2B_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace t2b

@@ -1,0 +1,270 @@
+"""Batch decode engine: the reference's per-step decode composition on B200.
+
+One decode step for ``B`` rows (one new token each) follows the op order of
+``build_batch_decode_fused_op`` (``src/models/quantized_qwen3/batch_decode_fused.py:426-539``)
+and the math of ``QuantizedQwenForCausalLM.forward`` (``model.py:453-478``),
+as 5 fused launches per layer:
+
+    embed_rows                      x = E[tok]            (+ sum of squares)
+    per layer:
+      qkv_norm_rope_kvwrite         RMSNorm, [q;k;v] GEMV, QK-norm, RoPE, KV write
+      decode_attention              split-K GQA attention over the bf16 cache
+      oproj_residual                x += o_proj(ctx)      (+ sum of squares)
+      upgate_swiglu                 RMSNorm, [gate|up] GEMV, silu(g)*u
+      down_residual                 x += down(h)          (+ sum of squares)
+    rms_norm_rows                   final norm -> bf16
+    lm_head                         bf16 logits GEMM (fp32 out)
+    argmax_rows                     greedy token
+
+The whole step is captured once in a CUDA graph and replayed; the kernels
+chain with programmatic dependent launch.  The residual stream is fp32; the
+activations entering each linear are bf16 (A16).  KV caches are bf16
+``[B][n_kv][max_ctx][head_dim]`` per layer -- the reference's host-synced
+packet cache (``decode_packet_cache.py``) becomes a device-resident cache
+written by the qkv epilogue, so no per-layer host copy remains.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from . import weights as W
+from .config import QuantizedQwenConfig
+from .rope import rope_angles
+
+
+@dataclass
+class LayerWeights:
+    qkv: W.W4Weight
+    o_proj: W.W4Weight
+    gate_up: W.W4Weight
+    down: W.W4Weight
+    input_layernorm: torch.Tensor
+    post_attention_layernorm: torch.Tensor
+    q_norm: torch.Tensor | None
+    k_norm: torch.Tensor | None
+
+    @property
+    def algorithmic_bytes(self) -> int:
+        b = sum(w.nbytes_algorithmic for w in (self.qkv, self.o_proj, self.gate_up, self.down))
+        b += 2 * (self.input_layernorm.numel() + self.post_attention_layernorm.numel())
+        if self.q_norm is not None:
+            b += 2 * (self.q_norm.numel() + self.k_norm.numel())
+        return b
+
+
+def load_layer(layer: dict, cfg: QuantizedQwenConfig, device="cuda") -> LayerWeights:
+    def bf(t):
+        return None if t is None else t.to(device=device, dtype=torch.bfloat16).contiguous()
+
+    return LayerWeights(
+        qkv=W.concat_rows([layer["q_proj"], layer["k_proj"], layer["v_proj"]], device),
+        o_proj=W.from_autogptq(layer["o_proj"], device),
+        gate_up=W.pair_blocks(layer["gate_proj"], layer["up_proj"], device),
+        down=W.from_autogptq(layer["down_proj"], device),
+        input_layernorm=bf(layer["input_layernorm"]),
+        post_attention_layernorm=bf(layer["post_attention_layernorm"]),
+        q_norm=bf(layer.get("q_norm")) if cfg.qk_norm else None,
+        k_norm=bf(layer.get("k_norm")) if cfg.qk_norm else None,
+    )
+
+
+class DecodeEngine:
+    """Greedy batch decoder over device-resident W4A16 weights.
+
+    ``model`` is the dict produced by ``synth.random_model`` (AutoGPTQ linears
+    per layer, bf16 ``embed``, ``final_norm``, optional untied ``lm_head``).
+    """
+
+    def __init__(self, cfg: QuantizedQwenConfig, model: dict, batch: int, max_ctx: int, device="cuda",
+                 use_graph: bool = True):
+        cfg.validate()
+        if max_ctx % 64:
+            raise ValueError("max_ctx must be a multiple of 64")
+        self.cfg, self.B, self.max_ctx, self.device = cfg, batch, max_ctx, torch.device(device)
+        self.use_graph = use_graph
+        dev = self.device
+        self.layers = [load_layer(l, cfg, dev) for l in model["layers"]]
+        if len(self.layers) != cfg.n_layers:
+            raise ValueError("layer count does not match the config")
+        self.embed = model["embed"].to(dev, torch.bfloat16).contiguous()
+        lm = model.get("lm_head")
+        self.lm_head = self.embed if lm is None else lm.to(dev, torch.bfloat16).contiguous()
+        self.final_norm = model["final_norm"].to(dev, torch.bfloat16).contiguous()
+        self.angles = rope_angles(cfg.head_dim, max_ctx, cfg.rope_base).to(dev)
+
+        B, H, hd = batch, cfg.emb_dim, cfg.head_dim
+        f32, bf = torch.float32, torch.bfloat16
+        self.x = torch.zeros(B, H, dtype=f32, device=dev)
+        self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
+        self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
+        self.q = torch.zeros(B, cfg.q_dim, dtype=bf, device=dev)
+        self.attn = torch.zeros(B, cfg.q_dim, dtype=bf, device=dev)
+        self.h = torch.zeros(B, cfg.hidden_dim, dtype=bf, device=dev)
+        self.xn = torch.zeros(B, H, dtype=bf, device=dev)
+        self.logits = torch.zeros(B, cfg.vocab_size, dtype=f32, device=dev)
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.next_tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        kv_shape = (B, cfg.n_kv_groups, max_ctx, hd)
+        self.k_cache = [torch.zeros(kv_shape, dtype=bf, device=dev) for _ in range(cfg.n_layers)]
+        self.v_cache = [torch.zeros(kv_shape, dtype=bf, device=dev) for _ in range(cfg.n_layers)]
+
+        L = _lib.load()
+        nq, nkv = cfg.n_heads, cfg.n_kv_groups
+        sizes = {
+            "qkv": L.t2b_qkv_workspace_bytes(B, H, nq, nkv, hd),
+            "attn": L.t2b_decode_attention_workspace_bytes(B, nq, nkv, hd, max_ctx),
+            "o": L.t2b_oproj_residual_workspace_bytes(B, H, cfg.q_dim),
+            "ug": L.t2b_upgate_swiglu_workspace_bytes(B, H, cfg.hidden_dim),
+            "down": L.t2b_down_residual_workspace_bytes(B, H, cfg.hidden_dim),
+            "argmax": L.t2b_argmax_workspace_bytes(B, cfg.vocab_size),
+        }
+        # one workspace per op kind: consecutive ops never share counters
+        self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
+        torch.cuda.synchronize(dev)   # repacked weights complete before any PDL launch reads them
+        self.graph = None
+        self._step_graph = None
+
+    # -- byte accounting (algorithmic, for the roofline) ---------------------
+    def weight_bytes(self) -> int:
+        b = sum(l.algorithmic_bytes for l in self.layers)
+        b += self.lm_head.numel() * 2 + self.final_norm.numel() * 2
+        return b
+
+    def step_bytes(self, ctx_lens: list[int] | None = None) -> int:
+        """Algorithmic HBM bytes of one decode step with per-row context lengths (keys attended)."""
+        cfg = self.cfg
+        kv_tok = 2 * cfg.n_kv_groups * cfg.head_dim * 2
+        if ctx_lens is None:
+            ctx_lens = [int(p) + 1 for p in self.pos.tolist()]
+        kv_read = sum(ctx_lens) * kv_tok * cfg.n_layers
+        kv_write = self.B * kv_tok * cfg.n_layers
+        emb = self.B * cfg.emb_dim * 2
+        return self.weight_bytes() + kv_read + kv_write + emb
+
+    # -- launch sequence -----------------------------------------------------
+    def _ws(self, k):
+        t, n = self.ws[k]
+        return _lib.ptr(t), n
+
+    def enqueue_layer(self, li: int, st: int) -> None:
+        cfg, B = self.cfg, self.B
+        H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
+        L = _lib.lib()
+        lw = self.layers[li]
+        p = _lib.ptr
+        _lib.check("t2b_qkv_norm_rope_kvwrite", L.t2b_qkv_norm_rope_kvwrite(
+            p(lw.qkv.qw), p(lw.qkv.meta), p(self.x), p(self.ssq_a), p(lw.input_layernorm), cfg.rms_norm_eps,
+            p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
+            p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
+        _lib.check("t2b_decode_attention", L.t2b_decode_attention(
+            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), B, nq, nkv, hd,
+            self.max_ctx, *self._ws("attn"), st))
+        _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
+            p(lw.o_proj.qw), p(lw.o_proj.meta), p(self.attn), p(self.x), p(self.ssq_b), B, H, cfg.q_dim,
+            *self._ws("o"), st))
+        _lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
+            p(lw.gate_up.qw), p(lw.gate_up.meta), p(self.x), p(self.ssq_b), p(lw.post_attention_layernorm),
+            cfg.rms_norm_eps, p(self.h), p(self.ssq_a), B, H, cfg.hidden_dim, *self._ws("ug"), st))
+        _lib.check("t2b_down_residual", L.t2b_down_residual(
+            p(lw.down.qw), p(lw.down.meta), p(self.h), p(self.x), p(self.ssq_a), B, H, cfg.hidden_dim,
+            *self._ws("down"), st))
+
+    def enqueue_step(self) -> None:
+        """Enqueue one full decode step on the current stream (tokens/pos already on device)."""
+        cfg, B = self.cfg, self.B
+        L = _lib.lib()
+        st = _lib.stream()
+        p = _lib.ptr
+        _lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a), B,
+                                                      cfg.emb_dim, cfg.vocab_size, st))
+        for li in range(cfg.n_layers):
+            self.enqueue_layer(li, st)
+        _lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
+                                                            cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
+        torch.mm(self.xn, self.lm_head.t(), out_dtype=torch.float32, out=self.logits)
+        _lib.check("t2b_argmax_rows", L.t2b_argmax_rows(p(self.logits), 2, B, cfg.vocab_size, cfg.vocab_size,
+                                                        p(self.next_tokens), *self._ws("argmax"), st))
+
+    def kernels_per_step(self) -> int:
+        """Launches of this library's kernels per step (the lm_head GEMM is cuBLAS)."""
+        return 1 + 5 * self.cfg.n_layers + 1 + 1
+
+    # -- graph capture -------------------------------------------------------
+    def capture(self) -> None:
+        """Capture ``step + (tokens <- next, pos += 1)`` as one CUDA graph."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm up cuBLAS / lazy init outside the capture
+                self.enqueue_step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.enqueue_step()
+        self._step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._step_graph):
+            self.enqueue_step()
+            self.tokens.copy_(self.next_tokens)
+            self.pos.add_(1)
+
+    def run_step(self) -> None:
+        """One step from the device-resident tokens / pos (outputs ``next_tokens``, ``logits``)."""
+        if self.use_graph:
+            if self.graph is None:
+                self.capture()
+            self.graph.replay()
+        else:
+            self.enqueue_step()
+
+    def advance(self) -> None:
+        """Greedy self-feeding step: run, then tokens <- next_tokens, pos += 1 (all on device)."""
+        if self.use_graph:
+            if self._step_graph is None:
+                self.capture()
+            self._step_graph.replay()
+        else:
+            self.enqueue_step()
+            self.tokens.copy_(self.next_tokens)
+            self.pos.add_(1)
+
+    # -- host-facing API (the reference runner's decode_step, qwen_npu.py:166-236) --
+    def decode_step(self, tokens, positions) -> torch.Tensor:
+        """tokens / positions: host sequences of length B -> next greedy tokens (host int32 [B])."""
+        self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32), non_blocking=True)
+        self.pos.copy_(torch.as_tensor(positions, dtype=torch.int32), non_blocking=True)
+        self.run_step()
+        return self.next_tokens.cpu()
+
+    def prefill(self, prompts: torch.Tensor) -> None:
+        """Fill the KV caches by stepping through ``prompts [B, P]`` (teacher forcing).
+
+        Leaves ``next_tokens`` = the greedy token after the prompt, and
+        ``tokens``/``pos`` ready for ``advance()``.
+        """
+        P = prompts.shape[1]
+        prompts = prompts.to(self.device, torch.int32)
+        for t in range(P):
+            self.tokens.copy_(prompts[:, t])
+            self.pos.fill_(t)
+            self.run_step()
+        self.tokens.copy_(self.next_tokens)
+        self.pos.fill_(P)
+
+    def generate(self, prompts: torch.Tensor, new_tokens: int) -> torch.Tensor:
+        """Greedy decode ``new_tokens`` per row after ``prompts`` -> ``[B, new_tokens]``."""
+        self.prefill(prompts)
+        out = [self.next_tokens.clone()]
+        for _ in range(new_tokens - 1):
+            self.advance()
+            out.append(self.next_tokens.clone())
+        return torch.stack(out, dim=1)
+
+    def release(self) -> None:
+        self.graph = None
+        self._step_graph = None
