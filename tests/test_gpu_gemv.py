@@ -67,7 +67,7 @@ def test_golden_gemv_batches(M):
 
 
 @pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 3072), (6144, 1024), (1024, 2048), (256, 512), (128, 256)])
-@pytest.mark.parametrize("M", [1, 4, 8, 13, 64])
+@pytest.mark.parametrize("M", [1, 4, 8, 13, 16, 17, 33, 64, 100])
 def test_gemm_shapes_vs_oracle(N, K, M):
     g = torch.Generator().manual_seed(N * 7 + K + M)
     lin = synth.random_linear(N, K, g)
@@ -113,3 +113,18 @@ def test_shape_errors_raise():
         dw = W.W4Weight(torch.zeros(100, 128, dtype=torch.uint8, device="cuda"),
                         torch.zeros(100, 2, dtype=torch.int32, device="cuda"), 100, 256)
         gemm(dw, torch.zeros(1, 256, dtype=torch.bfloat16, device="cuda"))
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 16])
+@pytest.mark.parametrize("N,K", [(1024, 3072), (4096, 1024), (256, 12288)])
+def test_tcgen05_forced_small_batch(monkeypatch, M, N, K):
+    """The tensor-core path at any row count (padded to 16) matches the oracle."""
+    monkeypatch.setenv("T2B_TC_MIN_M", "1")
+    g = torch.Generator().manual_seed(M + N + K)
+    lin = synth.random_linear(N, K, g)
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    ref = oracle.GroupedW4A16Linear(lin.qweight, lin.qzeros, lin.scales)(x.float())
+    y = gemm(dw, x.cuda(), torch.float32)
+    assert rel_err(y, ref) <= 1e-4

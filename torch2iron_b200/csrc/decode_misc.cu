@@ -8,27 +8,25 @@
 namespace t2b {
 
 // ---------------------------------------------------------------------------
-// AutoGPTQ-v1 -> T2B layout.  qweight [K/8, N] int32 is a transpose away from
-// qw [N][K/2] (the 8 nibbles of word [k/8, n] are q[n, k..k+7] in order, low
-// nibble first); meta packs the fp16 scale with zero = stored + 1
-// (packed_format.py:103-106).
+// AutoGPTQ-v1 -> T2B tiled layout (see linear_common.cuh).  Word j of piece p
+// of row r in block (nt, g) is AutoGPTQ qweight word [g*16 + 4p + j, n]
+// unchanged (its 8 nibbles are q[n, k..k+7] in order, low nibble first);
+// meta packs the fp16 scale with zero = stored + 1 (packed_format.py:103-106).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ int mapped_row(int n, int dst_row0, int block_rows, int block_stride) {
+  return dst_row0 + (n / block_rows) * block_stride + n % block_rows;
+}
+
 __global__ void repack_qweight_kernel(const int32_t* __restrict__ qweight, uint32_t* __restrict__ qw, int K8, int N,
-                                      int dst_row0, int block_rows, int block_stride) {
-  __shared__ int32_t tile[32][33];
-  const int n0 = blockIdx.x * 32, k80 = blockIdx.y * 32;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int k8 = k80 + i, n = n0 + threadIdx.x;
-    tile[i][threadIdx.x] = (k8 < K8 && n < N) ? qweight[(size_t)k8 * N + n] : 0;
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int n = n0 + i, k8 = k80 + threadIdx.x;
-    if (n < N && k8 < K8) {
-      const int dst = dst_row0 + (n / block_rows) * block_stride + n % block_rows;
-      qw[(size_t)dst * K8 + k8] = (uint32_t)tile[threadIdx.x][i];
-    }
-  }
+                                      int G, int dst_row0, int block_rows, int block_stride) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)K8 * N) return;
+  const int k8 = (int)(idx / N), n = (int)(idx - (long long)k8 * N);
+  const int dst = mapped_row(n, dst_row0, block_rows, block_stride);
+  const int nt = dst >> 7, r = dst & 127;
+  const int g = k8 >> 4, pc = (k8 & 15) >> 2, j = k8 & 3;
+  const size_t word = ((((size_t)nt * G + g) * 4 + pc) * 128 + r) * 4 + j;
+  qw[word] = (uint32_t)qweight[idx];
 }
 
 __global__ void repack_meta_kernel(const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
@@ -39,8 +37,8 @@ __global__ void repack_meta_kernel(const int32_t* __restrict__ qzeros, const uin
   const int g = idx / N, n = idx - g * N;
   const uint32_t zw = (uint32_t)qzeros[(size_t)g * (N / 8) + n / 8];
   const uint32_t z = ((zw >> (4 * (n % 8))) & 0xFu) + 1u;
-  const int dst = dst_row0 + (n / block_rows) * block_stride + n % block_rows;
-  meta[(size_t)dst * G + g] = (uint32_t)scales[(size_t)g * N + n] | (z << 16);
+  const int dst = mapped_row(n, dst_row0, block_rows, block_stride);
+  meta[((size_t)(dst >> 7) * G + g) * 128 + (dst & 127)] = (uint32_t)scales[(size_t)g * N + n] | (z << 16);
 }
 
 int repack_autogptq(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales, int K, int N, int group,
@@ -49,9 +47,9 @@ int repack_autogptq(const int32_t* qweight, const int32_t* qzeros, const uint16_
   if (block_rows <= 0) return T2B_ERR_ARG;
   if (block_stride == 0) block_stride = block_rows;  // single block: rows map 1:1 (offset dst_row0)
   const int K8 = K / 8, G = K / 128;
-  dim3 g1((N + 31) / 32, (K8 + 31) / 32), b1(32, 8);
-  repack_qweight_kernel<<<g1, b1, 0, st>>>(qweight, reinterpret_cast<uint32_t*>(qw), K8, N, dst_row0, block_rows,
-                                           block_stride);
+  const long long words = (long long)K8 * N;
+  repack_qweight_kernel<<<(unsigned)((words + 255) / 256), 256, 0, st>>>(
+      qweight, reinterpret_cast<uint32_t*>(qw), K8, N, G, dst_row0, block_rows, block_stride);
   repack_meta_kernel<<<(G * N + 255) / 256, 256, 0, st>>>(qzeros, scales, meta, G, N, dst_row0, block_rows,
                                                           block_stride);
   return cudaGetLastError() == cudaSuccess ? T2B_OK : T2B_ERR_LAUNCH;

@@ -1,0 +1,191 @@
+// Shared pieces of the W4A16 linear kernels (CUDA-core GEMV and tcgen05
+// GEMM): parameters, the tiled T2B weight layout, the split-K fixup and the
+// fused decode-layer epilogues.
+//
+// T2B weight layout (one [N, K] linear, group 128, N % 128 == 0):
+//   qw   block (nt, g) = 128 rows x 128 k = 8192 bytes at ((nt*G + g) * 8192);
+//        inside a block, piece p (k 32p..32p+31) of row r is 16 bytes at
+//        p*2048 + r*16: four little-endian words, word j nibble i = q[k = 32p+8j+i]
+//        (unsigned AutoGPTQ nibbles -- word j of piece p IS AutoGPTQ qweight
+//        word [g*16 + 4p + j, n]).
+//   meta block (nt, g) = 128 uint32 at ((nt*G + g) * 128): fp16 scale | zero << 16.
+// One block is one contiguous 8 KB + 512 B pair, so a (128-row tile, group)
+// stage is a single bulk copy, and a warp reading one piece of 32 rows reads
+// 512 contiguous bytes.
+#pragma once
+
+#include "t2b_common.cuh"
+
+namespace t2b {
+
+enum Prologue { PRO_ACT = 0, PRO_RMSNORM = 1 };
+enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+
+constexpr int TILE_N = 128;          // weight rows per output tile
+constexpr int GROUP = 128;           // quantization group along K
+constexpr int BLOCK_BYTES = TILE_N * GROUP / 2;
+
+struct LinearParams {
+  const uint8_t* qw;      // T2B: tiled blocks; QPARAM: [N][K/2 + 2G] rows
+  const uint32_t* meta;   // T2B meta blocks
+  int w_ld;               // QPARAM bytes per row
+  int N, K, G;
+  const void* x;          // activations [M][x_ld]
+  int x_dtype, x_ld;
+  const float* ssq;       // PRO_RMSNORM: sum of squares per row
+  const __nv_bfloat16* norm_w;
+  float eps;
+  int M, kslice, ksplit;  // kslice: k per CTA (multiple of 128)
+  float* ws_part;         // [mblocks][ksplit][MB][N]
+  int* ws_cnt;            // [mblocks][N/128]
+  void* y;                // EPI_STORE output / EPI_SWIGLU h / EPI_QKV q_out
+  int y_dtype, y_ld;
+  float* resid;           // EPI_RESIDUAL fp32 [M][y_ld]
+  float* ssq_out;
+  float* ssq_clear;
+  const __nv_bfloat16* qn_w;
+  const __nv_bfloat16* kn_w;
+  const float* angles;
+  const int* pos;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int n_heads, n_kv, head_dim, max_ctx;
+  int* err;
+};
+
+T2B_DEV size_t qw_block_offset(int nt, int g, int G) { return ((size_t)nt * G + g) * BLOCK_BYTES; }
+T2B_DEV size_t meta_block_offset(int nt, int g, int G) { return ((size_t)nt * G + g) * TILE_N; }
+
+// ---------------------------------------------------------------------------
+// Split-K: publish this CTA's [MB][128] partial (already in `tile_acc`) and,
+// if it is the last of the tile's k-splits, leave the full sum in `tile_acc`.
+// Returns false for CTAs that must exit.
+// ---------------------------------------------------------------------------
+template <int MB>
+T2B_DEV bool splitk_fixup(const LinearParams& p, float* tile_acc, int tile, int split, int mblk, int nthreads) {
+  if (p.ksplit == 1) return true;
+  float* part = p.ws_part + ((size_t)(mblk * p.ksplit + split) * MB) * p.N + (size_t)tile * TILE_N;
+  for (int idx = threadIdx.x; idx < MB * TILE_N; idx += nthreads) {
+    const int b = idx / TILE_N, lr = idx - b * TILE_N;
+    part[(size_t)b * p.N + lr] = tile_acc[idx];
+  }
+  if (!split_ticket(p.ws_cnt + mblk * (p.N / TILE_N) + tile, p.ksplit)) return false;
+  for (int idx = threadIdx.x; idx < MB * TILE_N; idx += nthreads) {
+    const int b = idx / TILE_N, lr = idx - b * TILE_N;
+    const float* base = p.ws_part + ((size_t)mblk * p.ksplit * MB + b) * p.N + (size_t)tile * TILE_N + lr;
+    float s = 0.f;
+    for (int sp = 0; sp < p.ksplit; ++sp) s += ldcg(base + (size_t)sp * MB * p.N);
+    tile_acc[idx] = s;
+  }
+  __syncthreads();
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues over a finished [MB][128] fp32 tile (rows tile*128.., batch rows
+// m0..m0+MB-1).  `scratch` holds >= 8*MB floats.  256 threads.
+// ---------------------------------------------------------------------------
+template <int MB, int EPI>
+T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0) {
+  constexpr int NT = 256;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = tile * TILE_N;
+  if (EPI == EPI_STORE) {
+    for (int idx = threadIdx.x; idx < MB * TILE_N; idx += NT) {
+      const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
+      if (m < p.M) store_act(p.y, p.y_dtype, (size_t)m * p.y_ld + row0 + lr, tile_acc[idx]);
+    }
+  } else if (EPI == EPI_RESIDUAL) {
+    // each warp's 32 elements share one batch row -> one atomic per warp per pass
+    for (int base = 0; base < MB * TILE_N; base += NT) {
+      const int idx = base + threadIdx.x;
+      const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
+      const bool live = idx < MB * TILE_N && m < p.M;
+      float sq = 0.f;
+      if (live) {
+        float* xr = p.resid + (size_t)m * p.y_ld + row0 + lr;
+        const float v = *xr + tile_acc[idx];
+        *xr = v;
+        sq = v * v;
+      }
+      sq = warp_sum(sq);
+      if (lane == 0 && live) atomicAdd(p.ssq_out + m, sq);
+    }
+  } else if (EPI == EPI_SWIGLU) {
+    // tile = 64 gate rows then the matching 64 up rows (model.py:215-216)
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.y);
+    for (int idx = threadIdx.x; idx < MB * 64; idx += NT) {
+      const int b = idx >> 6, t = idx & 63, m = m0 + b;
+      if (m < p.M) {
+        const float g = tile_acc[b * TILE_N + t];
+        const float u = tile_acc[b * TILE_N + 64 + t];
+        const float silu = g / (1.f + expf(-g));
+        h[(size_t)m * p.y_ld + tile * 64 + t] = __float2bfloat16_rn(silu * u);
+      }
+    }
+  } else {  // EPI_QKV
+    const int hd = p.head_dim;
+    const int hpt = TILE_N / hd;  // heads per tile (1 or 2)
+    const int nq = p.n_heads, nkv = p.n_kv;
+    for (int pair = warp; pair < MB * hpt; pair += NT / 32) {
+      const int b = pair / hpt, hl = pair - b * hpt;
+      const int head = (row0 / hd) + hl;
+      float ss = 0.f;
+      for (int d = lane; d < hd; d += 32) {
+        const float v = tile_acc[b * TILE_N + hl * hd + d];
+        ss += v * v;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) {
+        const bool normed = (head < nq && p.qn_w) || (head >= nq && head < nq + nkv && p.kn_w);
+        scratch[pair] = normed ? rsqrtf(ss / (float)hd + p.eps) : 1.f;   // model.py:179-180 per head
+      }
+    }
+    __syncthreads();
+    __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(p.y);
+    for (int idx = threadIdx.x; idx < MB * TILE_N; idx += NT) {
+      const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
+      if (m >= p.M) continue;
+      const int hl = lr / hd, d = lr - hl * hd;
+      const int head = (row0 / hd) + hl;
+      const float* tv = tile_acc + b * TILE_N + hl * hd;
+      const int pos = p.pos[m];
+      if (head >= nq + nkv) {  // value head: stored as projected (model.py:250,263)
+        const int kvh = head - nq - nkv;
+        p.v_cache[(((size_t)m * nkv + kvh) * p.max_ctx + pos) * hd + d] = __float2bfloat16_rn(tv[d]);
+        continue;
+      }
+      const bool is_q = head < nq;
+      const __nv_bfloat16* nw = is_q ? p.qn_w : p.kn_w;
+      const float rs = scratch[b * hpt + hl];
+      const int d0 = d & ~1;
+      float x0 = tv[d0], x1 = tv[d0 + 1];
+      if (nw) {
+        x0 = (x0 * rs) * __bfloat162float(nw[d0]);
+        x1 = (x1 * rs) * __bfloat162float(nw[d0 + 1]);
+      }
+      // interleaved RoPE (model.py:184-196): out[2i] = x0 c - x1 s ; out[2i+1] = x1 c + x0 s
+      const float c = p.angles[(size_t)pos * hd + d0];
+      const float s = p.angles[(size_t)pos * hd + d0 + 1];
+      const float o = (d & 1) ? (x1 * c + x0 * s) : (x0 * c - x1 * s);
+      if (is_q) {
+        q_out[(size_t)m * p.y_ld + head * hd + d] = __float2bfloat16_rn(o);
+      } else {
+        const int kvh = head - nq;
+        p.k_cache[(((size_t)m * nkv + kvh) * p.max_ctx + pos) * hd + d] = __float2bfloat16_rn(o);
+      }
+    }
+  }
+}
+
+// Clears p.ssq_clear (M floats) from one designated CTA, after the PDL wait.
+T2B_DEV void maybe_clear_ssq(const LinearParams& p, bool designated) {
+  if (p.ssq_clear != nullptr && designated)
+    for (int i = threadIdx.x; i < p.M; i += blockDim.x) p.ssq_clear[i] = 0.f;
+}
+
+// Host side: shared launch helpers (defined in w4a16_gemv.cu).
+int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t linear_workspace_bytes(int M, int N, int K);
+
+}  // namespace t2b

@@ -27,8 +27,8 @@ PAIR_BLOCK = 64
 
 @dataclass
 class W4Weight:
-    qw: torch.Tensor      # uint8 [N, K/2]
-    meta: torch.Tensor    # int32 [N, K/128] (uint32 bit pattern)
+    qw: torch.Tensor      # uint8, N*K/2 bytes in 8 KB (128-row x 128-k) blocks; shape [N, K/2]
+    meta: torch.Tensor    # int32 [N, K/128] storage, 128-entry blocks (uint32: fp16 scale | zero << 16)
     out_features: int
     in_features: int
 
@@ -44,6 +44,8 @@ class W4Weight:
 
 
 def _empty(n: int, k: int, device) -> W4Weight:
+    if n % 128 or k % 256:
+        raise ValueError(f"T2B weights need out_features % 128 == 0 and in_features % 256 == 0, got [{n}, {k}]")
     return W4Weight(torch.empty(n, k // 2, dtype=torch.uint8, device=device),
                     torch.empty(n, k // 128, dtype=torch.int32, device=device), n, k)
 
@@ -86,10 +88,15 @@ def pair_blocks(gate: AutoGPTQLinear, up: AutoGPTQLinear, device="cuda") -> W4We
 
 
 def dequantize(w: W4Weight) -> torch.Tensor:
-    """Dense fp32 ``[N, K]`` view of a T2B weight (host-side check helper)."""
-    qw = w.qw.to(torch.int32)
-    q = torch.stack((qw & 0xF, qw >> 4), dim=-1).reshape(w.out_features, w.in_features).float()
-    meta = w.meta.to(torch.int64) & 0xFFFFFFFF
+    """Dense fp32 ``[N, K]`` view of a T2B weight (host-side check helper).
+
+    Undoes the tiled block order: block (nt, g) = [piece 4][row 128][16 B].
+    """
+    n, k = w.out_features, w.in_features
+    g = k // 128
+    qb = w.qw.reshape(n // 128, g, 4, 128, 16).permute(0, 3, 1, 2, 4).reshape(n, k // 2).to(torch.int32)
+    q = torch.stack((qb & 0xF, qb >> 4), dim=-1).reshape(n, k).float()
+    meta = w.meta.reshape(n // 128, g, 128).permute(0, 2, 1).reshape(n, g).to(torch.int64) & 0xFFFFFFFF
     scale = (meta & 0xFFFF).to(torch.int16).view(torch.float16).float()
     zero = ((meta >> 16) & 0x1F).float()
     return (q - zero.repeat_interleave(128, dim=1)) * scale.repeat_interleave(128, dim=1)
