@@ -246,7 +246,6 @@ def test_small_model_generate_vs_oracle_batch24():
         eng.tokens.copy_(ref[:, t - 1].to(torch.int32).cuda())
         eng.pos.fill_(P + t - 1)
         eng.run_step()
-        ref_logits = None
         hits += (eng.next_tokens.cpu().long() == ref[:, t]).sum().item()
         total += B
     assert agree >= 0.99 and hits / total >= 0.99
