@@ -83,10 +83,10 @@ T2B_DEV bool splitk_fixup(const LinearParams& p, float* tile_acc, int tile, int 
 
 // ---------------------------------------------------------------------------
 // Epilogues over a finished [MB][128] fp32 tile (rows tile*128.., batch rows
-// m0..m0+MB-1).  `scratch` holds >= 8*MB floats.  256 threads.
+// m0..m0+MB-1).  `scratch` holds >= 2*MB floats.  256 threads.
 // ---------------------------------------------------------------------------
-template <int MB, int EPI>
-T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0) {
+template <int EPI>
+T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB) {
   constexpr int NT = 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = tile * TILE_N;

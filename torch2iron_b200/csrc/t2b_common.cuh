@@ -143,3 +143,32 @@ T2B_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 }
 
 }  // namespace t2b
+
+namespace t2b {
+// ---------------------------------------------------------------------------
+// Thread-block clusters / distributed shared memory
+// ---------------------------------------------------------------------------
+T2B_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA in the cluster must call this (hardware barrier).
+T2B_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in cluster CTA `rank`.
+T2B_DEV uint32_t map_peer(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+T2B_DEV float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+}  // namespace t2b

@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
 
   // ---- 5. split-K fixup + epilogue --------------------------------------
   if (!splitk_fixup<MB>(p, tile_acc, tile, split, mblk, GV_THREADS)) return;
-  tile_epilogue<MB, EPI>(p, tile_acc, scratch, tile, m0);
+  tile_epilogue<EPI>(p, tile_acc, scratch, tile, m0, MB);
 }
 
 // ---------------------------------------------------------------------------
@@ -258,6 +258,7 @@ static int gemv_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, si
 // tcgen05 path (w4a16_tc.cu)
 int tc_launch(LinearParams& p, int pro, int epi, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t tc_ws_bytes(int M, int N, int K);
+bool tc_supported(int M, int N, int K);
 
 // Rows at or above this count take the tcgen05 path (env T2B_TC_MIN_M overrides).
 static int tc_min_m() {
@@ -269,8 +270,8 @@ static int tc_min_m() {
   return 16;
 }
 
-static bool use_tc(int M, int wfmt, int x_dtype) {
-  return wfmt == T2B_WFMT_T2B && x_dtype != T2B_DTYPE_F16 && M >= tc_min_m();
+static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {
+  return wfmt == T2B_WFMT_T2B && x_dtype != T2B_DTYPE_F16 && M >= tc_min_m() && tc_supported(M, N, K);
 }
 
 size_t linear_workspace_bytes(int M, int N, int K) {
@@ -285,7 +286,7 @@ int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t 
   if (p.N % TILE_N || p.K % 256) return T2B_ERR_SHAPE;
   p.G = p.K / GROUP;
   const int xdt = (pro == PRO_RMSNORM) ? T2B_DTYPE_F32 : p.x_dtype;
-  if (use_tc(p.M, wfmt, xdt)) return tc_launch(p, pro, epi, ws, ws_bytes, st);
+  if (use_tc(p.M, p.N, p.K, wfmt, xdt)) return tc_launch(p, pro, epi, ws, ws_bytes, st);
   return gemv_launch(p, pro, epi, wfmt, ws, ws_bytes, st);
 }
 

@@ -101,53 +101,93 @@ __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
   return c;
 }
 
-template <int BP, int S>
-struct TcSmem {
-  static constexpr int X_GROUP = BP * 256;                 // bf16 [2 atoms][BP][128 B]
-  static constexpr int OFF_X = 0;
-  static constexpr int OFF_RAW = OFF_X + S * X_GROUP;      // [S][8 KB]
-  static constexpr int OFF_META = OFF_RAW + S * BLOCK_BYTES;
-  static constexpr int OFF_TILE = OFF_META + S * TILE_N * 4;
-  static constexpr int OFF_XSUM = OFF_TILE + BP * TILE_N * 4;
-  static constexpr int OFF_SCR = OFF_XSUM + S * BP * 4;
-  static constexpr int OFF_BAR = OFF_SCR + 8 * BP * 4;
-  static constexpr int NBAR = S + 5;                         // raw_full[S], a_full[2], a_empty[2], acc_full
-  static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
-  static constexpr int OFF_FLAG = OFF_TMEM + 8;
-  static constexpr int BYTES = OFF_FLAG + 8 + 1024;          // + slack to 1024-align the base
-  static constexpr uint32_t A_COL = 0;                       // 2 stages x 64 columns
-  static constexpr uint32_t ACC_COL = 128;                   // S accumulators x BP columns
-  static constexpr uint32_t TMEM_COLS = pow2_cols(128 + S * BP);
+// Shared-memory plan of one CTA (S groups, BP padded batch rows).
+struct TcLayout {
+  int x_group, off_raw, off_meta, off_tile, off_xsum, off_scr, off_bar, off_tmem, off_flag, bytes;
+  __host__ __device__ TcLayout(int BP, int S) {
+    x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group
+    off_raw = S * x_group;                   // [S][8 KB] raw int4 blocks
+    off_meta = off_raw + S * BLOCK_BYTES;    // [S][128] meta words
+    off_tile = off_meta + S * TILE_N * 4;    // fp32 [BP][128] partial tile
+    off_xsum = off_tile + BP * TILE_N * 4;   // fp32 [S][BP] per-group activation sums
+    off_scr = off_xsum + S * BP * 4;         // fp32 [8*BP] scratch
+    off_bar = off_scr + 8 * BP * 4;          // raw_full[S], a_full[2], a_empty[2], acc_full
+    off_tmem = off_bar + (S + 5) * 8;
+    off_flag = off_tmem + 8;
+    bytes = off_flag + 8 + 1024;             // + slack to 1024-align the base
+  }
 };
+
+constexpr uint32_t A_COL = 0;      // two 64-column A stages
+constexpr uint32_t ACC_COL = 128;  // S accumulators of BP columns each
 
 T2B_DEV uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int BP, int S, int PRO, int EPI>
+// One 8-k activation chunk: bf16 values (as fp32) of batch row m, k..k+7.
+template <int PRO>
+T2B_DEV void load_x8(const LinearParams& p, int m, int k, float r, float (&v)[8]) {
+  if (PRO == PRO_RMSNORM) {
+    const float* xr = reinterpret_cast<const float*>(p.x) + (size_t)m * p.x_ld + k;
+    const float4 a0 = *reinterpret_cast<const float4*>(xr);
+    const float4 a1 = *reinterpret_cast<const float4*>(xr + 4);
+    const uint4 wn = *reinterpret_cast<const uint4*>(p.norm_w + k);
+    const float xv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const uint32_t ww[4] = {wn.x, wn.y, wn.z, wn.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float w = (e & 1) ? __uint_as_float(ww[e >> 1] & 0xffff0000u) : __uint_as_float(ww[e >> 1] << 16);
+      v[e] = round_bf16((xv[e] * r) * w);  // model.py:179-181, A16
+    }
+  } else if (p.x_dtype == T2B_DTYPE_BF16) {
+    const uint4 xb =
+        *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + (size_t)m * p.x_ld + k);
+    const uint32_t ww[4] = {xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = (e & 1) ? __uint_as_float(ww[e >> 1] & 0xffff0000u) : __uint_as_float(ww[e >> 1] << 16);
+  } else {  // fp32 activations rounded to bf16
+    const float* xr = reinterpret_cast<const float*>(p.x) + (size_t)m * p.x_ld + k;
+    const float4 a0 = *reinterpret_cast<const float4*>(xr);
+    const float4 a1 = *reinterpret_cast<const float4*>(xr + 4);
+    const float xv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = round_bf16(xv[e]);
+  }
+}
+
+// grid (N/128, KS, mblocks), cluster (1, KS, 1): the KS CTAs of a cluster are
+// the k-splits of one 128-row tile (S groups each); their partial tiles are
+// summed through distributed shared memory, each CTA finishing BP/KS rows.
+template <int BP, int PRO, int EPI>
 __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) {
-  using L = TcSmem<BP, S>;
+  const int S = p.kslice / GROUP;
+  const int KS = p.ksplit;
+  const TcLayout L(BP, S);
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  uint8_t* xs = sm + L::OFF_X;
-  uint8_t* raw = sm + L::OFF_RAW;
-  const uint32_t* rmeta = reinterpret_cast<const uint32_t*>(sm + L::OFF_META);
-  float* tile_acc = reinterpret_cast<float*>(sm + L::OFF_TILE);
-  float* xsum = reinterpret_cast<float*>(sm + L::OFF_XSUM);
-  float* scratch = reinterpret_cast<float*>(sm + L::OFF_SCR);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint8_t* xs = sm;
+  uint8_t* raw = sm + L.off_raw;
+  const uint32_t* rmeta = reinterpret_cast<const uint32_t*>(sm + L.off_meta);
+  float* tile_acc = reinterpret_cast<float*>(sm + L.off_tile);
+  float* xsum = reinterpret_cast<float*>(sm + L.off_xsum);
+  float* scratch = reinterpret_cast<float*>(sm + L.off_scr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.off_bar);
   uint64_t* raw_full = bars;
   uint64_t* a_full = bars + S;
   uint64_t* a_empty = bars + S + 2;
   uint64_t* acc_full = bars + S + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::OFF_TMEM);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::OFF_FLAG);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.off_tmem);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.off_flag);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y, mblk = blockIdx.z;
   const int g0 = split * S;
   const int m0 = mblk * BP;
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < ACC_COL + (uint32_t)(S * BP)) tmem_cols <<= 1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) mbar_init(&raw_full[i], 1);
@@ -165,7 +205,7 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
     for (int gl = 0; gl < S; ++gl) {
       mbar_arrive_expect_tx(&raw_full[gl], BLOCK_BYTES + TILE_N * 4);
       bulk_g2s(raw + gl * BLOCK_BYTES, p.qw + qw_block_offset(tile, g0 + gl, p.G), BLOCK_BYTES, &raw_full[gl]);
-      bulk_g2s(sm + L::OFF_META + gl * TILE_N * 4, p.meta + meta_block_offset(tile, g0 + gl, p.G), TILE_N * 4,
+      bulk_g2s(sm + L.off_meta + gl * TILE_N * 4, p.meta + meta_block_offset(tile, g0 + gl, p.G), TILE_N * 4,
                &raw_full[gl]);
     }
   }
@@ -176,7 +216,7 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
   // TMEM is taken only after the wait: a dependent grid parked on its own
   // wait never holds columns this grid still needs.
   if (warp == 4) {
-    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
 
@@ -188,50 +228,40 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
     }
     __syncthreads();
   }
-  for (int t = threadIdx.x; t < S * BP * 16; t += 256) {
-    const int c16 = t & 15, gb = t >> 4;
-    const int gl = gb / BP, b = gb - gl * BP;
-    const int m = m0 + b;
-    const int k = (g0 + gl) * GROUP + c16 * 8;
-    float v[8];
+  {
+    constexpr int UNR = 4;
+    const int total = S * BP * 16;  // (group, row, 8-k chunk) tasks; a multiple of 256
+    for (int t0 = threadIdx.x; t0 < total; t0 += 256 * UNR) {
+      float v[UNR][8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = 0.f;
-    if (m < p.M) {
-      if (PRO == PRO_RMSNORM) {
-        const float* xr = reinterpret_cast<const float*>(p.x) + (size_t)m * p.x_ld + k;
-        const float4 a0 = *reinterpret_cast<const float4*>(xr);
-        const float4 a1 = *reinterpret_cast<const float4*>(xr + 4);
-        const uint4 wn = *reinterpret_cast<const uint4*>(p.norm_w + k);
-        const float xv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const uint32_t ww[4] = {wn.x, wn.y, wn.z, wn.w};
-        const float r = scratch[b];
+      for (int u = 0; u < UNR; ++u) {
+        const int t = t0 + u * 256;
+        const int c16 = t & 15, gb = t >> 4;
+        const int gl = gb / BP, b = gb - gl * BP;
+        const int m = m0 + b;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float w = (e & 1) ? __uint_as_float(ww[e >> 1] & 0xffff0000u) : __uint_as_float(ww[e >> 1] << 16);
-          v[e] = round_bf16((xv[e] * r) * w);   // model.py:179-181, A16
-        }
-      } else if (p.x_dtype == T2B_DTYPE_BF16) {
-        const uint4 xb = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) +
-                                                         (size_t)m * p.x_ld + k);
-        const uint32_t ww[4] = {xb.x, xb.y, xb.z, xb.w};
+        for (int e = 0; e < 8; ++e) v[u][e] = 0.f;
+        if (t < total && m < p.M) load_x8<PRO>(p, m, (g0 + gl) * GROUP + c16 * 8, scratch[b < BP ? b : 0], v[u]);
+      }
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          v[e] = (e & 1) ? __uint_as_float(ww[e >> 1] & 0xffff0000u) : __uint_as_float(ww[e >> 1] << 16);
-      } else {  // fp32 activations rounded to bf16
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = round_bf16(reinterpret_cast<const float*>(p.x)[(size_t)m * p.x_ld + k + e]);
+      for (int u = 0; u < UNR; ++u) {
+        const int t = t0 + u * 256;
+        if (t >= total) break;  // warp-uniform: total is a multiple of 256
+        const int c16 = t & 15, gb = t >> 4;
+        const int gl = gb / BP, b = gb - gl * BP;
+        const uint4 packed = make_uint4(pack_bf16x2(v[u][0], v[u][4]), pack_bf16x2(v[u][1], v[u][5]),
+                                        pack_bf16x2(v[u][2], v[u][6]), pack_bf16x2(v[u][3], v[u][7]));
+        const int atom = c16 >> 3, cc = c16 & 7;
+        *reinterpret_cast<uint4*>(xs + gl * L.x_group + atom * (BP * 128) + b * 128 + ((cc ^ (b & 7)) << 4)) =
+            packed;
+        float sum = ((v[u][0] + v[u][1]) + (v[u][2] + v[u][3])) + ((v[u][4] + v[u][5]) + (v[u][6] + v[u][7]));
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (c16 == 0) xsum[gl * BP + b] = sum;
       }
     }
-    const uint4 packed = make_uint4(pack_bf16x2(v[0], v[4]), pack_bf16x2(v[1], v[5]), pack_bf16x2(v[2], v[6]),
-                                    pack_bf16x2(v[3], v[7]));
-    const int atom = c16 >> 3, cc = c16 & 7;
-    *reinterpret_cast<uint4*>(xs + gl * L::X_GROUP + atom * (BP * 128) + b * 128 + ((cc ^ (b & 7)) << 4)) = packed;
-    float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-    s += __shfl_xor_sync(0xffffffffu, s, 8);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    if (c16 == 0) xsum[gl * BP + b] = s;
   }
   fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
   maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0);
@@ -266,7 +296,7 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
           cols[4 * j + 2] = ((w[j] >> 8) & 0x000F000Fu) | 0x43004300u;
           cols[4 * j + 3] = ((w[j] >> 12) & 0x000F000Fu) | 0x43004300u;
         }
-        tmem_st16(lane_base + L::A_COL + stage * 64 + pc * 16, cols);
+        tmem_st16(lane_base + A_COL + stage * 64 + pc * 16, cols);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -282,11 +312,11 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
         break;
       }
       tc_fence_after();
-      const uint32_t xg = smem_u32(xs + gl * L::X_GROUP);
+      const uint32_t xg = smem_u32(xs + gl * L.x_group);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint64_t bdesc = sdesc_sw128(xg + (ks >> 2) * (BP * 128) + (ks & 3) * 32);
-        mma_ts(tbase + L::ACC_COL + gl * BP, tbase + L::A_COL + stage * 64 + ks * 8, bdesc, IDESC, ks > 0);
+        mma_ts(tbase + ACC_COL + gl * BP, tbase + A_COL + stage * 64 + ks * 8, bdesc, IDESC, ks > 0);
       }
       mma_commit(&a_empty[stage]);
     }
@@ -304,20 +334,19 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
 #pragma unroll
     for (int b = 0; b < BP; ++b) y[b] = 0.f;
     if (ok) {
-#pragma unroll
       for (int gl = 0; gl < S; ++gl) {
         const uint32_t mw = rmeta[gl * TILE_N + r];
-        const float s = __half2float(__ushort_as_half((unsigned short)(mw & 0xffffu)));
+        const float sc = __half2float(__ushort_as_half((unsigned short)(mw & 0xffffu)));
         const float zo = 128.f + (float)((mw >> 16) & 0x1fu);
 #pragma unroll
         for (int cb = 0; cb < BP / 16; ++cb) {
           uint32_t v[16];
-          tmem_ld16(lane_base + L::ACC_COL + gl * BP + cb * 16, v);
+          tmem_ld16(lane_base + ACC_COL + gl * BP + cb * 16, v);
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int b = cb * 16 + e;
-            y[b] = fmaf(s, __uint_as_float(v[e]) - zo * xsum[gl * BP + b], y[b]);
+            y[b] = fmaf(sc, __uint_as_float(v[e]) - zo * xsum[gl * BP + b], y[b]);
           }
         }
       }
@@ -329,73 +358,98 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
   __syncthreads();
   if (warp == 4) {
     tc_fence_after();
-    tmem_dealloc(tbase, L::TMEM_COLS);
+    tmem_dealloc(tbase, tmem_cols);
   }
-  if (*abort_flag) return;
 
-  if (!splitk_fixup<BP>(p, tile_acc, tile, split, mblk, 256)) return;
-  tile_epilogue<BP, EPI>(p, tile_acc, scratch, tile, m0);
+  // ---- cluster split-K: sum the KS partial tiles through DSMEM ----
+  // (every CTA passes both cluster barriers, aborted or not)
+  const float* fin = tile_acc;
+  int rows = BP, mrow0 = m0;
+  if (KS > 1) {
+    const uint32_t rank = cluster_ctarank();
+    rows = BP / KS;
+    mrow0 = m0 + (int)rank * rows;
+    float* red = reinterpret_cast<float*>(xs);  // X tile is dead once acc_full fired
+    cluster_sync();
+    const uint32_t my_tile = smem_u32(tile_acc) + rank * rows * TILE_N * 4;
+    for (int i = threadIdx.x; i < rows * TILE_N / 4; i += 256) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < KS; ++q) {
+        const float4 v = ld_dsmem_f4(map_peer(my_tile + i * 16, (uint32_t)q));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      reinterpret_cast<float4*>(red)[i] = acc;
+    }
+    cluster_sync();
+    fin = red;
+  }
+  __syncthreads();
+  if (*abort_flag) return;
+  tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows);
 }
 
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static int pick_bp(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : 64; }
+struct TcPlan {
+  int BP, KS, S, mblocks;
+  size_t smem;
+  bool ok;
+};
 
-// groups per CTA (1, 2 or 4): grow while the grid keeps >= 2 CTAs per SM,
-// or while the split count would exceed 24 (workspace size).
-static int pick_s(int N, int K, int mblocks) {
+static TcPlan tc_plan(int M, int N, int K) {
+  TcPlan pl{};
   const int G = K / GROUP;
-  const long tiles = (long)(N / TILE_N) * mblocks;
-  int s = 1;
-  while (s < 4 && G % (2 * s) == 0 && (tiles * (G / (2 * s)) >= 2L * 148 || G / s > 24)) s *= 2;
-  return s;
+  pl.BP = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+  pl.KS = 1;
+  for (int ks : {8, 4, 2})
+    if (G % ks == 0) {
+      pl.KS = ks;
+      break;
+    }
+  pl.S = G / pl.KS;
+  auto fits = [&](int bp) { return pl.S * bp <= 384 && TcLayout(bp, pl.S).bytes <= 220 * 1024; };
+  while (pl.BP > 16 && !fits(pl.BP)) pl.BP >>= 1;
+  pl.ok = fits(pl.BP) && pl.KS <= pl.BP && N % TILE_N == 0;
+  pl.mblocks = (M + pl.BP - 1) / pl.BP;
+  pl.smem = (size_t)TcLayout(pl.BP, pl.S).bytes;
+  return pl;
 }
 
-size_t tc_ws_bytes(int M, int N, int K) {
-  const int BP = pick_bp(M);
-  const int mblocks = (M + BP - 1) / BP;
-  const int ksplit = (K / GROUP) / pick_s(N, K, mblocks);
-  if (ksplit == 1) return 0;
-  size_t part = ((size_t)mblocks * ksplit * BP * N * sizeof(float) + 255) & ~size_t(255);
-  return part + (((size_t)mblocks * (N / TILE_N) * sizeof(int) + 255) & ~size_t(255));
-}
+size_t tc_ws_bytes(int, int, int) { return 0; }  // split-K stays on chip (cluster DSMEM)
 
-template <int BP, int S, int PRO, int EPI>
-static int tc_launch_t(LinearParams& p, dim3 grid, cudaStream_t st) {
-  auto kern = w4a16_tc_kernel<BP, S, PRO, EPI>;
-  const size_t smem = TcSmem<BP, S>::BYTES;
-  if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
-  return launch_pdl(kern, grid, dim3(256), smem, st, p);
+bool tc_supported(int M, int N, int K) { return tc_plan(M, N, K).ok; }
+
+template <int BP, int PRO, int EPI>
+static int tc_launch_t(LinearParams& p, const TcPlan& pl, cudaStream_t st) {
+  auto kern = w4a16_tc_kernel<BP, PRO, EPI>;
+  if (allow_smem(kern, pl.smem) != T2B_OK) return T2B_ERR_LAUNCH;
+  dim3 grid(p.N / TILE_N, pl.KS, pl.mblocks);
+  return launch_pdl_cluster(kern, grid, dim3(256), pl.smem, st, pl.KS, p);
 }
 
 template <int PRO, int EPI>
-static int tc_dispatch(LinearParams& p, int BP, int S, dim3 grid, cudaStream_t st) {
-#define T2B_TCASE(bp, s) \
-  if (BP == bp && S == s) return tc_launch_t<bp, s, PRO, EPI>(p, grid, st);
-  T2B_TCASE(16, 1) T2B_TCASE(16, 2) T2B_TCASE(16, 4) T2B_TCASE(32, 1) T2B_TCASE(32, 2) T2B_TCASE(32, 4)
-  T2B_TCASE(64, 1) T2B_TCASE(64, 2) T2B_TCASE(64, 4)
-#undef T2B_TCASE
+static int tc_dispatch(LinearParams& p, const TcPlan& pl, cudaStream_t st) {
+  if (pl.BP == 16) return tc_launch_t<16, PRO, EPI>(p, pl, st);
+  if (pl.BP == 32) return tc_launch_t<32, PRO, EPI>(p, pl, st);
+  if (pl.BP == 64) return tc_launch_t<64, PRO, EPI>(p, pl, st);
   return T2B_ERR_ARG;
 }
 
-int tc_launch(LinearParams& p, int pro, int epi, void* ws, size_t ws_bytes, cudaStream_t st) {
-  const int BP = pick_bp(p.M);
-  const int mblocks = (p.M + BP - 1) / BP;
-  const int S = pick_s(p.N, p.K, mblocks);
-  p.kslice = S * GROUP;
-  p.ksplit = p.K / p.kslice;
-  if (ws_bytes < tc_ws_bytes(p.M, p.N, p.K) || (p.ksplit > 1 && ws == nullptr)) return T2B_ERR_WORKSPACE;
+int tc_launch(LinearParams& p, int pro, int epi, void*, size_t, cudaStream_t st) {
+  const TcPlan pl = tc_plan(p.M, p.N, p.K);
+  if (!pl.ok) return T2B_ERR_SHAPE;
   if (p.x_dtype == T2B_DTYPE_F16 && pro == PRO_ACT) return T2B_ERR_ARG;
-  size_t part = ((size_t)mblocks * p.ksplit * BP * p.N * sizeof(float) + 255) & ~size_t(255);
-  p.ws_part = reinterpret_cast<float*>(ws);
-  p.ws_cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + part);
-  dim3 grid(p.N / TILE_N, p.ksplit, mblocks);
-  if (pro == PRO_ACT && epi == EPI_STORE) return tc_dispatch<PRO_ACT, EPI_STORE>(p, BP, S, grid, st);
-  if (pro == PRO_RMSNORM && epi == EPI_STORE) return tc_dispatch<PRO_RMSNORM, EPI_STORE>(p, BP, S, grid, st);
-  if (pro == PRO_ACT && epi == EPI_RESIDUAL) return tc_dispatch<PRO_ACT, EPI_RESIDUAL>(p, BP, S, grid, st);
-  if (pro == PRO_RMSNORM && epi == EPI_SWIGLU) return tc_dispatch<PRO_RMSNORM, EPI_SWIGLU>(p, BP, S, grid, st);
-  if (pro == PRO_RMSNORM && epi == EPI_QKV) return tc_dispatch<PRO_RMSNORM, EPI_QKV>(p, BP, S, grid, st);
+  p.kslice = pl.S * GROUP;
+  p.ksplit = pl.KS;
+  if (pro == PRO_ACT && epi == EPI_STORE) return tc_dispatch<PRO_ACT, EPI_STORE>(p, pl, st);
+  if (pro == PRO_RMSNORM && epi == EPI_STORE) return tc_dispatch<PRO_RMSNORM, EPI_STORE>(p, pl, st);
+  if (pro == PRO_ACT && epi == EPI_RESIDUAL) return tc_dispatch<PRO_ACT, EPI_RESIDUAL>(p, pl, st);
+  if (pro == PRO_RMSNORM && epi == EPI_SWIGLU) return tc_dispatch<PRO_RMSNORM, EPI_SWIGLU>(p, pl, st);
+  if (pro == PRO_RMSNORM && epi == EPI_QKV) return tc_dispatch<PRO_RMSNORM, EPI_QKV>(p, pl, st);
   return T2B_ERR_ARG;
 }
 
