@@ -77,6 +77,12 @@ T2B_DEV void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr)
       : "memory");
 }
+T2B_DEV void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
 T2B_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row core groups 1024 B apart.
@@ -162,7 +168,7 @@ T2B_DEV void load_x8(const LinearParams& p, int m, int k, float r, float (&v)[8]
 // the k-splits of one 128-row tile (S groups each); their partial tiles are
 // summed through distributed shared memory, each CTA finishing BP/KS rows.
 template <int BP, int PRO, int EPI>
-__global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) {
+__global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) {
   const int S = p.kslice / GROUP;
   const int KS = p.ksplit;
   const TcLayout L(BP, S);
@@ -324,35 +330,38 @@ __global__ void __launch_bounds__(256, 1) w4a16_tc_kernel(const LinearParams p) 
   }
 
   // ---- drain: y[b] = sum_g s_g * (P_g[b] - (128+z_g) * xsum_g[b]) ----
-  if (warp < 4) {
-    const int r = warp * 32 + lane;
-    const uint32_t lane_base = tbase + ((uint32_t)(warp * 32) << 16);
+  // warps w and w+4 share TMEM lane quarter w%4 and split the BP columns.
+  {
+    constexpr int HB = BP / 2;
+    const int q4 = warp & 3, half = warp >> 2;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     const bool ok = (*abort_flag == 0) && mbar_wait_bounded(acc_full, 0, p.err);
     if (!ok) *abort_flag = 1;
     tc_fence_after();
-    float y[BP];
+    float y[HB];
 #pragma unroll
-    for (int b = 0; b < BP; ++b) y[b] = 0.f;
+    for (int b = 0; b < HB; ++b) y[b] = 0.f;
     if (ok) {
       for (int gl = 0; gl < S; ++gl) {
         const uint32_t mw = rmeta[gl * TILE_N + r];
         const float sc = __half2float(__ushort_as_half((unsigned short)(mw & 0xffffu)));
         const float zo = 128.f + (float)((mw >> 16) & 0x1fu);
 #pragma unroll
-        for (int cb = 0; cb < BP / 16; ++cb) {
-          uint32_t v[16];
-          tmem_ld16(lane_base + ACC_COL + gl * BP + cb * 16, v);
+        for (int cb = 0; cb < HB / 8; ++cb) {
+          uint32_t v[8];
+          tmem_ld8(lane_base + ACC_COL + gl * BP + half * HB + cb * 8, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int b = cb * 16 + e;
-            y[b] = fmaf(sc, __uint_as_float(v[e]) - zo * xsum[gl * BP + b], y[b]);
+          for (int e = 0; e < 8; ++e) {
+            const int b = cb * 8 + e;
+            y[b] = fmaf(sc, __uint_as_float(v[e]) - zo * xsum[gl * BP + half * HB + b], y[b]);
           }
         }
       }
     }
 #pragma unroll
-    for (int b = 0; b < BP; ++b) tile_acc[b * TILE_N + r] = y[b];
+    for (int b = 0; b < HB; ++b) tile_acc[(half * HB + b) * TILE_N + r] = y[b];
   }
   tc_fence_before();
   __syncthreads();
@@ -400,21 +409,33 @@ struct TcPlan {
   bool ok;
 };
 
+// Cluster size KS (k-splits of a tile) is the smallest divisor of G in
+// {1,2,4,8} that brings the grid to at least one CTA per SM; each CTA then
+// takes S = G/KS groups.  BP shrinks (more row blocks) when S*BP would not
+// fit TMEM or shared memory.
 static TcPlan tc_plan(int M, int N, int K) {
   TcPlan pl{};
   const int G = K / GROUP;
+  const int tiles = N / TILE_N;
   pl.BP = M <= 16 ? 16 : M <= 32 ? 32 : 64;
-  pl.KS = 1;
-  for (int ks : {8, 4, 2})
-    if (G % ks == 0) {
+  auto mblk = [&](int bp) { return (M + bp - 1) / bp; };
+  pl.KS = 0;
+  for (int ks : {1, 2, 4, 8})
+    if (G % ks == 0 && ks <= pl.BP && (long)tiles * ks * mblk(pl.BP) >= 148) {
       pl.KS = ks;
       break;
     }
+  if (pl.KS == 0)
+    for (int ks : {8, 4, 2, 1})
+      if (G % ks == 0 && ks <= pl.BP) {
+        pl.KS = ks;
+        break;
+      }
   pl.S = G / pl.KS;
   auto fits = [&](int bp) { return pl.S * bp <= 384 && TcLayout(bp, pl.S).bytes <= 220 * 1024; };
-  while (pl.BP > 16 && !fits(pl.BP)) pl.BP >>= 1;
+  while (pl.BP > 16 && (!fits(pl.BP) || pl.KS > pl.BP)) pl.BP >>= 1;
   pl.ok = fits(pl.BP) && pl.KS <= pl.BP && N % TILE_N == 0;
-  pl.mblocks = (M + pl.BP - 1) / pl.BP;
+  pl.mblocks = mblk(pl.BP);
   pl.smem = (size_t)TcLayout(pl.BP, pl.S).bytes;
   return pl;
 }
