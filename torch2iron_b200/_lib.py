@@ -12,7 +12,7 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "libt2b.so"
+LIB_PATH = Path(os.environ.get("T2B_LIBRARY") or Path(__file__).resolve().parent / "libt2b.so")
 
 T2B_OK = 0
 DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}

@@ -23,6 +23,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build"
 LIB = PKG / "libt2b.so"
+TRACE_LIB = PKG / "libt2b_trace.so"   # -DT2B_TRACE: device phase timestamps (diagnostics only)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
@@ -40,16 +41,16 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
-def _stale() -> bool:
-    if not LIB.exists():
+def _stale(lib: Path) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     deps = list(CSRC.glob("*")) + list((ROOT / "include").glob("*.h"))
     return any(p.stat().st_mtime > t for p in deps)
 
 
-def _compile(src: Path, extra: list[str]) -> Path:
-    obj = BUILD / (src.stem + ".o")
+def _compile(src: Path, extra: list[str], suffix: str = "") -> Path:
+    obj = BUILD / (src.stem + suffix + ".o")
     cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
@@ -59,21 +60,26 @@ def _compile(src: Path, extra: list[str]) -> Path:
     return obj
 
 
-def build(force: bool = False, verbose_ptxas: bool = False) -> Path:
-    if not force and not _stale():
-        return LIB
+def build(force: bool = False, verbose_ptxas: bool = False, trace: bool = False) -> Path:
+    lib = TRACE_LIB if trace else LIB
+    if not force and not _stale(lib):
+        return lib
     BUILD.mkdir(exist_ok=True)
     extra = ["-Xptxas", "-v"] if verbose_ptxas else []
+    suffix = ""
+    if trace:
+        extra = extra + ["-DT2B_TRACE"]
+        suffix = "_trace"
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, extra), sources()))
-    tmp = LIB.with_suffix(".so.tmp")
+        objs = list(ex.map(lambda s: _compile(s, extra, suffix), sources()))
+    tmp = lib.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose_ptxas="--ptxas-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose_ptxas="--ptxas-v" in sys.argv, trace="--trace" in sys.argv))

@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
   AttnSmem<HD, QPG>& S = *reinterpret_cast<AttnSmem<HD, QPG>*>(smem_raw);
   const int kvh = blockIdx.x, m = blockIdx.y, split = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  T2B_TRACE_BEGIN(10, P.n_heads);
 
   if (tid == 0) {
     mbar_init(&S.bar[0], 1);
@@ -69,6 +70,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
   }
   grid_dep_wait();
   grid_dep_launch();
+  T2B_TRACE_MARK(1);
 
   const int n_keys = P.pos ? P.pos[m] + 1 : P.n_keys;
   // key range of this split, in whole 64-key tiles
@@ -121,6 +123,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
       ok = false;
       break;
     }
+    if (t == 0) T2B_TRACE_MARK(2);
     const int key0 = (t_begin + t) * AT_TILE;
     const int nk = min(AT_TILE, n_keys - key0);
     // scores: one (head, key) per thread-iteration; 16-byte K chunks rotated by
@@ -195,6 +198,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
       issue(t + 2, buf);
     }
   }
+  T2B_TRACE_MARK(3);
   if (!ok) return;  // timeout already recorded in P.err
 
   const size_t obase = (size_t)m * P.n_heads * HD + (size_t)kvh * QPG * HD;
@@ -353,3 +357,5 @@ extern "C" int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, u
   P.n_kv = n_groups;
   return attention_launch(P, 1, head_dim, packet_seq_len, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
+
+T2B_TRACE_DUMP_FN(t2b_trace_dump_attn)

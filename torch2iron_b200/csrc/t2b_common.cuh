@@ -172,3 +172,61 @@ T2B_DEV float4 ld_dsmem_f4(uint32_t addr) {
   return v;
 }
 }  // namespace t2b
+
+// ---------------------------------------------------------------------------
+// Device phase tracing (compiled in only with -DT2B_TRACE; see
+// `python -m torch2iron_b200.build --trace`).  Each CTA takes a record in
+// arrival order and stamps %globaltimer at phase boundaries; the host reads
+// the records back with t2b_trace_dump().  The product build has no trace
+// code and no trace symbols.
+// ---------------------------------------------------------------------------
+#ifdef T2B_TRACE
+namespace t2b {
+struct TraceRec {
+  unsigned long long t[8];
+  int tag, bx, by, bz, nblocks, key, pad0, pad1;
+};
+constexpr int TRACE_CAP = 1 << 15;
+// one buffer per translation unit (no relocatable device code); records carry
+// global timestamps, so the host merges the per-unit dumps by time
+static __device__ TraceRec g_trace[TRACE_CAP];
+static __device__ unsigned int g_trace_n;
+}  // namespace t2b
+// Defines the unit's read-back entry point: copies up to max_records records
+// (96 bytes each) to host `dst`, returns the count, resets if `reset`.
+#define T2B_TRACE_DUMP_FN(fname)                                                                          \
+  extern "C" __attribute__((visibility("default"))) int fname(void* dst, int max_records, int reset) {    \
+    unsigned int n = 0;                                                                                   \
+    if (cudaMemcpyFromSymbol(&n, t2b::g_trace_n, sizeof(n)) != cudaSuccess) return -1;                    \
+    int m = (int)(n < (unsigned)t2b::TRACE_CAP ? n : (unsigned)t2b::TRACE_CAP);                           \
+    if (m > max_records) m = max_records;                                                                 \
+    if (m > 0 && cudaMemcpyFromSymbol(dst, t2b::g_trace, (size_t)m * sizeof(t2b::TraceRec)) != cudaSuccess) \
+      return -1;                                                                                          \
+    if (reset) {                                                                                          \
+      unsigned int z = 0;                                                                                 \
+      if (cudaMemcpyToSymbol(t2b::g_trace_n, &z, sizeof(z)) != cudaSuccess) return -1;                    \
+    }                                                                                                     \
+    return m;                                                                                             \
+  }
+#define T2B_TRACE_BEGIN(tagv, keyv)                                                              \
+  __shared__ int t2b_trace_slot;                                                                 \
+  if (threadIdx.x == 0) {                                                                        \
+    const unsigned s_ = atomicAdd(&t2b::g_trace_n, 1u);                                          \
+    t2b_trace_slot = (int)(s_ & (t2b::TRACE_CAP - 1));                                           \
+    t2b::TraceRec& r_ = t2b::g_trace[t2b_trace_slot];                                            \
+    r_.tag = (tagv);                                                                             \
+    r_.bx = blockIdx.x;                                                                          \
+    r_.by = blockIdx.y;                                                                          \
+    r_.bz = blockIdx.z;                                                                          \
+    r_.nblocks = gridDim.x * gridDim.y * gridDim.z;                                              \
+    r_.key = (keyv);                                                                             \
+    for (int i_ = 0; i_ < 8; ++i_) r_.t[i_] = 0;                                                 \
+    r_.t[0] = t2b::globaltimer_ns();                                                             \
+  }
+#define T2B_TRACE_MARK(phase) \
+  if (threadIdx.x == 0) t2b::g_trace[t2b_trace_slot].t[(phase)] = t2b::globaltimer_ns();
+#else
+#define T2B_TRACE_BEGIN(tagv, keyv)
+#define T2B_TRACE_MARK(phase)
+#define T2B_TRACE_DUMP_FN(fname)
+#endif

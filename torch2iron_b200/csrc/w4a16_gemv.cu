@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
   const int row0 = tile * TILE_N;
   const int k0 = split * p.kslice;
   const int m0 = mblk * MB;
+  T2B_TRACE_BEGIN(20 + EPI, p.N);
 
   // ---- 1. weight prefetch (independent of the previous kernel) ----------
   uint4 wv[CH][4];
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
 
   grid_dep_wait();
   grid_dep_launch();
+  T2B_TRACE_MARK(1);
 
   // ---- 2. prologue: activations of this k-slice into shared fp32 --------
   if (PRO == PRO_RMSNORM) {
@@ -110,6 +112,7 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
   }
   maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0);
   __syncthreads();
+  T2B_TRACE_MARK(2);
 
   // ---- 3. dequant + FMA -------------------------------------------------
   float acc[4][MB];
@@ -185,8 +188,12 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
   __syncthreads();
 
   // ---- 5. split-K fixup + epilogue --------------------------------------
+  T2B_TRACE_MARK(3);
   if (!splitk_fixup<MB>(p, tile_acc, tile, split, mblk, GV_THREADS)) return;
+  T2B_TRACE_MARK(4);
   tile_epilogue<EPI>(p, tile_acc, scratch, tile, m0, MB);
+  __syncthreads();
+  T2B_TRACE_MARK(5);
 }
 
 // ---------------------------------------------------------------------------
@@ -436,3 +443,5 @@ extern "C" int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, const 
                                  float* ssq_out, int M, int H, int I, void* ws, size_t ws_bytes, void* stream) {
   return t2b_oproj_residual(qw, meta, h, x_resid, ssq_out, M, H, I, ws, ws_bytes, stream);
 }
+
+T2B_TRACE_DUMP_FN(t2b_trace_dump_gemv)

@@ -194,6 +194,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
   const int m0 = mblk * BP;
   uint32_t tmem_cols = 32;
   while (tmem_cols < ACC_COL + (uint32_t)(S * BP)) tmem_cols <<= 1;
+  T2B_TRACE_BEGIN(1 + EPI, p.N);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) mbar_init(&raw_full[i], 1);
@@ -218,6 +219,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
 
   grid_dep_wait();
   grid_dep_launch();
+  T2B_TRACE_MARK(1);
 
   // TMEM is taken only after the wait: a dependent grid parked on its own
   // wait never holds columns this grid still needs.
@@ -276,6 +278,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   constexpr uint32_t IDESC = idesc_bf16(TILE_N, BP);
+  T2B_TRACE_MARK(2);
 
   if (warp < 4) {
     // ---- producers: row r's nibbles -> bf16x2 (128+q) -> TMEM lane r ----
@@ -309,6 +312,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[stage]);
     }
+    T2B_TRACE_MARK(3);
   } else if (warp == 4 && lane == 0) {
     // ---- MMA issuer ----
     for (int gl = 0; gl < S; ++gl) {
@@ -338,6 +342,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     const bool ok = (*abort_flag == 0) && mbar_wait_bounded(acc_full, 0, p.err);
     if (!ok) *abort_flag = 1;
+    T2B_TRACE_MARK(4);
     tc_fence_after();
     float y[HB];
 #pragma unroll
@@ -370,6 +375,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
     tmem_dealloc(tbase, tmem_cols);
   }
 
+  T2B_TRACE_MARK(5);
   // ---- cluster split-K: sum the KS partial tiles through DSMEM ----
   // (every CTA passes both cluster barriers, aborted or not)
   const float* fin = tile_acc;
@@ -396,8 +402,11 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
     fin = red;
   }
   __syncthreads();
+  T2B_TRACE_MARK(6);
   if (*abort_flag) return;
   tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows);
+  __syncthreads();
+  T2B_TRACE_MARK(7);
 }
 
 // ---------------------------------------------------------------------------
@@ -475,3 +484,5 @@ int tc_launch(LinearParams& p, int pro, int epi, void*, size_t, cudaStream_t st)
 }
 
 }  // namespace t2b
+
+T2B_TRACE_DUMP_FN(t2b_trace_dump_tc)
