@@ -91,6 +91,21 @@ T2B_API int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt, c
                    void* stream);
 
 /*
+ * t2b_w4a16_gemm without a workspace argument, for callers that cannot
+ * allocate device memory (a host runtime that owns the device heap and
+ * forbids outside allocations, or a latency-critical thread where
+ * cudaMalloc/cudaFree could block).  No counterpart in the reference: it is
+ * an addition of this library.  Scratch is a fixed array inside the library
+ * (t2b_w4a16_gemm_noalloc_max_workspace() bytes, held on every GPU that loads
+ * it); larger workspace needs return T2B_ERR_WORKSPACE.  All calls share
+ * that array: calls that may overlap on the GPU race.  The first call on a
+ * device resolves the array's address; issue it before any stream capture.
+ */
+T2B_API size_t t2b_w4a16_gemm_noalloc_max_workspace(void);
+T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype,
+                                   void* y, int y_dtype, int M, int N, int K, int group_size, void* stream);
+
+/*
  * Fused attention input block for one decoder layer, one new token per row:
  *   xn = RMSNorm(x_resid; ssq, ln_w, eps)              (model.py:172-181)
  *   [q;k;v] = xn . Wqkv^T                              (model.py:248-250)

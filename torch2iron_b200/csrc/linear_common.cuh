@@ -187,5 +187,6 @@ T2B_DEV void maybe_clear_ssq(const LinearParams& p, bool designated) {
 // Host side: shared launch helpers (defined in w4a16_gemv.cu).
 int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t linear_workspace_bytes(int M, int N, int K);
+void linear_workspace_layout(int M, int N, int K, size_t* partial_bytes, size_t* counter_bytes);
 
 }  // namespace t2b

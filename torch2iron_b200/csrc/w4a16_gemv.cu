@@ -281,6 +281,20 @@ static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {
   return wfmt == T2B_WFMT_T2B && x_dtype != T2B_DTYPE_F16 && M >= tc_min_m() && tc_supported(M, N, K);
 }
 
+// Split of the CUDA-core path's workspace: fp32 partials, then the tile
+// counters (which must be zero before a call).  Zero sizes when the call
+// needs no workspace.
+void linear_workspace_layout(int M, int N, int K, size_t* partial_bytes, size_t* counter_bytes) {
+  *partial_bytes = 0;
+  *counter_bytes = 0;
+  if (M < 1 || N % TILE_N || K % 256 || gemv_ws_bytes(M, N, K) == 0) return;
+  const int MB = pick_mb(M);
+  const int mblocks = (M + MB - 1) / MB;
+  const int ksplit = K / pick_kslice(N, K, mblocks);
+  *partial_bytes = ((size_t)mblocks * ksplit * MB * N * sizeof(float) + 255) & ~size_t(255);
+  *counter_bytes = (((size_t)mblocks * (N / TILE_N) * sizeof(int) + 255) & ~size_t(255));
+}
+
 size_t linear_workspace_bytes(int M, int N, int K) {
   // the path is chosen per call from M; size for the larger so either fits
   const size_t a = gemv_ws_bytes(M, N, K);
