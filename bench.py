@@ -240,20 +240,20 @@ def kernel_profile(eng, steps):
             lw = eng.layers[li]
             H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
             rec("qkv_norm_rope_kvwrite", lambda: L.t2b_qkv_norm_rope_kvwrite(
-                p(lw.qkv.qw), p(lw.qkv.meta), p(eng.x), p(eng.ssq_a), p(lw.input_layernorm), cfg.rms_norm_eps,
+                p(lw.qkv.qw), p(lw.qkv.meta), p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps,
                 p(lw.q_norm), p(lw.k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[li]),
                 p(eng.v_cache[li]), p(eng.ssq_b), B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st))
             rec("decode_attention", lambda: L.t2b_decode_attention(
                 p(eng.q), p(eng.k_cache[li]), p(eng.v_cache[li]), p(eng.pos), p(eng.attn), B, nq, nkv, hd,
                 eng.max_ctx, *eng._ws("attn"), st))
             rec("oproj_residual", lambda: L.t2b_oproj_residual(
-                p(lw.o_proj.qw), p(lw.o_proj.meta), p(eng.attn), p(eng.x), p(eng.ssq_b), B, H, cfg.q_dim,
+                p(lw.o_proj.qw), p(lw.o_proj.meta), p(eng.attn), p(eng.x), p(eng.ssq_b), p(lw.post_attention_layernorm), p(eng.xw), B, H, cfg.q_dim,
                 *eng._ws("o"), st))
             rec("upgate_swiglu", lambda: L.t2b_upgate_swiglu(
-                p(lw.gate_up.qw), p(lw.gate_up.meta), p(eng.x), p(eng.ssq_b), p(lw.post_attention_layernorm),
+                p(lw.gate_up.qw), p(lw.gate_up.meta), p(eng.xw), p(eng.ssq_b),
                 cfg.rms_norm_eps, p(eng.h), p(eng.ssq_a), B, H, cfg.hidden_dim, *eng._ws("ug"), st))
             rec("down_residual", lambda: L.t2b_down_residual(
-                p(lw.down.qw), p(lw.down.meta), p(eng.h), p(eng.x), p(eng.ssq_a), B, H, cfg.hidden_dim,
+                p(lw.down.qw), p(lw.down.meta), p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(li)), p(eng.xw), B, H, cfg.hidden_dim,
                 *eng._ws("down"), st))
         rec("lm_head(cublas)", lambda: torch.mm(eng.xn, eng.lm_head.t(), out_dtype=torch.float32, out=eng.logits))
     torch.cuda.synchronize()

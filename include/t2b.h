@@ -107,23 +107,26 @@ T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int
 
 /*
  * Fused attention input block for one decoder layer, one new token per row:
- *   xn = RMSNorm(x_resid; ssq, ln_w, eps)              (model.py:172-181)
+ *   xn = RMSNorm(x) = (x * ln_w) * rsqrt(ssq/H + eps)  (model.py:172-181)
  *   [q;k;v] = xn . Wqkv^T                              (model.py:248-250)
  *   q,k = RMSNorm_head(q|k; q_norm_w|k_norm_w, eps)    (model.py:252-253; skipped if NULL)
  *   q,k = interleaved RoPE(angles[pos[m]])             (model.py:184-196)
  *   q_out[m] = q ; k_cache/v_cache[m][kv][pos[m]] = k, v   (model.py:256-264)
- * x_resid fp32 [M,H]; ssq fp32 [M] (sum of squares of each x_resid row);
+ * The RMSNorm input arrives split: xw bf16 [M,H] = bf16(x * ln_w) (written by
+ * the producer of x: t2b_embed_rows / t2b_down_residual) and ssq fp32 [M] =
+ * sum of x^2; the row scale is applied after the contraction.
  * angles fp32 [max_ctx, head_dim]; caches bf16 [M][n_kv][max_ctx][head_dim];
  * q_out bf16 [M][n_heads*head_dim].  ssq_clear (may be NULL): fp32 [M] zeroed.
  * Replaces RMSNorm + W4A16KGroupGEMM(q) + W4A16PairedKGroupGEMM(k,v) +
  * 2x RMSNormRoPE + CopyPresentPacketKV (batch_decode_fused.py:426-474).
  */
 T2B_API size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, int head_dim);
-T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const float* x_resid, const float* ssq,
-                              const uint16_t* ln_w, float eps, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
-                              const float* angles, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
-                              uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
-                              int head_dim, int max_ctx, void* workspace, size_t workspace_bytes, void* stream);
+T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq,
+                                      float eps, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                                      const float* angles, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
+                                      uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
+                                      int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
+                                      void* stream);
 
 /*
  * GQA decode attention, one query token per row, over the bf16 cache:
@@ -148,46 +151,51 @@ T2B_API int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, uint
                          void* stream);
 
 /*
- * x_resid[M,H] += attn[M,K] . Wo^T ; ssq_out[m] += sum_n x_resid[m,n]^2.
+ * x_resid[M,H] += attn[M,K] . Wo^T ; ssq_out[m] += sum_n x_resid[m,n]^2 ;
+ * xw_out = bf16(x_resid * next_norm_w) (both NULL to skip) -- the split
+ * RMSNorm input of the following block.
  * ssq_out must be zero before the call (zeroed by the preceding block's ssq_clear).
  * Replaces W4A16KGroupGEMM(o) + ResidualAddRMSNorm (batch_decode_fused.py:485-498).
  */
 T2B_API size_t t2b_oproj_residual_workspace_bytes(int M, int H, int K);
 T2B_API int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* attn, float* x_resid,
-                       float* ssq_out, int M, int H, int K, void* workspace, size_t workspace_bytes, void* stream);
+                               float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int K,
+                               void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * h[M,I] = silu(xn . Wg^T) * (xn . Wu^T), xn = RMSNorm(x_resid; ssq, ln_w, eps).
- * qw/meta hold gate/up interleaved in 64-row blocks (block b: gate rows
- * 64b..64b+63, then up rows 64b..64b+63).  ssq_clear as above.
+ * h[M,I] = silu(xn . Wg^T) * (xn . Wu^T), xn = RMSNorm(x) given as (xw, ssq)
+ * like t2b_qkv_norm_rope_kvwrite.  qw/meta hold gate/up interleaved in
+ * 64-row blocks (block b: gate rows 64b..64b+63, then up rows 64b..64b+63).
  * Replaces RMSNorm + W4A16PairedKGroupGEMM(gate,up) + SiLUMul
  * (batch_decode_fused.py:499-506, model.py:215-216).
  */
 T2B_API size_t t2b_upgate_swiglu_workspace_bytes(int M, int H, int I);
-T2B_API int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const float* x_resid, const float* ssq,
-                      const uint16_t* ln_w, float eps, uint16_t* h_out, float* ssq_clear, int M, int H, int I,
-                      void* workspace, size_t workspace_bytes, void* stream);
+T2B_API int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq,
+                              float eps, uint16_t* h_out, float* ssq_clear, int M, int H, int I, void* workspace,
+                              size_t workspace_bytes, void* stream);
 
 /*
- * x_resid[M,H] += h[M,I] . Wd^T ; ssq_out as for t2b_oproj_residual.
+ * x_resid[M,H] += h[M,I] . Wd^T ; ssq_out / xw_out as for t2b_oproj_residual.
  * Replaces W4A16KGroupGEMM(down) + ResidualAddRMSNorm (batch_decode_fused.py:507-530).
  */
 T2B_API size_t t2b_down_residual_workspace_bytes(int M, int H, int I);
-T2B_API int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* h, float* x_resid, float* ssq_out,
-                      int M, int H, int I, void* workspace, size_t workspace_bytes, void* stream);
+T2B_API int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* h, float* x_resid,
+                              float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int I,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * x_resid[m] = float(table[tokens[m]]) ; ssq_out[m] = sum x_resid[m]^2.
+ * x_resid[m] = float(table[tokens[m]]) ; ssq_out[m] = sum x_resid[m]^2 ;
+ * xw_out = bf16(x_resid * norm_w) (both NULL to skip).
  * Replaces the host-side embedding of qwen_npu.py:180-185 (model.py:469).
  */
-T2B_API int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* x_resid, float* ssq_out, int M, int H,
-                   int vocab, void* stream);
+T2B_API int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* x_resid, float* ssq_out,
+                           const uint16_t* norm_w, uint16_t* xw_out, int M, int H, int vocab, void* stream);
 
 /*
  * out[m] = bf16(RMSNorm(x_resid[m]; ssq, w, eps)) -- the final norm (model.py:409,477).
  */
-T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out, int M,
-                      int H, void* stream);
+T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out,
+                              int M, int H, void* stream);
 
 /*
  * Greedy pick: idx[m] = argmax_v logits[m, v] (lowest index on ties), logits

@@ -152,8 +152,7 @@ def _one_layer(cfg, batch, ctx, pos_list, seed):
 
 
 def _run_engine_layer(eng, x, pos):
-    eng.x.copy_(x.cuda())
-    eng.ssq_a.copy_((x.double() ** 2).sum(-1).float().cuda())
+    eng.set_hidden(x)
     eng.pos.copy_(pos.cuda())
     eng.enqueue_layer(0, _lib.stream())
     torch.cuda.synchronize()

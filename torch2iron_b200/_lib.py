@@ -35,17 +35,17 @@ SIGNATURES = {
     "t2b_w4a16_gemm_noalloc_max_workspace": (Z, []),
     "t2b_w4a16_gemm_noalloc": (I, [P, P, I, P, I, P, I, I, I, I, I, P]),
     "t2b_qkv_workspace_bytes": (Z, [I, I, I, I, I]),
-    "t2b_qkv_norm_rope_kvwrite": (I, [P, P, P, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_qkv_norm_rope_kvwrite": (I, [P, P, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_decode_attention_workspace_bytes": (Z, [I, I, I, I, I]),
     "t2b_decode_attention": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_packet_attention": (I, [P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_oproj_residual_workspace_bytes": (Z, [I, I, I]),
-    "t2b_oproj_residual": (I, [P, P, P, P, P, I, I, I, P, Z, P]),
+    "t2b_oproj_residual": (I, [P, P, P, P, P, P, P, I, I, I, P, Z, P]),
     "t2b_upgate_swiglu_workspace_bytes": (Z, [I, I, I]),
-    "t2b_upgate_swiglu": (I, [P, P, P, P, P, F, P, P, I, I, I, P, Z, P]),
+    "t2b_upgate_swiglu": (I, [P, P, P, P, F, P, P, I, I, I, P, Z, P]),
     "t2b_down_residual_workspace_bytes": (Z, [I, I, I]),
-    "t2b_down_residual": (I, [P, P, P, P, P, I, I, I, P, Z, P]),
-    "t2b_embed_rows": (I, [P, P, P, P, I, I, I, P]),
+    "t2b_down_residual": (I, [P, P, P, P, P, P, P, I, I, I, P, Z, P]),
+    "t2b_embed_rows": (I, [P, P, P, P, P, P, I, I, I, P]),
     "t2b_rms_norm_rows": (I, [P, P, P, F, P, I, I, P]),
     "t2b_argmax_workspace_bytes": (Z, [I, I]),
     "t2b_argmax_rows": (I, [P, I, I, I, I, P, P, Z, P]),

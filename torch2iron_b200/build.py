@@ -73,7 +73,7 @@ def build(force: bool = False, verbose_ptxas: bool = False, trace: bool = False)
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, extra, suffix), sources()))
     tmp = lib.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")

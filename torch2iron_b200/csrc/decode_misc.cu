@@ -9,10 +9,22 @@ namespace t2b {
 
 // ---------------------------------------------------------------------------
 // AutoGPTQ-v1 -> T2B tiled layout (see linear_common.cuh).  Word j of piece p
-// of row r in block (nt, g) is AutoGPTQ qweight word [g*16 + 4p + j, n]
-// unchanged (its 8 nibbles are q[n, k..k+7] in order, low nibble first);
-// meta packs the fp16 scale with zero = stored + 1 (packed_format.py:103-106).
+// of row r in block (nt, g) holds the 8 nibbles of AutoGPTQ qweight word
+// [g*16 + 4p + j, n] (q[n, k..k+7]) reordered even-k first: nibble slot t
+// holds k+2t for t < 4 and k+2(t-4)+1 for t >= 4, so (w >> 4t) & 0x000F000F
+// yields the adjacent pair (k+2t, k+2t+1).  Meta packs the fp16 scale with
+// zero = stored + 1 (packed_format.py:103-106).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t even_odd_nibbles(uint32_t w) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    r |= ((w >> (8 * t)) & 0xFu) << (4 * t);            // k = 2t
+    r |= ((w >> (8 * t + 4)) & 0xFu) << (4 * (t + 4));  // k = 2t+1
+  }
+  return r;
+}
+
 __device__ __forceinline__ int mapped_row(int n, int dst_row0, int block_rows, int block_stride) {
   return dst_row0 + (n / block_rows) * block_stride + n % block_rows;
 }
@@ -26,7 +38,7 @@ __global__ void repack_qweight_kernel(const int32_t* __restrict__ qweight, uint3
   const int nt = dst >> 7, r = dst & 127;
   const int g = k8 >> 4, pc = (k8 & 15) >> 2, j = k8 & 3;
   const size_t word = ((((size_t)nt * G + g) * 4 + pc) * 128 + r) * 4 + j;
-  qw[word] = (uint32_t)qweight[idx];
+  qw[word] = even_odd_nibbles((uint32_t)qweight[idx]);
 }
 
 __global__ void repack_meta_kernel(const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales,
@@ -60,7 +72,9 @@ int repack_autogptq(const int32_t* qweight, const int32_t* qzeros, const uint16_
 // squares for the first RMSNorm (model.py:469 then :179).
 // ---------------------------------------------------------------------------
 __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ tokens,
-                                  float* __restrict__ x, float* __restrict__ ssq, int H, int vocab, int* err) {
+                                  float* __restrict__ x, float* __restrict__ ssq,
+                                  const __nv_bfloat16* __restrict__ norm_w, __nv_bfloat16* __restrict__ xw, int H,
+                                  int vocab, int* err) {
   grid_dep_wait();
   grid_dep_launch();
   const int m = blockIdx.x;
@@ -73,6 +87,7 @@ __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, const
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     const float v = __bfloat162float(table[(size_t)tok * H + i]);
     x[(size_t)m * H + i] = v;
+    if (xw) xw[(size_t)m * H + i] = __float2bfloat16_rn(v * __bfloat162float(norm_w[i]));
     s += v * v;
   }
   __shared__ float red[32];
@@ -178,11 +193,13 @@ int argmax_rows(const void* logits, int dtype, int M, int V, int ld, int* idx, v
   return launch_pdl(argmax_rows_kernel, dim3(nch, M), dim3(AM_THREADS), 0, st, logits, dtype, V, ld, idx, wv, wi, cnt);
 }
 
-int embed_rows(const uint16_t* table, const int* tokens, float* x, float* ssq, int M, int H, int vocab, int* err,
-               cudaStream_t st) {
+int embed_rows(const uint16_t* table, const int* tokens, float* x, float* ssq, const uint16_t* norm_w, uint16_t* xw,
+               int M, int H, int vocab, int* err, cudaStream_t st) {
   if (M < 1 || H < 1) return T2B_ERR_SHAPE;
   const __nv_bfloat16* t = reinterpret_cast<const __nv_bfloat16*>(table);
-  return launch_pdl(embed_rows_kernel, dim3(M), dim3(256), 0, st, t, tokens, x, ssq, H, vocab, err);
+  const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(xw);
+  return launch_pdl(embed_rows_kernel, dim3(M), dim3(256), 0, st, t, tokens, x, ssq, w, o, H, vocab, err);
 }
 
 int rms_norm_rows(const float* x, const float* ssq, const uint16_t* w, float eps, uint16_t* out, int M, int H,
@@ -380,10 +397,11 @@ extern "C" int t2b_repack_autogptq(const int32_t* qweight, const int32_t* qzeros
                          S_(stream));
 }
 
-extern "C" int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* x_resid, float* ssq_out, int M,
-                              int H, int vocab, void* stream) {
+extern "C" int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* x_resid, float* ssq_out,
+                              const uint16_t* norm_w, uint16_t* xw_out, int M, int H, int vocab, void* stream) {
   if (!table || !tokens || !x_resid || !ssq_out) return T2B_ERR_ARG;
-  return embed_rows(table, tokens, x_resid, ssq_out, M, H, vocab, nullptr, S_(stream));
+  if ((norm_w == nullptr) != (xw_out == nullptr)) return T2B_ERR_ARG;
+  return embed_rows(table, tokens, x_resid, ssq_out, norm_w, xw_out, M, H, vocab, nullptr, S_(stream));
 }
 
 extern "C" int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out,

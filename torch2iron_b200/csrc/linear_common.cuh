@@ -5,14 +5,17 @@
 // T2B weight layout (one [N, K] linear, group 128, N % 128 == 0):
 //   qw   block (nt, g) = 128 rows x 128 k = 8192 bytes at ((nt*G + g) * 8192);
 //        inside a block, piece p (k 32p..32p+31) of row r is 16 bytes at
-//        p*2048 + r*16: four little-endian words, word j nibble i = q[k = 32p+8j+i]
-//        (unsigned AutoGPTQ nibbles -- word j of piece p IS AutoGPTQ qweight
-//        word [g*16 + 4p + j, n]).
+//        p*2048 + r*16: four little-endian words; word j covers k0 = 32p+8j and
+//        holds unsigned AutoGPTQ nibbles even-k first: nibble slot t = q[k0+2t]
+//        for t < 4, q[k0+2(t-4)+1] for t >= 4.  So (w >> 4t) & 0x000F000F puts
+//        the adjacent pair (k0+2t, k0+2t+1) in the two 16-bit halves.
 //   meta block (nt, g) = 128 uint32 at ((nt*G + g) * 128): fp16 scale | zero << 16.
 // One block is one contiguous 8 KB + 512 B pair, so a (128-row tile, group)
 // stage is a single bulk copy, and a warp reading one piece of 32 rows reads
 // 512 contiguous bytes.
 #pragma once
+
+#include <cuda.h>
 
 #include "t2b_common.cuh"
 
@@ -26,15 +29,15 @@ constexpr int GROUP = 128;           // quantization group along K
 constexpr int BLOCK_BYTES = TILE_N * GROUP / 2;
 
 struct LinearParams {
+  CUtensorMap xmap;       // tcgen05 path: 2-D tiled map of x (bf16 [M][K]), 64 x BP box, 128B swizzle
   const uint8_t* qw;      // T2B: tiled blocks; QPARAM: [N][K/2 + 2G] rows
   const uint32_t* meta;   // T2B meta blocks
   int w_ld;               // QPARAM bytes per row
   int N, K, G;
   const void* x;          // activations [M][x_ld]
   int x_dtype, x_ld;
-  const float* ssq;       // PRO_RMSNORM: sum of squares per row
-  const __nv_bfloat16* norm_w;
-  float eps;
+  const float* ssq;       // PRO_RMSNORM: sum of squares of the un-normalised row
+  float eps;              // PRO_RMSNORM: x is bf16(row * norm weight); y *= rsqrt(ssq/K + eps)
   int M, kslice, ksplit;  // kslice: k per CTA (multiple of 128)
   float* ws_part;         // [mblocks][ksplit][MB][N]
   int* ws_cnt;            // [mblocks][N/128]
@@ -42,6 +45,8 @@ struct LinearParams {
   int y_dtype, y_ld;
   float* resid;           // EPI_RESIDUAL fp32 [M][y_ld]
   float* ssq_out;
+  const __nv_bfloat16* next_w;  // EPI_RESIDUAL: next RMSNorm weight [N] (nullable)
+  __nv_bfloat16* xw_out;        // EPI_RESIDUAL: bf16(resid * next_w) [M][y_ld] (nullable)
   float* ssq_clear;
   const __nv_bfloat16* qn_w;
   const __nv_bfloat16* kn_w;
@@ -96,17 +101,19 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
       if (m < p.M) store_act(p.y, p.y_dtype, (size_t)m * p.y_ld + row0 + lr, tile_acc[idx]);
     }
   } else if (EPI == EPI_RESIDUAL) {
-    // each warp's 32 elements share one batch row -> one atomic per warp per pass
+    // x += y ; sum of squares for the next RMSNorm ; bf16(x * w_next) for its GEMM.
+    // Each warp's 32 elements share one batch row -> one atomic per warp per pass.
     for (int base = 0; base < MB * TILE_N; base += NT) {
       const int idx = base + threadIdx.x;
       const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
       const bool live = idx < MB * TILE_N && m < p.M;
       float sq = 0.f;
       if (live) {
-        float* xr = p.resid + (size_t)m * p.y_ld + row0 + lr;
-        const float v = *xr + tile_acc[idx];
-        *xr = v;
+        const size_t o = (size_t)m * p.y_ld + row0 + lr;
+        const float v = p.resid[o] + tile_acc[idx];
+        p.resid[o] = v;
         sq = v * v;
+        if (p.xw_out) p.xw_out[o] = __float2bfloat16_rn(v * __bfloat162float(p.next_w[row0 + lr]));
       }
       sq = warp_sum(sq);
       if (lane == 0 && live) atomicAdd(p.ssq_out + m, sq);

@@ -103,9 +103,8 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
       if (PRO == PRO_ACT) {
         v = load_act(p.x, p.x_dtype, (size_t)m * p.x_ld + k0 + kk);
       } else {
-        // model.py:179-181: x * rsqrt(mean(x^2)+eps), then * weight; A16 -> bf16
-        const float xv = reinterpret_cast<const float*>(p.x)[(size_t)m * p.x_ld + k0 + kk];
-        v = round_bf16((xv * scratch[b]) * __bfloat162float(p.norm_w[k0 + kk]));
+        // model.py:179-181: x holds bf16(row * weight); times rsqrt(mean(row^2)+eps)
+        v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.x)[(size_t)m * p.x_ld + k0 + kk]) * scratch[b];
       }
     }
     xs[b * S::XS_LD + kk + (kk >> 5) * 4] = v;
@@ -144,14 +143,25 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
         const uint32_t w = wd == 0 ? wv[c][i].x : wd == 1 ? wv[c][i].y : wd == 2 ? wv[c][i].z : wv[c][i].w;
         const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
         // (128+q)*s - (128+z)*s is exact in fp32: (q - z) * s
-        wf[i][0] = fmaf(nib_f(lo, 0x7054), sc[i], zc[i]);
-        wf[i][1] = fmaf(nib_f(hi, 0x7054), sc[i], zc[i]);
-        wf[i][2] = fmaf(nib_f(lo, 0x7154), sc[i], zc[i]);
-        wf[i][3] = fmaf(nib_f(hi, 0x7154), sc[i], zc[i]);
-        wf[i][4] = fmaf(nib_f(lo, 0x7254), sc[i], zc[i]);
-        wf[i][5] = fmaf(nib_f(hi, 0x7254), sc[i], zc[i]);
-        wf[i][6] = fmaf(nib_f(lo, 0x7354), sc[i], zc[i]);
-        wf[i][7] = fmaf(nib_f(hi, 0x7354), sc[i], zc[i]);
+        if (WFMT == T2B_WFMT_T2B) {  // nibble slots hold k 0,2,4,6,1,3,5,7
+          wf[i][0] = fmaf(nib_f(lo, 0x7054), sc[i], zc[i]);
+          wf[i][2] = fmaf(nib_f(hi, 0x7054), sc[i], zc[i]);
+          wf[i][4] = fmaf(nib_f(lo, 0x7154), sc[i], zc[i]);
+          wf[i][6] = fmaf(nib_f(hi, 0x7154), sc[i], zc[i]);
+          wf[i][1] = fmaf(nib_f(lo, 0x7254), sc[i], zc[i]);
+          wf[i][3] = fmaf(nib_f(hi, 0x7254), sc[i], zc[i]);
+          wf[i][5] = fmaf(nib_f(lo, 0x7354), sc[i], zc[i]);
+          wf[i][7] = fmaf(nib_f(hi, 0x7354), sc[i], zc[i]);
+        } else {  // reference qparam: natural order, low nibble = even k
+          wf[i][0] = fmaf(nib_f(lo, 0x7054), sc[i], zc[i]);
+          wf[i][1] = fmaf(nib_f(hi, 0x7054), sc[i], zc[i]);
+          wf[i][2] = fmaf(nib_f(lo, 0x7154), sc[i], zc[i]);
+          wf[i][3] = fmaf(nib_f(hi, 0x7154), sc[i], zc[i]);
+          wf[i][4] = fmaf(nib_f(lo, 0x7254), sc[i], zc[i]);
+          wf[i][5] = fmaf(nib_f(hi, 0x7254), sc[i], zc[i]);
+          wf[i][6] = fmaf(nib_f(lo, 0x7354), sc[i], zc[i]);
+          wf[i][7] = fmaf(nib_f(hi, 0x7354), sc[i], zc[i]);
+        }
       }
 #pragma unroll
       for (int b = 0; b < MB; ++b) {
@@ -278,7 +288,7 @@ static int tc_min_m() {
 }
 
 static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {
-  return wfmt == T2B_WFMT_T2B && x_dtype != T2B_DTYPE_F16 && M >= tc_min_m() && tc_supported(M, N, K);
+  return wfmt == T2B_WFMT_T2B && x_dtype == T2B_DTYPE_BF16 && M >= tc_min_m() && tc_supported(M, N, K);
 }
 
 // Split of the CUDA-core path's workspace: fp32 partials, then the tile
@@ -306,8 +316,7 @@ int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t 
   if (p.M < 1 || p.N <= 0 || p.K <= 0) return T2B_ERR_SHAPE;
   if (p.N % TILE_N || p.K % 256) return T2B_ERR_SHAPE;
   p.G = p.K / GROUP;
-  const int xdt = (pro == PRO_RMSNORM) ? T2B_DTYPE_F32 : p.x_dtype;
-  if (use_tc(p.M, p.N, p.K, wfmt, xdt)) return tc_launch(p, pro, epi, ws, ws_bytes, st);
+  if (use_tc(p.M, p.N, p.K, wfmt, p.x_dtype)) return tc_launch(p, pro, epi, ws, ws_bytes, st);
   return gemv_launch(p, pro, epi, wfmt, ws, ws_bytes, st);
 }
 
@@ -369,25 +378,23 @@ extern "C" size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, i
   return linear_workspace_bytes(M, (n_heads + 2 * n_kv) * head_dim, H);
 }
 
-extern "C" int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const float* x_resid,
-                                         const float* ssq, const uint16_t* ln_w, float eps, const uint16_t* q_norm_w,
+extern "C" int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
+                                         const float* ssq, float eps, const uint16_t* q_norm_w,
                                          const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
                                          uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, float* ssq_clear,
                                          int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
                                          size_t ws_bytes, void* stream) {
   if (head_dim != 64 && head_dim != 128) return T2B_ERR_SHAPE;
   if (n_kv < 1 || n_heads % n_kv || max_ctx < 1) return T2B_ERR_SHAPE;
-  if (!qw || !meta || !x_resid || !ssq || !ln_w || !angles || !pos || !q_out || !k_cache || !v_cache)
-    return T2B_ERR_ARG;
+  if (!qw || !meta || !xw || !ssq || !angles || !pos || !q_out || !k_cache || !v_cache) return T2B_ERR_ARG;
   if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return T2B_ERR_ARG;
-  if (!al(qw, 16)) return T2B_ERR_ALIGN;
+  if (!al(qw, 16) || !al(xw, 16)) return T2B_ERR_ALIGN;
   const int N = (n_heads + 2 * n_kv) * head_dim;
   LinearParams p = gemv_base(qw, meta, H / 2, M, N, H);
-  p.x = x_resid;
-  p.x_dtype = T2B_DTYPE_F32;
+  p.x = xw;
+  p.x_dtype = T2B_DTYPE_BF16;
   p.x_ld = H;
   p.ssq = ssq;
-  p.norm_w = reinterpret_cast<const __nv_bfloat16*>(ln_w);
   p.eps = eps;
   p.y = q_out;
   p.y_ld = n_heads * head_dim;
@@ -411,9 +418,11 @@ extern "C" size_t t2b_oproj_residual_workspace_bytes(int M, int H, int K) {
 }
 
 extern "C" int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* attn, float* x_resid,
-                                  float* ssq_out, int M, int H, int K, void* ws, size_t ws_bytes, void* stream) {
+                                  float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int K,
+                                  void* ws, size_t ws_bytes, void* stream) {
   if (!qw || !meta || !attn || !x_resid || !ssq_out) return T2B_ERR_ARG;
-  if (!al(qw, 16)) return T2B_ERR_ALIGN;
+  if ((next_norm_w == nullptr) != (xw_out == nullptr)) return T2B_ERR_ARG;
+  if (!al(qw, 16) || !al(attn, 16)) return T2B_ERR_ALIGN;
   LinearParams p = gemv_base(qw, meta, K / 2, M, H, K);
   p.x = attn;
   p.x_dtype = T2B_DTYPE_BF16;
@@ -421,6 +430,8 @@ extern "C" int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const
   p.resid = x_resid;
   p.y_ld = H;
   p.ssq_out = ssq_out;
+  p.next_w = reinterpret_cast<const __nv_bfloat16*>(next_norm_w);
+  p.xw_out = reinterpret_cast<__nv_bfloat16*>(xw_out);
   return linear_launch(p, PRO_ACT, EPI_RESIDUAL, T2B_WFMT_T2B, ws, ws_bytes, S_(stream));
 }
 
@@ -429,18 +440,17 @@ extern "C" size_t t2b_upgate_swiglu_workspace_bytes(int M, int H, int I) {
   return linear_workspace_bytes(M, 2 * I, H);
 }
 
-extern "C" int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const float* x_resid, const float* ssq,
-                                 const uint16_t* ln_w, float eps, uint16_t* h_out, float* ssq_clear, int M, int H,
-                                 int I, void* ws, size_t ws_bytes, void* stream) {
+extern "C" int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq,
+                                 float eps, uint16_t* h_out, float* ssq_clear, int M, int H, int I, void* ws,
+                                 size_t ws_bytes, void* stream) {
   if (I % 64) return T2B_ERR_SHAPE;
-  if (!qw || !meta || !x_resid || !ssq || !ln_w || !h_out) return T2B_ERR_ARG;
-  if (!al(qw, 16)) return T2B_ERR_ALIGN;
+  if (!qw || !meta || !xw || !ssq || !h_out) return T2B_ERR_ARG;
+  if (!al(qw, 16) || !al(xw, 16)) return T2B_ERR_ALIGN;
   LinearParams p = gemv_base(qw, meta, H / 2, M, 2 * I, H);
-  p.x = x_resid;
-  p.x_dtype = T2B_DTYPE_F32;
+  p.x = xw;
+  p.x_dtype = T2B_DTYPE_BF16;
   p.x_ld = H;
   p.ssq = ssq;
-  p.norm_w = reinterpret_cast<const __nv_bfloat16*>(ln_w);
   p.eps = eps;
   p.y = h_out;
   p.y_ld = I;
@@ -454,8 +464,9 @@ extern "C" size_t t2b_down_residual_workspace_bytes(int M, int H, int I) {
 }
 
 extern "C" int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* h, float* x_resid,
-                                 float* ssq_out, int M, int H, int I, void* ws, size_t ws_bytes, void* stream) {
-  return t2b_oproj_residual(qw, meta, h, x_resid, ssq_out, M, H, I, ws, ws_bytes, stream);
+                                 float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int I,
+                                 void* ws, size_t ws_bytes, void* stream) {
+  return t2b_oproj_residual(qw, meta, h, x_resid, ssq_out, next_norm_w, xw_out, M, H, I, ws, ws_bytes, stream);
 }
 
 T2B_TRACE_DUMP_FN(t2b_trace_dump_gemv)

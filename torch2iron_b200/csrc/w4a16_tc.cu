@@ -111,14 +111,14 @@ __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
 struct TcLayout {
   int x_group, off_raw, off_meta, off_tile, off_xsum, off_scr, off_bar, off_tmem, off_flag, bytes;
   __host__ __device__ TcLayout(int BP, int S) {
-    x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group
+    x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group (TMA, 128B swizzle)
     off_raw = S * x_group;                   // [S][8 KB] raw int4 blocks
     off_meta = off_raw + S * BLOCK_BYTES;    // [S][128] meta words
     off_tile = off_meta + S * TILE_N * 4;    // fp32 [BP][128] partial tile
     off_xsum = off_tile + BP * TILE_N * 4;   // fp32 [S][BP] per-group activation sums
-    off_scr = off_xsum + S * BP * 4;         // fp32 [8*BP] scratch
-    off_bar = off_scr + 8 * BP * 4;          // raw_full[S], a_full[2], a_empty[2], acc_full
-    off_tmem = off_bar + (S + 5) * 8;
+    off_scr = off_xsum + S * BP * 4;         // fp32 [8*BP] scratch (row scales, epilogue)
+    off_bar = off_scr + 8 * BP * 4;          // raw_full[S], a_full[2], a_empty[2], acc_full, x_full
+    off_tmem = off_bar + (S + 6) * 8;
     off_flag = off_tmem + 8;
     bytes = off_flag + 8 + 1024;             // + slack to 1024-align the base
   }
@@ -127,48 +127,20 @@ struct TcLayout {
 constexpr uint32_t A_COL = 0;      // two 64-column A stages
 constexpr uint32_t ACC_COL = 128;  // S accumulators of BP columns each
 
-T2B_DEV uint32_t pack_bf16x2(float lo, float hi) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-// One 8-k activation chunk: bf16 values (as fp32) of batch row m, k..k+7.
-template <int PRO>
-T2B_DEV void load_x8(const LinearParams& p, int m, int k, float r, float (&v)[8]) {
-  if (PRO == PRO_RMSNORM) {
-    const float* xr = reinterpret_cast<const float*>(p.x) + (size_t)m * p.x_ld + k;
-    const float4 a0 = *reinterpret_cast<const float4*>(xr);
-    const float4 a1 = *reinterpret_cast<const float4*>(xr + 4);
-    const uint4 wn = *reinterpret_cast<const uint4*>(p.norm_w + k);
-    const float xv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const uint32_t ww[4] = {wn.x, wn.y, wn.z, wn.w};
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float w = (e & 1) ? __uint_as_float(ww[e >> 1] & 0xffff0000u) : __uint_as_float(ww[e >> 1] << 16);
-      v[e] = round_bf16((xv[e] * r) * w);  // model.py:179-181, A16
-    }
-  } else if (p.x_dtype == T2B_DTYPE_BF16) {
-    const uint4 xb =
-        *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + (size_t)m * p.x_ld + k);
-    const uint32_t ww[4] = {xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      v[e] = (e & 1) ? __uint_as_float(ww[e >> 1] & 0xffff0000u) : __uint_as_float(ww[e >> 1] << 16);
-  } else {  // fp32 activations rounded to bf16
-    const float* xr = reinterpret_cast<const float*>(p.x) + (size_t)m * p.x_ld + k;
-    const float4 a0 = *reinterpret_cast<const float4*>(xr);
-    const float4 a1 = *reinterpret_cast<const float4*>(xr + 4);
-    const float xv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = round_bf16(xv[e]);
-  }
+// 2-D tiled TMA load (no multicast): box of `tmap` at (x, y) -> smem, tx bytes on bar.
+T2B_DEV void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // grid (N/128, KS, mblocks), cluster (1, KS, 1): the KS CTAs of a cluster are
 // the k-splits of one 128-row tile (S groups each); their partial tiles are
 // summed through distributed shared memory, each CTA finishing BP/KS rows.
 template <int BP, int PRO, int EPI>
-__global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) {
+__global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant__ LinearParams p) {
   const int S = p.kslice / GROUP;
   const int KS = p.ksplit;
   const TcLayout L(BP, S);
@@ -180,11 +152,13 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
   float* tile_acc = reinterpret_cast<float*>(sm + L.off_tile);
   float* xsum = reinterpret_cast<float*>(sm + L.off_xsum);
   float* scratch = reinterpret_cast<float*>(sm + L.off_scr);
+  float* rowscale = scratch + 4 * BP;  // [BP]; scratch[0..2*BP) is the epilogue's
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.off_bar);
   uint64_t* raw_full = bars;
   uint64_t* a_full = bars + S;
   uint64_t* a_empty = bars + S + 2;
   uint64_t* acc_full = bars + S + 4;
+  uint64_t* x_full = bars + S + 5;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.off_tmem);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.off_flag);
 
@@ -203,6 +177,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
     mbar_init(&a_empty[0], 1);
     mbar_init(&a_empty[1], 1);
     mbar_init(acc_full, 1);
+    mbar_init(x_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -221,67 +196,34 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
   grid_dep_launch();
   T2B_TRACE_MARK(1);
 
+  // activations: one 64-k x BP-row box per (group, 64-k atom), swizzled by TMA
+  // into the UMMA K-major layout; rows past M arrive as zeros.
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(x_full, (uint32_t)(S * L.x_group));
+    for (int gl = 0; gl < S; ++gl)
+      for (int atom = 0; atom < 2; ++atom)
+        tma_load_2d(xs + gl * L.x_group + atom * (BP * 128), &p.xmap, (g0 + gl) * GROUP + atom * 64, m0, x_full);
+  }
   // TMEM is taken only after the wait: a dependent grid parked on its own
   // wait never holds columns this grid still needs.
   if (warp == 4) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
-
-  // ---- X tile: bf16, 128B-swizzled K-major, k permuted 0,4,1,5,2,6,3,7 ----
-  if (PRO == PRO_RMSNORM) {
-    for (int b = threadIdx.x; b < BP; b += 256) {
-      const int m = m0 + b;
-      scratch[b] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;
-    }
-    __syncthreads();
+  if (PRO == PRO_RMSNORM && threadIdx.x >= 128 && threadIdx.x < 128 + BP) {
+    const int b = threadIdx.x - 128, m = m0 + b;
+    rowscale[b] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;   // model.py:179-180
   }
-  {
-    constexpr int UNR = 4;
-    const int total = S * BP * 16;  // (group, row, 8-k chunk) tasks; a multiple of 256
-    for (int t0 = threadIdx.x; t0 < total; t0 += 256 * UNR) {
-      float v[UNR][8];
-#pragma unroll
-      for (int u = 0; u < UNR; ++u) {
-        const int t = t0 + u * 256;
-        const int c16 = t & 15, gb = t >> 4;
-        const int gl = gb / BP, b = gb - gl * BP;
-        const int m = m0 + b;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[u][e] = 0.f;
-        if (t < total && m < p.M) load_x8<PRO>(p, m, (g0 + gl) * GROUP + c16 * 8, scratch[b < BP ? b : 0], v[u]);
-      }
-#pragma unroll
-      for (int u = 0; u < UNR; ++u) {
-        const int t = t0 + u * 256;
-        if (t >= total) break;  // warp-uniform: total is a multiple of 256
-        const int c16 = t & 15, gb = t >> 4;
-        const int gl = gb / BP, b = gb - gl * BP;
-        const uint4 packed = make_uint4(pack_bf16x2(v[u][0], v[u][4]), pack_bf16x2(v[u][1], v[u][5]),
-                                        pack_bf16x2(v[u][2], v[u][6]), pack_bf16x2(v[u][3], v[u][7]));
-        const int atom = c16 >> 3, cc = c16 & 7;
-        *reinterpret_cast<uint4*>(xs + gl * L.x_group + atom * (BP * 128) + b * 128 + ((cc ^ (b & 7)) << 4)) =
-            packed;
-        float sum = ((v[u][0] + v[u][1]) + (v[u][2] + v[u][3])) + ((v[u][4] + v[u][5]) + (v[u][6] + v[u][7]));
-        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        if (c16 == 0) xsum[gl * BP + b] = sum;
-      }
-    }
-  }
-  fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
   maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  constexpr uint32_t IDESC = idesc_bf16(TILE_N, BP);
   T2B_TRACE_MARK(2);
+  constexpr uint32_t IDESC = idesc_bf16(TILE_N, BP);
 
   if (warp < 4) {
-    // ---- producers: row r's nibbles -> bf16x2 (128+q) -> TMEM lane r ----
+    // ---- producers: row r's nibbles -> bf16x2 (128+q) pairs -> TMEM lane r ----
     const int r = warp * 32 + lane;
     const uint32_t lane_base = tbase + ((uint32_t)(warp * 32) << 16);
     for (int gl = 0; gl < S; ++gl) {
@@ -300,6 +242,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
         uint32_t cols[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
+          // slot t holds k 2t, slot t+4 holds k 2t+1: each mask-or is the pair (2t, 2t+1)
           cols[4 * j + 0] = (w[j] & 0x000F000Fu) | 0x43004300u;
           cols[4 * j + 1] = ((w[j] >> 4) & 0x000F000Fu) | 0x43004300u;
           cols[4 * j + 2] = ((w[j] >> 8) & 0x000F000Fu) | 0x43004300u;
@@ -313,27 +256,57 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
       if (lane == 0) mbar_arrive(&a_full[stage]);
     }
     T2B_TRACE_MARK(3);
-  } else if (warp == 4 && lane == 0) {
-    // ---- MMA issuer ----
-    for (int gl = 0; gl < S; ++gl) {
-      const int stage = gl & 1;
-      if (!mbar_wait_bounded(&a_full[stage], (gl >> 1) & 1, p.err)) {
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t xg = smem_u32(xs + gl * L.x_group);
+  } else if (warp == 4) {
+    // ---- MMA issuer (one lane) ----
+    if (lane == 0) {
+      bool ok = mbar_wait_bounded(x_full, 0, p.err);
+      for (int gl = 0; ok && gl < S; ++gl) {
+        const int stage = gl & 1;
+        if (!mbar_wait_bounded(&a_full[stage], (gl >> 1) & 1, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xg = smem_u32(xs + gl * L.x_group);
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint64_t bdesc = sdesc_sw128(xg + (ks >> 2) * (BP * 128) + (ks & 3) * 32);
-        mma_ts(tbase + ACC_COL + gl * BP, tbase + A_COL + stage * 64 + ks * 8, bdesc, IDESC, ks > 0);
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t bdesc = sdesc_sw128(xg + (ks >> 2) * (BP * 128) + (ks & 3) * 32);
+          mma_ts(tbase + ACC_COL + gl * BP, tbase + A_COL + stage * 64 + ks * 8, bdesc, IDESC, ks > 0);
+        }
+        mma_commit(&a_empty[stage]);
       }
-      mma_commit(&a_empty[stage]);
+      if (!ok) *abort_flag = 1;
+      mma_commit(acc_full);
     }
-    mma_commit(acc_full);
+    __syncwarp();
+  } else {
+    // ---- warps 5-7: per-(group, row) activation sums from the swizzled X tile ----
+    const bool ok = mbar_wait_bounded(x_full, 0, p.err);
+    if (!ok) *abort_flag = 1;
+    const int total = S * BP * 16;  // (group, row, 16-byte chunk); 16 lanes per (group, row)
+    for (int t = threadIdx.x - 160; t < ((total + 95) / 96) * 96; t += 96) {
+      float sum = 0.f;
+      const int c16 = t & 15, gb = t >> 4;
+      if (ok && t < total) {
+        const int gl = gb / BP, b = gb - gl * BP;
+        const int atom = c16 >> 3, cc = c16 & 7;
+        const uint4 v =
+            *reinterpret_cast<const uint4*>(xs + gl * L.x_group + atom * (BP * 128) + b * 128 + ((cc ^ (b & 7)) << 4));
+        const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sum += __uint_as_float(ww[e] << 16) + __uint_as_float(ww[e] & 0xffff0000u);
+      }
+      // lanes 16j..16j+15 of a warp hold one (group, row) when 96 divides 16: reduce over 16 lanes
+      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      if (c16 == 0 && t < total) xsum[gb] = sum;
+    }
   }
+  __syncthreads();  // xsum complete; every role past its loop
 
-  // ---- drain: y[b] = sum_g s_g * (P_g[b] - (128+z_g) * xsum_g[b]) ----
+  // ---- drain: y[b] = r_b * sum_g s_g * (P_g[b] - (128+z_g) * xsum_g[b]) ----
   // warps w and w+4 share TMEM lane quarter w%4 and split the BP columns.
   {
     constexpr int HB = BP / 2;
@@ -366,7 +339,10 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const LinearParams p) 
       }
     }
 #pragma unroll
-    for (int b = 0; b < HB; ++b) tile_acc[(half * HB + b) * TILE_N + r] = y[b];
+    for (int b = 0; b < HB; ++b) {
+      const float v = (PRO == PRO_RMSNORM) ? y[b] * rowscale[half * HB + b] : y[b];
+      tile_acc[(half * HB + b) * TILE_N + r] = v;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -469,10 +445,47 @@ static int tc_dispatch(LinearParams& p, const TcPlan& pl, cudaStream_t st) {
   return T2B_ERR_ARG;
 }
 
+// cuTensorMapEncodeTiled, resolved through the runtime (no link-time libcuda
+// dependency, so the library loads on hosts without a driver).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// 2-D tiled tensor map over the bf16 activations [M][x_ld]: box 64 k x BP rows,
+// 128-byte swizzle (the UMMA K-major canonical layout); out-of-range rows read 0.
+static int make_x_map(LinearParams& p, int BP) {
+  if (reinterpret_cast<uintptr_t>(p.x) & 15) return T2B_ERR_ALIGN;
+  if ((p.x_ld * 2) % 16) return T2B_ERR_ALIGN;
+  cuuint64_t dims[2] = {(cuuint64_t)p.K, (cuuint64_t)p.M};
+  cuuint64_t strides[1] = {(cuuint64_t)p.x_ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)BP};
+  cuuint32_t estr[2] = {1, 1};
+  const EncodeTiledFn encode = encode_tiled();
+  if (encode == nullptr) return T2B_ERR_LAUNCH;
+  CUresult r = encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p.x), dims,
+                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? T2B_OK : T2B_ERR_ARG;
+}
+
 int tc_launch(LinearParams& p, int pro, int epi, void*, size_t, cudaStream_t st) {
   const TcPlan pl = tc_plan(p.M, p.N, p.K);
   if (!pl.ok) return T2B_ERR_SHAPE;
-  if (p.x_dtype == T2B_DTYPE_F16 && pro == PRO_ACT) return T2B_ERR_ARG;
+  if (p.x_dtype != T2B_DTYPE_BF16) return T2B_ERR_ARG;
+  const int mx = make_x_map(p, pl.BP);
+  if (mx != T2B_OK) return mx;
   p.kslice = pl.S * GROUP;
   p.ksplit = pl.KS;
   if (pro == PRO_ACT && epi == EPI_STORE) return tc_dispatch<PRO_ACT, EPI_STORE>(p, pl, st);

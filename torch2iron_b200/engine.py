@@ -99,6 +99,7 @@ class DecodeEngine:
         B, H, hd = batch, cfg.emb_dim, cfg.head_dim
         f32, bf = torch.float32, torch.bfloat16
         self.x = torch.zeros(B, H, dtype=f32, device=dev)
+        self.xw = torch.zeros(B, H, dtype=bf, device=dev)        # bf16(x * next norm weight)
         self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
         self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
         self.q = torch.zeros(B, cfg.q_dim, dtype=bf, device=dev)
@@ -151,6 +152,10 @@ class DecodeEngine:
         t, n = self.ws[k]
         return _lib.ptr(t), n
 
+    def next_norm_weight(self, li: int) -> torch.Tensor:
+        """Weight of the RMSNorm that follows layer li's MLP (next layer's input norm, or the final norm)."""
+        return self.layers[li + 1].input_layernorm if li + 1 < len(self.layers) else self.final_norm
+
     def enqueue_layer(self, li: int, st: int) -> None:
         cfg, B = self.cfg, self.B
         H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
@@ -158,21 +163,21 @@ class DecodeEngine:
         lw = self.layers[li]
         p = _lib.ptr
         _lib.check("t2b_qkv_norm_rope_kvwrite", L.t2b_qkv_norm_rope_kvwrite(
-            p(lw.qkv.qw), p(lw.qkv.meta), p(self.x), p(self.ssq_a), p(lw.input_layernorm), cfg.rms_norm_eps,
+            p(lw.qkv.qw), p(lw.qkv.meta), p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
             p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
         _lib.check("t2b_decode_attention", L.t2b_decode_attention(
             p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), B, nq, nkv, hd,
             self.max_ctx, *self._ws("attn"), st))
         _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
-            p(lw.o_proj.qw), p(lw.o_proj.meta), p(self.attn), p(self.x), p(self.ssq_b), B, H, cfg.q_dim,
-            *self._ws("o"), st))
+            p(lw.o_proj.qw), p(lw.o_proj.meta), p(self.attn), p(self.x), p(self.ssq_b),
+            p(lw.post_attention_layernorm), p(self.xw), B, H, cfg.q_dim, *self._ws("o"), st))
         _lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
-            p(lw.gate_up.qw), p(lw.gate_up.meta), p(self.x), p(self.ssq_b), p(lw.post_attention_layernorm),
-            cfg.rms_norm_eps, p(self.h), p(self.ssq_a), B, H, cfg.hidden_dim, *self._ws("ug"), st))
+            p(lw.gate_up.qw), p(lw.gate_up.meta), p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
+            p(self.ssq_a), B, H, cfg.hidden_dim, *self._ws("ug"), st))
         _lib.check("t2b_down_residual", L.t2b_down_residual(
-            p(lw.down.qw), p(lw.down.meta), p(self.h), p(self.x), p(self.ssq_a), B, H, cfg.hidden_dim,
-            *self._ws("down"), st))
+            p(lw.down.qw), p(lw.down.meta), p(self.h), p(self.x), p(self.ssq_a), p(self.next_norm_weight(li)),
+            p(self.xw), B, H, cfg.hidden_dim, *self._ws("down"), st))
 
     def enqueue_step(self) -> None:
         """Enqueue one full decode step on the current stream (tokens/pos already on device)."""
@@ -180,7 +185,8 @@ class DecodeEngine:
         L = _lib.lib()
         st = _lib.stream()
         p = _lib.ptr
-        _lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a), B,
+        _lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a),
+                                                      p(self.layers[0].input_layernorm), p(self.xw), B,
                                                       cfg.emb_dim, cfg.vocab_size, st))
         for li in range(cfg.n_layers):
             self.enqueue_layer(li, st)
@@ -189,6 +195,12 @@ class DecodeEngine:
         torch.mm(self.xn, self.lm_head.t(), out_dtype=torch.float32, out=self.logits)
         _lib.check("t2b_argmax_rows", L.t2b_argmax_rows(p(self.logits), 2, B, cfg.vocab_size, cfg.vocab_size,
                                                         p(self.next_tokens), *self._ws("argmax"), st))
+
+    def set_hidden(self, x: torch.Tensor) -> None:
+        """Load a residual-stream state (fp32 [B, H]) and its split norm input for layer 0."""
+        self.x.copy_(x.to(self.device, torch.float32))
+        self.ssq_a.copy_((self.x.double() ** 2).sum(-1).float())
+        self.xw.copy_((self.x * self.layers[0].input_layernorm.float()).to(torch.bfloat16))
 
     def kernels_per_step(self) -> int:
         """Launches of this library's kernels per step (the lm_head GEMM is cuBLAS)."""

@@ -90,12 +90,15 @@ def pair_blocks(gate: AutoGPTQLinear, up: AutoGPTQLinear, device="cuda") -> W4We
 def dequantize(w: W4Weight) -> torch.Tensor:
     """Dense fp32 ``[N, K]`` view of a T2B weight (host-side check helper).
 
-    Undoes the tiled block order: block (nt, g) = [piece 4][row 128][16 B].
+    Undoes the tiled block order (block (nt, g) = [piece 4][row 128][16 B])
+    and the even-k-first nibble order inside each 32-bit word.
     """
     n, k = w.out_features, w.in_features
     g = k // 128
-    qb = w.qw.reshape(n // 128, g, 4, 128, 16).permute(0, 3, 1, 2, 4).reshape(n, k // 2).to(torch.int32)
-    q = torch.stack((qb & 0xF, qb >> 4), dim=-1).reshape(n, k).float()
+    qb = w.qw.reshape(n // 128, g, 4, 128, 16).permute(0, 3, 1, 2, 4).reshape(n, k // 8, 4).to(torch.int32)
+    nib = torch.stack((qb & 0xF, qb >> 4), dim=-1).reshape(n, k // 8, 8)   # nibble slots 0..7 of each word
+    order = torch.tensor([0, 4, 1, 5, 2, 6, 3, 7], device=nib.device)      # slot holding k = 0..7
+    q = nib[:, :, order].reshape(n, k).float()
     meta = w.meta.reshape(n // 128, g, 128).permute(0, 2, 1).reshape(n, g).to(torch.int64) & 0xFFFFFFFF
     scale = (meta & 0xFFFF).to(torch.int16).view(torch.float16).float()
     zero = ((meta >> 16) & 0x1F).float()
