@@ -86,12 +86,24 @@ T2B_DEV bool splitk_fixup(const LinearParams& p, float* tile_acc, int tile, int 
   return true;
 }
 
+// Epilogue inputs staged in shared memory ahead of time (any may be null:
+// the epilogue then reads global memory).
+struct EpiCache {
+  const int* pos;              // [MB] positions of the epilogue rows
+  const float* angles;         // [MB][head_dim] their RoPE rows
+  const __nv_bfloat16* qn;     // [head_dim]
+  const __nv_bfloat16* kn;     // [head_dim]
+  const float* resid;          // [MB][128] residual tile rows
+  const __nv_bfloat16* next_w; // [128] next-norm weight slice of this tile
+};
+
 // ---------------------------------------------------------------------------
 // Epilogues over a finished [MB][128] fp32 tile (rows tile*128.., batch rows
 // m0..m0+MB-1).  `scratch` holds >= 2*MB floats.  256 threads.
 // ---------------------------------------------------------------------------
 template <int EPI>
-T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB) {
+T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB,
+                           const EpiCache& ec = EpiCache{}) {
   constexpr int NT = 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = tile * TILE_N;
@@ -110,10 +122,13 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
       float sq = 0.f;
       if (live) {
         const size_t o = (size_t)m * p.y_ld + row0 + lr;
-        const float v = p.resid[o] + tile_acc[idx];
+        const float v = (ec.resid ? ec.resid[idx] : p.resid[o]) + tile_acc[idx];
         p.resid[o] = v;
         sq = v * v;
-        if (p.xw_out) p.xw_out[o] = __float2bfloat16_rn(v * __bfloat162float(p.next_w[row0 + lr]));
+        if (p.xw_out) {
+          const float w = __bfloat162float(ec.next_w ? ec.next_w[lr] : p.next_w[row0 + lr]);
+          p.xw_out[o] = __float2bfloat16_rn(v * w);
+        }
       }
       sq = warp_sum(sq);
       if (lane == 0 && live) atomicAdd(p.ssq_out + m, sq);
@@ -156,14 +171,14 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
       const int hl = lr / hd, d = lr - hl * hd;
       const int head = (row0 / hd) + hl;
       const float* tv = tile_acc + b * TILE_N + hl * hd;
-      const int pos = p.pos[m];
+      const int pos = ec.pos ? ec.pos[b] : p.pos[m];
       if (head >= nq + nkv) {  // value head: stored as projected (model.py:250,263)
         const int kvh = head - nq - nkv;
         p.v_cache[(((size_t)m * nkv + kvh) * p.max_ctx + pos) * hd + d] = __float2bfloat16_rn(tv[d]);
         continue;
       }
       const bool is_q = head < nq;
-      const __nv_bfloat16* nw = is_q ? p.qn_w : p.kn_w;
+      const __nv_bfloat16* nw = is_q ? (ec.qn ? ec.qn : p.qn_w) : (ec.kn ? ec.kn : p.kn_w);
       const float rs = scratch[b * hpt + hl];
       const int d0 = d & ~1;
       float x0 = tv[d0], x1 = tv[d0 + 1];
@@ -172,8 +187,9 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
         x1 = (x1 * rs) * __bfloat162float(nw[d0 + 1]);
       }
       // interleaved RoPE (model.py:184-196): out[2i] = x0 c - x1 s ; out[2i+1] = x1 c + x0 s
-      const float c = p.angles[(size_t)pos * hd + d0];
-      const float s = p.angles[(size_t)pos * hd + d0 + 1];
+      const float* ar = ec.angles ? ec.angles + (size_t)b * hd : p.angles + (size_t)pos * hd;
+      const float c = ar[d0];
+      const float s = ar[d0 + 1];
       const float o = (d & 1) ? (x1 * c + x0 * s) : (x0 * c - x1 * s);
       if (is_q) {
         q_out[(size_t)m * p.y_ld + head * hd + d] = __float2bfloat16_rn(o);

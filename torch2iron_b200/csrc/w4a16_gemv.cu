@@ -284,7 +284,7 @@ static int tc_min_m() {
     const int v = atoi(e);
     if (v > 0) return v;
   }
-  return 16;
+  return 2;
 }
 
 static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {

@@ -108,8 +108,10 @@ __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
 }
 
 // Shared-memory plan of one CTA (S groups, BP padded batch rows).
+constexpr int EP_BYTES = 9 * 1024;  // staged epilogue inputs: <= 8 KB of rows + 1 KB of weights
+
 struct TcLayout {
-  int x_group, off_raw, off_meta, off_tile, off_xsum, off_scr, off_bar, off_tmem, off_flag, bytes;
+  int x_group, off_raw, off_meta, off_tile, off_xsum, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
   __host__ __device__ TcLayout(int BP, int S) {
     x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group (TMA, 128B swizzle)
     off_raw = S * x_group;                   // [S][8 KB] raw int4 blocks
@@ -117,7 +119,8 @@ struct TcLayout {
     off_tile = off_meta + S * TILE_N * 4;    // fp32 [BP][128] partial tile
     off_xsum = off_tile + BP * TILE_N * 4;   // fp32 [S][BP] per-group activation sums
     off_scr = off_xsum + S * BP * 4;         // fp32 [8*BP] scratch (row scales, epilogue)
-    off_bar = off_scr + 8 * BP * 4;          // raw_full[S], a_full[2], a_empty[2], acc_full, x_full
+    off_ep = off_scr + 8 * BP * 4;           // epilogue inputs staged after the PDL wait
+    off_bar = off_ep + EP_BYTES;             // raw_full[S], a_full[2], a_empty[2], acc_full, x_full
     off_tmem = off_bar + (S + 6) * 8;
     off_flag = off_tmem + 8;
     bytes = off_flag + 8 + 1024;             // + slack to 1024-align the base
@@ -134,6 +137,68 @@ T2B_DEV void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint6
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Epilogue inputs that do not depend on this kernel's result, copied to
+// shared memory right after the PDL wait so the tail after the reduction
+// touches no global memory it must wait for: for EPI_QKV the rows'
+// positions, their RoPE angle rows and the two QK-norm weights; for
+// EPI_RESIDUAL the residual rows of this tile and the next-norm weights.
+// Staged only when it fits EP_BYTES.
+template <int EPI>
+T2B_DEV bool epilogue_staged(const LinearParams& p, int rows) {
+  if (EPI == EPI_QKV) return rows <= 64 && rows * p.head_dim * 4 <= 8 * 1024 - 256;
+  if (EPI == EPI_RESIDUAL) return rows * TILE_N * 4 <= 8 * 1024;
+  return false;
+}
+
+template <int EPI>
+T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int tile, int m0, int rows, int t, int nt) {
+  if (!epilogue_staged<EPI>(p, rows)) return;
+  if (EPI == EPI_QKV) {
+    const int hd = p.head_dim;
+    int* pos_s = reinterpret_cast<int*>(ep + 8 * 1024 - 256);
+    float* ang = reinterpret_cast<float*>(ep);
+    __nv_bfloat16* qn = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
+    __nv_bfloat16* kn = qn + 256;
+    for (int i = t; i < rows * hd; i += nt) {
+      const int b = i / hd, d = i - b * hd, m = m0 + b;
+      ang[i] = (m < p.M) ? p.angles[(size_t)p.pos[m] * hd + d] : 0.f;
+    }
+    for (int i = t; i < rows; i += nt) pos_s[i] = (m0 + i < p.M) ? p.pos[m0 + i] : 0;
+    if (p.qn_w)
+      for (int i = t; i < hd; i += nt) {
+        qn[i] = p.qn_w[i];
+        kn[i] = p.kn_w[i];
+      }
+  } else if (EPI == EPI_RESIDUAL) {
+    float* res = reinterpret_cast<float*>(ep);
+    __nv_bfloat16* nw = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
+    for (int i = t; i < rows * TILE_N; i += nt) {
+      const int b = i / TILE_N, c = i - b * TILE_N, m = m0 + b;
+      res[i] = (m < p.M) ? p.resid[(size_t)m * p.y_ld + tile * TILE_N + c] : 0.f;
+    }
+    if (p.next_w)
+      for (int i = t; i < TILE_N; i += nt) nw[i] = p.next_w[tile * TILE_N + i];
+  }
+}
+
+template <int EPI>
+T2B_DEV EpiCache staged_epilogue_inputs(const LinearParams& p, uint8_t* ep, int rows) {
+  EpiCache c{};
+  if (!epilogue_staged<EPI>(p, rows)) return c;
+  if (EPI == EPI_QKV) {
+    c.angles = reinterpret_cast<const float*>(ep);
+    c.pos = reinterpret_cast<const int*>(ep + 8 * 1024 - 256);
+    if (p.qn_w) {
+      c.qn = reinterpret_cast<const __nv_bfloat16*>(ep + 8 * 1024);
+      c.kn = c.qn + 256;
+    }
+  } else if (EPI == EPI_RESIDUAL) {
+    c.resid = reinterpret_cast<const float*>(ep);
+    if (p.next_w) c.next_w = reinterpret_cast<const __nv_bfloat16*>(ep + 8 * 1024);
+  }
+  return c;
 }
 
 // grid (N/128, KS, mblocks), cluster (1, KS, 1): the KS CTAs of a cluster are
@@ -166,6 +231,9 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   const int tile = blockIdx.x, split = blockIdx.y, mblk = blockIdx.z;
   const int g0 = split * S;
   const int m0 = mblk * BP;
+  // rows this CTA finishes in the epilogue (its cluster rank's share)
+  const int ep_rows = BP / KS;
+  const int ep_m0 = m0 + (KS > 1 ? (int)cluster_ctarank() : 0) * ep_rows;
   uint32_t tmem_cols = 32;
   while (tmem_cols < ACC_COL + (uint32_t)(S * BP)) tmem_cols <<= 1;
   T2B_TRACE_BEGIN(1 + EPI, p.N);
@@ -280,7 +348,8 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     }
     __syncwarp();
   } else {
-    // ---- warps 5-7: per-(group, row) activation sums from the swizzled X tile ----
+    // ---- warps 5-7: stage the epilogue inputs, then per-(group, row) activation sums ----
+    stage_epilogue_inputs<EPI>(p, sm + L.off_ep, tile, ep_m0, ep_rows, threadIdx.x - 160, 96);
     const bool ok = mbar_wait_bounded(x_full, 0, p.err);
     if (!ok) *abort_flag = 1;
     const int total = S * BP * 16;  // (group, row, 16-byte chunk); 16 lanes per (group, row)
@@ -380,7 +449,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   __syncthreads();
   T2B_TRACE_MARK(6);
   if (*abort_flag) return;
-  tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows);
+  tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows, staged_epilogue_inputs<EPI>(p, sm + L.off_ep, rows));
   __syncthreads();
   T2B_TRACE_MARK(7);
 }
