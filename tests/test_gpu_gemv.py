@@ -2,8 +2,10 @@
 
 Bar: each GEMV/GEMM within 1e-2 relative error
 (max-abs error / max |ref|) of fp32-accumulated dequantized math.  The
-kernel dequantizes exactly and accumulates in fp32, so fp32 outputs are held
-to 1e-4 and 16-bit outputs to 1e-2.
+CUDA-core path (1 row, fp16/fp32 activations, reference qparam rows)
+dequantizes exactly in fp32, so its fp32 outputs are held to 1e-4; the
+tensor-core path (2+ bf16 rows) dequantizes to bf16 like the reference's NPU
+kernels and is held to the 1e-2 bar.
 """
 
 import pytest
@@ -67,7 +69,7 @@ def test_golden_gemv_batches(M):
 
 
 @pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 3072), (6144, 1024), (1024, 2048), (256, 512), (128, 256)])
-@pytest.mark.parametrize("M", [1, 4, 8, 13, 16, 17, 33, 64, 100])
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 13, 16, 17, 33, 64, 100, 128, 200])
 def test_gemm_shapes_vs_oracle(N, K, M):
     g = torch.Generator().manual_seed(N * 7 + K + M)
     lin = synth.random_linear(N, K, g)
@@ -76,7 +78,7 @@ def test_gemm_shapes_vs_oracle(N, K, M):
     x = torch.randn(M, K, generator=g).to(torch.bfloat16)
     ref = oracle.GroupedW4A16Linear(lin.qweight, lin.qzeros, lin.scales)(x.float())
     y = gemm(dw, x.cuda(), torch.float32)
-    assert rel_err(y, ref) <= 1e-4
+    assert rel_err(y, ref) <= (1e-4 if M == 1 else 1e-2)
     yb = gemm(dw, x.cuda(), torch.bfloat16)
     assert rel_err(yb, ref) <= 1e-2
 
@@ -127,4 +129,4 @@ def test_tcgen05_forced_small_batch(monkeypatch, M, N, K):
     x = torch.randn(M, K, generator=g).to(torch.bfloat16)
     ref = oracle.GroupedW4A16Linear(lin.qweight, lin.qzeros, lin.scales)(x.float())
     y = gemm(dw, x.cuda(), torch.float32)
-    assert rel_err(y, ref) <= 1e-4
+    assert rel_err(y, ref) <= 1e-2

@@ -1,32 +1,31 @@
 // W4A16 group-128 GEMM on the 5th-generation tensor cores (tcgen05), for
-// decode batches of 16..64 rows per CTA, with the same fused prologues /
+// decode batches of 2..256 rows per CTA, with the same fused prologues /
 // epilogues as the CUDA-core GEMV.
 //
 // Swap-AB formulation: D[128 weight rows, Bp batch rows] = W_tile[128, k] . X[Bp, k]^T
-//   * MMA M = 128 (one T2B weight tile), N = Bp (batch padded to 16/32/64), K = 16.
-//   * A (weights) lives in TENSOR MEMORY: producer warps unpack each nibble
-//     pair straight into a bf16x2 register ((w >> 4j) & 0x000F000F | 0x4300_4300
-//     = the exact bf16 values 128+q) and tcgen05.st it into TMEM -- no shared
-//     memory round trip for the 4x-expanded weights.
-//   * B (activations) is written once per CTA into shared memory in the
-//     128-byte-swizzled K-major layout and read by the MMA through a UMMA
-//     shared-memory descriptor.
-//   * Scale and zero are applied per group AFTER the MMA: each group g gets
-//     its own fp32 TMEM accumulator P_g = sum_k (128+q) x, and the drain
-//     computes y += s_g * (P_g - (128+z_g) * sum_k x).  Products are exact,
-//     the weights are never rounded, and the per-weight ALU cost is ~1 op.
-//   * K order: a bf16x2 register holds nibbles (j, j+4) of a word, so within
-//     every 8-k block the MMA sees k in the order 0,4,1,5,2,6,3,7; the X tile
-//     is written in the same order, so the contraction is unchanged.
+//   * MMA M = 128 (one T2B weight tile), N = Bp (batch padded to 16..256), K = 16.
+//   * A (weights) lives in TENSOR MEMORY: producer warps turn each nibble
+//     pair into bf16x2 (128+q) with one mask-or ((w >> 4t) & 0x000F000F |
+//     0x4300_4300; the layout stores even-k nibbles first so the pair is
+//     (k, k+1)), subtract (128+z) exactly and multiply by the group scale in
+//     bf16x2 -- the bf16 dequant (q - z) * s of the reference's NPU kernels --
+//     and tcgen05.st the result into TMEM: no shared-memory round trip for
+//     the 4x-expanded weights.
+//   * B (activations) arrives by one 2-D tiled TMA copy per 64-k atom, with
+//     128-byte swizzle, straight into the UMMA K-major layout; rows past M
+//     are zero-filled by the copy.
+//   * One fp32 TMEM accumulator of Bp columns collects all groups.
 //   * Raw int4 blocks (8 KB + 512 B of meta per 128x128 tile-group) arrive by
 //     1-D TMA bulk copies issued BEFORE the programmatic-dependent-launch
 //     wait, so weight streaming overlaps the previous kernel's tail.
+//   * The k-splits of a tile form a thread-block cluster; partial tiles are
+//     summed through distributed shared memory, each CTA finishing Bp/KS rows.
 //
 // Roles (256 threads): warps 0-3 own TMEM lane quarters 0-3 (weight rows
-// 32w..32w+31): dequant producers, then accumulator drain.  Warp 4 allocates
-// TMEM and one lane issues the MMAs.  All 8 warps build the X tile.  Every
+// 32w..32w+31) and produce A; warp 4 allocates TMEM and one lane issues the
+// MMAs; warps 5-7 stage the epilogue inputs; all 8 warps drain TMEM.  Every
 // mbarrier wait is time-bounded; on timeout the CTA records T2B_ERR_TIMEOUT,
-// frees its TMEM and exits.
+// frees its TMEM, still passes its cluster barriers, and skips its epilogue.
 
 #include "linear_common.cuh"
 #include "launch.cuh"
@@ -111,14 +110,13 @@ __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
 constexpr int EP_BYTES = 9 * 1024;  // staged epilogue inputs: <= 8 KB of rows + 1 KB of weights
 
 struct TcLayout {
-  int x_group, off_raw, off_meta, off_tile, off_xsum, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
+  int x_group, off_raw, off_meta, off_tile, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
   __host__ __device__ TcLayout(int BP, int S) {
     x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group (TMA, 128B swizzle)
     off_raw = S * x_group;                   // [S][8 KB] raw int4 blocks
     off_meta = off_raw + S * BLOCK_BYTES;    // [S][128] meta words
     off_tile = off_meta + S * TILE_N * 4;    // fp32 [BP][128] partial tile
-    off_xsum = off_tile + BP * TILE_N * 4;   // fp32 [S][BP] per-group activation sums
-    off_scr = off_xsum + S * BP * 4;         // fp32 [8*BP] scratch (row scales, epilogue)
+    off_scr = off_tile + BP * TILE_N * 4;    // fp32 [8*BP] scratch (row scales, epilogue)
     off_ep = off_scr + 8 * BP * 4;           // epilogue inputs staged after the PDL wait
     off_bar = off_ep + EP_BYTES;             // raw_full[S], a_full[2], a_empty[2], acc_full, x_full
     off_tmem = off_bar + (S + 6) * 8;
@@ -128,7 +126,7 @@ struct TcLayout {
 };
 
 constexpr uint32_t A_COL = 0;      // two 64-column A stages
-constexpr uint32_t ACC_COL = 128;  // S accumulators of BP columns each
+constexpr uint32_t ACC_COL = 128;  // one accumulator of BP columns
 
 // 2-D tiled TMA load (no multicast): box of `tmap` at (x, y) -> smem, tx bytes on bar.
 T2B_DEV void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
@@ -157,26 +155,32 @@ T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int tile,
   if (!epilogue_staged<EPI>(p, rows)) return;
   if (EPI == EPI_QKV) {
     const int hd = p.head_dim;
-    int* pos_s = reinterpret_cast<int*>(ep + 8 * 1024 - 256);
-    float* ang = reinterpret_cast<float*>(ep);
-    __nv_bfloat16* qn = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
-    __nv_bfloat16* kn = qn + 256;
-    for (int i = t; i < rows * hd; i += nt) {
-      const int b = i / hd, d = i - b * hd, m = m0 + b;
-      ang[i] = (m < p.M) ? p.angles[(size_t)p.pos[m] * hd + d] : 0.f;
+    int* __restrict__ pos_s = reinterpret_cast<int*>(ep + 8 * 1024 - 256);
+    float* __restrict__ ang = reinterpret_cast<float*>(ep);
+    __nv_bfloat16* __restrict__ qn = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
+    __nv_bfloat16* __restrict__ kn = qn + 256;
+    // each thread takes whole 4-float chunks of an angle row: position and
+    // angle loads of different chunks are independent and overlap
+    for (int i = t; i < rows * hd / 4; i += nt) {
+      const int b = (i * 4) / hd, d = i * 4 - b * hd, m = m0 + b;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < p.M) v = __ldg(reinterpret_cast<const float4*>(p.angles + (size_t)__ldg(p.pos + m) * hd + d));
+      *reinterpret_cast<float4*>(ang + i * 4) = v;
     }
-    for (int i = t; i < rows; i += nt) pos_s[i] = (m0 + i < p.M) ? p.pos[m0 + i] : 0;
+    for (int i = t; i < rows; i += nt) pos_s[i] = (m0 + i < p.M) ? __ldg(p.pos + m0 + i) : 0;
     if (p.qn_w)
       for (int i = t; i < hd; i += nt) {
         qn[i] = p.qn_w[i];
         kn[i] = p.kn_w[i];
       }
   } else if (EPI == EPI_RESIDUAL) {
-    float* res = reinterpret_cast<float*>(ep);
-    __nv_bfloat16* nw = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
-    for (int i = t; i < rows * TILE_N; i += nt) {
-      const int b = i / TILE_N, c = i - b * TILE_N, m = m0 + b;
-      res[i] = (m < p.M) ? p.resid[(size_t)m * p.y_ld + tile * TILE_N + c] : 0.f;
+    float* __restrict__ res = reinterpret_cast<float*>(ep);
+    __nv_bfloat16* __restrict__ nw = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
+    for (int i = t; i < rows * TILE_N / 4; i += nt) {
+      const int b = (i * 4) / TILE_N, c = i * 4 - b * TILE_N, m = m0 + b;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < p.M) v = *reinterpret_cast<const float4*>(p.resid + (size_t)m * p.y_ld + tile * TILE_N + c);
+      *reinterpret_cast<float4*>(res + i * 4) = v;
     }
     if (p.next_w)
       for (int i = t; i < TILE_N; i += nt) nw[i] = p.next_w[tile * TILE_N + i];
@@ -215,7 +219,6 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   uint8_t* raw = sm + L.off_raw;
   const uint32_t* rmeta = reinterpret_cast<const uint32_t*>(sm + L.off_meta);
   float* tile_acc = reinterpret_cast<float*>(sm + L.off_tile);
-  float* xsum = reinterpret_cast<float*>(sm + L.off_xsum);
   float* scratch = reinterpret_cast<float*>(sm + L.off_scr);
   float* rowscale = scratch + 4 * BP;  // [BP]; scratch[0..2*BP) is the epilogue's
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.off_bar);
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   const int ep_rows = BP / KS;
   const int ep_m0 = m0 + (KS > 1 ? (int)cluster_ctarank() : 0) * ep_rows;
   uint32_t tmem_cols = 32;
-  while (tmem_cols < ACC_COL + (uint32_t)(S * BP)) tmem_cols <<= 1;
+  while (tmem_cols < ACC_COL + (uint32_t)BP) tmem_cols <<= 1;
   T2B_TRACE_BEGIN(1 + EPI, p.N);
 
   if (threadIdx.x == 0) {
@@ -291,7 +294,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   constexpr uint32_t IDESC = idesc_bf16(TILE_N, BP);
 
   if (warp < 4) {
-    // ---- producers: row r's nibbles -> bf16x2 (128+q) pairs -> TMEM lane r ----
+    // ---- producers: row r's nibbles -> bf16 (q - z) * s pairs -> TMEM lane r ----
     const int r = warp * 32 + lane;
     const uint32_t lane_base = tbase + ((uint32_t)(warp * 32) << 16);
     for (int gl = 0; gl < S; ++gl) {
@@ -303,6 +306,11 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
         *abort_flag = 1;
         break;
       }
+      const uint32_t mw = rmeta[gl * TILE_N + r];
+      const __nv_bfloat16 sb = __float2bfloat16_rn(__half2float(__ushort_as_half((unsigned short)(mw & 0xffffu))));
+      const __nv_bfloat16 zb = __float2bfloat16_rn(128.f + (float)((mw >> 16) & 0x1fu));
+      const __nv_bfloat162 s2 = __halves2bfloat162(sb, sb);
+      const __nv_bfloat162 z2 = __halves2bfloat162(zb, zb);
 #pragma unroll
       for (int pc = 0; pc < 4; ++pc) {
         const uint4 v = *reinterpret_cast<const uint4*>(raw + gl * BLOCK_BYTES + pc * 2048 + r * 16);
@@ -310,11 +318,14 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
         uint32_t cols[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          // slot t holds k 2t, slot t+4 holds k 2t+1: each mask-or is the pair (2t, 2t+1)
-          cols[4 * j + 0] = (w[j] & 0x000F000Fu) | 0x43004300u;
-          cols[4 * j + 1] = ((w[j] >> 4) & 0x000F000Fu) | 0x43004300u;
-          cols[4 * j + 2] = ((w[j] >> 8) & 0x000F000Fu) | 0x43004300u;
-          cols[4 * j + 3] = ((w[j] >> 12) & 0x000F000Fu) | 0x43004300u;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            // slot t holds k 2t, slot t+4 holds k 2t+1: the mask-or is the pair (2t, 2t+1) as 128+q
+            const uint32_t biased = ((w[j] >> (4 * t)) & 0x000F000Fu) | 0x43004300u;
+            const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(&biased);
+            const __nv_bfloat162 d2 = __hmul2(__hsub2(q2, z2), s2);   // (q - z) exact, one rounding of * s
+            cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d2);
+          }
         }
         tmem_st16(lane_base + A_COL + stage * 64 + pc * 16, cols);
       }
@@ -325,7 +336,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     }
     T2B_TRACE_MARK(3);
   } else if (warp == 4) {
-    // ---- MMA issuer (one lane) ----
+    // ---- MMA issuer (one lane): all groups into one accumulator ----
     if (lane == 0) {
       bool ok = mbar_wait_bounded(x_full, 0, p.err);
       for (int gl = 0; ok && gl < S; ++gl) {
@@ -339,7 +350,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint64_t bdesc = sdesc_sw128(xg + (ks >> 2) * (BP * 128) + (ks & 3) * 32);
-          mma_ts(tbase + ACC_COL + gl * BP, tbase + A_COL + stage * 64 + ks * 8, bdesc, IDESC, ks > 0);
+          mma_ts(tbase + ACC_COL, tbase + A_COL + stage * 64 + ks * 8, bdesc, IDESC, (gl > 0 || ks > 0) ? 1u : 0u);
         }
         mma_commit(&a_empty[stage]);
       }
@@ -348,35 +359,12 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     }
     __syncwarp();
   } else {
-    // ---- warps 5-7: stage the epilogue inputs, then per-(group, row) activation sums ----
+    // ---- warps 5-7: stage the epilogue inputs (one parallel pass) ----
     stage_epilogue_inputs<EPI>(p, sm + L.off_ep, tile, ep_m0, ep_rows, threadIdx.x - 160, 96);
-    const bool ok = mbar_wait_bounded(x_full, 0, p.err);
-    if (!ok) *abort_flag = 1;
-    const int total = S * BP * 16;  // (group, row, 16-byte chunk); 16 lanes per (group, row)
-    for (int t = threadIdx.x - 160; t < ((total + 95) / 96) * 96; t += 96) {
-      float sum = 0.f;
-      const int c16 = t & 15, gb = t >> 4;
-      if (ok && t < total) {
-        const int gl = gb / BP, b = gb - gl * BP;
-        const int atom = c16 >> 3, cc = c16 & 7;
-        const uint4 v =
-            *reinterpret_cast<const uint4*>(xs + gl * L.x_group + atom * (BP * 128) + b * 128 + ((cc ^ (b & 7)) << 4));
-        const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sum += __uint_as_float(ww[e] << 16) + __uint_as_float(ww[e] & 0xffff0000u);
-      }
-      // lanes 16j..16j+15 of a warp hold one (group, row) when 96 divides 16: reduce over 16 lanes
-      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      if (c16 == 0 && t < total) xsum[gb] = sum;
-    }
   }
-  __syncthreads();  // xsum complete; every role past its loop
 
-  // ---- drain: y[b] = r_b * sum_g s_g * (P_g[b] - (128+z_g) * xsum_g[b]) ----
-  // warps w and w+4 share TMEM lane quarter w%4 and split the BP columns.
+  // ---- drain: tile_acc[b][r] = D[r][b] (* row scale); warps w and w+4 share
+  // TMEM lane quarter w%4 and split the BP columns ----
   {
     constexpr int HB = BP / 2;
     const int q4 = warp & 3, half = warp >> 2;
@@ -386,31 +374,20 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     if (!ok) *abort_flag = 1;
     T2B_TRACE_MARK(4);
     tc_fence_after();
-    float y[HB];
-#pragma unroll
-    for (int b = 0; b < HB; ++b) y[b] = 0.f;
-    if (ok) {
-      for (int gl = 0; gl < S; ++gl) {
-        const uint32_t mw = rmeta[gl * TILE_N + r];
-        const float sc = __half2float(__ushort_as_half((unsigned short)(mw & 0xffffu)));
-        const float zo = 128.f + (float)((mw >> 16) & 0x1fu);
-#pragma unroll
-        for (int cb = 0; cb < HB / 8; ++cb) {
-          uint32_t v[8];
-          tmem_ld8(lane_base + ACC_COL + gl * BP + half * HB + cb * 8, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int b = cb * 8 + e;
-            y[b] = fmaf(sc, __uint_as_float(v[e]) - zo * xsum[gl * BP + half * HB + b], y[b]);
-          }
-        }
+#pragma unroll 4
+    for (int cb = 0; cb < HB / 8; ++cb) {
+      uint32_t v[8];
+      if (ok) {
+        tmem_ld8(lane_base + ACC_COL + half * HB + cb * 8, v);
+        tmem_ld_wait();
       }
-    }
 #pragma unroll
-    for (int b = 0; b < HB; ++b) {
-      const float v = (PRO == PRO_RMSNORM) ? y[b] * rowscale[half * HB + b] : y[b];
-      tile_acc[(half * HB + b) * TILE_N + r] = v;
+      for (int e = 0; e < 8; ++e) {
+        const int b = half * HB + cb * 8 + e;
+        float y = ok ? __uint_as_float(v[e]) : 0.f;
+        if (PRO == PRO_RMSNORM) y *= rowscale[b];
+        tile_acc[b * TILE_N + r] = y;
+      }
     }
   }
   tc_fence_before();
@@ -463,33 +440,43 @@ struct TcPlan {
   bool ok;
 };
 
-// Cluster size KS (k-splits of a tile) is the smallest divisor of G in
-// {1,2,4,8} that brings the grid to at least one CTA per SM; each CTA then
-// takes S = G/KS groups.  BP shrinks (more row blocks) when S*BP would not
-// fit TMEM or shared memory.
+// Groups per CTA S and cluster size KS = G/S (k-splits of a tile): the
+// largest S <= 4 that keeps KS <= 8 and the grid at >= 64 CTAs (or as many
+// as the shape allows).  Bp covers the batch up to 256 rows per CTA; shared
+// memory bounds S * Bp.
 static TcPlan tc_plan(int M, int N, int K) {
   TcPlan pl{};
   const int G = K / GROUP;
   const int tiles = N / TILE_N;
-  pl.BP = M <= 16 ? 16 : M <= 32 ? 32 : 64;
-  auto mblk = [&](int bp) { return (M + bp - 1) / bp; };
-  pl.KS = 0;
-  for (int ks : {1, 2, 4, 8})
-    if (G % ks == 0 && ks <= pl.BP && (long)tiles * ks * mblk(pl.BP) >= 148) {
-      pl.KS = ks;
+  int bp = 16;
+  while (bp < M && bp < 256) bp <<= 1;
+  pl.BP = bp;
+  pl.S = 0;
+  auto fits = [&](int bp_, int s_) { return TcLayout(bp_, s_).bytes <= 200 * 1024; };
+  for (int s_ : {4, 3, 2, 1}) {
+    if (G % s_ || G / s_ > 8 || G / s_ > bp) continue;
+    if (!fits(bp, s_)) continue;
+    const long ctas = (long)tiles * (G / s_) * ((M + bp - 1) / bp);
+    if (ctas >= 64 || s_ == 1) {
+      pl.S = s_;
       break;
     }
-  if (pl.KS == 0)
-    for (int ks : {8, 4, 2, 1})
-      if (G % ks == 0 && ks <= pl.BP) {
-        pl.KS = ks;
-        break;
+  }
+  if (pl.S == 0) {  // long K: smallest S with KS <= 8 that fits, shrinking Bp if needed
+    for (int s_ = (G + 7) / 8; s_ <= G && pl.S == 0; ++s_) {
+      if (G % s_) continue;
+      int b = bp;
+      while (b > 16 && !fits(b, s_)) b >>= 1;
+      if (fits(b, s_) && G / s_ <= b) {
+        pl.S = s_;
+        pl.BP = b;
       }
-  pl.S = G / pl.KS;
-  auto fits = [&](int bp) { return pl.S * bp <= 384 && TcLayout(bp, pl.S).bytes <= 220 * 1024; };
-  while (pl.BP > 16 && (!fits(pl.BP) || pl.KS > pl.BP)) pl.BP >>= 1;
-  pl.ok = fits(pl.BP) && pl.KS <= pl.BP && N % TILE_N == 0;
-  pl.mblocks = mblk(pl.BP);
+    }
+  }
+  pl.ok = pl.S > 0 && N % TILE_N == 0;
+  if (!pl.ok) return pl;
+  pl.KS = G / pl.S;
+  pl.mblocks = (M + pl.BP - 1) / pl.BP;
   pl.smem = (size_t)TcLayout(pl.BP, pl.S).bytes;
   return pl;
 }
@@ -511,6 +498,8 @@ static int tc_dispatch(LinearParams& p, const TcPlan& pl, cudaStream_t st) {
   if (pl.BP == 16) return tc_launch_t<16, PRO, EPI>(p, pl, st);
   if (pl.BP == 32) return tc_launch_t<32, PRO, EPI>(p, pl, st);
   if (pl.BP == 64) return tc_launch_t<64, PRO, EPI>(p, pl, st);
+  if (pl.BP == 128) return tc_launch_t<128, PRO, EPI>(p, pl, st);
+  if (pl.BP == 256) return tc_launch_t<256, PRO, EPI>(p, pl, st);
   return T2B_ERR_ARG;
 }
 
