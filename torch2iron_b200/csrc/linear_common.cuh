@@ -172,6 +172,8 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
       const int head = (row0 / hd) + hl;
       const float* tv = tile_acc + b * TILE_N + hl * hd;
       const int pos = ec.pos ? ec.pos[b] : p.pos[m];
+      const bool in_cache = pos >= 0 && pos < p.max_ctx;   // a bad position writes nothing
+      if (head >= nq && !in_cache) continue;
       if (head >= nq + nkv) {  // value head: stored as projected (model.py:250,263)
         const int kvh = head - nq - nkv;
         p.v_cache[(((size_t)m * nkv + kvh) * p.max_ctx + pos) * hd + d] = __float2bfloat16_rn(tv[d]);
@@ -187,7 +189,7 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
         x1 = (x1 * rs) * __bfloat162float(nw[d0 + 1]);
       }
       // interleaved RoPE (model.py:184-196): out[2i] = x0 c - x1 s ; out[2i+1] = x1 c + x0 s
-      const float* ar = ec.angles ? ec.angles + (size_t)b * hd : p.angles + (size_t)pos * hd;
+      const float* ar = ec.angles ? ec.angles + (size_t)b * hd : p.angles + (size_t)(in_cache ? pos : 0) * hd;
       const float c = ar[d0];
       const float s = ar[d0 + 1];
       const float o = (d & 1) ? (x1 * c + x0 * s) : (x0 * c - x1 * s);

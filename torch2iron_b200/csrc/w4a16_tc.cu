@@ -107,7 +107,10 @@ __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
 }
 
 // Shared-memory plan of one CTA (S groups, BP padded batch rows).
-constexpr int EP_BYTES = 9 * 1024;  // staged epilogue inputs: <= 8 KB of rows + 1 KB of weights
+// Staged epilogue inputs: EP_ROWS_BYTES of per-row data (angle rows or
+// residual rows), then 256 bytes of row positions, then 1 KB of weights.
+constexpr int EP_ROWS_BYTES = 32 * 1024;
+constexpr int EP_BYTES = EP_ROWS_BYTES + 256 + 1024;
 
 struct TcLayout {
   int x_group, off_raw, off_meta, off_tile, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
@@ -145,8 +148,8 @@ T2B_DEV void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint6
 // Staged only when it fits EP_BYTES.
 template <int EPI>
 T2B_DEV bool epilogue_staged(const LinearParams& p, int rows) {
-  if (EPI == EPI_QKV) return rows <= 64 && rows * p.head_dim * 4 <= 8 * 1024 - 256;
-  if (EPI == EPI_RESIDUAL) return rows * TILE_N * 4 <= 8 * 1024;
+  if (EPI == EPI_QKV) return rows <= 64 && rows * p.head_dim * 4 <= EP_ROWS_BYTES;
+  if (EPI == EPI_RESIDUAL) return rows * TILE_N * 4 <= EP_ROWS_BYTES;
   return false;
 }
 
@@ -155,16 +158,19 @@ T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int tile,
   if (!epilogue_staged<EPI>(p, rows)) return;
   if (EPI == EPI_QKV) {
     const int hd = p.head_dim;
-    int* __restrict__ pos_s = reinterpret_cast<int*>(ep + 8 * 1024 - 256);
+    int* __restrict__ pos_s = reinterpret_cast<int*>(ep + EP_ROWS_BYTES);
     float* __restrict__ ang = reinterpret_cast<float*>(ep);
-    __nv_bfloat16* __restrict__ qn = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
+    __nv_bfloat16* __restrict__ qn = reinterpret_cast<__nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
     __nv_bfloat16* __restrict__ kn = qn + 256;
     // each thread takes whole 4-float chunks of an angle row: position and
     // angle loads of different chunks are independent and overlap
     for (int i = t; i < rows * hd / 4; i += nt) {
       const int b = (i * 4) / hd, d = i * 4 - b * hd, m = m0 + b;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m < p.M) v = __ldg(reinterpret_cast<const float4*>(p.angles + (size_t)__ldg(p.pos + m) * hd + d));
+      if (m < p.M) {
+        const int ps = __ldg(p.pos + m);
+        if (ps >= 0 && ps < p.max_ctx) v = __ldg(reinterpret_cast<const float4*>(p.angles + (size_t)ps * hd + d));
+      }
       *reinterpret_cast<float4*>(ang + i * 4) = v;
     }
     for (int i = t; i < rows; i += nt) pos_s[i] = (m0 + i < p.M) ? __ldg(p.pos + m0 + i) : 0;
@@ -175,7 +181,7 @@ T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int tile,
       }
   } else if (EPI == EPI_RESIDUAL) {
     float* __restrict__ res = reinterpret_cast<float*>(ep);
-    __nv_bfloat16* __restrict__ nw = reinterpret_cast<__nv_bfloat16*>(ep + 8 * 1024);
+    __nv_bfloat16* __restrict__ nw = reinterpret_cast<__nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
     for (int i = t; i < rows * TILE_N / 4; i += nt) {
       const int b = (i * 4) / TILE_N, c = i * 4 - b * TILE_N, m = m0 + b;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -193,14 +199,14 @@ T2B_DEV EpiCache staged_epilogue_inputs(const LinearParams& p, uint8_t* ep, int 
   if (!epilogue_staged<EPI>(p, rows)) return c;
   if (EPI == EPI_QKV) {
     c.angles = reinterpret_cast<const float*>(ep);
-    c.pos = reinterpret_cast<const int*>(ep + 8 * 1024 - 256);
+    c.pos = reinterpret_cast<const int*>(ep + EP_ROWS_BYTES);
     if (p.qn_w) {
-      c.qn = reinterpret_cast<const __nv_bfloat16*>(ep + 8 * 1024);
+      c.qn = reinterpret_cast<const __nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
       c.kn = c.qn + 256;
     }
   } else if (EPI == EPI_RESIDUAL) {
     c.resid = reinterpret_cast<const float*>(ep);
-    if (p.next_w) c.next_w = reinterpret_cast<const __nv_bfloat16*>(ep + 8 * 1024);
+    if (p.next_w) c.next_w = reinterpret_cast<const __nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
   }
   return c;
 }
@@ -302,6 +308,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
       bool ok = true;
       if (gl >= 2) ok = mbar_wait_bounded(&a_empty[stage], ((gl - 2) >> 1) & 1, p.err);
       if (ok) ok = mbar_wait_bounded(&raw_full[gl], 0, p.err);
+      ok = __all_sync(0xffffffffu, ok);  // the warp takes the same branch before tcgen05.st
       if (!ok) {
         *abort_flag = 1;
         break;
@@ -370,7 +377,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     const int q4 = warp & 3, half = warp >> 2;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
-    const bool ok = (*abort_flag == 0) && mbar_wait_bounded(acc_full, 0, p.err);
+    const bool ok = __all_sync(0xffffffffu, (*abort_flag == 0) && mbar_wait_bounded(acc_full, 0, p.err));
     if (!ok) *abort_flag = 1;
     T2B_TRACE_MARK(4);
     tc_fence_after();
