@@ -18,6 +18,8 @@
 // tile = chunk, and slots whose mask <= 0.5 are skipped
 // (attention_reference.py:153-154).
 
+#include <algorithm>
+
 #include "t2b_common.cuh"
 #include "launch.cuh"
 
@@ -26,8 +28,8 @@ namespace t2b {
 constexpr int AT_THREADS = 128;
 constexpr int AT_TILE = 64;
 constexpr int AT_STAGES = 2;
-constexpr int AT_CTAS_PER_SM = 3;
-constexpr int AT_MAX_ROWS = 1024;
+constexpr int AT_MAX_CTAS_PER_SM = 4;  // workspace bound; the grid uses the measured occupancy
+constexpr int AT_MAX_ROWS = 256;
 
 struct AttnParams {
   const __nv_bfloat16* q;    // [rows][n_heads*hd]
@@ -54,12 +56,14 @@ struct AttnSmem {
   __nv_bfloat16 k[AT_STAGES][AT_TILE][HD];
   __nv_bfloat16 v[AT_STAGES][AT_TILE][HD];
   __nv_bfloat16 msk[AT_STAGES][AT_TILE];
+  __nv_bfloat16 qb[AT_STAGES][QPG * HD];  // q heads of a unit, copied with the unit's first tile
   float p[QPG][AT_TILE];
   float corr[QPG];
   float mrun[QPG];
   float lrun[QPG];
   int row_start[AT_MAX_ROWS + 1];  // first global tile index of row m (all its kv heads)
   int row_tiles[AT_MAX_ROWS];      // tiles per unit of row m
+  int row_keys[AT_MAX_ROWS];       // keys attended by row m
   uint64_t bar[AT_STAGES];
 };
 
@@ -68,7 +72,7 @@ struct TileRef {
 };
 
 // Keys attended by row m: pos[m] + 1, kept inside the cache whatever pos holds.
-T2B_DEV int keys_of_row(const AttnParams& P, int m) {
+T2B_DEV int keys_of_row_global(const AttnParams& P, int m) {
   if (!P.pos) return P.n_keys;
   const int k = P.pos[m] + 1;
   return k < 1 ? 1 : (k > P.n_keys ? P.n_keys : k);
@@ -120,7 +124,9 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
   // ---- tile list: tiles per unit of each row, exclusive prefix over rows ----
   const int rows = P.rows;
   for (int m = tid; m < rows; m += AT_THREADS) {
-    S.row_tiles[m] = (keys_of_row(P, m) + AT_TILE - 1) / AT_TILE;
+    const int nk = keys_of_row_global(P, m);
+    S.row_keys[m] = nk;
+    S.row_tiles[m] = (nk + AT_TILE - 1) / AT_TILE;
   }
   __syncthreads();
   if (warp == 0) {
@@ -146,18 +152,21 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
   const int t_lo = range_lo(c, T, NP), t_hi = range_lo(c + 1, T, NP);
   const int count = t_hi - t_lo;
 
-  auto issue = [&](int i) {  // tile i of this CTA into stage i % AT_STAGES
+  auto issue = [&](int i) {  // tile i of this CTA into stage i % AT_STAGES (+ q on a unit's first tile)
     const TileRef r = locate(S, rows, t_lo + i);
-    const int nk = min(AT_TILE, keys_of_row(P, r.m) - r.j * AT_TILE);
+    const int nk = min(AT_TILE, S.row_keys[r.m] - r.j * AT_TILE);
     const uint32_t bytes = (uint32_t)nk * HD * 2;
     const int st = i % AT_STAGES;
     const long long base =
         (long long)r.m * P.stride_row + (long long)r.h * P.stride_head + (long long)r.j * P.tile_stride;
     const uint32_t mbytes = P.mask0 ? (uint32_t)AT_TILE * 2 : 0u;
-    mbar_arrive_expect_tx(&S.bar[st], 2 * bytes + mbytes);
+    const bool with_q = (i == 0) || (r.j == 0);
+    const uint32_t qbytes = with_q ? (uint32_t)(QPG * HD * 2) : 0u;
+    mbar_arrive_expect_tx(&S.bar[st], 2 * bytes + mbytes + qbytes);
     bulk_g2s(&S.k[st][0][0], P.k0 + base, bytes, &S.bar[st]);
     bulk_g2s(&S.v[st][0][0], P.v0 + base, bytes, &S.bar[st]);
     if (P.mask0) bulk_g2s(&S.msk[st][0], P.mask0 + base, mbytes, &S.bar[st]);
+    if (with_q) bulk_g2s(&S.qb[st][0], P.q + (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD, qbytes, &S.bar[st]);
   };
   if (tid == 0)
     for (int i = 0; i < AT_STAGES && i < count; ++i) issue(i);
@@ -169,11 +178,13 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
     const TileRef r = locate(S, rows, t_lo + i);
     const bool unit_begin = (i == 0) || (r.j == 0);
     const bool unit_end = (i == count - 1) || (r.j == r.nt - 1);
-    if (unit_begin) {  // new unit: its q heads, fresh softmax state
-      for (int e = tid; e < QH; e += AT_THREADS) {
-        const int hh = e / HD, d = e - hh * HD;
-        S.q[hh][d] = __bfloat162float(P.q[(size_t)r.m * P.n_heads * HD + (r.h * QPG + hh) * HD + d]);
-      }
+    const int st = i % AT_STAGES;
+    // every thread takes the same outcome, so no thread is left at a barrier
+    const bool ok = __syncthreads_and(mbar_wait_bounded(&S.bar[st], (i / AT_STAGES) & 1, P.err));
+    if (!ok) break;  // timeout recorded in P.err
+    if (i == 0) T2B_TRACE_MARK(2);
+    if (unit_begin) {  // new unit: its q heads (arrived with this tile), fresh softmax state
+      for (int e = tid; e < QH; e += AT_THREADS) S.q[e / HD][e % HD] = __bfloat162float(S.qb[st][e]);
       if (tid < QPG) {
         S.mrun[tid] = -INFINITY;
         S.lrun[tid] = 0.f;
@@ -182,12 +193,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
       for (int e = 0; e < NPAIR; ++e) o[e][0] = o[e][1] = 0.f;
       __syncthreads();
     }
-    const int st = i % AT_STAGES;
-    // every thread takes the same outcome, so no thread is left at a barrier
-    const bool ok = __syncthreads_and(mbar_wait_bounded(&S.bar[st], (i / AT_STAGES) & 1, P.err));
-    if (!ok) break;  // timeout recorded in P.err
-    if (i == 0) T2B_TRACE_MARK(2);
-    const int nk = min(AT_TILE, keys_of_row(P, r.m) - r.j * AT_TILE);
+    const int nk = min(AT_TILE, S.row_keys[r.m] - r.j * AT_TILE);
     // scores: one (head, key) per thread-iteration; 16-byte K chunks rotated by
     // key index so the 8 lanes of a quarter-warp hit distinct banks
     for (int sidx = tid; sidx < QPG * AT_TILE; sidx += AT_THREADS) {
@@ -324,26 +330,43 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
 
 // ---------------------------------------------------------------------------
 
-static int grid_ctas(int rows, int n_kv, int max_keys) {
-  const long long tiles = (long long)rows * n_kv * ((max_keys + AT_TILE - 1) / AT_TILE);
-  long long g = 148LL * AT_CTAS_PER_SM;
-  if (tiles < g) g = tiles;
+static long long max_tiles(int rows, int n_kv, int max_keys) {
+  return (long long)rows * n_kv * ((max_keys + AT_TILE - 1) / AT_TILE);
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return n > 0 ? n : 148;
+}
+
+// Grid bound used to size the workspace (independent of the device).
+static int grid_bound(int rows, int n_kv, int max_keys) {
+  const long long g = std::min<long long>(max_tiles(rows, n_kv, max_keys), 160LL * AT_MAX_CTAS_PER_SM);
   return (int)(g < 1 ? 1 : g);
 }
 
 size_t attention_workspace_bytes(int rows, int n_heads, int n_kv, int head_dim, int max_keys) {
   const int qpg = n_heads / n_kv;
-  const int g = grid_ctas(rows, n_kv, max_keys);
+  const int g = grid_bound(rows, n_kv, max_keys);
   size_t part = (size_t)g * 2 * qpg * (head_dim + 2) * sizeof(float);
   part = (part + 255) & ~size_t(255);
   return part + (((size_t)rows * n_kv * sizeof(int) + 255) & ~size_t(255));
 }
 
+// One wave: as many CTAs as are resident at once (capped by the tile count
+// and the workspace bound).
 template <int HD, int QPG>
-static int attn_launch_t(AttnParams& P, int grid, cudaStream_t st) {
+static int attn_launch_t(AttnParams& P, int max_grid, cudaStream_t st) {
   auto kern = decode_attention_kernel<HD, QPG>;
   const size_t smem = sizeof(AttnSmem<HD, QPG>);
   if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, AT_THREADS, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  per_sm = std::min(per_sm, AT_MAX_CTAS_PER_SM);
+  const int grid = std::max(1, std::min(max_grid, sm_count() * per_sm));
   return launch_pdl(kern, dim3(grid), dim3(AT_THREADS), smem, st, P);
 }
 
@@ -354,7 +377,7 @@ int attention_launch(AttnParams& P, int rows, int head_dim, int max_keys, void* 
   const int qpg = P.n_heads / P.n_kv;
   const size_t need = attention_workspace_bytes(rows, P.n_heads, P.n_kv, head_dim, max_keys);
   if (ws_bytes < need || !ws) return T2B_ERR_WORKSPACE;
-  const int grid = grid_ctas(rows, P.n_kv, max_keys);
+  const int grid = grid_bound(rows, P.n_kv, max_keys);
   size_t part = (size_t)grid * 2 * qpg * (head_dim + 2) * sizeof(float);
   part = (part + 255) & ~size_t(255);
   P.ws = reinterpret_cast<float*>(ws);
