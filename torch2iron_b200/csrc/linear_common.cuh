@@ -86,6 +86,8 @@ T2B_DEV bool splitk_fixup(const LinearParams& p, float* tile_acc, int tile, int 
   return true;
 }
 
+
+
 // Epilogue inputs staged in shared memory ahead of time (any may be null:
 // the epilogue then reads global memory).
 struct EpiCache {
@@ -98,6 +100,79 @@ struct EpiCache {
 };
 
 // ---------------------------------------------------------------------------
+// QKV epilogue (model.py:248-264): per 128-row tile = 128/HD heads of q, k or v
+// for MB batch rows.  q/k heads: per-head RMSNorm (when weights are given),
+// then interleaved RoPE on (x[2i], x[2i+1]) pairs; q goes to q_out, k/v to the
+// cache at the row's position.  Work item = (row, dimension pair): float2
+// reads, one bf16x2 store, no runtime division.
+// ---------------------------------------------------------------------------
+template <int HD>
+T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB,
+                          const EpiCache& ec) {
+  constexpr int NT = 256;
+  constexpr int HPT = TILE_N / HD;  // heads per tile
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head0 = tile * HPT;
+  const int nq = p.n_heads, nkv = p.n_kv;
+  // per (row, head) inverse RMS over the head (model.py:179-180 on q/k heads)
+  for (int pair = warp; pair < MB * HPT; pair += NT / 32) {
+    const int b = pair / HPT, hl = pair - b * HPT;
+    const int head = head0 + hl;
+    float ss = 0.f;
+#pragma unroll
+    for (int d = lane; d < HD; d += 32) {
+      const float v = tile_acc[b * TILE_N + hl * HD + d];
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) {
+      const bool normed = (head < nq && p.qn_w) || (head >= nq && head < nq + nkv && p.kn_w);
+      scratch[pair] = normed ? rsqrtf(ss / (float)HD + p.eps) : 1.f;
+    }
+  }
+  __syncthreads();
+  __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(p.y);
+  const __nv_bfloat16* qn = ec.qn ? ec.qn : p.qn_w;
+  const __nv_bfloat16* kn = ec.kn ? ec.kn : p.kn_w;
+  for (int it = threadIdx.x; it < MB * (TILE_N / 2); it += NT) {
+    const int b = it / (TILE_N / 2), pr = it - b * (TILE_N / 2);   // pr: pair index inside the tile
+    const int m = m0 + b;
+    if (m >= p.M) continue;
+    const int hl = (2 * pr) / HD, d0 = 2 * pr - hl * HD;
+    const int head = head0 + hl;
+    const int pos = ec.pos ? ec.pos[b] : p.pos[m];
+    const bool in_cache = pos >= 0 && pos < p.max_ctx;   // a bad position writes no cache entry
+    const float2 xv = *reinterpret_cast<const float2*>(tile_acc + b * TILE_N + 2 * pr);
+    if (head >= nq + nkv) {  // value head: stored as projected (model.py:250,263)
+      if (in_cache)
+        *reinterpret_cast<__nv_bfloat162*>(
+            &p.v_cache[(((size_t)m * nkv + (head - nq - nkv)) * p.max_ctx + pos) * HD + d0]) =
+            __floats2bfloat162_rn(xv.x, xv.y);
+      continue;
+    }
+    const bool is_q = head < nq;
+    if (!is_q && !in_cache) continue;
+    const __nv_bfloat16* nw = is_q ? qn : kn;
+    float x0 = xv.x, x1 = xv.y;
+    if (nw) {
+      const float rs = scratch[b * HPT + hl];
+      const __nv_bfloat162 w2 = *reinterpret_cast<const __nv_bfloat162*>(nw + d0);
+      x0 = (x0 * rs) * __low2float(w2);
+      x1 = (x1 * rs) * __high2float(w2);
+    }
+    // interleaved RoPE (model.py:184-196): (x0, x1) -> (x0 c - x1 s, x1 c + x0 s)
+    const float2 cs = *reinterpret_cast<const float2*>(
+        ec.angles ? ec.angles + (size_t)b * HD + d0 : p.angles + (size_t)(in_cache ? pos : 0) * HD + d0);
+    const __nv_bfloat162 o = __floats2bfloat162_rn(x0 * cs.x - x1 * cs.y, x1 * cs.x + x0 * cs.y);
+    if (is_q)
+      *reinterpret_cast<__nv_bfloat162*>(&q_out[(size_t)m * p.y_ld + head * HD + d0]) = o;
+    else
+      *reinterpret_cast<__nv_bfloat162*>(&p.k_cache[(((size_t)m * nkv + (head - nq)) * p.max_ctx + pos) * HD + d0]) =
+          o;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Epilogues over a finished [MB][128] fp32 tile (rows tile*128.., batch rows
 // m0..m0+MB-1).  `scratch` holds >= 2*MB floats.  256 threads.
 // ---------------------------------------------------------------------------
@@ -105,7 +180,7 @@ template <int EPI>
 T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB,
                            const EpiCache& ec = EpiCache{}) {
   constexpr int NT = 256;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int row0 = tile * TILE_N;
   if (EPI == EPI_STORE) {
     for (int idx = threadIdx.x; idx < MB * TILE_N; idx += NT) {
@@ -146,60 +221,8 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
       }
     }
   } else {  // EPI_QKV
-    const int hd = p.head_dim;
-    const int hpt = TILE_N / hd;  // heads per tile (1 or 2)
-    const int nq = p.n_heads, nkv = p.n_kv;
-    for (int pair = warp; pair < MB * hpt; pair += NT / 32) {
-      const int b = pair / hpt, hl = pair - b * hpt;
-      const int head = (row0 / hd) + hl;
-      float ss = 0.f;
-      for (int d = lane; d < hd; d += 32) {
-        const float v = tile_acc[b * TILE_N + hl * hd + d];
-        ss += v * v;
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) {
-        const bool normed = (head < nq && p.qn_w) || (head >= nq && head < nq + nkv && p.kn_w);
-        scratch[pair] = normed ? rsqrtf(ss / (float)hd + p.eps) : 1.f;   // model.py:179-180 per head
-      }
-    }
-    __syncthreads();
-    __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(p.y);
-    for (int idx = threadIdx.x; idx < MB * TILE_N; idx += NT) {
-      const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
-      if (m >= p.M) continue;
-      const int hl = lr / hd, d = lr - hl * hd;
-      const int head = (row0 / hd) + hl;
-      const float* tv = tile_acc + b * TILE_N + hl * hd;
-      const int pos = ec.pos ? ec.pos[b] : p.pos[m];
-      const bool in_cache = pos >= 0 && pos < p.max_ctx;   // a bad position writes nothing
-      if (head >= nq && !in_cache) continue;
-      if (head >= nq + nkv) {  // value head: stored as projected (model.py:250,263)
-        const int kvh = head - nq - nkv;
-        p.v_cache[(((size_t)m * nkv + kvh) * p.max_ctx + pos) * hd + d] = __float2bfloat16_rn(tv[d]);
-        continue;
-      }
-      const bool is_q = head < nq;
-      const __nv_bfloat16* nw = is_q ? (ec.qn ? ec.qn : p.qn_w) : (ec.kn ? ec.kn : p.kn_w);
-      const float rs = scratch[b * hpt + hl];
-      const int d0 = d & ~1;
-      float x0 = tv[d0], x1 = tv[d0 + 1];
-      if (nw) {
-        x0 = (x0 * rs) * __bfloat162float(nw[d0]);
-        x1 = (x1 * rs) * __bfloat162float(nw[d0 + 1]);
-      }
-      // interleaved RoPE (model.py:184-196): out[2i] = x0 c - x1 s ; out[2i+1] = x1 c + x0 s
-      const float* ar = ec.angles ? ec.angles + (size_t)b * hd : p.angles + (size_t)(in_cache ? pos : 0) * hd;
-      const float c = ar[d0];
-      const float s = ar[d0 + 1];
-      const float o = (d & 1) ? (x1 * c + x0 * s) : (x0 * c - x1 * s);
-      if (is_q) {
-        q_out[(size_t)m * p.y_ld + head * hd + d] = __float2bfloat16_rn(o);
-      } else {
-        const int kvh = head - nq;
-        p.k_cache[(((size_t)m * nkv + kvh) * p.max_ctx + pos) * hd + d] = __float2bfloat16_rn(o);
-      }
-    }
+    if (p.head_dim == 128) qkv_epilogue<128>(p, tile_acc, scratch, tile, m0, MB, ec);
+    else qkv_epilogue<64>(p, tile_acc, scratch, tile, m0, MB, ec);
   }
 }
 
