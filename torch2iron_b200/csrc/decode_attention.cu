@@ -1,17 +1,32 @@
-// GQA decode attention over a bf16 KV cache, persistent and tile-balanced.
+// GQA decode attention over a bf16 KV cache: persistent, tile-balanced,
+// tensor-core tile math.
 //
-// Work: every (batch row m, kv head h) "unit" attends q[m, h*qpg .. +qpg]
-// (all q heads of the GQA group in one pass, so each K/V byte is read once)
-// over keys 0..pos[m], cut into 64-key tiles.  All tiles of all units form
-// one list (row-major units); a fixed grid of ~3 CTAs per SM splits the list
-// into equal contiguous ranges, so every SM streams the same number of KV
-// bytes in a single wave whatever the context lengths.  Each CTA pulls its
-// tiles through a shared-memory ring with 1-D TMA bulk copies (issued ahead,
-// completion on mbarriers with time-bounded waits) and keeps an fp32 online
-// softmax (running max / sum; model.py:266-279, and the chunked update of
-// llama_chunked_attention/kernel.cc:111-257) for the unit it is in.  A unit
-// cut between CTAs leaves one partial (o, max, sum) per CTA; the last CTA to
-// finish it (ticket counter, re-armed) merges them.
+// Work: every (batch row m, kv head h) "unit" attends the qpg q heads of its
+// GQA group (q[m, h*qpg .. +qpg], so each K/V byte is read once) over keys
+// 0..pos[m], cut into 64-key tiles.  All tiles of all units form one list
+// (row-major units); the grid (the CTAs resident at once) splits the list into
+// equal contiguous ranges, so every CTA streams the same number of KV bytes in
+// a single wave whatever the context lengths.
+//
+// Data movement: K and V tiles arrive by 3-D TMA boxes (64 dims x 64 keys, or
+// 64 dims x 16 keys for a tile that ends inside the context, so at most 15
+// unused keys are read) in the 128-byte swizzled layout, which keeps the
+// ldmatrix reads below free of bank conflicts.  The boxes land in a ring of
+// shared-memory stages refilled ahead of use; completion is counted on
+// mbarriers whose waits are time-bounded.
+//
+// Math (mma.sync m16n8k16, bf16 operands, fp32 accumulation), keys on the M
+// side and the group's q heads on N (up to 8): warp w owns keys 16w..16w+15 of
+// every tile and keeps its own online softmax for them (running max and sum
+// per head, in the log2 domain; model.py:266-279, and the chunked update of
+// llama_chunked_attention/kernel.cc:111-257):
+//   S^T [16 keys x 8 heads]  = K_w . q^T                  HD/16 MMAs
+//   P^T = 2^(S^T * log2(e)/sqrt(HD) - max), bf16, moved into the B-operand
+//         layout in registers (movmatrix.trans)
+//   O^T [HD x 8 heads]      += V_w^T . P^T                HD/16 MMAs
+// At a unit's end the four warps' (o, max, sum) are combined in shared memory.
+// A unit cut between CTAs leaves one normalised partial (o, max, sum) per CTA;
+// the last CTA to finish it (ticket counter, re-armed) merges them.
 //
 // The same kernel reads the reference's packet cache
 // ([group][chunk][K 64*hd | V 64*hd | mask 64], decode_packet_cache.py:11-43):
@@ -19,57 +34,107 @@
 // (attention_reference.py:153-154).
 
 #include <algorithm>
+#include <math.h>
 
 #include "t2b_common.cuh"
 #include "launch.cuh"
+#include "tmap.cuh"
 
 namespace t2b {
 
 constexpr int AT_THREADS = 128;
-constexpr int AT_TILE = 64;
-constexpr int AT_STAGES = 2;
+constexpr int AT_WARPS = AT_THREADS / 32;
+constexpr int AT_TILE = 64;            // keys per ring stage
+constexpr int AT_SUB = 16;             // keys per warp slice, and per box of a partial tile
 constexpr int AT_MAX_CTAS_PER_SM = 4;  // workspace bound; the grid uses the measured occupancy
 constexpr int AT_MAX_ROWS = 256;
+constexpr int AT_MERGE_BATCH = 32;     // partial records weighed per pass of a cross-CTA merge
 
 struct AttnParams {
-  const __nv_bfloat16* q;    // [rows][n_heads*hd]
-  const __nv_bfloat16* k0;   // key 0 of (row 0, kv head 0)
-  const __nv_bfloat16* v0;
-  const __nv_bfloat16* mask0;  // nullable (packet mode)
-  long long stride_row;      // elements between batch rows
-  long long stride_head;     // elements between kv heads
-  long long tile_stride;     // elements between 64-key tiles
-  const int* pos;            // nullable: keys = pos[m] + 1 (clamped to [1, n_keys]), else n_keys
-  int n_keys;                // packet mode: keys per unit; cache mode: max_ctx
+  CUtensorMap kmap_full;  // box: 64 dims x 64 keys
+  CUtensorMap vmap_full;
+  CUtensorMap kmap_sub;   // box: 64 dims x 16 keys
+  CUtensorMap vmap_sub;
+  const __nv_bfloat16* q;      // [rows][n_heads*hd]
+  const __nv_bfloat16* mask0;  // nullable (packet mode): mask of (unit u, tile j) at mask0 + u*mask_unit + j*mask_tile
+  long long mask_unit, mask_tile;
+  int tile_y, unit_z, tile_z;  // TMA coordinates of (unit u, tile j): y = j*tile_y, z = u*unit_z + j*tile_z
+  const int* pos;              // nullable: keys = pos[m] + 1 (clamped to [1, n_keys]), else n_keys
+  int n_keys;                  // packet mode: keys per unit; cache mode: max_ctx
   int rows;
-  __nv_bfloat16* out;        // [rows][n_heads*hd]
+  __nv_bfloat16* out;          // [rows][n_heads*hd]
   int n_heads, n_kv;
-  float scale;
-  float* ws;                 // partial records [grid][2][qpg][hd + 2]
-  int* cnt;                  // [rows][n_kv] tickets
+  float scale_log2;            // log2(e) / sqrt(hd)
+  float* ws;                   // partial records [grid][2][qpg][hd + 2]
+  int* cnt;                    // [rows][n_kv] tickets
   int* err;
 };
 
-template <int HD, int QPG>
-struct AttnSmem {
-  float q[QPG][HD];
-  __nv_bfloat16 k[AT_STAGES][AT_TILE][HD];
-  __nv_bfloat16 v[AT_STAGES][AT_TILE][HD];
-  __nv_bfloat16 msk[AT_STAGES][AT_TILE];
-  __nv_bfloat16 qb[AT_STAGES][QPG * HD];  // q heads of a unit, copied with the unit's first tile
-  float p[QPG][AT_TILE];
-  float corr[QPG];
-  float mrun[QPG];
-  float lrun[QPG];
-  int row_start[AT_MAX_ROWS + 1];  // first global tile index of row m (all its kv heads)
-  int row_tiles[AT_MAX_ROWS];      // tiles per unit of row m
-  int row_keys[AT_MAX_ROWS];       // keys attended by row m
-  uint64_t bar[AT_STAGES];
+template <int HD>
+struct AtGeom {
+  static constexpr int HALVES = HD / 64;                 // 128-byte swizzle spans per key row
+  static constexpr int STAGES = HD >= 128 ? 3 : 4;
+  static constexpr int HALF_BYTES = AT_TILE * 128;       // 64 keys x 64 dims
+  static constexpr int KV_BYTES = HALVES * HALF_BYTES;   // K (or V) of one tile
+  static constexpr int STAGE_BYTES = 2 * KV_BYTES;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
 };
+
+template <int HD, int QPG>
+struct AttnAux {
+  static constexpr int STAGES = AtGeom<HD>::STAGES;
+  __nv_bfloat16 qb[STAGES][QPG * HD];  // q heads of a unit, copied with the unit's first tile
+  __nv_bfloat16 msk[STAGES][AT_TILE];
+  float ow[AT_WARPS][QPG][HD];         // per-warp (o, max, sum) at a unit's end
+  float mw[AT_WARPS][QPG];
+  float lw[AT_WARPS][QPG];
+  float wpart[AT_MERGE_BATCH][QPG];    // cross-CTA merge weights
+  float mh[QPG], dh[QPG];
+  int row_start[AT_MAX_ROWS + 1];      // first global tile index of row m (all its kv heads)
+  int row_tiles[AT_MAX_ROWS];          // tiles per unit of row m
+  int row_keys[AT_MAX_ROWS];           // keys attended by row m
+  int flag;
+  uint64_t bar[STAGES];
+};
+
+template <int HD, int QPG>
+constexpr size_t attn_smem_bytes() {
+  return 1024 + AtGeom<HD>::RING_BYTES + sizeof(AttnAux<HD, QPG>);
+}
 
 struct TileRef {
   int m, h, j, nt;  // unit (m, h), tile j of nt
 };
+
+// ---- warp-level tensor-core helpers (sm_80+ forms, valid on sm_100a) ----
+T2B_DEV void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+T2B_DEV void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+T2B_DEV uint32_t movm_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+T2B_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+T2B_DEV uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
 
 // Keys attended by row m: pos[m] + 1, kept inside the cache whatever pos holds.
 T2B_DEV int keys_of_row_global(const AttnParams& P, int m) {
@@ -78,8 +143,8 @@ T2B_DEV int keys_of_row_global(const AttnParams& P, int m) {
   return k < 1 ? 1 : (k > P.n_keys ? P.n_keys : k);
 }
 
-template <int HD, int QPG>
-T2B_DEV TileRef locate(const AttnSmem<HD, QPG>& S, int rows, int t) {
+template <class Aux>
+T2B_DEV TileRef locate(const Aux& S, int rows, int t) {
   int lo = 0, hi = rows - 1;  // last row with row_start <= t
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -99,22 +164,48 @@ T2B_DEV TileRef locate(const AttnSmem<HD, QPG>& S, int rows, int t) {
 T2B_DEV int range_lo(long long c, long long T, long long NP) { return (int)(c * T / NP); }
 T2B_DEV int cta_of_tile(long long t, long long T, long long NP) { return (int)(((t + 1) * NP + T - 1) / T - 1); }
 
-template <int HD, int QPG>
-T2B_DEV int record_slot(const AttnSmem<HD, QPG>& S, int rows, long long T, long long NP, int cta, int m, int h) {
-  const TileRef f = locate(S, rows, range_lo(cta, T, NP));
-  return (f.m == m && f.h == h) ? 0 : 1;  // slot 0: the CTA's first unit, slot 1: its last
+// Last-arrival ticket for a unit's partial records: every thread's record
+// stores precede thread 0's fenced increment (CTA barrier, then a gpu-scope
+// fence); the last arrival re-arms the counter and fences before its reads.
+template <class Aux>
+T2B_DEV bool unit_ticket(Aux& S, int* counter, int arrivals) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(counter, 1);
+    const int last = prev == arrivals - 1;
+    if (last) {
+      atomicExch(counter, 0);
+      __threadfence();
+    }
+    S.flag = last;
+  }
+  __syncthreads();
+  return S.flag != 0;
 }
 
 template <int HD, int QPG>
-__global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const AttnParams P) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  AttnSmem<HD, QPG>& S = *reinterpret_cast<AttnSmem<HD, QPG>*>(smem_raw);
+__global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __grid_constant__ AttnParams P) {
+  using G = AtGeom<HD>;
+  using Aux = AttnAux<HD, QPG>;
+  constexpr int STAGES = G::STAGES;
+  constexpr int NT16 = HD / 16;  // k-steps of K.q^T, and 16-dim m-tiles of O^T
+  constexpr int REC = HD + 2;
+  constexpr int NPAIR = QPG * HD / 2;
+  constexpr int EPT = (NPAIR + AT_THREADS - 1) / AT_THREADS;
+  static_assert(QPG >= 1 && QPG <= 8, "q heads per kv head: 1..8");
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* ring =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Aux& S = *reinterpret_cast<Aux*>(ring + G::RING_BYTES);
+  const uint32_t ring_s = smem_u32(ring);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
   const int c = blockIdx.x;
   T2B_TRACE_BEGIN(10, P.n_heads);
 
   if (tid == 0) {
-    for (int i = 0; i < AT_STAGES; ++i) mbar_init(&S.bar[i], 1);
+    for (int i = 0; i < STAGES; ++i) mbar_init(&S.bar[i], 1);
     fence_mbar_init();
   }
   grid_dep_wait();
@@ -152,178 +243,270 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const Attn
   const int t_lo = range_lo(c, T, NP), t_hi = range_lo(c + 1, T, NP);
   const int count = t_hi - t_lo;
 
-  auto issue = [&](int i) {  // tile i of this CTA into stage i % AT_STAGES (+ q on a unit's first tile)
+  // tile i of this CTA into stage i % STAGES (+ q on a unit's first tile here)
+  auto issue = [&](int i) {
     const TileRef r = locate(S, rows, t_lo + i);
     const int nk = min(AT_TILE, S.row_keys[r.m] - r.j * AT_TILE);
-    const uint32_t bytes = (uint32_t)nk * HD * 2;
-    const int st = i % AT_STAGES;
-    const long long base =
-        (long long)r.m * P.stride_row + (long long)r.h * P.stride_head + (long long)r.j * P.tile_stride;
-    const uint32_t mbytes = P.mask0 ? (uint32_t)AT_TILE * 2 : 0u;
+    const int st = i % STAGES;
+    const bool full = nk == AT_TILE;
+    const int nbox = full ? 1 : (nk + AT_SUB - 1) / AT_SUB;
+    const uint32_t box_bytes = full ? (uint32_t)G::HALF_BYTES : (uint32_t)(AT_SUB * 128);
     const bool with_q = (i == 0) || (r.j == 0);
     const uint32_t qbytes = with_q ? (uint32_t)(QPG * HD * 2) : 0u;
-    mbar_arrive_expect_tx(&S.bar[st], 2 * bytes + mbytes + qbytes);
-    bulk_g2s(&S.k[st][0][0], P.k0 + base, bytes, &S.bar[st]);
-    bulk_g2s(&S.v[st][0][0], P.v0 + base, bytes, &S.bar[st]);
-    if (P.mask0) bulk_g2s(&S.msk[st][0], P.mask0 + base, mbytes, &S.bar[st]);
-    if (with_q) bulk_g2s(&S.qb[st][0], P.q + (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD, qbytes, &S.bar[st]);
+    const uint32_t mbytes = P.mask0 ? (uint32_t)(AT_TILE * 2) : 0u;
+    mbar_arrive_expect_tx(&S.bar[st], 2u * G::HALVES * nbox * box_bytes + qbytes + mbytes);
+    const int u = r.m * P.n_kv + r.h;
+    const int y0 = r.j * P.tile_y;
+    const int z = u * P.unit_z + r.j * P.tile_z;
+    unsigned char* kdst = ring + st * G::STAGE_BYTES;
+    unsigned char* vdst = kdst + G::KV_BYTES;
+    const void* km = full ? (const void*)&P.kmap_full : (const void*)&P.kmap_sub;
+    const void* vm = full ? (const void*)&P.vmap_full : (const void*)&P.vmap_sub;
+    for (int hf = 0; hf < G::HALVES; ++hf)
+      for (int b = 0; b < nbox; ++b) {
+        const int off = hf * G::HALF_BYTES + b * AT_SUB * 128;
+        tma_load_3d(kdst + off, km, hf * 64, y0 + b * AT_SUB, z, &S.bar[st]);
+        tma_load_3d(vdst + off, vm, hf * 64, y0 + b * AT_SUB, z, &S.bar[st]);
+      }
+    if (P.mask0) bulk_g2s(&S.msk[st][0], P.mask0 + u * P.mask_unit + r.j * P.mask_tile, mbytes, &S.bar[st]);
+    if (with_q)
+      bulk_g2s(&S.qb[st][0], P.q + (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD, qbytes, &S.bar[st]);
   };
   if (tid == 0)
-    for (int i = 0; i < AT_STAGES && i < count; ++i) issue(i);
+    for (int i = 0; i < STAGES && i < count; ++i) issue(i);
 
-  constexpr int NPAIR = (QPG * HD / 2 + AT_THREADS - 1) / AT_THREADS;
-  float o[NPAIR][2];
-  constexpr int QH = QPG * HD;
+  const int kb = AT_SUB * warp;  // this warp's first key in a tile
+  const int h0 = 2 * t4, h1 = h0 + 1;
+  float o[NT16][4];
+  uint32_t qf[NT16][2];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads h0, h1 (log2 domain)
+
   for (int i = 0; i < count; ++i) {
     const TileRef r = locate(S, rows, t_lo + i);
     const bool unit_begin = (i == 0) || (r.j == 0);
     const bool unit_end = (i == count - 1) || (r.j == r.nt - 1);
-    const int st = i % AT_STAGES;
+    const int st = i % STAGES;
     // every thread takes the same outcome, so no thread is left at a barrier
-    const bool ok = __syncthreads_and(mbar_wait_bounded(&S.bar[st], (i / AT_STAGES) & 1, P.err));
+    const bool ok = __syncthreads_and(mbar_wait_bounded(&S.bar[st], (i / STAGES) & 1, P.err));
     if (!ok) break;  // timeout recorded in P.err
     if (i == 0) T2B_TRACE_MARK(2);
-    if (unit_begin) {  // new unit: its q heads (arrived with this tile), fresh softmax state
-      for (int e = tid; e < QH; e += AT_THREADS) S.q[e / HD][e % HD] = __bfloat162float(S.qb[st][e]);
-      if (tid < QPG) {
-        S.mrun[tid] = -INFINITY;
-        S.lrun[tid] = 0.f;
+    if (unit_begin) {  // new unit: B operand q^T (heads >= QPG are zero columns), fresh softmax state
+      const __nv_bfloat16* qs = &S.qb[st][0];
+#pragma unroll
+      for (int ks = 0; ks < NT16; ++ks) {
+        qf[ks][0] = g < QPG ? *reinterpret_cast<const uint32_t*>(qs + g * HD + ks * 16 + 2 * t4) : 0u;
+        qf[ks][1] = g < QPG ? *reinterpret_cast<const uint32_t*>(qs + g * HD + ks * 16 + 2 * t4 + 8) : 0u;
       }
 #pragma unroll
-      for (int e = 0; e < NPAIR; ++e) o[e][0] = o[e][1] = 0.f;
-      __syncthreads();
+      for (int mt = 0; mt < NT16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
     }
     const int nk = min(AT_TILE, S.row_keys[r.m] - r.j * AT_TILE);
-    // scores: one (head, key) per thread-iteration; 16-byte K chunks rotated by
-    // key index so the 8 lanes of a quarter-warp hit distinct banks
-    for (int sidx = tid; sidx < QPG * AT_TILE; sidx += AT_THREADS) {
-      const int hh = sidx / AT_TILE, j = sidx - hh * AT_TILE;
-      float sc = -INFINITY;
-      bool live = j < nk;
-      if (live && P.mask0) live = __bfloat162float(S.msk[st][j]) > 0.5f;
-      if (live) {
-        float a = 0.f;
-#pragma unroll
-        for (int c0 = 0; c0 < HD / 8; ++c0) {
-          const int cc = (c0 + j) & (HD / 8 - 1);
-          const uint4 kv = *reinterpret_cast<const uint4*>(&S.k[st][j][cc * 8]);
-          const float* qq = &S.q[hh][cc * 8];
-          const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            a = fmaf(qq[2 * e], __uint_as_float(w[e] << 16), a);
-            a = fmaf(qq[2 * e + 1], __uint_as_float(w[e] & 0xffff0000u), a);
-          }
+    if (kb < nk) {  // warp-uniform
+      unsigned char* kst = ring + st * G::STAGE_BYTES;
+      unsigned char* vst = kst + G::KV_BYTES;
+      if (nk < kb + AT_SUB) {
+        // keys past the context in this slice: their P is 0, but 0 * (stale
+        // V) must not turn into NaN, so the rows are cleared
+        const int nz = (kb + AT_SUB - nk) * G::HALVES * 8;
+        for (int e = lane; e < nz; e += 32) {
+          const int row = nk + e / (G::HALVES * 8), cc = e % (G::HALVES * 8);
+          *reinterpret_cast<uint4*>(vst + (cc >> 3) * G::HALF_BYTES + row * 128 + (cc & 7) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
         }
-        sc = a * P.scale;
+        __syncwarp();
       }
-      S.p[hh][j] = sc;
-    }
-    __syncthreads();
-    // online softmax update, one warp per head
-    for (int hh = warp; hh < QPG; hh += AT_THREADS / 32) {
-      const float s0 = S.p[hh][lane], s1 = S.p[hh][lane + 32];
-      const float tmax = warp_max(fmaxf(s0, s1));
-      const float mold = S.mrun[hh];
-      const float mnew = fmaxf(mold, tmax);
-      float p0 = 0.f, p1 = 0.f, corr = 1.f;
-      if (mnew != -INFINITY) {
-        p0 = __expf(s0 - mnew);
-        p1 = __expf(s1 - mnew);
-        corr = (mold == -INFINITY) ? 0.f : __expf(mold - mnew);
-      }
-      S.p[hh][lane] = p0;
-      S.p[hh][lane + 32] = p1;
-      const float psum = warp_sum(p0 + p1);
-      if (lane == 0) {
-        S.lrun[hh] = S.lrun[hh] * corr + psum;
-        S.mrun[hh] = mnew;
-        S.corr[hh] = corr;
-      }
-    }
-    __syncthreads();
-    // o = o * corr + P . V
+      // S^T = K_w . q^T
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      const int krow = kb + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-    for (int e = 0; e < NPAIR; ++e) {
-      const int pr = tid + e * AT_THREADS;
-      if (pr < QPG * HD / 2) {
-        const int hh = pr / (HD / 2), d2 = pr - hh * (HD / 2);
-        const float corr = S.corr[hh];
-        float a0 = o[e][0] * corr, a1 = o[e][1] * corr;
-        for (int j = 0; j < nk; ++j) {
-          const float pj = S.p[hh][j];
-          const uint32_t vv = *reinterpret_cast<const uint32_t*>(&S.v[st][j][2 * d2]);
-          a0 = fmaf(pj, __uint_as_float(vv << 16), a0);
-          a1 = fmaf(pj, __uint_as_float(vv & 0xffff0000u), a1);
-        }
-        o[e][0] = a0;
-        o[e][1] = a1;
+      for (int ks = 0; ks < NT16; ++ks) {
+        const int ch = (ks & 3) * 2 + (lane >> 4);
+        uint32_t a[4];
+        ldsm_x4(a, smem_u32(kst) + (ks >> 2) * G::HALF_BYTES + krow * 128 + ((ch ^ (krow & 7)) << 4));
+        mma_bf16(s, a, qf[ks][0], qf[ks][1]);
+      }
+      // online softmax over this warp's 16 keys (rows g, g+8; heads h0, h1)
+      const int k0 = kb + g, k1 = k0 + 8;
+      bool live0 = k0 < nk, live1 = k1 < nk;
+      if (P.mask0) {
+        live0 = live0 && __bfloat162float(S.msk[st][k0]) > 0.5f;
+        live1 = live1 && __bfloat162float(S.msk[st][k1]) > 0.5f;
+      }
+      const float x0 = live0 ? s[0] * P.scale_log2 : -INFINITY;
+      const float x1 = live0 ? s[1] * P.scale_log2 : -INFINITY;
+      const float x2 = live1 ? s[2] * P.scale_log2 : -INFINITY;
+      const float x3 = live1 ? s[3] * P.scale_log2 : -INFINITY;
+      float tm0 = fmaxf(x0, x2), tm1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, off));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, off));
+      }
+      const float n0 = fmaxf(m0, tm0), n1 = fmaxf(m1, tm1);
+      const float c0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - n0);
+      const float c1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - n1);
+      const float p0 = live0 ? exp2f(x0 - n0) : 0.f;
+      const float p1 = live0 ? exp2f(x1 - n1) : 0.f;
+      const float p2 = live1 ? exp2f(x2 - n0) : 0.f;
+      const float p3 = live1 ? exp2f(x3 - n1) : 0.f;
+      m0 = n0;
+      m1 = n1;
+      l0 = l0 * c0 + p0 + p2;
+      l1 = l1 * c1 + p1 + p3;
+#pragma unroll
+      for (int mt = 0; mt < NT16; ++mt) {
+        o[mt][0] *= c0;
+        o[mt][1] *= c1;
+        o[mt][2] *= c0;
+        o[mt][3] *= c1;
+      }
+      // P^T as the B operand: transpose the two 8x8 (key x head) blocks
+      const uint32_t b0 = movm_t(pack_bf16(p0, p1));
+      const uint32_t b1 = movm_t(pack_bf16(p2, p3));
+      // O^T += V_w^T . P^T
+      const int vkey = kb + ((lane >> 4) << 3) + (lane & 7);
+#pragma unroll
+      for (int mt = 0; mt < NT16; ++mt) {
+        const int dch = 2 * mt + ((lane >> 3) & 1);
+        uint32_t a[4];
+        ldsm_x4_t(a, smem_u32(vst) + (dch >> 3) * G::HALF_BYTES + vkey * 128 + (((dch & 7) ^ (vkey & 7)) << 4));
+        mma_bf16(o[mt], a, b0, b1);
       }
     }
-    __syncthreads();  // stage consumed; softmax state final for this tile
-    if (tid == 0 && i + AT_STAGES < count) {
+    __syncthreads();  // stage consumed
+    if (tid == 0 && i + STAGES < count) {
       fence_proxy_async();
-      issue(i + AT_STAGES);
+      issue(i + STAGES);
     }
     if (!unit_end) continue;
 
-    // ---- unit (or this CTA's share of it) done ----
+    // ---- unit (or this CTA's share of it) done: combine the four warps ----
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    if (g == 0) {
+      if (h0 < QPG) {
+        S.mw[warp][h0] = m0;
+        S.lw[warp][h0] = l0;
+      }
+      if (h1 < QPG) {
+        S.mw[warp][h1] = m1;
+        S.lw[warp][h1] = l1;
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < NT16; ++mt) {
+      if (h0 < QPG) {
+        S.ow[warp][h0][16 * mt + g] = o[mt][0];
+        S.ow[warp][h0][16 * mt + g + 8] = o[mt][2];
+      }
+      if (h1 < QPG) {
+        S.ow[warp][h1][16 * mt + g] = o[mt][1];
+        S.ow[warp][h1][16 * mt + g + 8] = o[mt][3];
+      }
+    }
+    __syncthreads();
+    const int u = r.m * P.n_kv + r.h;
     const size_t obase = (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD;
     const int unit_t0 = S.row_start[r.m] + r.h * r.nt;  // global index of the unit's first tile
     const int c1 = cta_of_tile(unit_t0, T, NP), c2 = cta_of_tile(unit_t0 + r.nt - 1, T, NP);
-    if (c1 == c2) {  // the whole unit ran here
+    const bool whole = c1 == c2;
+    // record slot: 0 for the unit this CTA's range starts in, 1 for a later one
+    float* rec = P.ws + ((size_t)c * 2 + (t_lo >= unit_t0 ? 0 : 1)) * QPG * REC;
 #pragma unroll
-      for (int e = 0; e < NPAIR; ++e) {
-        const int pr = tid + e * AT_THREADS;
-        if (pr < QPG * HD / 2) {
-          const int hh = pr / (HD / 2), d2 = pr - hh * (HD / 2);
-          const float l = S.lrun[hh];
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          *reinterpret_cast<__nv_bfloat162*>(&P.out[obase + hh * HD + 2 * d2]) =
-              __floats2bfloat162_rn(o[e][0] * inv, o[e][1] * inv);
+    for (int k = 0; k < EPT; ++k) {
+      const int e = tid + k * AT_THREADS;
+      if (e < NPAIR) {
+        const int hh = (2 * e) / HD, d = (2 * e) % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < AT_WARPS; ++w) M = fmaxf(M, S.mw[w][hh]);
+        float den = 0.f, a0 = 0.f, a1 = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+          for (int w = 0; w < AT_WARPS; ++w) {
+            const float mw = S.mw[w][hh];
+            const float wt = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+            den += wt * S.lw[w][hh];
+            a0 += wt * S.ow[w][hh][d];
+            a1 += wt * S.ow[w][hh][d + 1];
+          }
+        }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        if (whole) {
+          *reinterpret_cast<__nv_bfloat162*>(&P.out[obase + hh * HD + d]) = __floats2bfloat162_rn(a0 * inv, a1 * inv);
+        } else {
+          *reinterpret_cast<float2*>(&rec[hh * REC + d]) = make_float2(a0 * inv, a1 * inv);
+          if (d == 0) *reinterpret_cast<float2*>(&rec[hh * REC + HD]) = make_float2(M, den);
         }
       }
-      continue;
     }
-    // partial: publish (o, max, sum); the unit's last CTA merges every part
-    constexpr int REC = HD + 2;
-    float* mine = P.ws + ((size_t)c * 2 + record_slot(S, rows, T, NP, c, r.m, r.h)) * QPG * REC;
-#pragma unroll
-    for (int e = 0; e < NPAIR; ++e) {
-      const int pr = tid + e * AT_THREADS;
-      if (pr < QPG * HD / 2) {
-        const int hh = pr / (HD / 2), d2 = pr - hh * (HD / 2);
-        mine[hh * REC + 2 * d2] = o[e][0];
-        mine[hh * REC + 2 * d2 + 1] = o[e][1];
-      }
-    }
-    if (tid < QPG) {
-      mine[tid * REC + HD] = S.mrun[tid];
-      mine[tid * REC + HD + 1] = S.lrun[tid];
-    }
-    if (!split_ticket(P.cnt + (size_t)r.m * P.n_kv + r.h, c2 - c1 + 1)) continue;
-    for (int e = tid; e < QH; e += AT_THREADS) {
-      const int hh = e / HD, d = e - hh * HD;
-      float mx = -INFINITY;
-      for (int cc = c1; cc <= c2; ++cc) {
-        const int sl = record_slot(S, rows, T, NP, cc, r.m, r.h);
-        mx = fmaxf(mx, ldcg(P.ws + ((size_t)cc * 2 + sl) * QPG * REC + hh * REC + HD));
-      }
-      float num = 0.f, den = 0.f;
-      if (mx != -INFINITY) {
-        for (int cc = c1; cc <= c2; ++cc) {
-          const int sl = record_slot(S, rows, T, NP, cc, r.m, r.h);
-          const float* rr = P.ws + ((size_t)cc * 2 + sl) * QPG * REC + hh * REC;
-          const float ms = ldcg(rr + HD);
-          if (ms == -INFINITY) continue;
-          const float w = __expf(ms - mx);
-          num += w * ldcg(rr + d);
-          den += w * ldcg(rr + HD + 1);
+    if (whole) continue;
+
+    // ---- partial: the unit's last CTA merges every part ----
+    if (!unit_ticket(S, P.cnt + u, c2 - c1 + 1)) continue;
+    const int n = c2 - c1 + 1;
+    const int first_slot = range_lo(c1, T, NP) >= unit_t0 ? 0 : 1;
+    auto part = [&](int p) -> const float* {
+      return P.ws + ((size_t)(c1 + p) * 2 + (p == 0 ? first_slot : 0)) * QPG * REC;
+    };
+    for (int hh = warp; hh < QPG; hh += AT_WARPS) {  // per head: max and weighted sum over the parts
+      float M = -INFINITY;
+      for (int p = lane; p < n; p += 32) M = fmaxf(M, ldcg(part(p) + hh * REC + HD));
+      M = warp_max(M);
+      float den = 0.f;
+      if (M != -INFINITY)
+        for (int p = lane; p < n; p += 32) {
+          const float mp = ldcg(part(p) + hh * REC + HD);
+          if (mp != -INFINITY) den += exp2f(mp - M) * ldcg(part(p) + hh * REC + HD + 1);
         }
+      den = warp_sum(den);
+      if (lane == 0) {
+        S.mh[hh] = M;
+        S.dh[hh] = den;
       }
-      P.out[obase + hh * HD + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
     }
     __syncthreads();
+    float acc[EPT][2];
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) acc[k][0] = acc[k][1] = 0.f;
+    for (int b0 = 0; b0 < n; b0 += AT_MERGE_BATCH) {
+      const int nb = min(AT_MERGE_BATCH, n - b0);
+      for (int e = tid; e < nb * QPG; e += AT_THREADS) {
+        const int p = e / QPG, hh = e - p * QPG;
+        const float* rr = part(b0 + p) + hh * REC;
+        const float mp = ldcg(rr + HD), M = S.mh[hh], den = S.dh[hh];
+        S.wpart[p][hh] = (mp == -INFINITY || !(den > 0.f)) ? 0.f : exp2f(mp - M) * ldcg(rr + HD + 1) / den;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < EPT; ++k) {
+        const int e = tid + k * AT_THREADS;
+        if (e < NPAIR) {
+          const int hh = (2 * e) / HD, d = (2 * e) % HD;
+#pragma unroll 4
+          for (int p = 0; p < nb; ++p) {
+            const float wt = S.wpart[p][hh];
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(part(b0 + p) + hh * REC + d));
+            acc[k][0] += wt * v.x;
+            acc[k][1] += wt * v.y;
+          }
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      const int e = tid + k * AT_THREADS;
+      if (e < NPAIR) {
+        const int hh = (2 * e) / HD, d = (2 * e) % HD;
+        *reinterpret_cast<__nv_bfloat162*>(&P.out[obase + hh * HD + d]) = __floats2bfloat162_rn(acc[k][0], acc[k][1]);
+      }
+    }
   }
   T2B_TRACE_MARK(3);
 }
@@ -355,12 +538,36 @@ size_t attention_workspace_bytes(int rows, int n_heads, int n_kv, int head_dim, 
   return part + (((size_t)rows * n_kv * sizeof(int) + 255) & ~size_t(255));
 }
 
+// Four tensor maps over a K and a V region viewed as [units][keys][hd] bf16
+// (keys `key_stride` bytes apart, units `unit_stride` bytes apart), boxes of
+// 64 dims x 64 keys and 64 dims x 16 keys, 128-byte swizzle; keys past
+// `keys` read as zero.
+static int make_kv_maps(AttnParams& P, const void* k, const void* v, int hd, long long keys, long long units,
+                        long long key_stride, long long unit_stride) {
+  const EncodeTiledFn encode = encode_tiled();
+  if (encode == nullptr) return T2B_ERR_LAUNCH;
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) return T2B_ERR_ALIGN;
+  if ((key_stride | unit_stride) & 15) return T2B_ERR_ALIGN;
+  cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)keys, (cuuint64_t)units};
+  cuuint64_t strides[2] = {(cuuint64_t)key_stride, (cuuint64_t)unit_stride};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMap* maps[4] = {&P.kmap_full, &P.vmap_full, &P.kmap_sub, &P.vmap_sub};
+  for (int i = 0; i < 4; ++i) {
+    cuuint32_t box[3] = {64, (cuuint32_t)(i < 2 ? AT_TILE : AT_SUB), 1};
+    CUresult r = encode(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(i % 2 ? v : k), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return T2B_ERR_ARG;
+  }
+  return T2B_OK;
+}
+
 // One wave: as many CTAs as are resident at once (capped by the tile count
 // and the workspace bound).
 template <int HD, int QPG>
 static int attn_launch_t(AttnParams& P, int max_grid, cudaStream_t st) {
   auto kern = decode_attention_kernel<HD, QPG>;
-  const size_t smem = sizeof(AttnSmem<HD, QPG>);
+  const size_t smem = attn_smem_bytes<HD, QPG>();
   if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, AT_THREADS, smem) != cudaSuccess || per_sm < 1)
@@ -383,8 +590,8 @@ int attention_launch(AttnParams& P, int rows, int head_dim, int max_keys, void* 
   P.ws = reinterpret_cast<float*>(ws);
   P.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + part);
   P.rows = rows;
-  P.scale = 1.f / sqrtf((float)head_dim);
-#define T2B_ACASE(hd, qpg_)                                          \
+  P.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+#define T2B_ACASE(hd, qpg_) \
   if (head_dim == hd && qpg == qpg_) return attn_launch_t<hd, qpg_>(P, grid, st);
   T2B_ACASE(128, 1) T2B_ACASE(128, 2) T2B_ACASE(128, 4) T2B_ACASE(128, 8)
   T2B_ACASE(64, 1) T2B_ACASE(64, 2) T2B_ACASE(64, 4) T2B_ACASE(64, 8)
@@ -408,15 +615,19 @@ extern "C" int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, 
                                     const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv, int head_dim,
                                     int max_ctx, void* ws, size_t ws_bytes, void* stream) {
   if (!q || !k_cache || !v_cache || !pos || !out) return T2B_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) return T2B_ERR_ALIGN;
-  if (max_ctx % 8) return T2B_ERR_SHAPE;  // keeps every 64-key tile 16-byte aligned
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+       reinterpret_cast<uintptr_t>(q)) & 15)
+    return T2B_ERR_ALIGN;
+  if (max_ctx % 8 || (head_dim != 64 && head_dim != 128) || M < 1 || n_kv < 1) return T2B_ERR_SHAPE;
   AttnParams P{};
+  const int mk = make_kv_maps(P, k_cache, v_cache, head_dim, max_ctx, (long long)M * n_kv, (long long)head_dim * 2,
+                              (long long)max_ctx * head_dim * 2);
+  if (mk != T2B_OK) return mk;
   P.q = reinterpret_cast<const __nv_bfloat16*>(q);
-  P.k0 = reinterpret_cast<const __nv_bfloat16*>(k_cache);
-  P.v0 = reinterpret_cast<const __nv_bfloat16*>(v_cache);
-  P.stride_head = (long long)max_ctx * head_dim;
-  P.stride_row = (long long)n_kv * P.stride_head;
-  P.tile_stride = (long long)AT_TILE * head_dim;
+  P.mask0 = nullptr;
+  P.tile_y = AT_TILE;
+  P.unit_z = 1;
+  P.tile_z = 0;
   P.pos = pos;
   P.n_keys = max_ctx;
   P.out = reinterpret_cast<__nv_bfloat16*>(out);
@@ -430,16 +641,22 @@ extern "C" int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, u
                                     size_t ws_bytes, void* stream) {
   if (!q || !packet || !out) return T2B_ERR_ARG;
   if (chunk != AT_TILE || packet_seq_len < chunk || packet_seq_len % chunk) return T2B_ERR_SHAPE;
-  if (reinterpret_cast<uintptr_t>(packet) & 15) return T2B_ERR_ALIGN;
-  const long long chunk_el = 2LL * chunk * head_dim + chunk;
+  if (head_dim != 64 && head_dim != 128) return T2B_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(packet) | reinterpret_cast<uintptr_t>(q)) & 15) return T2B_ERR_ALIGN;
+  const long long chunk_el = 2LL * chunk * head_dim + chunk;  // K, V, mask of one chunk
+  const long long n_chunks = packet_seq_len / chunk;
+  const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(packet);
   AttnParams P{};
+  const int mk = make_kv_maps(P, base, base + (long long)chunk * head_dim, head_dim, chunk, n_groups * n_chunks,
+                              (long long)head_dim * 2, chunk_el * 2);
+  if (mk != T2B_OK) return mk;
   P.q = reinterpret_cast<const __nv_bfloat16*>(q);
-  P.k0 = reinterpret_cast<const __nv_bfloat16*>(packet);
-  P.v0 = P.k0 + (long long)chunk * head_dim;
-  P.mask0 = P.k0 + 2LL * chunk * head_dim;
-  P.stride_head = (long long)(packet_seq_len / chunk) * chunk_el;
-  P.stride_row = 0;
-  P.tile_stride = chunk_el;
+  P.mask0 = base + 2LL * chunk * head_dim;
+  P.mask_unit = n_chunks * chunk_el;
+  P.mask_tile = chunk_el;
+  P.tile_y = 0;
+  P.unit_z = (int)n_chunks;
+  P.tile_z = 1;
   P.pos = nullptr;
   P.n_keys = packet_seq_len;
   P.out = reinterpret_cast<__nv_bfloat16*>(out);

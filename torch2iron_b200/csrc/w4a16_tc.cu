@@ -29,6 +29,7 @@
 
 #include "linear_common.cuh"
 #include "launch.cuh"
+#include "tmap.cuh"
 
 namespace t2b {
 
@@ -508,24 +509,6 @@ static int tc_dispatch(LinearParams& p, const TcPlan& pl, cudaStream_t st) {
   if (pl.BP == 128) return tc_launch_t<128, PRO, EPI>(p, pl, st);
   if (pl.BP == 256) return tc_launch_t<256, PRO, EPI>(p, pl, st);
   return T2B_ERR_ARG;
-}
-
-// cuTensorMapEncodeTiled, resolved through the runtime (no link-time libcuda
-// dependency, so the library loads on hosts without a driver).
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      f = nullptr;
-    return reinterpret_cast<EncodeTiledFn>(f);
-  }();
-  return fn;
 }
 
 // 2-D tiled tensor map over the bf16 activations [M][x_ld]: box 64 k x BP rows,
