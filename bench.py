@@ -243,7 +243,7 @@ def kernel_profile(eng, steps):
                 p(lw.qkv.qw), p(lw.qkv.meta), p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps,
                 p(lw.q_norm), p(lw.k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[li]),
                 p(eng.v_cache[li]), p(eng.ssq_b), B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st))
-            rec("decode_attention", lambda: L.t2b_decode_attention(
+            rec("decode_attention", lambda: L.t2b_decode_attention_after_kvwrite(
                 p(eng.q), p(eng.k_cache[li]), p(eng.v_cache[li]), p(eng.pos), p(eng.attn), B, nq, nkv, hd,
                 eng.max_ctx, *eng._ws("attn"), st))
             rec("oproj_residual", lambda: L.t2b_oproj_residual(

@@ -140,6 +140,18 @@ T2B_API int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, con
                          size_t workspace_bytes, void* stream);
 
 /*
+ * Same contract as t2b_decode_attention, for use directly after
+ * t2b_qkv_norm_rope_kvwrite on the same stream (the fused decode layer,
+ * batch_decode_fused.py:426-484): pos and every cache tile older than the
+ * newest key are read while that kernel is still running, so the stream's
+ * preceding kernel may write only q and cache key pos[m] of each row.
+ */
+T2B_API int t2b_decode_attention_after_kvwrite(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                               const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv,
+                                               int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
+                                               void* stream);
+
+/*
  * Attention over the reference's packet cache
  * [group][chunk][K chunk*hd | V chunk*hd | mask chunk] (bf16), skipping slots
  * whose mask <= 0.5, all packet_seq_len slots scanned.  q, out bf16 [G][qpg][hd].

@@ -25,13 +25,13 @@ SMALL = QuantizedQwenConfig(vocab_size=512, emb_dim=256, n_layers=1, n_heads=4, 
                             hidden_dim=512, rms_norm_eps=1e-6, rope_base=1e6)
 
 
-def attention_call(q, kc, vc, pos, n_heads, n_kv, hd, max_ctx):
+def attention_call(q, kc, vc, pos, n_heads, n_kv, hd, max_ctx, fn="t2b_decode_attention"):
     B = q.shape[0]
     out = torch.empty_like(q)
     L = _lib.lib()
     n = max(L.t2b_decode_attention_workspace_bytes(B, n_heads, n_kv, hd, max_ctx), 256)
     ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
-    _lib.call("t2b_decode_attention", _lib.ptr(q), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pos), _lib.ptr(out), B,
+    _lib.call(fn, _lib.ptr(q), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pos), _lib.ptr(out), B,
               n_heads, n_kv, hd, max_ctx, _lib.ptr(ws), n, _lib.stream())
     torch.cuda.synchronize()
     return out
@@ -42,14 +42,24 @@ def attention_call(q, kc, vc, pos, n_heads, n_kv, hd, max_ctx):
     (1, 16, 8, 128, 4096, [4000]),        # split-K path (few CTAs)
     (2, 32, 8, 64, 2304, [2100, 63]),     # Llama shape
     (4, 32, 8, 128, 256, [64, 65, 127, 200]),
+    (64, 16, 8, 128, 256, [150] * 64),    # equal short units: ranges snapped to unit edges
+    (64, 16, 8, 128, 320, "ragged"),      # ragged contexts, short and long units mixed
+    (16, 16, 8, 128, 256, [130 + 7 * i for i in range(16)]),
+    (8, 4, 1, 128, 1024, "ragged"),       # Qwen3-8B tensor-parallel shard: 4 q heads on 1 kv head
+    (2, 8, 1, 128, 256, [255, 31]),       # 8 q heads per kv head
 ])
 def test_decode_attention_vs_oracle(B, nq, nkv, hd, ctx, positions):
     g = torch.Generator().manual_seed(407895018 + B + ctx)
+    if positions == "ragged":
+        positions = torch.randint(0, ctx, (B,), generator=g).tolist()
     q = torch.randn(B, nq * hd, generator=g).to(torch.bfloat16)
     kc = torch.randn(B, nkv, ctx, hd, generator=g).to(torch.bfloat16)
     vc = torch.randn(B, nkv, ctx, hd, generator=g).to(torch.bfloat16)
     pos = torch.tensor(positions, dtype=torch.int32)
     out = attention_call(q.cuda(), kc.cuda(), vc.cuda(), pos.cuda(), nq, nkv, hd, ctx)
+    early = attention_call(q.cuda(), kc.cuda(), vc.cuda(), pos.cuda(), nq, nkv, hd, ctx,
+                           fn="t2b_decode_attention_after_kvwrite")
+    assert torch.equal(out, early)   # same math; only the load order differs
     qpg = nq // nkv
     for r in range(B):
         n = positions[r] + 1

@@ -38,6 +38,7 @@ SIGNATURES = {
     "t2b_qkv_norm_rope_kvwrite": (I, [P, P, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_decode_attention_workspace_bytes": (Z, [I, I, I, I, I]),
     "t2b_decode_attention": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),
+    "t2b_decode_attention_after_kvwrite": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_packet_attention": (I, [P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_oproj_residual_workspace_bytes": (Z, [I, I, I]),
     "t2b_oproj_residual": (I, [P, P, P, P, P, P, P, I, I, I, P, Z, P]),

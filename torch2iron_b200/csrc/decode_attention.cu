@@ -68,6 +68,8 @@ struct AttnParams {
   float* ws;                   // partial records [grid][2][qpg][hd + 2]
   int* cnt;                    // [rows][n_kv] tickets
   int* err;
+  int kv_early;                // 1: pos and every tile but a unit's last may be read before the
+                               // dependency wait (the preceding kernel writes only q and key pos[m])
 };
 
 template <int HD>
@@ -137,9 +139,10 @@ T2B_DEV uint32_t pack_bf16(float lo, float hi) {
 }
 
 // Keys attended by row m: pos[m] + 1, kept inside the cache whatever pos holds.
+// (Read through L2: with kv_early it is read while the preceding kernel runs.)
 T2B_DEV int keys_of_row_global(const AttnParams& P, int m) {
   if (!P.pos) return P.n_keys;
-  const int k = P.pos[m] + 1;
+  const int k = __ldcg(P.pos + m) + 1;
   return k < 1 ? 1 : (k > P.n_keys ? P.n_keys : k);
 }
 
@@ -160,29 +163,41 @@ T2B_DEV TileRef locate(const Aux& S, int rows, int t) {
   return r;
 }
 
-// Contiguous split of T tiles over NP CTAs (NP <= T, so no range is empty).
+// Next tile of the list (call only while one remains).
+template <class Aux>
+T2B_DEV void next_tile(TileRef& r, const Aux& S, int n_kv) {
+  if (++r.j < r.nt) return;
+  r.j = 0;
+  if (++r.h < n_kv) return;
+  r.h = 0;
+  ++r.m;
+  r.nt = S.row_tiles[r.m];
+}
+
+// Even split of T tiles over NP CTAs, and the CTA holding tile t under it.
 T2B_DEV int range_lo(long long c, long long T, long long NP) { return (int)(c * T / NP); }
 T2B_DEV int cta_of_tile(long long t, long long T, long long NP) { return (int)(((t + 1) * NP + T - 1) / T - 1); }
 
-// Last-arrival ticket for a unit's partial records: every thread's record
-// stores precede thread 0's fenced increment (CTA barrier, then a gpu-scope
-// fence); the last arrival re-arms the counter and fences before its reads.
+// First tile of CTA c's range: the even split c*T/NP, moved to the nearer
+// end of its unit when that unit is short (at most snap_max tiles), so a
+// short unit is never cut between CTAs (a range may then be empty).  Only
+// units longer than snap_max are cut, and only at even-split points, so the
+// CTAs holding the first and last tile of such a unit are cta_of_tile() of
+// those tiles.
 template <class Aux>
-T2B_DEV bool unit_ticket(Aux& S, int* counter, int arrivals) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const int prev = atomicAdd(counter, 1);
-    const int last = prev == arrivals - 1;
-    if (last) {
-      atomicExch(counter, 0);
-      __threadfence();
-    }
-    S.flag = last;
-  }
-  __syncthreads();
-  return S.flag != 0;
+T2B_DEV int range_start(const Aux& S, int rows, long long c, long long T, long long NP, int snap_max) {
+  if (c <= 0) return 0;
+  if (c >= NP) return (int)T;
+  const int b = range_lo(c, T, NP);
+  const TileRef r = locate(S, rows, b);
+  if (r.j == 0 || r.nt > snap_max) return b;
+  return 2 * r.j <= r.nt ? b - r.j : b - r.j + r.nt;
 }
+
+// A unit cut between CTAs c1..c2 (its tiles t0 .. t0+nt-1).
+struct SplitUnit {
+  int m, h, t0, c1, c2;
+};
 
 template <int HD, int QPG>
 __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __grid_constant__ AttnParams P) {
@@ -198,7 +213,6 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
   unsigned char* ring =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Aux& S = *reinterpret_cast<Aux*>(ring + G::RING_BYTES);
-  const uint32_t ring_s = smem_u32(ring);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
   const int c = blockIdx.x;
@@ -208,9 +222,13 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
     for (int i = 0; i < STAGES; ++i) mbar_init(&S.bar[i], 1);
     fence_mbar_init();
   }
-  grid_dep_wait();
-  grid_dep_launch();
-  T2B_TRACE_MARK(1);
+  // With kv_early the tile list is built and the loads of tiles older than
+  // the newest key are issued while the preceding kernel still runs.
+  if (!P.kv_early) {
+    grid_dep_wait();
+    grid_dep_launch();
+    T2B_TRACE_MARK(1);
+  }
 
   // ---- tile list: tiles per unit of each row, exclusive prefix over rows ----
   const int rows = P.rows;
@@ -238,23 +256,33 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
   }
   __syncthreads();
   const long long T = S.row_start[rows];
-  const long long NP = T < (long long)gridDim.x ? T : (long long)gridDim.x;  // active CTAs
-  if (c >= NP) return;
-  const int t_lo = range_lo(c, T, NP), t_hi = range_lo(c + 1, T, NP);
-  const int count = t_hi - t_lo;
+  const long long NP = T < (long long)gridDim.x ? T : (long long)gridDim.x;
+  const int snap_max = max(STAGES, (int)((3 * T) / (5 * NP)));
+  const int t_lo = c < NP ? range_start(S, rows, c, T, NP, snap_max) : 0;
+  const int count = c < NP ? range_start(S, rows, c + 1, T, NP, snap_max) - t_lo : 0;
+  if (count <= 0) {
+    if (P.kv_early) grid_dep_launch();
+    return;
+  }
 
-  // tile i of this CTA into stage i % STAGES (+ q on a unit's first tile here)
-  auto issue = [&](int i) {
-    const TileRef r = locate(S, rows, t_lo + i);
-    const int nk = min(AT_TILE, S.row_keys[r.m] - r.j * AT_TILE);
+  // Tile `r` (the i-th of this CTA) goes to stage i % STAGES, with q on a
+  // unit's first tile here: arm(), then load_kv() and load_q() (the last
+  // tile of a unit holds the key the preceding kernel writes).
+  auto tile_keys = [&](const TileRef& r) { return min(AT_TILE, S.row_keys[r.m] - r.j * AT_TILE); };
+  auto with_q = [&](int i, const TileRef& r) { return (i == 0) || (r.j == 0); };
+  auto arm = [&](int i, const TileRef& r) {
+    const int nk = tile_keys(r);
+    const bool full = nk == AT_TILE;
+    const uint32_t kv = full ? (uint32_t)G::KV_BYTES : (uint32_t)(G::HALVES * ((nk + AT_SUB - 1) / AT_SUB) * AT_SUB * 128);
+    const uint32_t qbytes = with_q(i, r) ? (uint32_t)(QPG * HD * 2) : 0u;
+    const uint32_t mbytes = P.mask0 ? (uint32_t)(AT_TILE * 2) : 0u;
+    mbar_arrive_expect_tx(&S.bar[i % STAGES], 2u * kv + qbytes + mbytes);
+  };
+  auto load_kv = [&](int i, const TileRef& r) {
+    const int nk = tile_keys(r);
     const int st = i % STAGES;
     const bool full = nk == AT_TILE;
     const int nbox = full ? 1 : (nk + AT_SUB - 1) / AT_SUB;
-    const uint32_t box_bytes = full ? (uint32_t)G::HALF_BYTES : (uint32_t)(AT_SUB * 128);
-    const bool with_q = (i == 0) || (r.j == 0);
-    const uint32_t qbytes = with_q ? (uint32_t)(QPG * HD * 2) : 0u;
-    const uint32_t mbytes = P.mask0 ? (uint32_t)(AT_TILE * 2) : 0u;
-    mbar_arrive_expect_tx(&S.bar[st], 2u * G::HALVES * nbox * box_bytes + qbytes + mbytes);
     const int u = r.m * P.n_kv + r.h;
     const int y0 = r.j * P.tile_y;
     const int z = u * P.unit_z + r.j * P.tile_z;
@@ -268,28 +296,64 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         tma_load_3d(kdst + off, km, hf * 64, y0 + b * AT_SUB, z, &S.bar[st]);
         tma_load_3d(vdst + off, vm, hf * 64, y0 + b * AT_SUB, z, &S.bar[st]);
       }
-    if (P.mask0) bulk_g2s(&S.msk[st][0], P.mask0 + u * P.mask_unit + r.j * P.mask_tile, mbytes, &S.bar[st]);
-    if (with_q)
-      bulk_g2s(&S.qb[st][0], P.q + (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD, qbytes, &S.bar[st]);
+    if (P.mask0)
+      bulk_g2s(&S.msk[st][0], P.mask0 + u * P.mask_unit + r.j * P.mask_tile, (uint32_t)(AT_TILE * 2), &S.bar[st]);
   };
-  if (tid == 0)
-    for (int i = 0; i < STAGES && i < count; ++i) issue(i);
+  auto load_q = [&](int i, const TileRef& r) {
+    if (with_q(i, r))
+      bulk_g2s(&S.qb[i % STAGES][0], P.q + (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD,
+               (uint32_t)(QPG * HD * 2), &S.bar[i % STAGES]);
+  };
+  TileRef cur = locate(S, rows, t_lo);  // consumer position
+  TileRef pro = cur;                    // producer position (thread 0)
+  int issued = 0;
+  const int first = min(STAGES, count);
+  if (P.kv_early) {
+    if (tid == 0)
+      for (int i = 0; i < first; ++i) {
+        arm(i, pro);
+        if (pro.j < pro.nt - 1) load_kv(i, pro);
+        if (i + 1 < first) next_tile(pro, S, P.n_kv);
+      }
+    grid_dep_wait();
+    grid_dep_launch();
+    T2B_TRACE_MARK(1);
+    pro = cur;
+    if (tid == 0)
+      for (int i = 0; i < first; ++i) {
+        if (pro.j == pro.nt - 1) load_kv(i, pro);
+        load_q(i, pro);
+        if (i + 1 < count) next_tile(pro, S, P.n_kv);
+      }
+  } else if (tid == 0) {
+    for (int i = 0; i < first; ++i) {
+      arm(i, pro);
+      load_kv(i, pro);
+      load_q(i, pro);
+      if (i + 1 < count) next_tile(pro, S, P.n_kv);
+    }
+  }
+  issued = first;
 
   const int kb = AT_SUB * warp;  // this warp's first key in a tile
   const int h0 = 2 * t4, h1 = h0 + 1;
   float o[NT16][4];
   uint32_t qf[NT16][2];
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads h0, h1 (log2 domain)
+  SplitUnit split[2];  // units of this range cut between CTAs: ticketed after the last tile
+  int n_split = 0;
 
   for (int i = 0; i < count; ++i) {
-    const TileRef r = locate(S, rows, t_lo + i);
+    if (i > 0) next_tile(cur, S, P.n_kv);
+    const TileRef r = cur;
     const bool unit_begin = (i == 0) || (r.j == 0);
     const bool unit_end = (i == count - 1) || (r.j == r.nt - 1);
     const int st = i % STAGES;
     // every thread takes the same outcome, so no thread is left at a barrier
     const bool ok = __syncthreads_and(mbar_wait_bounded(&S.bar[st], (i / STAGES) & 1, P.err));
-    if (!ok) break;  // timeout recorded in P.err
+    if (!ok) return;  // timeout recorded in P.err; no ticket is taken, so no CTA merges
     if (i == 0) T2B_TRACE_MARK(2);
+    if (i == count - 1) T2B_TRACE_MARK(3);
     if (unit_begin) {  // new unit: B operand q^T (heads >= QPG are zero columns), fresh softmax state
       const __nv_bfloat16* qs = &S.qb[st][0];
 #pragma unroll
@@ -317,15 +381,16 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         }
         __syncwarp();
       }
-      // S^T = K_w . q^T
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      // S^T = K_w . q^T, two accumulation chains
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
       const int krow = kb + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const uint32_t kaddr = smem_u32(kst) + krow * 128;
 #pragma unroll
       for (int ks = 0; ks < NT16; ++ks) {
         const int ch = (ks & 3) * 2 + (lane >> 4);
         uint32_t a[4];
-        ldsm_x4(a, smem_u32(kst) + (ks >> 2) * G::HALF_BYTES + krow * 128 + ((ch ^ (krow & 7)) << 4));
-        mma_bf16(s, a, qf[ks][0], qf[ks][1]);
+        ldsm_x4(a, kaddr + (ks >> 2) * G::HALF_BYTES + ((ch ^ (krow & 7)) << 4));
+        mma_bf16((ks & 1) ? sb : sa, a, qf[ks][0], qf[ks][1]);
       }
       // online softmax over this warp's 16 keys (rows g, g+8; heads h0, h1)
       const int k0 = kb + g, k1 = k0 + 8;
@@ -334,10 +399,10 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         live0 = live0 && __bfloat162float(S.msk[st][k0]) > 0.5f;
         live1 = live1 && __bfloat162float(S.msk[st][k1]) > 0.5f;
       }
-      const float x0 = live0 ? s[0] * P.scale_log2 : -INFINITY;
-      const float x1 = live0 ? s[1] * P.scale_log2 : -INFINITY;
-      const float x2 = live1 ? s[2] * P.scale_log2 : -INFINITY;
-      const float x3 = live1 ? s[3] * P.scale_log2 : -INFINITY;
+      const float x0 = live0 ? (sa[0] + sb[0]) * P.scale_log2 : -INFINITY;
+      const float x1 = live0 ? (sa[1] + sb[1]) * P.scale_log2 : -INFINITY;
+      const float x2 = live1 ? (sa[2] + sb[2]) * P.scale_log2 : -INFINITY;
+      const float x3 = live1 ? (sa[3] + sb[3]) * P.scale_log2 : -INFINITY;
       float tm0 = fmaxf(x0, x2), tm1 = fmaxf(x1, x3);
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
@@ -367,18 +432,23 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
       const uint32_t b1 = movm_t(pack_bf16(p2, p3));
       // O^T += V_w^T . P^T
       const int vkey = kb + ((lane >> 4) << 3) + (lane & 7);
+      const uint32_t vaddr = smem_u32(vst) + vkey * 128;
 #pragma unroll
       for (int mt = 0; mt < NT16; ++mt) {
         const int dch = 2 * mt + ((lane >> 3) & 1);
         uint32_t a[4];
-        ldsm_x4_t(a, smem_u32(vst) + (dch >> 3) * G::HALF_BYTES + vkey * 128 + (((dch & 7) ^ (vkey & 7)) << 4));
+        ldsm_x4_t(a, vaddr + (dch >> 3) * G::HALF_BYTES + (((dch & 7) ^ (vkey & 7)) << 4));
         mma_bf16(o[mt], a, b0, b1);
       }
     }
     __syncthreads();  // stage consumed
-    if (tid == 0 && i + STAGES < count) {
+    if (i == count - 1) T2B_TRACE_MARK(4);
+    if (tid == 0 && issued < count) {
       fence_proxy_async();
-      issue(i + STAGES);
+      arm(issued, pro);
+      load_kv(issued, pro);
+      load_q(issued, pro);
+      if (++issued < count) next_tile(pro, S, P.n_kv);
     }
     if (!unit_end) continue;
 
@@ -410,11 +480,15 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
       }
     }
     __syncthreads();
-    const int u = r.m * P.n_kv + r.h;
     const size_t obase = (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD;
     const int unit_t0 = S.row_start[r.m] + r.h * r.nt;  // global index of the unit's first tile
-    const int c1 = cta_of_tile(unit_t0, T, NP), c2 = cta_of_tile(unit_t0 + r.nt - 1, T, NP);
-    const bool whole = c1 == c2;
+    bool whole = r.nt <= snap_max;
+    int c1 = c, c2 = c;
+    if (!whole) {
+      c1 = cta_of_tile(unit_t0, T, NP);
+      c2 = cta_of_tile(unit_t0 + r.nt - 1, T, NP);
+      whole = c1 == c2;
+    }
     // record slot: 0 for the unit this CTA's range starts in, 1 for a later one
     float* rec = P.ws + ((size_t)c * 2 + (t_lo >= unit_t0 ? 0 : 1)) * QPG * REC;
 #pragma unroll
@@ -445,14 +519,39 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         }
       }
     }
-    if (whole) continue;
+    if (i == count - 1) T2B_TRACE_MARK(5);
+    if (!whole && n_split < 2) split[n_split++] = SplitUnit{r.m, r.h, unit_t0, c1, c2};
+  }
+  if (n_split == 0) {
+    T2B_TRACE_MARK(6);
+    return;
+  }
 
-    // ---- partial: the unit's last CTA merges every part ----
-    if (!unit_ticket(S, P.cnt + u, c2 - c1 + 1)) continue;
-    const int n = c2 - c1 + 1;
-    const int first_slot = range_lo(c1, T, NP) >= unit_t0 ? 0 : 1;
+  // ---- tickets for the cut units; the last CTA to arrive at a unit merges it ----
+  __syncthreads();  // every record store of this CTA precedes thread 0's fence
+  if (tid == 0) {
+    __threadfence();
+    int last = 0;
+    for (int k = 0; k < n_split; ++k) {
+      int* cnt = P.cnt + split[k].m * P.n_kv + split[k].h;
+      const int prev = atomicAdd(cnt, 1);
+      if (prev == split[k].c2 - split[k].c1) {
+        atomicExch(cnt, 0);  // re-armed for the next launch
+        last |= 1 << k;
+      }
+    }
+    if (last) __threadfence();
+    S.flag = last;
+  }
+  __syncthreads();
+  const int last = S.flag;
+  for (int k = 0; k < n_split; ++k) {
+    if (!((last >> k) & 1)) continue;
+    const SplitUnit su = split[k];
+    const int n = su.c2 - su.c1 + 1;
+    const int first_slot = range_start(S, rows, su.c1, T, NP, snap_max) >= su.t0 ? 0 : 1;
     auto part = [&](int p) -> const float* {
-      return P.ws + ((size_t)(c1 + p) * 2 + (p == 0 ? first_slot : 0)) * QPG * REC;
+      return P.ws + ((size_t)(su.c1 + p) * 2 + (p == 0 ? first_slot : 0)) * QPG * REC;
     };
     for (int hh = warp; hh < QPG; hh += AT_WARPS) {  // per head: max and weighted sum over the parts
       float M = -INFINITY;
@@ -473,7 +572,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
     __syncthreads();
     float acc[EPT][2];
 #pragma unroll
-    for (int k = 0; k < EPT; ++k) acc[k][0] = acc[k][1] = 0.f;
+    for (int e = 0; e < EPT; ++e) acc[e][0] = acc[e][1] = 0.f;
     for (int b0 = 0; b0 < n; b0 += AT_MERGE_BATCH) {
       const int nb = min(AT_MERGE_BATCH, n - b0);
       for (int e = tid; e < nb * QPG; e += AT_THREADS) {
@@ -484,31 +583,33 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
       }
       __syncthreads();
 #pragma unroll
-      for (int k = 0; k < EPT; ++k) {
-        const int e = tid + k * AT_THREADS;
+      for (int e2 = 0; e2 < EPT; ++e2) {
+        const int e = tid + e2 * AT_THREADS;
         if (e < NPAIR) {
           const int hh = (2 * e) / HD, d = (2 * e) % HD;
 #pragma unroll 4
           for (int p = 0; p < nb; ++p) {
             const float wt = S.wpart[p][hh];
             const float2 v = __ldcg(reinterpret_cast<const float2*>(part(b0 + p) + hh * REC + d));
-            acc[k][0] += wt * v.x;
-            acc[k][1] += wt * v.y;
+            acc[e2][0] += wt * v.x;
+            acc[e2][1] += wt * v.y;
           }
         }
       }
       __syncthreads();
     }
+    const size_t obase = (size_t)su.m * P.n_heads * HD + (size_t)su.h * QPG * HD;
 #pragma unroll
-    for (int k = 0; k < EPT; ++k) {
-      const int e = tid + k * AT_THREADS;
+    for (int e2 = 0; e2 < EPT; ++e2) {
+      const int e = tid + e2 * AT_THREADS;
       if (e < NPAIR) {
         const int hh = (2 * e) / HD, d = (2 * e) % HD;
-        *reinterpret_cast<__nv_bfloat162*>(&P.out[obase + hh * HD + d]) = __floats2bfloat162_rn(acc[k][0], acc[k][1]);
+        *reinterpret_cast<__nv_bfloat162*>(&P.out[obase + hh * HD + d]) =
+            __floats2bfloat162_rn(acc[e2][0], acc[e2][1]);
       }
     }
   }
-  T2B_TRACE_MARK(3);
+  T2B_TRACE_MARK(6);
 }
 
 // ---------------------------------------------------------------------------
@@ -611,9 +712,9 @@ extern "C" size_t t2b_decode_attention_workspace_bytes(int M, int n_heads, int n
   return attention_workspace_bytes(M, n_heads, n_kv, head_dim, max_ctx);
 }
 
-extern "C" int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                    const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv, int head_dim,
-                                    int max_ctx, void* ws, size_t ws_bytes, void* stream) {
+static int decode_attention_impl(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                 const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv, int head_dim,
+                                 int max_ctx, void* ws, size_t ws_bytes, void* stream, int kv_early) {
   if (!q || !k_cache || !v_cache || !pos || !out) return T2B_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
        reinterpret_cast<uintptr_t>(q)) & 15)
@@ -633,7 +734,23 @@ extern "C" int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, 
   P.out = reinterpret_cast<__nv_bfloat16*>(out);
   P.n_heads = n_heads;
   P.n_kv = n_kv;
+  P.kv_early = kv_early;
   return attention_launch(P, M, head_dim, max_ctx, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                    const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv, int head_dim,
+                                    int max_ctx, void* ws, size_t ws_bytes, void* stream) {
+  return decode_attention_impl(q, k_cache, v_cache, pos, out, M, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes,
+                               stream, 0);
+}
+
+extern "C" int t2b_decode_attention_after_kvwrite(const uint16_t* q, const uint16_t* k_cache,
+                                                  const uint16_t* v_cache, const int32_t* pos, uint16_t* out, int M,
+                                                  int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
+                                                  size_t ws_bytes, void* stream) {
+  return decode_attention_impl(q, k_cache, v_cache, pos, out, M, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes,
+                               stream, 1);
 }
 
 extern "C" int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, uint16_t* out, int n_groups,

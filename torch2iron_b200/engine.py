@@ -166,7 +166,7 @@ class DecodeEngine:
             p(lw.qkv.qw), p(lw.qkv.meta), p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
             p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
-        _lib.check("t2b_decode_attention", L.t2b_decode_attention(
+        _lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
             p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), B, nq, nkv, hd,
             self.max_ctx, *self._ws("attn"), st))
         _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
