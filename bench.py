@@ -163,6 +163,12 @@ def run_reference(args, cfg):
 # ---------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_attention_kernel<128, 2> launch
+# captured with ncu on this workload (64 rows x 8 kv heads, ctx 133: 144 keys loaded per unit).
+NCU_ATTN = {"dram_bytes": 38_076_672 + 4_096, "units": 64 * 8, "keys_loaded": 144, "head_dim": 128,
+            "source": "ncu capture, profiles/decode_attention_qwen3_0.6b_bs64_ctx133.md, scaled by keys loaded"}
+
+
 def gemv_batch1(eng, peak):
     """Batch-1 GEMV sweep over every linear of the model (qkv, o, gate_up, down per
     layer) captured in one CUDA graph; the working set (~229 MB) exceeds L2."""
@@ -296,11 +302,13 @@ def run_t2b(args, cfg):
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push("timed")   # profiler filter: ncu --nvtx --nvtx-include "timed/"
         e0.record()
         for _ in range(args.steps):
             eng.advance()
         e1.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ms], device="cuda")
@@ -362,6 +370,14 @@ def run_t2b(args, cfg):
         }
         dur_ms = prof[dom][0]
         achieved = kernel_bytes[dom] / (dur_ms * 1e-3) / 1e9
+        traffic, traffic_src = None, None
+        if dom == "decode_attention" and cfg.head_dim == NCU_ATTN["head_dim"]:
+            # ncu DRAM bytes of one capture, scaled by the keys this launch loads
+            # (tiles load whole 16-key boxes at the end of each unit)
+            loaded = 64 * (mid_ctx // 64) + 16 * -(-(mid_ctx % 64) // 16)
+            per_key = NCU_ATTN["dram_bytes"] / (NCU_ATTN["units"] * NCU_ATTN["keys_loaded"])
+            traffic = int(per_key * B * cfg.n_kv_groups * loaded)
+            traffic_src = NCU_ATTN["source"]
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
@@ -377,7 +393,8 @@ def run_t2b(args, cfg):
                     "frac_of_peak": round(avg_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4),
                     "peak_gbs": peak, "peak_source": peak_kind},
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "traffic_source": traffic_src,
                          "bytes_per_launch": kernel_bytes[dom], "avg_launch_us": round(dur_ms * 1000, 2),
                          "peak_source": peak_kind,
                          "kernel_avg_us": {k: round(v[0] * 1000, 2) for k, v in prof.items()}},
