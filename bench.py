@@ -56,24 +56,49 @@ def parse():
 # clocks
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event reasons of this rank's GPU, sampled every 10 ms
+    through NVML (read-only queries) while the timed region runs; nvidia-smi
+    (200 ms) when NVML is unavailable."""
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index, self.samples, self._stop = index, [], threading.Event()
+        self._nvml = None
+        try:
+            import pynvml
+            self._h = torch.cuda._get_pynvml_handler(index)
+            self._nvml = pynvml
+            self._bits = (pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                          pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap)
+            self._max = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._nvml = None
         self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample(self):
+        if self._nvml is not None:
+            nv = self._nvml
+            sm = float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+            mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            return [sm, self._max] + [bool(mask & b) for b in self._bits]
+        out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+        parts = [p.strip() for p in out.stdout.strip().split(",")]
+        if len(parts) != 6 or not parts[0].replace(".", "").isdigit():
+            return None
+        return [float(parts[0]), float(parts[1])] + [x.lower() == "active" for x in parts[2:]]
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                parts = [p.strip() for p in out.stdout.strip().split(",")]
-                if len(parts) == 6:
-                    self.samples.append(parts)
+                smp = self._sample()
+                if smp is not None:
+                    self.samples.append(smp)
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.01 if self._nvml is not None else 0.2)
 
     def __enter__(self):
         self._t.start()
@@ -86,12 +111,10 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[2 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+        reasons = sorted({self.NAMES[i] for s in self.samples for i in range(4) if s[2 + i]})
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons, "samples": len(self.samples),
+                "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
 def peaks():
@@ -139,20 +162,28 @@ def model_to_cpu(model):
     return out
 
 
+def arm_config(args, world):
+    """The workload description both arms report (identical for the reference arm)."""
+    c0 = args.prompt + args.warmup + 1
+    c1 = c0 + args.steps - 1
+    return {"workload": f"config2 {args.model} greedy decode, {args.batch} rows/GPU, prompt {args.prompt}, "
+                        f"timed ctx {c0}..{c1}",
+            "model": args.model, "global_batch": world * args.batch, "seq_len": c1, "parallelism": f"dp{world}"}
+
+
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     model = synth.random_model(cfg, seed=args.seed, device="cpu")
-    ctx = args.prompt + args.warmup
+    ctx = args.prompt + args.warmup + 1
     rate, dt, cores = cpu_decode_rate(cfg, model, args.batch, ctx, max(1, min(args.steps, args.cpu_sample_steps)),
                                       args.seed)
     line = {"metric": METRIC, "value": round(rate, 3), "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1000 * args.batch / rate, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4-weights/fp32-compute", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"config2 {args.model} greedy decode, bs {args.batch}, ctx {ctx}",
-                       "model": args.model, "global_batch": args.batch, "seq_len": ctx, "parallelism": "cpu"},
+            "config": dict(arm_config(args, args.gpus), l2="host memory (CPU path)"),
             "cpu_baseline": {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": f"{max(1, min(args.steps, args.cpu_sample_steps))} decode steps x {args.batch} "
                                        f"rows at ctx {ctx} ({dt:.1f} s)"},
@@ -383,11 +414,8 @@ def run_t2b(args, cfg):
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4-weights/bf16-activations/fp32-accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
-            "config": {"workload": f"config2 {args.model} greedy decode, {B} rows/GPU, prompt {P}, "
-                                   f"timed ctx {ctx_lens[0]}..{ctx_lens[-1]}",
-                       "model": args.model, "global_batch": world * B, "seq_len": ctx_lens[-1],
-                       "parallelism": f"dp{world}", "l2": "working set > L2 every step (weights+lm_head+KV "
-                                                         f"~{avg_bytes / 1e9:.2f} GB/step/GPU)"},
+            "config": dict(arm_config(args, world), l2="working set > L2 every step (weights+lm_head+KV "
+                                                           f"~{avg_bytes / 1e9:.2f} GB/step/GPU)"),
             "hbm": {"algorithmic_bytes_per_step": int(avg_bytes),
                     "achieved_gbs": round(avg_bytes / (ms / args.steps * 1e-3) / 1e9, 1),
                     "frac_of_peak": round(avg_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4),
@@ -405,7 +433,7 @@ def run_t2b(args, cfg):
         }
         if not args.no_gemv:
             line["gemv_b1"] = gemv_batch1(eng, peak)
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:   # host-core baseline: rank 0 at N=1 only
             mcpu = model_to_cpu(model)
             rate, dt, cores = cpu_decode_rate(cfg, mcpu, B, mid_ctx, args.cpu_sample_steps, args.seed)
             line["cpu_baseline"] = {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",

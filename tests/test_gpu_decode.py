@@ -258,3 +258,27 @@ def test_small_model_generate_vs_oracle_batch24():
         hits += (eng.next_tokens.cpu().long() == ref[:, t]).sum().item()
         total += B
     assert agree >= 0.99 and hits / total >= 0.99
+
+
+@pytest.mark.parametrize("M,V,dtype", [
+    (64, 151936, torch.float32),   # Qwen3 vocab: 19 chunks per row, float4 loads
+    (3, 128256, torch.float32),    # Llama vocab
+    (2, 5000, torch.float32),      # one chunk per row
+    (4, 20001, torch.bfloat16),    # scalar-load path, ragged last chunk
+])
+def test_argmax_rows_vs_torch(M, V, dtype):
+    g = torch.Generator().manual_seed(7 + M + V)
+    logits = torch.randn(M, V, generator=g).to(dtype)
+    logits[0, V // 3] = logits[0, V - 5] = 50.0       # tie: lowest index wins
+    if M > 1:
+        logits[1, V - 1] = 60.0                        # maximum in the last element
+    L = _lib.lib()
+    n = max(L.t2b_argmax_workspace_bytes(M, V), 256)
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    out = torch.empty(M, dtype=torch.int32, device="cuda")
+    lg = logits.cuda()
+    code = {torch.float32: 2, torch.bfloat16: 0}[dtype]
+    for _ in range(3):                                 # the counters re-arm between calls
+        _lib.call("t2b_argmax_rows", _lib.ptr(lg), code, M, V, V, _lib.ptr(out), _lib.ptr(ws), n, _lib.stream())
+        torch.cuda.synchronize()
+        assert torch.equal(out.cpu().long(), torch.argmax(logits.float(), dim=1))

@@ -114,8 +114,11 @@ __global__ void rms_norm_rows_kernel(const float* __restrict__ x, const float* _
 
 // ---------------------------------------------------------------------------
 // Row argmax over a [M, V] logits matrix: grid (chunks, M); each CTA reduces
-// a chunk to (value, index), the last CTA of a row reduces the chunks.
-// Ties resolve to the lowest index (torch.argmax).
+// an 8192-wide chunk (fp32 rows: 8 float4 loads per thread, all in flight)
+// to (value, index), folds it into the row's 64-bit key with atomicMax, and
+// the last CTA of the row (ticket) writes the index and re-arms both words.
+// Key = order-preserving bits of the value << 32 | ~index, so ties resolve to
+// the lowest index (torch.argmax); NaN entries are skipped.
 // ---------------------------------------------------------------------------
 constexpr int AM_THREADS = 256;
 constexpr int AM_CHUNK = 8192;
@@ -127,15 +130,45 @@ T2B_DEV void argmax_merge(float& v, int& i, float v2, int i2) {
   }
 }
 
-__global__ void argmax_rows_kernel(const void* __restrict__ logits, int dtype, int V, int ld, int* __restrict__ idx,
-                                   float* ws_val, int* ws_idx, int* cnt) {
+T2B_DEV unsigned long long argmax_key(float v, int i) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)i);
+}
+
+template <bool F32X4>
+__global__ void __launch_bounds__(AM_THREADS) argmax_rows_kernel(const void* __restrict__ logits, int dtype, int V,
+                                                                 int ld, int* __restrict__ idx,
+                                                                 unsigned long long* __restrict__ keys,
+                                                                 int* __restrict__ cnt) {
   grid_dep_wait();
   grid_dep_launch();
   const int m = blockIdx.y, c = blockIdx.x, nch = gridDim.x;
   const int v0 = c * AM_CHUNK, v1 = min(V, v0 + AM_CHUNK);
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int v = v0 + threadIdx.x; v < v1; v += AM_THREADS) argmax_merge(best, bi, load_act(logits, dtype, (size_t)m * ld + v), v);
+  if (F32X4) {
+    const float* row = reinterpret_cast<const float*>(logits) + (size_t)m * ld;
+    float4 x[AM_CHUNK / (4 * AM_THREADS)];
+#pragma unroll
+    for (int u = 0; u < AM_CHUNK / (4 * AM_THREADS); ++u) {
+      const int v = v0 + (u * AM_THREADS + (int)threadIdx.x) * 4;
+      x[u] = v < v1 ? __ldg(reinterpret_cast<const float4*>(row + v)) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    }
+#pragma unroll
+    for (int u = 0; u < AM_CHUNK / (4 * AM_THREADS); ++u) {
+      const int v = v0 + (u * AM_THREADS + (int)threadIdx.x) * 4;
+      if (v < v1) {
+        argmax_merge(best, bi, x[u].x, v);
+        argmax_merge(best, bi, x[u].y, v + 1);
+        argmax_merge(best, bi, x[u].z, v + 2);
+        argmax_merge(best, bi, x[u].w, v + 3);
+      }
+    }
+  } else {
+    for (int v = v0 + threadIdx.x; v < v1; v += AM_THREADS)
+      argmax_merge(best, bi, load_act(logits, dtype, (size_t)m * ld + v), v);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
@@ -150,29 +183,25 @@ __global__ void argmax_rows_kernel(const void* __restrict__ logits, int dtype, i
     si[warp] = bi;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < AM_THREADS / 32; ++w) argmax_merge(best, bi, sv[w], si[w]);
-    if (nch == 1) idx[m] = bi;
-    else {
-      ws_val[(size_t)m * nch + c] = best;
-      ws_idx[(size_t)m * nch + c] = bi;
-    }
+  if (threadIdx.x != 0) return;
+  for (int w = 1; w < AM_THREADS / 32; ++w) argmax_merge(best, bi, sv[w], si[w]);
+  if (nch == 1) {
+    idx[m] = bi;
+    return;
   }
-  if (nch == 1) return;
-  if (!split_ticket(cnt + m, nch)) return;
-  if (threadIdx.x == 0) {
-    float b = -INFINITY;
-    int ii = 0x7fffffff;
-    for (int k = 0; k < nch; ++k) argmax_merge(b, ii, __ldcg(ws_val + (size_t)m * nch + k), __ldcg(ws_idx + (size_t)m * nch + k));
-    idx[m] = ii;
+  atomicMax(keys + m, argmax_key(best, bi));
+  __threadfence();
+  if (atomicAdd(cnt + m, 1) == nch - 1) {
+    const unsigned long long k = atomicExch(keys + m, 0ull);
+    idx[m] = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    atomicExch(cnt + m, 0);
   }
 }
 
 size_t argmax_workspace_bytes(int M, int V) {
   const int nch = (V + AM_CHUNK - 1) / AM_CHUNK;
   if (nch == 1) return 0;
-  size_t a = (((size_t)M * nch * 4 + 255) & ~size_t(255));
-  return 2 * a + (((size_t)M * 4 + 255) & ~size_t(255));
+  return (((size_t)M * 8 + 255) & ~size_t(255)) + (((size_t)M * 4 + 255) & ~size_t(255));
 }
 
 int argmax_rows(const void* logits, int dtype, int M, int V, int ld, int* idx, void* ws, size_t ws_bytes,
@@ -181,16 +210,18 @@ int argmax_rows(const void* logits, int dtype, int M, int V, int ld, int* idx, v
   const int nch = (V + AM_CHUNK - 1) / AM_CHUNK;
   const size_t need = argmax_workspace_bytes(M, V);
   if (ws_bytes < need || (need && !ws)) return T2B_ERR_WORKSPACE;
-  float* wv = nullptr;
-  int* wi = nullptr;
+  unsigned long long* keys = nullptr;
   int* cnt = nullptr;
   if (need) {
-    const size_t a = (((size_t)M * nch * 4 + 255) & ~size_t(255));
-    wv = reinterpret_cast<float*>(ws);
-    wi = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + a);
-    cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + 2 * a);
+    keys = reinterpret_cast<unsigned long long*>(ws);
+    cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * 8 + 255) & ~size_t(255)));
   }
-  return launch_pdl(argmax_rows_kernel, dim3(nch, M), dim3(AM_THREADS), 0, st, logits, dtype, V, ld, idx, wv, wi, cnt);
+  const bool x4 = dtype == T2B_DTYPE_F32 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+  if (x4)
+    return launch_pdl(argmax_rows_kernel<true>, dim3(nch, M), dim3(AM_THREADS), 0, st, logits, dtype, V, ld, idx,
+                      keys, cnt);
+  return launch_pdl(argmax_rows_kernel<false>, dim3(nch, M), dim3(AM_THREADS), 0, st, logits, dtype, V, ld, idx, keys,
+                    cnt);
 }
 
 int embed_rows(const uint16_t* table, const int* tokens, float* x, float* ssq, const uint16_t* norm_w, uint16_t* xw,

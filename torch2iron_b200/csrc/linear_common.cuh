@@ -227,9 +227,10 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
 }
 
 // Clears p.ssq_clear (M floats) from one designated CTA, after the PDL wait.
-T2B_DEV void maybe_clear_ssq(const LinearParams& p, bool designated) {
+// Threads t = 0..nt-1 of the designated CTA zero the next producer's ssq buffer.
+T2B_DEV void maybe_clear_ssq(const LinearParams& p, bool designated, int t, int nt) {
   if (p.ssq_clear != nullptr && designated)
-    for (int i = threadIdx.x; i < p.M; i += blockDim.x) p.ssq_clear[i] = 0.f;
+    for (int i = t; i < p.M; i += nt) p.ssq_clear[i] = 0.f;
 }
 
 // Host side: shared launch helpers (defined in w4a16_gemv.cu).

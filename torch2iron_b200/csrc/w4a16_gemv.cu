@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
     }
     xs[b * S::XS_LD + kk + (kk >> 5) * 4] = v;
   }
-  maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0);
+  maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0, threadIdx.x, GV_THREADS);
   __syncthreads();
   T2B_TRACE_MARK(2);
 

@@ -114,23 +114,22 @@ constexpr int EP_ROWS_BYTES = 32 * 1024;
 constexpr int EP_BYTES = EP_ROWS_BYTES + 256 + 1024;
 
 struct TcLayout {
-  int x_group, off_raw, off_meta, off_tile, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
-  __host__ __device__ TcLayout(int BP, int S) {
+  int x_group, off_raw, off_meta, off_tile, off_recv, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
+  __host__ __device__ TcLayout(int BP, int S, int KS) {
     x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group (TMA, 128B swizzle)
     off_raw = S * x_group;                   // [S][8 KB] raw int4 blocks
     off_meta = off_raw + S * BLOCK_BYTES;    // [S][128] meta words
     off_tile = off_meta + S * TILE_N * 4;    // fp32 [BP][128] partial tile
-    off_scr = off_tile + BP * TILE_N * 4;    // fp32 [8*BP] scratch (row scales, epilogue)
+    off_recv = off_tile + BP * TILE_N * 4;   // fp32 [KS-1][BP/KS][128] peers' partials of this CTA's rows
+    off_scr = off_recv + (BP - BP / KS) * TILE_N * 4;  // fp32 [8*BP] scratch (row scales, epilogue)
     off_ep = off_scr + 8 * BP * 4;           // epilogue inputs staged after the PDL wait
-    off_bar = off_ep + EP_BYTES;             // raw_full[S], a_full[2], a_empty[2], acc_full, x_full
-    off_tmem = off_bar + (S + 6) * 8;
+    off_bar = off_ep + EP_BYTES;             // raw_full[S], a_full[NA], a_empty[NA], acc_full, x_full, recv_full
+    off_tmem = off_bar + (S + 17) * 8;       // (NA <= 7)
     off_flag = off_tmem + 8;
     bytes = off_flag + 8 + 1024;             // + slack to 1024-align the base
   }
 };
 
-constexpr uint32_t A_COL = 0;      // two 64-column A stages
-constexpr uint32_t ACC_COL = 128;  // one accumulator of BP columns
 
 // 2-D tiled TMA load (no multicast): box of `tmap` at (x, y) -> smem, tx bytes on bar.
 T2B_DEV void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
@@ -212,28 +211,66 @@ T2B_DEV EpiCache staged_epilogue_inputs(const LinearParams& p, uint8_t* ep, int 
   return c;
 }
 
+// TMEM columns (512 per SM): the fp32 accumulator at [0, BP), then NA
+// 64-column A stages, one per group up to what fits; the first NA groups are
+// dequantised before the PDL wait, later groups reuse the stages as a ring.
+__host__ __device__ constexpr uint32_t tc_a0(int BP) { return BP <= 64 ? 64u : (uint32_t)BP; }
+__host__ __device__ constexpr int tc_stages(int BP, int S) {
+  return S < (int)((512u - tc_a0(BP)) / 64u) ? S : (int)((512u - tc_a0(BP)) / 64u);
+}
+__host__ __device__ constexpr uint32_t tc_tmem_cols(int BP, int S) {
+  return pow2_cols(tc_a0(BP) + 64u * (uint32_t)tc_stages(BP, S));
+}
+
+T2B_DEV void st_dsmem_s32(uint32_t addr, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+// Bulk copy of this CTA's shared memory into a cluster peer's, completing on
+// the peer's mbarrier (dst and bar are shared::cluster addresses of the peer).
+T2B_DEV void bulk_s2s_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+T2B_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+T2B_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
 // grid (N/128, KS, mblocks), cluster (1, KS, 1): the KS CTAs of a cluster are
-// the k-splits of one 128-row tile (S groups each); their partial tiles are
-// summed through distributed shared memory, each CTA finishing BP/KS rows.
+// the k-splits of one 128-row tile (S groups each); each CTA finishes BP/KS
+// rows.  After the drain, one thread pushes each peer's rows of the partial
+// tile with one bulk shared->shared::cluster copy that completes on the
+// peer's receive mbarrier (armed at start; a cluster barrier split around the
+// PDL wait makes sure every peer initialised it first).  A final cluster
+// barrier keeps every CTA alive until the copies into it have landed.
+//
+// Order: weight bulk copies, TMEM allocation and the dequantisation of all S
+// groups into TMEM run BEFORE griddepcontrol.wait (weights are constant);
+// dependents are released only once every CTA holds its TMEM, so a later
+// grid's allocation can only wait for an earlier grid's columns, never the
+// reverse.  After the wait: activation TMA, MMAs, row scales, drain, cluster
+// sum, fused epilogue.
 template <int BP, int PRO, int EPI>
 __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant__ LinearParams p) {
   const int S = p.kslice / GROUP;
   const int KS = p.ksplit;
-  const TcLayout L(BP, S);
+  const TcLayout L(BP, S, KS);
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* xs = sm;
   uint8_t* raw = sm + L.off_raw;
   const uint32_t* rmeta = reinterpret_cast<const uint32_t*>(sm + L.off_meta);
   float* tile_acc = reinterpret_cast<float*>(sm + L.off_tile);
+  float* recv = reinterpret_cast<float*>(sm + L.off_recv);
   float* scratch = reinterpret_cast<float*>(sm + L.off_scr);
   float* rowscale = scratch + 4 * BP;  // [BP]; scratch[0..2*BP) is the epilogue's
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.off_bar);
-  uint64_t* raw_full = bars;
-  uint64_t* a_full = bars + S;
-  uint64_t* a_empty = bars + S + 2;
-  uint64_t* acc_full = bars + S + 4;
-  uint64_t* x_full = bars + S + 5;
+  const int NA = tc_stages(BP, S);     // A stages in TMEM
+  uint64_t* raw_full = bars;           // [S]
+  uint64_t* a_full = bars + S;         // [NA]
+  uint64_t* a_empty = bars + S + NA;   // [NA]
+  uint64_t* acc_full = bars + S + 2 * NA;
+  uint64_t* x_full = bars + S + 2 * NA + 1;
+  uint64_t* recv_full = bars + S + 2 * NA + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.off_tmem);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.off_flag);
 
@@ -241,25 +278,28 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   const int tile = blockIdx.x, split = blockIdx.y, mblk = blockIdx.z;
   const int g0 = split * S;
   const int m0 = mblk * BP;
-  // rows this CTA finishes in the epilogue (its cluster rank's share)
-  const int ep_rows = BP / KS;
-  const int ep_m0 = m0 + (KS > 1 ? (int)cluster_ctarank() : 0) * ep_rows;
-  uint32_t tmem_cols = 32;
-  while (tmem_cols < ACC_COL + (uint32_t)BP) tmem_cols <<= 1;
+  const uint32_t rank = KS > 1 ? cluster_ctarank() : 0u;
+  const int rows = BP / KS;  // rows this CTA finishes
+  const int mrow0 = m0 + (int)rank * rows;
+  const uint32_t tmem_cols = tc_tmem_cols(BP, S);
+  const uint32_t a0 = tc_a0(BP);
   T2B_TRACE_BEGIN(1 + EPI, p.N);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) mbar_init(&raw_full[i], 1);
-    mbar_init(&a_full[0], 4);
-    mbar_init(&a_full[1], 4);
-    mbar_init(&a_empty[0], 1);
-    mbar_init(&a_empty[1], 1);
+    for (int i = 0; i < NA; ++i) {
+      mbar_init(&a_full[i], 4);
+      mbar_init(&a_empty[i], 1);
+    }
     mbar_init(acc_full, 1);
     mbar_init(x_full, 1);
+    mbar_init(recv_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    if (KS > 1) mbar_arrive_expect_tx(recv_full, (uint32_t)((BP - rows) * TILE_N * 4));
   }
   __syncthreads();
+  if (KS > 1) cluster_arrive();  // this CTA's receive barrier is armed (wait: before the pushes)
   // raw weight blocks of this CTA: constant data, fetched before the PDL wait
   if (threadIdx.x == 0) {
     for (int gl = 0; gl < S; ++gl) {
@@ -269,48 +309,33 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
                &raw_full[gl]);
     }
   }
-
-  grid_dep_wait();
-  grid_dep_launch();
-  T2B_TRACE_MARK(1);
-
-  // activations: one 64-k x BP-row box per (group, 64-k atom), swizzled by TMA
-  // into the UMMA K-major layout; rows past M arrive as zeros.
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(x_full, (uint32_t)(S * L.x_group));
-    for (int gl = 0; gl < S; ++gl)
-      for (int atom = 0; atom < 2; ++atom)
-        tma_load_2d(xs + gl * L.x_group + atom * (BP * 128), &p.xmap, (g0 + gl) * GROUP + atom * 64, m0, x_full);
-  }
-  // TMEM is taken only after the wait: a dependent grid parked on its own
-  // wait never holds columns this grid still needs.
   if (warp == 4) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
-  if (PRO == PRO_RMSNORM && threadIdx.x >= 128 && threadIdx.x < 128 + BP) {
-    const int b = threadIdx.x - 128, m = m0 + b;
-    rowscale[b] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;   // model.py:179-180
-  }
-  maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  T2B_TRACE_MARK(2);
+  grid_dep_launch();  // this CTA holds its TMEM: dependents may start
+  T2B_TRACE_MARK(1);
   constexpr uint32_t IDESC = idesc_bf16(TILE_N, BP);
 
   if (warp < 4) {
-    // ---- producers: row r's nibbles -> bf16 (q - z) * s pairs -> TMEM lane r ----
+    // ---- producers: row r's nibbles -> bf16 (q - z) * s pairs -> TMEM lane r, A stage gl % NA ----
     const int r = warp * 32 + lane;
     const uint32_t lane_base = tbase + ((uint32_t)(warp * 32) << 16);
     for (int gl = 0; gl < S; ++gl) {
-      const int stage = gl & 1;
+      const int stage = gl % NA;
       bool ok = true;
-      if (gl >= 2) ok = mbar_wait_bounded(&a_empty[stage], ((gl - 2) >> 1) & 1, p.err);
-      if (ok) ok = mbar_wait_bounded(&raw_full[gl], 0, p.err);
-      ok = __all_sync(0xffffffffu, ok);  // the warp takes the same branch before tcgen05.st
-      if (!ok) {
+      if (gl >= NA) {
+        // the stage frees when the MMAs of group gl - NA retire, which needs
+        // this grid's activations: wait for the previous grid first
+        if (gl == NA) grid_dep_wait();
+        ok = mbar_wait_bounded(&a_empty[stage], (gl / NA - 1) & 1, p.err);
+      }
+      ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&raw_full[gl], 0, p.err));
+      if (!ok) {  // the warp takes the same branch before tcgen05.st
         *abort_flag = 1;
         break;
       }
@@ -335,21 +360,28 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
             cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d2);
           }
         }
-        tmem_st16(lane_base + A_COL + stage * 64 + pc * 16, cols);
+        tmem_st16(lane_base + a0 + stage * 64 + pc * 16, cols);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[stage]);
     }
-    T2B_TRACE_MARK(3);
+    T2B_TRACE_MARK(2);
+    grid_dep_wait();
   } else if (warp == 4) {
-    // ---- MMA issuer (one lane): all groups into one accumulator ----
+    grid_dep_wait();
+    // ---- activations (one 64-k x BP-row TMA box per group and 64-k atom, swizzled
+    // into the UMMA K-major layout; rows past M arrive as zeros), then the MMAs ----
     if (lane == 0) {
+      mbar_arrive_expect_tx(x_full, (uint32_t)(S * L.x_group));
+      for (int gl = 0; gl < S; ++gl)
+        for (int atom = 0; atom < 2; ++atom)
+          tma_load_2d(xs + gl * L.x_group + atom * (BP * 128), &p.xmap, (g0 + gl) * GROUP + atom * 64, m0, x_full);
       bool ok = mbar_wait_bounded(x_full, 0, p.err);
       for (int gl = 0; ok && gl < S; ++gl) {
-        const int stage = gl & 1;
-        if (!mbar_wait_bounded(&a_full[stage], (gl >> 1) & 1, p.err)) {
+        const int stage = gl % NA;
+        if (!mbar_wait_bounded(&a_full[stage], (gl / NA) & 1, p.err)) {
           ok = false;
           break;
         }
@@ -358,21 +390,29 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint64_t bdesc = sdesc_sw128(xg + (ks >> 2) * (BP * 128) + (ks & 3) * 32);
-          mma_ts(tbase + ACC_COL, tbase + A_COL + stage * 64 + ks * 8, bdesc, IDESC, (gl > 0 || ks > 0) ? 1u : 0u);
+          mma_ts(tbase, tbase + a0 + stage * 64 + ks * 8, bdesc, IDESC, (gl > 0 || ks > 0) ? 1u : 0u);
         }
-        mma_commit(&a_empty[stage]);
+        if (gl + NA < S) mma_commit(&a_empty[stage]);
       }
       if (!ok) *abort_flag = 1;
       mma_commit(acc_full);
     }
     __syncwarp();
   } else {
-    // ---- warps 5-7: stage the epilogue inputs (one parallel pass) ----
-    stage_epilogue_inputs<EPI>(p, sm + L.off_ep, tile, ep_m0, ep_rows, threadIdx.x - 160, 96);
+    // ---- warps 5-7: ssq buffer hand-off, row scales, epilogue inputs ----
+    grid_dep_wait();
+    maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0, threadIdx.x - 160, 96);
+    if (PRO == PRO_RMSNORM)
+      for (int b = threadIdx.x - 160; b < BP; b += 96) {
+        const int m = m0 + b;
+        rowscale[b] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;   // model.py:179-180
+      }
+    stage_epilogue_inputs<EPI>(p, sm + L.off_ep, tile, mrow0, rows, threadIdx.x - 160, 96);
   }
+  __syncthreads();  // row scales and staged inputs visible
 
-  // ---- drain: tile_acc[b][r] = D[r][b] (* row scale); warps w and w+4 share
-  // TMEM lane quarter w%4 and split the BP columns ----
+  // ---- drain: D[r][b] (* row scale) -> the owning CTA's slot [rank][b - q*rows][r];
+  // warps w and w+4 share TMEM lane quarter w%4 and split the BP columns ----
   {
     constexpr int HB = BP / 2;
     const int q4 = warp & 3, half = warp >> 2;
@@ -380,24 +420,33 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     const bool ok = __all_sync(0xffffffffu, (*abort_flag == 0) && mbar_wait_bounded(acc_full, 0, p.err));
     if (!ok) *abort_flag = 1;
-    T2B_TRACE_MARK(4);
+    T2B_TRACE_MARK(3);
     tc_fence_after();
-#pragma unroll 4
-    for (int cb = 0; cb < HB / 8; ++cb) {
-      uint32_t v[8];
+    constexpr int CB = HB < 32 ? HB : 32;  // columns per TMEM load round
+#pragma unroll 1
+    for (int c0 = 0; c0 < HB; c0 += CB) {
+      uint32_t v[CB];
       if (ok) {
-        tmem_ld8(lane_base + ACC_COL + half * HB + cb * 8, v);
+        if (CB >= 16) {
+#pragma unroll
+          for (int cb = 0; cb < CB / 16; ++cb)
+            tmem_ld16(lane_base + half * HB + c0 + cb * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[cb * 16]));
+        } else {
+          tmem_ld8(lane_base + half * HB + c0, *reinterpret_cast<uint32_t(*)[8]>(&v[0]));
+        }
         tmem_ld_wait();
       }
+      if (c0 == 0) T2B_TRACE_MARK(4);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int b = half * HB + cb * 8 + e;
+      for (int e = 0; e < CB; ++e) {
+        const int b = half * HB + c0 + e;
         float y = ok ? __uint_as_float(v[e]) : 0.f;
         if (PRO == PRO_RMSNORM) y *= rowscale[b];
         tile_acc[b * TILE_N + r] = y;
       }
     }
   }
+  T2B_TRACE_MARK(5);
   tc_fence_before();
   __syncthreads();
   if (warp == 4) {
@@ -405,38 +454,46 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     tmem_dealloc(tbase, tmem_cols);
   }
 
-  T2B_TRACE_MARK(5);
-  // ---- cluster split-K: sum the KS partial tiles through DSMEM ----
-  // (every CTA passes both cluster barriers, aborted or not)
-  const float* fin = tile_acc;
-  int rows = BP, mrow0 = m0;
+  // ---- cluster split-K: push each peer's rows, sum the rows pushed here ----
+  // (every CTA passes both cluster barrier phases, aborted or not; an aborted
+  // CTA still pushes so no peer waits out its receive barrier)
   if (KS > 1) {
-    const uint32_t rank = cluster_ctarank();
-    rows = BP / KS;
-    mrow0 = m0 + (int)rank * rows;
-    float* red = reinterpret_cast<float*>(xs);  // X tile is dead once acc_full fired
-    cluster_sync();
-    const uint32_t my_tile = smem_u32(tile_acc) + rank * rows * TILE_N * 4;
-    for (int i = threadIdx.x; i < rows * TILE_N / 4; i += 256) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    cluster_wait();
+    if (threadIdx.x == 0) {
+      fence_proxy_async();  // the drain's shared-memory stores, seen by the bulk copies
       for (int q = 0; q < KS; ++q) {
-        const float4 v = ld_dsmem_f4(map_peer(my_tile + i * 16, (uint32_t)q));
+        if (q == (int)rank) continue;
+        const int slot = (int)rank < q ? (int)rank : (int)rank - 1;  // this CTA's slot at rank q
+        bulk_s2s_peer(map_peer(smem_u32(recv + slot * rows * TILE_N), (uint32_t)q), tile_acc + q * rows * TILE_N,
+                      (uint32_t)(rows * TILE_N * 4), map_peer(smem_u32(recv_full), (uint32_t)q));
+      }
+    }
+    const bool ok = __syncthreads_and(mbar_wait_bounded(recv_full, 0, p.err));
+    if (!ok && threadIdx.x == 0) *abort_flag = 1;
+    // sums go to receive slot 0: the other owners' rows of tile_acc may still
+    // be read by this CTA's outgoing copies
+    for (int i = threadIdx.x; i < rows * TILE_N / 4; i += 256) {
+      float4 acc = reinterpret_cast<const float4*>(tile_acc + rank * rows * TILE_N)[i];
+      for (int q = 0; q < KS - 1; ++q) {
+        const float4 v = reinterpret_cast<const float4*>(recv + q * rows * TILE_N)[i];
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
         acc.w += v.w;
       }
-      reinterpret_cast<float4*>(red)[i] = acc;
+      reinterpret_cast<float4*>(recv)[i] = acc;
     }
-    cluster_sync();
-    fin = red;
+    __syncthreads();
   }
-  __syncthreads();
+  const float* fin = KS > 1 ? recv : tile_acc;
   T2B_TRACE_MARK(6);
-  if (*abort_flag) return;
-  tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows, staged_epilogue_inputs<EPI>(p, sm + L.off_ep, rows));
+  if (!*abort_flag)
+    tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows, staged_epilogue_inputs<EPI>(p, sm + L.off_ep, rows));
   __syncthreads();
   T2B_TRACE_MARK(7);
+  // every peer has received this CTA's pushes (it waited for them before
+  // arriving here), so this CTA's shared memory may be released
+  if (KS > 1) cluster_sync();
 }
 
 // ---------------------------------------------------------------------------
@@ -460,7 +517,7 @@ static TcPlan tc_plan(int M, int N, int K) {
   while (bp < M && bp < 256) bp <<= 1;
   pl.BP = bp;
   pl.S = 0;
-  auto fits = [&](int bp_, int s_) { return TcLayout(bp_, s_).bytes <= 200 * 1024; };
+  auto fits = [&](int bp_, int s_) { return TcLayout(bp_, s_, G / s_).bytes <= 210 * 1024; };
   for (int s_ : {4, 3, 2, 1}) {
     if (G % s_ || G / s_ > 8 || G / s_ > bp) continue;
     if (!fits(bp, s_)) continue;
@@ -485,7 +542,13 @@ static TcPlan tc_plan(int M, int N, int K) {
   if (!pl.ok) return pl;
   pl.KS = G / pl.S;
   pl.mblocks = (M + pl.BP - 1) / pl.BP;
-  pl.smem = (size_t)TcLayout(pl.BP, pl.S).bytes;
+  pl.smem = (size_t)TcLayout(pl.BP, pl.S, pl.KS).bytes;
+  // A CTA holding more than half of the SM's 512 TMEM columns runs alone on
+  // its SM (more than half of the shared memory requested): a second one
+  // there would only sit in tcgen05.alloc until the first frees its columns.
+  // (No wait cycle either way: a CTA frees its TMEM before the cluster
+  // barrier, the only point where it waits for its peers.)
+  if (tc_tmem_cols(pl.BP, pl.S) > 256 && pl.smem < 120 * 1024) pl.smem = 120 * 1024;
   return pl;
 }
 
