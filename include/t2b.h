@@ -43,6 +43,12 @@
 extern "C" {
 #endif
 
+/*
+ * Status codes.  T2B_ERR_ALIGN: weights, activations, q/out, KV caches, RoPE
+ * angles and the fp32 residual stream must be 16-byte aligned, bf16 norm
+ * weights and bf16 outputs of the fused layer ops 8-byte aligned (any
+ * cudaMalloc / torch allocation is).
+ */
 #define T2B_OK 0
 #define T2B_ERR_SHAPE 1
 #define T2B_ERR_ALIGN 2

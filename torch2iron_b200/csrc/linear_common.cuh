@@ -103,78 +103,69 @@ struct EpiCache {
 // QKV epilogue (model.py:248-264): per 128-row tile = 128/HD heads of q, k or v
 // for MB batch rows.  q/k heads: per-head RMSNorm (when weights are given),
 // then interleaved RoPE on (x[2i], x[2i+1]) pairs; q goes to q_out, k/v to the
-// cache at the row's position.  Work item = (row, dimension pair): float2
-// reads, one bf16x2 store, no runtime division.
+// cache at the row's position.  A warp owns one batch row of the tile per
+// pass, lane = 4 consecutive dims (float4 in, 8-byte bf16 store out): a head
+// is 32 lanes (HD 128) or 16 (HD 64), so its sum of squares is a warp
+// reduction in the same pass.  q_out, the caches and the angle table are
+// 16-byte aligned, the norm weights 8-byte (checked at the C ABI).
 // ---------------------------------------------------------------------------
+T2B_DEV uint2 pack_bf16x4(float a, float b, float c, float d) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+T2B_DEV float4 unpack_bf16x4(uint2 v) {
+  return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
+                     __uint_as_float(v.y & 0xffff0000u));
+}
+
 template <int HD>
-T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB,
-                          const EpiCache& ec) {
-  constexpr int NT = 256;
-  constexpr int HPT = TILE_N / HD;  // heads per tile
+T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile, int m0, int MB, const EpiCache& ec) {
+  constexpr int HPT = TILE_N / HD;    // heads per tile
+  constexpr int LPH = HD / 4;         // lanes per head
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head0 = tile * HPT;
+  const int hl = lane / LPH, d0 = (lane % LPH) * 4;
+  const int head = tile * HPT + hl;
   const int nq = p.n_heads, nkv = p.n_kv;
-  // per (row, head) inverse RMS over the head (model.py:179-180 on q/k heads)
-  for (int pair = warp; pair < MB * HPT; pair += NT / 32) {
-    const int b = pair / HPT, hl = pair - b * HPT;
-    const int head = head0 + hl;
-    float ss = 0.f;
-#pragma unroll
-    for (int d = lane; d < HD; d += 32) {
-      const float v = tile_acc[b * TILE_N + hl * HD + d];
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) {
-      const bool normed = (head < nq && p.qn_w) || (head >= nq && head < nq + nkv && p.kn_w);
-      scratch[pair] = normed ? rsqrtf(ss / (float)HD + p.eps) : 1.f;
-    }
-  }
-  __syncthreads();
+  const bool is_q = head < nq, is_v = head >= nq + nkv;
+  const __nv_bfloat16* nw = is_q ? (ec.qn ? ec.qn : p.qn_w) : (ec.kn ? ec.kn : p.kn_w);
+  if (is_v) nw = nullptr;
+  const float4 w = nw ? unpack_bf16x4(*reinterpret_cast<const uint2*>(nw + d0)) : make_float4(1.f, 1.f, 1.f, 1.f);
   __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(p.y);
-  const __nv_bfloat16* qn = ec.qn ? ec.qn : p.qn_w;
-  const __nv_bfloat16* kn = ec.kn ? ec.kn : p.kn_w;
-  for (int it = threadIdx.x; it < MB * (TILE_N / 2); it += NT) {
-    const int b = it / (TILE_N / 2), pr = it - b * (TILE_N / 2);   // pr: pair index inside the tile
+  for (int b = warp; b < MB; b += 8) {
     const int m = m0 + b;
-    if (m >= p.M) continue;
-    const int hl = (2 * pr) / HD, d0 = 2 * pr - hl * HD;
-    const int head = head0 + hl;
+    if (m >= p.M) break;  // warp-uniform
+    const float4 x = *reinterpret_cast<const float4*>(tile_acc + b * TILE_N + lane * 4);
+    float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+#pragma unroll
+    for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const int pos = ec.pos ? ec.pos[b] : p.pos[m];
     const bool in_cache = pos >= 0 && pos < p.max_ctx;   // a bad position writes no cache entry
-    const float2 xv = *reinterpret_cast<const float2*>(tile_acc + b * TILE_N + 2 * pr);
-    if (head >= nq + nkv) {  // value head: stored as projected (model.py:250,263)
+    if (is_v) {  // value head: stored as projected (model.py:250,263)
       if (in_cache)
-        *reinterpret_cast<__nv_bfloat162*>(
-            &p.v_cache[(((size_t)m * nkv + (head - nq - nkv)) * p.max_ctx + pos) * HD + d0]) =
-            __floats2bfloat162_rn(xv.x, xv.y);
+        *reinterpret_cast<uint2*>(&p.v_cache[(((size_t)m * nkv + (head - nq - nkv)) * p.max_ctx + pos) * HD + d0]) =
+            pack_bf16x4(x.x, x.y, x.z, x.w);
       continue;
     }
-    const bool is_q = head < nq;
     if (!is_q && !in_cache) continue;
-    const __nv_bfloat16* nw = is_q ? qn : kn;
-    float x0 = xv.x, x1 = xv.y;
-    if (nw) {
-      const float rs = scratch[b * HPT + hl];
-      const __nv_bfloat162 w2 = *reinterpret_cast<const __nv_bfloat162*>(nw + d0);
-      x0 = (x0 * rs) * __low2float(w2);
-      x1 = (x1 * rs) * __high2float(w2);
-    }
+    const float rs = nw ? rsqrtf(ss / (float)HD + p.eps) : 1.f;   // model.py:179-180 on the head
+    const float x0 = x.x * rs * w.x, x1 = x.y * rs * w.y, x2 = x.z * rs * w.z, x3 = x.w * rs * w.w;
     // interleaved RoPE (model.py:184-196): (x0, x1) -> (x0 c - x1 s, x1 c + x0 s)
-    const float2 cs = *reinterpret_cast<const float2*>(
+    const float4 cs = *reinterpret_cast<const float4*>(
         ec.angles ? ec.angles + (size_t)b * HD + d0 : p.angles + (size_t)(in_cache ? pos : 0) * HD + d0);
-    const __nv_bfloat162 o = __floats2bfloat162_rn(x0 * cs.x - x1 * cs.y, x1 * cs.x + x0 * cs.y);
+    const uint2 o = pack_bf16x4(x0 * cs.x - x1 * cs.y, x1 * cs.x + x0 * cs.y, x2 * cs.z - x3 * cs.w,
+                                x3 * cs.z + x2 * cs.w);
     if (is_q)
-      *reinterpret_cast<__nv_bfloat162*>(&q_out[(size_t)m * p.y_ld + head * HD + d0]) = o;
+      *reinterpret_cast<uint2*>(&q_out[(size_t)m * p.y_ld + head * HD + d0]) = o;
     else
-      *reinterpret_cast<__nv_bfloat162*>(&p.k_cache[(((size_t)m * nkv + (head - nq)) * p.max_ctx + pos) * HD + d0]) =
-          o;
+      *reinterpret_cast<uint2*>(&p.k_cache[(((size_t)m * nkv + (head - nq)) * p.max_ctx + pos) * HD + d0]) = o;
   }
 }
 
 // ---------------------------------------------------------------------------
 // Epilogues over a finished [MB][128] fp32 tile (rows tile*128.., batch rows
-// m0..m0+MB-1).  `scratch` holds >= 2*MB floats.  256 threads.
+// m0..m0+MB-1).  `scratch` holds >= 2*MB floats.  256 threads; each thread
+// takes 4 consecutive outputs (the residual stream and h are 16- / 8-byte
+// aligned with row strides of multiples of 4, checked at the C ABI).
 // ---------------------------------------------------------------------------
 template <int EPI>
 T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB,
@@ -189,20 +180,23 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
     }
   } else if (EPI == EPI_RESIDUAL) {
     // x += y ; sum of squares for the next RMSNorm ; bf16(x * w_next) for its GEMM.
-    // Each warp's 32 elements share one batch row -> one atomic per warp per pass.
-    for (int base = 0; base < MB * TILE_N; base += NT) {
-      const int idx = base + threadIdx.x;
+    // A warp's 128 elements are one batch row of the tile -> one atomic per warp per pass.
+    for (int base = 0; base < MB * TILE_N; base += NT * 4) {
+      const int idx = base + threadIdx.x * 4;
       const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
       const bool live = idx < MB * TILE_N && m < p.M;
       float sq = 0.f;
       if (live) {
         const size_t o = (size_t)m * p.y_ld + row0 + lr;
-        const float v = (ec.resid ? ec.resid[idx] : p.resid[o]) + tile_acc[idx];
-        p.resid[o] = v;
-        sq = v * v;
+        const float4 r = *reinterpret_cast<const float4*>(ec.resid ? ec.resid + idx : p.resid + o);
+        const float4 t = *reinterpret_cast<const float4*>(tile_acc + idx);
+        const float4 v = make_float4(r.x + t.x, r.y + t.y, r.z + t.z, r.w + t.w);
+        *reinterpret_cast<float4*>(p.resid + o) = v;
+        sq = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         if (p.xw_out) {
-          const float w = __bfloat162float(ec.next_w ? ec.next_w[lr] : p.next_w[row0 + lr]);
-          p.xw_out[o] = __float2bfloat16_rn(v * w);
+          const float4 w = unpack_bf16x4(
+              *reinterpret_cast<const uint2*>(ec.next_w ? ec.next_w + lr : p.next_w + row0 + lr));
+          *reinterpret_cast<uint2*>(p.xw_out + o) = pack_bf16x4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
         }
       }
       sq = warp_sum(sq);
@@ -211,18 +205,19 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
   } else if (EPI == EPI_SWIGLU) {
     // tile = 64 gate rows then the matching 64 up rows (model.py:215-216)
     __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.y);
-    for (int idx = threadIdx.x; idx < MB * 64; idx += NT) {
+    for (int idx = threadIdx.x * 4; idx < MB * 64; idx += NT * 4) {
       const int b = idx >> 6, t = idx & 63, m = m0 + b;
       if (m < p.M) {
-        const float g = tile_acc[b * TILE_N + t];
-        const float u = tile_acc[b * TILE_N + 64 + t];
-        const float silu = g / (1.f + expf(-g));
-        h[(size_t)m * p.y_ld + tile * 64 + t] = __float2bfloat16_rn(silu * u);
+        const float4 g = *reinterpret_cast<const float4*>(tile_acc + b * TILE_N + t);
+        const float4 u = *reinterpret_cast<const float4*>(tile_acc + b * TILE_N + 64 + t);
+        *reinterpret_cast<uint2*>(&h[(size_t)m * p.y_ld + tile * 64 + t]) =
+            pack_bf16x4(g.x / (1.f + expf(-g.x)) * u.x, g.y / (1.f + expf(-g.y)) * u.y,
+                        g.z / (1.f + expf(-g.z)) * u.z, g.w / (1.f + expf(-g.w)) * u.w);
       }
     }
   } else {  // EPI_QKV
-    if (p.head_dim == 128) qkv_epilogue<128>(p, tile_acc, scratch, tile, m0, MB, ec);
-    else qkv_epilogue<64>(p, tile_acc, scratch, tile, m0, MB, ec);
+    if (p.head_dim == 128) qkv_epilogue<128>(p, tile_acc, tile, m0, MB, ec);
+    else qkv_epilogue<64>(p, tile_acc, tile, m0, MB, ec);
   }
 }
 

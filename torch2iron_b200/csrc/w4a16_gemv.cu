@@ -389,6 +389,9 @@ extern "C" int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta
   if (!qw || !meta || !xw || !ssq || !angles || !pos || !q_out || !k_cache || !v_cache) return T2B_ERR_ARG;
   if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return T2B_ERR_ARG;
   if (!al(qw, 16) || !al(xw, 16)) return T2B_ERR_ALIGN;
+  // vectorised epilogue: float4 angle rows, 8-byte bf16 stores, 8-byte norm weights
+  if (!al(q_out, 16) || !al(k_cache, 16) || !al(v_cache, 16) || !al(angles, 16)) return T2B_ERR_ALIGN;
+  if ((q_norm_w && !al(q_norm_w, 8)) || (k_norm_w && !al(k_norm_w, 8))) return T2B_ERR_ALIGN;
   const int N = (n_heads + 2 * n_kv) * head_dim;
   LinearParams p = gemv_base(qw, meta, H / 2, M, N, H);
   p.x = xw;
@@ -423,6 +426,8 @@ extern "C" int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const
   if (!qw || !meta || !attn || !x_resid || !ssq_out) return T2B_ERR_ARG;
   if ((next_norm_w == nullptr) != (xw_out == nullptr)) return T2B_ERR_ARG;
   if (!al(qw, 16) || !al(attn, 16)) return T2B_ERR_ALIGN;
+  // vectorised epilogue: float4 residual rows, 8-byte bf16 stores
+  if (!al(x_resid, 16) || (xw_out && (!al(xw_out, 8) || !al(next_norm_w, 8)))) return T2B_ERR_ALIGN;
   LinearParams p = gemv_base(qw, meta, K / 2, M, H, K);
   p.x = attn;
   p.x_dtype = T2B_DTYPE_BF16;
@@ -445,7 +450,7 @@ extern "C" int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const 
                                  size_t ws_bytes, void* stream) {
   if (I % 64) return T2B_ERR_SHAPE;
   if (!qw || !meta || !xw || !ssq || !h_out) return T2B_ERR_ARG;
-  if (!al(qw, 16) || !al(xw, 16)) return T2B_ERR_ALIGN;
+  if (!al(qw, 16) || !al(xw, 16) || !al(h_out, 8)) return T2B_ERR_ALIGN;
   LinearParams p = gemv_base(qw, meta, H / 2, M, 2 * I, H);
   p.x = xw;
   p.x_dtype = T2B_DTYPE_BF16;
