@@ -46,6 +46,7 @@ def test_status_strings_and_host_side_errors():
 def test_workspace_queries():
     lib = _lib.load()
     assert lib.t2b_w4a16_gemm_workspace_bytes(1, 128, 256) >= 0
-    assert lib.t2b_w4a16_gemm_workspace_bytes(8, 1024, 3072) > 0
+    assert lib.t2b_w4a16_gemm_workspace_bytes(8, 1024, 3072) == 0     # k-slices meet in a cluster
+    assert lib.t2b_w4a16_gemm_workspace_bytes(1, 1024, 12288) > 0     # more than 8 k-slices: workspace
     assert lib.t2b_decode_attention_workspace_bytes(64, 16, 8, 128, 256) > 0   # tickets + partial records
     assert lib.t2b_decode_attention_workspace_bytes(1, 16, 8, 128, 4096) > 0

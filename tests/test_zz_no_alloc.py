@@ -43,11 +43,16 @@ def _noalloc(w, x):
     return y
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 1024, 3072), (4, 4096, 1024), (8, 1024, 2048), (3, 6144, 1024)])
-def test_noalloc_matches_allocating_entry_point(monkeypatch, M, N, K):
+@pytest.mark.parametrize("M,N,K,needs_ws", [
+    (1, 1024, 3072, False), (4, 4096, 1024, False), (8, 1024, 2048, False), (3, 6144, 1024, False),  # cluster split-K
+    (1, 1024, 12288, True), (2, 512, 16384, True),     # more k-slices than a cluster holds: workspace split-K
+])
+def test_noalloc_matches_allocating_entry_point(monkeypatch, M, N, K, needs_ws):
     monkeypatch.setenv("T2B_TC_MIN_M", "16")   # keep these row counts on the split-K CUDA-core path
     L = _lib.lib()
-    assert 0 < L.t2b_w4a16_gemm_workspace_bytes(M, N, K) <= L.t2b_w4a16_gemm_noalloc_max_workspace()
+    n = L.t2b_w4a16_gemm_workspace_bytes(M, N, K)
+    assert n <= L.t2b_w4a16_gemm_noalloc_max_workspace()
+    assert (n > 0) == needs_ws
     g = torch.Generator().manual_seed(M * 131 + N + K)
     lin = synth.random_linear(N, K, g)
     w = W.from_autogptq(lin)
@@ -64,7 +69,7 @@ def test_noalloc_matches_allocating_entry_point(monkeypatch, M, N, K):
 def test_noalloc_rejects_sizes_beyond_its_scratch():
     L = _lib.lib()
     cap = L.t2b_w4a16_gemm_noalloc_max_workspace()
-    M, N, K = 8, 65536, 8192          # needs more scratch than the library holds
+    M, N, K = 8, 65536, 16384         # needs more scratch than the library holds
     assert L.t2b_w4a16_gemm_workspace_bytes(M, N, K) > cap
     status = L.t2b_w4a16_gemm_noalloc(None, None, 0, None, 0, None, 0, M, N, K, 128, None)
     assert status == 5   # T2B_ERR_WORKSPACE, returned before anything is enqueued

@@ -174,6 +174,18 @@ T2B_DEV uint32_t map_peer(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
+// Bulk copy of this CTA's shared memory into a cluster peer's, completing on
+// the peer's mbarrier (dst and bar are shared::cluster addresses of the peer;
+// 16-byte aligned, bytes a multiple of 16).  The source must stay allocated
+// until the peer has seen the bytes arrive.
+T2B_DEV void bulk_s2s_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// The two halves of cluster_sync(), for work between arrival and waiting.
+T2B_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+T2B_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 T2B_DEV float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"

@@ -11,9 +11,15 @@
 //   * dequant per nibble: one PRMT builds the fp32 value 128+q, one FFMA
 //     turns it into (q - zero) * scale exactly (19-bit products), then one
 //     FFMA per batch row.
-//   * the 8 lanes of a row reduce with 3 xor-shuffles; k-slices (split-K)
-//     meet in a fp32 workspace and the last CTA of a tile (ticket counter)
-//     runs the epilogue on the full 128-row tile.
+//   * the 8 lanes of a row reduce with 3 xor-shuffles.  k-slices (split-K)
+//     of a tile form a thread-block cluster of up to 8 CTAs: every rank but
+//     0 pushes its [MB][128] partial into rank 0's shared memory with one
+//     bulk copy (completion on rank 0's mbarrier), and rank 0 sums and runs
+//     the epilogue on the full 128-row tile.  More than 8 k-slices meet in a
+//     fp32 workspace instead, where the last CTA of a tile (ticket counter)
+//     runs the epilogue.
+//   * the RMSNorm row scale rsqrt(ssq/K + eps) multiplies the finished dot
+//     products (it is loaded alongside the activations, not before them).
 //
 // Algorithmic parity: W[n,k] = (q - zero) * scale exactly as
 // src/models/fast_qwen3/fast_packed_format.py:158-160; fp32 accumulation as
@@ -28,13 +34,23 @@ namespace t2b {
 
 constexpr int GV_THREADS = 256;
 
+constexpr int GV_MAX_CLUSTER = 8;
+
+// Shared memory: xs | tile_acc | scratch | recv [ksplit-1][MB][128] (cluster
+// split-K only) | receive mbarrier.
 template <int MB, int CH>
 struct GemvSmem {
   static constexpr int XS_LD = CH * 288;  // 256 k per chunk, +4 floats pad per 32 (bank spread)
   static constexpr int XS_FLOATS = MB * XS_LD;
   static constexpr int TILE_FLOATS = MB * TILE_N;
   static constexpr size_t BYTES = sizeof(float) * (XS_FLOATS + TILE_FLOATS + 8 * MB);
+  static size_t bytes(int ksplit, bool cluster) {
+    return BYTES + (cluster ? sizeof(float) * (size_t)(ksplit - 1) * TILE_FLOATS + 16 : 0);
+  }
 };
+
+// k-slices of one tile reduced inside a cluster (else through the workspace)
+static inline bool gv_cluster(int ksplit) { return ksplit > 1 && ksplit <= GV_MAX_CLUSTER; }
 
 T2B_DEV uint4 ldg_stream(const void* p) {
   uint4 r;
@@ -53,6 +69,9 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
   float* xs = smem;
   float* tile_acc = smem + S::XS_FLOATS;
   float* scratch = tile_acc + S::TILE_FLOATS;   // [8*MB]
+  float* recv = scratch + 8 * MB;               // cluster split-K: [ksplit-1][MB][128]
+  const bool clus = p.ksplit > 1 && p.ksplit <= GV_MAX_CLUSTER;
+  uint64_t* recv_full = reinterpret_cast<uint64_t*>(recv + (clus ? (p.ksplit - 1) * S::TILE_FLOATS : 0));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y, mblk = blockIdx.z;
@@ -83,30 +102,34 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
     }
   }
 
+  // cluster split-K: rank 0's receive barrier, armed before any peer may push
+  const uint32_t rank = clus ? cluster_ctarank() : 0u;
+  if (clus) {
+    if (threadIdx.x == 0) {
+      mbar_init(recv_full, 1);
+      fence_mbar_init();
+      if (rank == 0) mbar_arrive_expect_tx(recv_full, (uint32_t)((p.ksplit - 1) * S::TILE_FLOATS * 4));
+    }
+    __syncthreads();
+    cluster_arrive();
+  }
+
   grid_dep_wait();
   grid_dep_launch();
   T2B_TRACE_MARK(1);
 
-  // ---- 2. prologue: activations of this k-slice into shared fp32 --------
-  if (PRO == PRO_RMSNORM) {
-    if (threadIdx.x < MB) {
-      const int m = m0 + threadIdx.x;
-      scratch[threadIdx.x] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;
-    }
-    __syncthreads();
+  // ---- 2. prologue: activations of this k-slice into shared fp32; the
+  // RMSNorm row scale (model.py:179-181: x holds bf16(row * weight), the dot
+  // product is then times rsqrt(mean(row^2)+eps)) loads alongside ----------
+  if (PRO == PRO_RMSNORM && threadIdx.x < MB) {
+    const int m = m0 + threadIdx.x;
+    scratch[threadIdx.x] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;
   }
   for (int idx = threadIdx.x; idx < MB * CH * 256; idx += GV_THREADS) {
     const int b = idx / (CH * 256), kk = idx - b * (CH * 256);
     const int m = m0 + b;
     float v = 0.f;
-    if (m < p.M) {
-      if (PRO == PRO_ACT) {
-        v = load_act(p.x, p.x_dtype, (size_t)m * p.x_ld + k0 + kk);
-      } else {
-        // model.py:179-181: x holds bf16(row * weight); times rsqrt(mean(row^2)+eps)
-        v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.x)[(size_t)m * p.x_ld + k0 + kk]) * scratch[b];
-      }
-    }
+    if (m < p.M) v = load_act(p.x, PRO == PRO_ACT ? p.x_dtype : (int)X_BF16, (size_t)m * p.x_ld + k0 + kk);
     xs[b * S::XS_LD + kk + (kk >> 5) * 4] = v;
   }
   maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0, threadIdx.x, GV_THREADS);
@@ -193,12 +216,38 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
       v += __shfl_xor_sync(0xffffffffu, v, 4);
+      if (PRO == PRO_RMSNORM) v *= scratch[b];
       if ((lane & 7) == 0) tile_acc[b * TILE_N + warp * 16 + i * 4 + (lane >> 3)] = v;
     }
   __syncthreads();
 
-  // ---- 5. split-K fixup + epilogue --------------------------------------
+  // ---- 5. split-K + epilogue --------------------------------------------
   T2B_TRACE_MARK(3);
+  if (clus) {
+    cluster_wait();  // every rank's receive barrier is armed
+    if (rank != 0) {
+      if (threadIdx.x == 0) {
+        fence_proxy_async();  // tile_acc's shared-memory stores, seen by the bulk copy
+        bulk_s2s_peer(map_peer(smem_u32(recv + (rank - 1) * S::TILE_FLOATS), 0u), tile_acc,
+                      (uint32_t)(S::TILE_FLOATS * 4), map_peer(smem_u32(recv_full), 0u));
+      }
+    } else {
+      const bool ok = __syncthreads_and(mbar_wait_bounded(recv_full, 0, p.err));
+      for (int idx = threadIdx.x; idx < S::TILE_FLOATS; idx += GV_THREADS) {
+        float v = tile_acc[idx];
+        for (int q = 0; q < p.ksplit - 1; ++q) v += recv[q * S::TILE_FLOATS + idx];
+        tile_acc[idx] = v;
+      }
+      __syncthreads();
+      T2B_TRACE_MARK(4);
+      if (ok) tile_epilogue<EPI>(p, tile_acc, scratch, tile, m0, MB);
+      __syncthreads();
+      T2B_TRACE_MARK(5);
+    }
+    // rank 0 arrives after its pushes landed: the senders' shared memory may go
+    cluster_sync();
+    return;
+  }
   if (!splitk_fixup<MB>(p, tile_acc, tile, split, mblk, GV_THREADS)) return;
   T2B_TRACE_MARK(4);
   tile_epilogue<EPI>(p, tile_acc, scratch, tile, m0, MB);
@@ -212,8 +261,12 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
 
 static int pick_mb(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
-// k-slice: 256 or 512 per CTA, chosen so the grid has about 1-4 CTAs per SM.
+// k-slice per CTA: the smallest of 256/512/1024 that keeps a tile's k-slices
+// within one cluster (<= 8), else 256/512 with the grid at about 1-4 CTAs
+// per SM (workspace split-K).
 static int pick_kslice(int N, int K, int mblocks) {
+  for (int ks : {256, 512, 1024})
+    if (K % ks == 0 && K / ks <= GV_MAX_CLUSTER) return ks;
   const long tiles = (long)(N / TILE_N) * mblocks;
   if (K % 512 == 0 && tiles * (K / 256) > 4L * 148) return 512;
   return 256;
@@ -223,7 +276,7 @@ static size_t gemv_ws_bytes(int M, int N, int K) {
   const int MB = pick_mb(M);
   const int mblocks = (M + MB - 1) / MB;
   const int ksplit = K / pick_kslice(N, K, mblocks);
-  if (ksplit == 1) return 0;
+  if (ksplit == 1 || gv_cluster(ksplit)) return 0;
   size_t part = ((size_t)mblocks * ksplit * MB * N * sizeof(float) + 255) & ~size_t(255);
   return part + (((size_t)mblocks * (N / TILE_N) * sizeof(int) + 255) & ~size_t(255));
 }
@@ -231,7 +284,10 @@ static size_t gemv_ws_bytes(int M, int N, int K) {
 template <int MB, int CH, int PRO, int EPI, int WFMT>
 static int gemv_launch_t(LinearParams& p, dim3 grid, cudaStream_t st) {
   auto kern = w4a16_gemv_kernel<MB, CH, PRO, EPI, WFMT>;
-  const size_t smem = GemvSmem<MB, CH>::BYTES;  // <= 23 KB for every instantiation
+  const bool clus = gv_cluster(p.ksplit);
+  const size_t smem = GemvSmem<MB, CH>::bytes(p.ksplit, clus);
+  if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
+  if (clus) return launch_pdl_cluster(kern, grid, dim3(GV_THREADS), smem, st, p.ksplit, p);
   return launch_pdl(kern, grid, dim3(GV_THREADS), smem, st, p);
 }
 
@@ -239,8 +295,8 @@ template <int PRO, int EPI, int WFMT>
 static int gemv_dispatch(LinearParams& p, int MB, int CH, dim3 grid, cudaStream_t st) {
 #define T2B_CASE(mb, ch) \
   if (MB == mb && CH == ch) return gemv_launch_t<mb, ch, PRO, EPI, WFMT>(p, grid, st);
-  T2B_CASE(1, 1) T2B_CASE(1, 2) T2B_CASE(2, 1) T2B_CASE(2, 2)
-  T2B_CASE(4, 1) T2B_CASE(4, 2) T2B_CASE(8, 1) T2B_CASE(8, 2)
+  T2B_CASE(1, 1) T2B_CASE(1, 2) T2B_CASE(1, 4) T2B_CASE(2, 1) T2B_CASE(2, 2) T2B_CASE(2, 4)
+  T2B_CASE(4, 1) T2B_CASE(4, 2) T2B_CASE(4, 4) T2B_CASE(8, 1) T2B_CASE(8, 2) T2B_CASE(8, 4)
 #undef T2B_CASE
   return T2B_ERR_ARG;
 }
@@ -250,7 +306,8 @@ static int gemv_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, si
   const int mblocks = (p.M + MB - 1) / MB;
   p.kslice = pick_kslice(p.N, p.K, mblocks);
   p.ksplit = p.K / p.kslice;
-  if (ws_bytes < gemv_ws_bytes(p.M, p.N, p.K) || (p.ksplit > 1 && ws == nullptr)) return T2B_ERR_WORKSPACE;
+  const bool need_ws = p.ksplit > 1 && !gv_cluster(p.ksplit);
+  if (ws_bytes < gemv_ws_bytes(p.M, p.N, p.K) || (need_ws && ws == nullptr)) return T2B_ERR_WORKSPACE;
   size_t part = ((size_t)mblocks * p.ksplit * MB * p.N * sizeof(float) + 255) & ~size_t(255);
   p.ws_part = reinterpret_cast<float*>(ws);
   p.ws_cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + part);

@@ -222,18 +222,6 @@ __host__ __device__ constexpr uint32_t tc_tmem_cols(int BP, int S) {
   return pow2_cols(tc_a0(BP) + 64u * (uint32_t)tc_stages(BP, S));
 }
 
-T2B_DEV void st_dsmem_s32(uint32_t addr, int v) {
-  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-// Bulk copy of this CTA's shared memory into a cluster peer's, completing on
-// the peer's mbarrier (dst and bar are shared::cluster addresses of the peer).
-T2B_DEV void bulk_s2s_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
-               : "memory");
-}
-T2B_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
-T2B_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // grid (N/128, KS, mblocks), cluster (1, KS, 1): the KS CTAs of a cluster are
 // the k-splits of one 128-row tile (S groups each); each CTA finishes BP/KS
