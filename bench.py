@@ -49,6 +49,10 @@ def parse():
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="tensor-parallel ranks (config 4: --model qwen3-8b --tp 8 under torchrun); "
+                         "the batch is then the global batch")
+    ap.add_argument("--ctx", type=int, default=4096, help="--tp: KV cache pre-filled to this many positions")
     return ap.parse_args()
 
 
@@ -448,11 +452,95 @@ def run_t2b(args, cfg):
         print(json.dumps(result), flush=True)
 
 
+def run_tp(args, cfg):
+    """Config 4: one model split over the torchrun ranks (tensor parallel), B rows
+    in total, the KV cache pre-filled with N(0,1) bf16 to --ctx positions; K timed
+    decode steps (eager: the two NCCL all-reduces per layer run on the decode
+    stream between the fused kernels)."""
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from torch2iron_b200.tp import TPDecodeEngine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.tp:
+        raise SystemExit(f"--tp {args.tp} needs {args.tp} ranks (torchrun --nproc-per-node {args.tp}), got {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    B, C = args.batch, args.ctx
+    max_ctx = ((C + args.warmup + args.steps + 1 + 63) // 64) * 64
+    model = synth.random_model(cfg, seed=args.seed, device="cuda")
+    eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank)
+    del model
+    torch.cuda.empty_cache()
+    g = torch.Generator(device="cuda").manual_seed(args.seed * 1000 + 7 + rank)
+    for kc, vc in zip(eng.k_cache, eng.v_cache):
+        kc[:, :, :C].normal_(generator=g)
+        vc[:, :, :C].normal_(generator=g)
+    tok = torch.randint(0, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(args.seed + 3))
+    eng.tokens.copy_(tok)
+    eng.pos.fill_(C)
+    for _ in range(args.warmup):
+        eng.advance()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            eng.advance()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    # bytes one GPU must move per step: its weight shard, lm_head slice, KV of its kv heads
+    lc = eng.lcfg
+    c_mid = C + args.warmup + 1 + args.steps // 2
+    kv_tok = 2 * lc.n_kv_groups * cfg.head_dim * 2
+    w_bytes = sum(l.algorithmic_bytes for l in eng.layers) + eng.lm_head.numel() * 2
+    gpu_bytes = w_bytes + B * c_mid * kv_tok * cfg.n_layers
+    peak, peak_kind = peaks()
+    if rank == 0:
+        value = B * args.steps / (ms / 1000)
+        per_gpu_gbs = gpu_bytes / (ms / args.steps * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4-weights/bf16-activations/fp32-accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) bf16 KV pre-fill, uniform-random token ids)",
+            "config": {"workload": f"config4 {args.model} greedy decode, {B} rows, tensor parallel over {world} "
+                                   f"GPUs, ctx {C + args.warmup + 1}..{C + args.warmup + args.steps}",
+                       "model": args.model, "global_batch": B, "seq_len": C + args.warmup + args.steps,
+                       "parallelism": f"tp{world}",
+                       "l2": f"working set > L2 every step (~{gpu_bytes / 1e9:.2f} GB/step/GPU)"},
+            "hbm": {"algorithmic_bytes_per_step_per_gpu": int(gpu_bytes), "achieved_gbs_per_gpu": round(per_gpu_gbs, 1),
+                    "frac_of_peak": round(per_gpu_gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_kind},
+            "gpu_launches": eng.kernels_per_step() * args.steps,
+            "collectives_per_step": 2 * cfg.n_layers + 2,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     cfg = PRESETS[args.model]
     if args.impl == "reference":
         run_reference(args, cfg)
+        return
+    if args.tp:
+        run_tp(args, cfg)
         return
     run_t2b(args, cfg)
 

@@ -220,6 +220,17 @@ T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint
  * dtype T2B_DTYPE_*, row stride ld.  Replaces the host argmax of
  * qwen_npu.py:321 / model.py:492.
  */
+/*
+ * Tensor-parallel residual step: after the all-reduce of the row-parallel
+ * o_proj / down partials y [M][H] (fp32), x_resid += y, ssq_out[m] =
+ * sum_n x_resid[m,n]^2 (overwritten) and xw_out = bf16(x_resid * next_norm_w)
+ * (both NULL to skip).  Replaces ResidualAddRMSNorm
+ * (src/torch2iron/operators/residual_add_rms_norm/kernel.cc:70-93) where the
+ * GEMM before it is split over GPUs (batch_decode_fused.py:485-498, 529-539).
+ */
+T2B_API int t2b_residual_norm_input(const float* y, float* x_resid, float* ssq_out, const uint16_t* next_norm_w,
+                                    uint16_t* xw_out, int M, int H, void* stream);
+
 T2B_API size_t t2b_argmax_workspace_bytes(int M, int V);
 T2B_API int t2b_argmax_rows(const void* logits, int dtype, int M, int V, int ld, int32_t* idx, void* workspace,
                     size_t workspace_bytes, void* stream);

@@ -1,0 +1,77 @@
+"""Tensor-parallel decode on 2 GPUs (NCCL) against the single-GPU engine on the
+same model: same greedy tokens and residual stream after a prefill.  Skipped
+when fewer than 2 GPUs are visible."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from torch2iron_b200.config import QuantizedQwenConfig
+
+pytestmark = pytest.mark.gpu
+
+CFG = QuantizedQwenConfig(vocab_size=512, emb_dim=256, n_layers=2, n_heads=4, n_kv_groups=2, head_dim=128,
+                          hidden_dim=1024, rms_norm_eps=1e-6, rope_base=1e6)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, batch, out_q):
+    import torch.distributed as dist
+    from torch2iron_b200 import synth
+    from torch2iron_b200.engine import DecodeEngine
+    from torch2iron_b200.tp import TPDecodeEngine
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        model = synth.random_model(CFG, seed=21)
+        prompts = torch.randint(0, CFG.vocab_size, (batch, 6), generator=torch.Generator().manual_seed(22))
+        eng = TPDecodeEngine(CFG, model, batch=batch, max_ctx=64, tp=world, rank=rank)
+        eng.prefill(prompts)
+        toks = [eng.next_tokens.cpu().clone()]
+        for _ in range(3):
+            eng.advance()
+            toks.append(eng.next_tokens.cpu().clone())
+        res = {"tokens": torch.stack(toks, 1), "x": eng.x.cpu().clone()}
+        if rank == 0:
+            ref = DecodeEngine(CFG, model, batch=batch, max_ctx=64, use_graph=False)
+            ref.prefill(prompts)
+            rt = [ref.next_tokens.cpu().clone()]
+            for _ in range(3):
+                ref.advance()
+                rt.append(ref.next_tokens.cpu().clone())
+            res.update(ref_tokens=torch.stack(rt, 1), ref_x=ref.x.cpu().clone())
+        torch.cuda.synchronize()
+        out_q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("batch", [1, 5])
+def test_tp2_engine_matches_single_gpu(batch):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    r0, r1 = res[0], res[1]
+    assert torch.equal(r0["tokens"], r1["tokens"])            # replicated greedy picks
+    assert torch.equal(r0["x"], r1["x"])                      # replicated residual stream
+    assert torch.equal(r0["tokens"], r0["ref_tokens"])
+    err = (r0["x"] - r0["ref_x"]).abs().max() / r0["ref_x"].abs().max()
+    assert err <= 1e-2

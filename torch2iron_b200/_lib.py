@@ -48,6 +48,7 @@ SIGNATURES = {
     "t2b_down_residual": (I, [P, P, P, P, P, P, P, I, I, I, P, Z, P]),
     "t2b_embed_rows": (I, [P, P, P, P, P, P, I, I, I, P]),
     "t2b_rms_norm_rows": (I, [P, P, P, F, P, I, I, P]),
+    "t2b_residual_norm_input": (I, [P, P, P, P, P, I, I, P]),
     "t2b_argmax_workspace_bytes": (Z, [I, I]),
     "t2b_argmax_rows": (I, [P, I, I, I, I, P, P, Z, P]),
     "t2b_rms_norm_rope": (I, [P, P, P, P, I, I, I, F, I, P]),

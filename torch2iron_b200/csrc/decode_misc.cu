@@ -112,6 +112,54 @@ __global__ void rms_norm_rows_kernel(const float* __restrict__ x, const float* _
     out[(size_t)m * H + i] = __float2bfloat16_rn((x[(size_t)m * H + i] * r) * __bfloat162float(w[i]));
 }
 
+// Residual add after a tensor-parallel all-reduce (the ResidualAddRMSNorm of
+// residual_add_rms_norm/kernel.cc:70-93 in split form): x += y, then the row's
+// sum of squares (written, not accumulated) and xw = bf16(x * w) -- the input
+// the next linear normalises (model.py:179-181).  One CTA per row, float4.
+__global__ void __launch_bounds__(256) residual_norm_input_kernel(const float* __restrict__ y, float* __restrict__ x,
+                                                                  float* __restrict__ ssq,
+                                                                  const __nv_bfloat16* __restrict__ w,
+                                                                  __nv_bfloat16* __restrict__ xw, int H) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int m = blockIdx.x;
+  float sq = 0.f;
+  for (int i = threadIdx.x * 4; i < H; i += 256 * 4) {
+    const size_t o = (size_t)m * H + i;
+    const float4 a = *reinterpret_cast<const float4*>(x + o);
+    const float4 b = *reinterpret_cast<const float4*>(y + o);
+    const float4 v = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+    *reinterpret_cast<float4*>(x + o) = v;
+    sq += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    if (xw) {
+      const uint2 wr = *reinterpret_cast<const uint2*>(w + i);
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x * __uint_as_float(wr.x << 16),
+                                                      v.y * __uint_as_float(wr.x & 0xffff0000u));
+      const __nv_bfloat162 hi = __floats2bfloat162_rn(v.z * __uint_as_float(wr.y << 16),
+                                                      v.w * __uint_as_float(wr.y & 0xffff0000u));
+      *reinterpret_cast<uint2*>(xw + o) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    }
+  }
+  sq = warp_sum(sq);
+  __shared__ float part[8];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < 8; ++k) t += part[k];
+    ssq[m] = t;
+  }
+}
+
+int residual_norm_input(const float* y, float* x, float* ssq, const uint16_t* w, uint16_t* xw, int M, int H,
+                        cudaStream_t st) {
+  if (M < 1 || H < 4 || H % 4) return T2B_ERR_SHAPE;
+  const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(w);
+  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(xw);
+  return launch_pdl(residual_norm_input_kernel, dim3(M), dim3(256), 0, st, y, x, ssq, wp, op, H);
+}
+
 // ---------------------------------------------------------------------------
 // Row argmax over a [M, V] logits matrix: grid (chunks, M); each CTA reduces
 // an 8192-wide chunk (fp32 rows: 8 float4 loads per thread, all in flight)
@@ -439,6 +487,16 @@ extern "C" int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const u
                                  int M, int H, void* stream) {
   if (!x_resid || !ssq || !w || !out) return T2B_ERR_ARG;
   return rms_norm_rows(x_resid, ssq, w, eps, out, M, H, S_(stream));
+}
+
+extern "C" int t2b_residual_norm_input(const float* y, float* x_resid, float* ssq_out, const uint16_t* next_norm_w,
+                                       uint16_t* xw_out, int M, int H, void* stream) {
+  if (!y || !x_resid || !ssq_out) return T2B_ERR_ARG;
+  if ((next_norm_w == nullptr) != (xw_out == nullptr)) return T2B_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(x_resid)) & 15) return T2B_ERR_ALIGN;
+  if (xw_out && ((reinterpret_cast<uintptr_t>(xw_out) | reinterpret_cast<uintptr_t>(next_norm_w)) & 7))
+    return T2B_ERR_ALIGN;
+  return residual_norm_input(y, x_resid, ssq_out, next_norm_w, xw_out, M, H, S_(stream));
 }
 
 extern "C" size_t t2b_argmax_workspace_bytes(int M, int V) {

@@ -1,0 +1,256 @@
+"""Tensor-parallel decode for the largest config (Qwen3-8B on 8 GPUs, one rank per GPU).
+
+The sharding follows the Megatron split the reference's own N-shard operator
+describes for its projections (``W4A16NShardGEMM``,
+``src/models/quantized_qwen3/operators/w4a16_gemm/op.py:336-399``), applied to a
+decoder layer (``model.py:240-327``):
+
+* q/k/v -- column-parallel by head: rank r owns q heads ``[r*nq/tp, (r+1)*nq/tp)``
+  and kv heads ``[r*nkv/tp, ...)``, so QK-norm, RoPE, the KV cache and the
+  attention over it stay on the rank (they are per head);
+* o_proj -- row-parallel: rank r holds the input columns of its q heads and
+  produces a partial ``[B, H]`` that is summed across ranks;
+* gate / up -- column-parallel (``I/tp`` rows each, interleaved in 64-row
+  blocks as on one GPU), SwiGLU local;
+* down -- row-parallel over the ``I/tp`` columns of the rank's gate/up rows;
+* lm_head -- vocab-parallel: each rank scores ``V/tp`` rows, takes its local
+  argmax, and the (value, index) pairs of all ranks are gathered (greedy
+  decoding needs no full logits row on any rank).
+
+Every split falls on a 128-wide quantization group (``H/tp``, ``I/tp`` and
+the head blocks are multiples of 128), so no scale or zero point is split.
+The residual stream, embedding and norms are replicated.  The two row-parallel
+partials per layer meet in an NCCL all-reduce (fp32 sum) on the decode
+stream, followed by ``t2b_residual_norm_input``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .synth import AutoGPTQLinear
+
+
+# ---------------------------------------------------------------------------
+# shard helpers on AutoGPTQ-v1 tensors (qweight [K/8, N], qzeros [G, N/8], scales [G, N])
+# ---------------------------------------------------------------------------
+def shard_out(lin: AutoGPTQLinear, n0: int, n1: int) -> AutoGPTQLinear:
+    """Output rows ``[n0, n1)`` of a linear (column-parallel shard)."""
+    if n0 % 8 or n1 % 8 or not 0 <= n0 < n1 <= lin.out_features:
+        raise ValueError(f"output split [{n0}, {n1}) must be 8-aligned inside [0, {lin.out_features})")
+    return AutoGPTQLinear(lin.qweight[:, n0:n1].contiguous(), lin.qzeros[:, n0 // 8:n1 // 8].contiguous(),
+                          lin.scales[:, n0:n1].contiguous(), lin.in_features, n1 - n0, lin.group_size)
+
+
+def shard_in(lin: AutoGPTQLinear, k0: int, k1: int) -> AutoGPTQLinear:
+    """Input columns ``[k0, k1)`` of a linear (row-parallel shard); group-aligned."""
+    g = lin.group_size
+    if k0 % g or k1 % g or not 0 <= k0 < k1 <= lin.in_features:
+        raise ValueError(f"input split [{k0}, {k1}) must fall on {g}-wide groups inside [0, {lin.in_features})")
+    return AutoGPTQLinear(lin.qweight[k0 // 8:k1 // 8].contiguous(), lin.qzeros[k0 // g:k1 // g].contiguous(),
+                          lin.scales[k0 // g:k1 // g].contiguous(), k1 - k0, lin.out_features, g)
+
+
+def check_tp(cfg, tp: int) -> None:
+    if tp < 1 or cfg.n_kv_groups % tp or cfg.n_heads % tp:
+        raise ValueError(f"tp={tp} must divide the {cfg.n_heads} q and {cfg.n_kv_groups} kv heads")
+    if (cfg.hidden_dim // tp) % 256 or cfg.hidden_dim % tp:
+        raise ValueError(f"intermediate {cfg.hidden_dim} / tp={tp} must be a multiple of 256")
+    if (cfg.n_heads // tp * cfg.head_dim) % 256:
+        raise ValueError("the q columns of a rank must be a multiple of 256 (o_proj K split)")
+    if cfg.vocab_size % tp:
+        raise ValueError(f"vocab {cfg.vocab_size} must divide by tp={tp}")
+
+
+def shard_layer(layer: dict, cfg, tp: int, rank: int) -> dict:
+    """The rank's share of one layer's AutoGPTQ linears; norms are shared."""
+    check_tp(cfg, tp)
+    hd = cfg.head_dim
+    nq, nkv, ib = cfg.n_heads // tp, cfg.n_kv_groups // tp, cfg.hidden_dim // tp
+    q0, kv0, i0 = rank * nq * hd, rank * nkv * hd, rank * ib
+    out = {
+        "q_proj": shard_out(layer["q_proj"], q0, q0 + nq * hd),
+        "k_proj": shard_out(layer["k_proj"], kv0, kv0 + nkv * hd),
+        "v_proj": shard_out(layer["v_proj"], kv0, kv0 + nkv * hd),
+        "o_proj": shard_in(layer["o_proj"], q0, q0 + nq * hd),
+        "gate_proj": shard_out(layer["gate_proj"], i0, i0 + ib),
+        "up_proj": shard_out(layer["up_proj"], i0, i0 + ib),
+        "down_proj": shard_in(layer["down_proj"], i0, i0 + ib),
+    }
+    for k in ("input_layernorm", "post_attention_layernorm", "q_norm", "k_norm"):
+        if k in layer:
+            out[k] = layer[k]
+    return out
+
+
+def local_config(cfg, tp: int):
+    """Shapes one rank computes with (heads, intermediate divided by tp)."""
+    check_tp(cfg, tp)
+    return cfg.scaled(n_heads=cfg.n_heads // tp, n_kv_groups=cfg.n_kv_groups // tp, hidden_dim=cfg.hidden_dim // tp)
+
+
+def vocab_slice(cfg, tp: int, rank: int) -> tuple[int, int]:
+    v = cfg.vocab_size // tp
+    return rank * v, (rank + 1) * v
+
+
+def merge_argmax(vals: torch.Tensor, idx: torch.Tensor, v_per_rank: int) -> torch.Tensor:
+    """Greedy token from per-rank (max, local index) pairs ``[tp, B]``: largest
+    value, ties to the lowest global index (torch.argmax over the full row)."""
+    glob = idx.to(torch.int64) + v_per_rank * torch.arange(vals.shape[0], device=vals.device)[:, None]
+    best = vals.max(dim=0, keepdim=True).values
+    cand = torch.where(vals == best, glob, torch.full_like(glob, torch.iinfo(torch.int64).max))
+    return cand.min(dim=0).values.to(torch.int32)
+
+
+# ---------------------------------------------------------------------------
+# the engine (one rank)
+# ---------------------------------------------------------------------------
+class TPDecodeEngine:
+    """Greedy batch decoder for one tensor-parallel rank.
+
+    ``model`` is the full synthetic model dict (``synth.random_model``); the
+    rank keeps its shard.  ``group`` is an initialised NCCL process group of
+    ``tp`` ranks.  All ``B`` rows run on every rank (replicated residual
+    stream); the collectives are issued on the current stream in eager mode.
+    """
+
+    def __init__(self, cfg, model: dict, batch: int, max_ctx: int, tp: int, rank: int, group=None,
+                 device="cuda"):
+        import torch.distributed as dist
+        from . import _lib
+        from . import weights as W
+        from .engine import load_layer
+        from .rope import rope_angles
+
+        self.dist, self.group, self.tp, self.rank = dist, group, tp, rank
+        self.cfg, self.lcfg = cfg, local_config(cfg, tp)
+        self.B, self.max_ctx, self.device = batch, max_ctx, torch.device(device)
+        if max_ctx % 64:
+            raise ValueError("max_ctx must be a multiple of 64")
+        dev, lc = self.device, self.lcfg
+        self.layers = [load_layer(shard_layer(l, cfg, tp, rank), lc, dev) for l in model["layers"]]
+        self.embed = model["embed"].to(dev, torch.bfloat16).contiguous()
+        lm = model.get("lm_head")
+        full_lm = model["embed"] if lm is None else lm
+        v0, v1 = vocab_slice(cfg, tp, rank)
+        self.v_local = v1 - v0
+        self.lm_head = full_lm[v0:v1].to(dev, torch.bfloat16).contiguous()
+        self.final_norm = model["final_norm"].to(dev, torch.bfloat16).contiguous()
+        self.angles = rope_angles(cfg.head_dim, max_ctx, cfg.rope_base).to(dev)
+        B, H, hd = batch, cfg.emb_dim, cfg.head_dim
+        f32, bf = torch.float32, torch.bfloat16
+        self.x = torch.zeros(B, H, dtype=f32, device=dev)
+        self.y = torch.zeros(B, H, dtype=f32, device=dev)        # row-parallel partial, all-reduced in place
+        self.xw = torch.zeros(B, H, dtype=bf, device=dev)
+        self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
+        self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
+        self.q = torch.zeros(B, lc.q_dim, dtype=bf, device=dev)
+        self.attn = torch.zeros(B, lc.q_dim, dtype=bf, device=dev)
+        self.h = torch.zeros(B, lc.hidden_dim, dtype=bf, device=dev)
+        self.xn = torch.zeros(B, H, dtype=bf, device=dev)
+        self.logits = torch.zeros(B, self.v_local, dtype=f32, device=dev)
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.local_idx = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.next_tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        kv_shape = (B, lc.n_kv_groups, max_ctx, hd)
+        self.k_cache = [torch.zeros(kv_shape, dtype=bf, device=dev) for _ in range(cfg.n_layers)]
+        self.v_cache = [torch.zeros(kv_shape, dtype=bf, device=dev) for _ in range(cfg.n_layers)]
+        L = _lib.load()
+        nq, nkv = lc.n_heads, lc.n_kv_groups
+        sizes = {
+            "qkv": L.t2b_qkv_workspace_bytes(B, H, nq, nkv, hd),
+            "attn": L.t2b_decode_attention_workspace_bytes(B, nq, nkv, hd, max_ctx),
+            "o": L.t2b_w4a16_gemm_workspace_bytes(B, H, lc.q_dim),
+            "ug": L.t2b_upgate_swiglu_workspace_bytes(B, H, lc.hidden_dim),
+            "down": L.t2b_w4a16_gemm_workspace_bytes(B, H, lc.hidden_dim),
+            "argmax": L.t2b_argmax_workspace_bytes(B, self.v_local),
+        }
+        self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
+        self._lib, self._W = _lib, W
+        torch.cuda.synchronize(dev)
+
+    def _ws(self, k):
+        t, n = self.ws[k]
+        return self._lib.ptr(t), n
+
+    def next_norm_weight(self, li: int) -> torch.Tensor:
+        return self.layers[li + 1].input_layernorm if li + 1 < len(self.layers) else self.final_norm
+
+    def _allreduce_residual(self, ssq_out, next_w):
+        lib, p = self._lib, self._lib.ptr
+        self.dist.all_reduce(self.y, group=self.group)
+        lib.check("t2b_residual_norm_input", lib.lib().t2b_residual_norm_input(
+            p(self.y), p(self.x), p(ssq_out), p(next_w), p(self.xw), self.B, self.cfg.emb_dim, lib.stream()))
+
+    def enqueue_layer(self, li: int) -> None:
+        cfg, lc, B = self.cfg, self.lcfg, self.B
+        H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, lc.n_heads, lc.n_kv_groups
+        lib = self._lib
+        L, p, st = lib.lib(), lib.ptr, lib.stream()
+        lw = self.layers[li]
+        lib.check("t2b_qkv_norm_rope_kvwrite", L.t2b_qkv_norm_rope_kvwrite(
+            p(lw.qkv.qw), p(lw.qkv.meta), p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
+            p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
+            p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
+        lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
+            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), B, nq, nkv, hd,
+            self.max_ctx, *self._ws("attn"), st))
+        lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
+            p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[torch.bfloat16], p(self.y),
+            lib.DTYPE[torch.float32], B, H, lc.q_dim, 128, *self._ws("o"), st))
+        self._allreduce_residual(self.ssq_b, lw.post_attention_layernorm)
+        lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
+            p(lw.gate_up.qw), p(lw.gate_up.meta), p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
+            p(self.ssq_a), B, H, lc.hidden_dim, *self._ws("ug"), st))
+        lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
+            p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[torch.bfloat16], p(self.y),
+            lib.DTYPE[torch.float32], B, H, lc.hidden_dim, 128, *self._ws("down"), st))
+        self._allreduce_residual(self.ssq_a, self.next_norm_weight(li))
+
+    def enqueue_step(self) -> None:
+        cfg, B = self.cfg, self.B
+        lib = self._lib
+        L, p, st = lib.lib(), lib.ptr, lib.stream()
+        lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a),
+                                                     p(self.layers[0].input_layernorm), p(self.xw), B, cfg.emb_dim,
+                                                     cfg.vocab_size, st))
+        for li in range(cfg.n_layers):
+            self.enqueue_layer(li)
+        lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
+                                                           cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
+        torch.mm(self.xn, self.lm_head.t(), out_dtype=torch.float32, out=self.logits)
+        lib.check("t2b_argmax_rows", L.t2b_argmax_rows(p(self.logits), 2, B, self.v_local, self.v_local,
+                                                       p(self.local_idx), *self._ws("argmax"), st))
+        val = self.logits.gather(1, self.local_idx.long()[:, None])[:, 0].contiguous()
+        vals = [torch.empty_like(val) for _ in range(self.tp)]
+        idxs = [torch.empty_like(self.local_idx) for _ in range(self.tp)]
+        self.dist.all_gather(vals, val, group=self.group)
+        self.dist.all_gather(idxs, self.local_idx, group=self.group)
+        self.next_tokens.copy_(merge_argmax(torch.stack(vals), torch.stack(idxs), self.v_local))
+
+    def kernels_per_step(self) -> int:
+        """Launches of this library's kernels per step (lm_head GEMM, NCCL and gathers excluded)."""
+        return 1 + 7 * self.cfg.n_layers + 2
+
+    def run_step(self) -> None:
+        self.enqueue_step()
+
+    def advance(self) -> None:
+        self.enqueue_step()
+        self.tokens.copy_(self.next_tokens)
+        self.pos.add_(1)
+
+    def prefill(self, prompts: torch.Tensor) -> None:
+        P = prompts.shape[1]
+        prompts = prompts.to(self.device, torch.int32)
+        for t in range(P):
+            self.tokens.copy_(prompts[:, t])
+            self.pos.fill_(t)
+            self.run_step()
+        self.tokens.copy_(self.next_tokens)
+        self.pos.fill_(P)
+
+    def release(self) -> None:
+        pass
