@@ -455,8 +455,8 @@ def run_t2b(args, cfg):
 def run_tp(args, cfg):
     """Config 4: one model split over the torchrun ranks (tensor parallel), B rows
     in total, the KV cache pre-filled with N(0,1) bf16 to --ctx positions; K timed
-    decode steps (eager: the two NCCL all-reduces per layer run on the decode
-    stream between the fused kernels)."""
+    decode steps (one CUDA graph per step, the two NCCL all-reduces per layer
+    captured between the fused kernels)."""
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -473,7 +473,7 @@ def run_tp(args, cfg):
     B, C = args.batch, args.ctx
     max_ctx = ((C + args.warmup + args.steps + 1 + 63) // 64) * 64
     model = synth.random_model(cfg, seed=args.seed, device="cuda")
-    eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank)
+    eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank, use_graph=True)
     del model
     torch.cuda.empty_cache()
     g = torch.Generator(device="cuda").manual_seed(args.seed * 1000 + 7 + rank)
@@ -528,6 +528,7 @@ def run_tp(args, cfg):
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    eng.release()   # graphs holding NCCL calls go before the process group
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

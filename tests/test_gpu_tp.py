@@ -34,13 +34,17 @@ def _rank(rank, world, port, batch, out_q):
     try:
         model = synth.random_model(CFG, seed=21)
         prompts = torch.randint(0, CFG.vocab_size, (batch, 6), generator=torch.Generator().manual_seed(22))
-        eng = TPDecodeEngine(CFG, model, batch=batch, max_ctx=64, tp=world, rank=rank)
-        eng.prefill(prompts)
-        toks = [eng.next_tokens.cpu().clone()]
-        for _ in range(3):
-            eng.advance()
-            toks.append(eng.next_tokens.cpu().clone())
-        res = {"tokens": torch.stack(toks, 1), "x": eng.x.cpu().clone()}
+        res = {}
+        for mode in ("eager", "graph"):
+            eng = TPDecodeEngine(CFG, model, batch=batch, max_ctx=64, tp=world, rank=rank, use_graph=mode == "graph")
+            eng.prefill(prompts)
+            toks = [eng.next_tokens.cpu().clone()]
+            for _ in range(3):
+                eng.advance()
+                toks.append(eng.next_tokens.cpu().clone())
+            res[mode] = {"tokens": torch.stack(toks, 1), "x": eng.x.cpu().clone()}
+            eng.release()
+        res.update(res["eager"])
         if rank == 0:
             ref = DecodeEngine(CFG, model, batch=batch, max_ctx=64, use_graph=False)
             ref.prefill(prompts)
@@ -73,5 +77,7 @@ def test_tp2_engine_matches_single_gpu(batch):
     assert torch.equal(r0["tokens"], r1["tokens"])            # replicated greedy picks
     assert torch.equal(r0["x"], r1["x"])                      # replicated residual stream
     assert torch.equal(r0["tokens"], r0["ref_tokens"])
+    assert torch.equal(r0["graph"]["tokens"], r0["tokens"])    # graph replay == eager
+    assert torch.equal(r0["graph"]["x"], r0["x"])
     err = (r0["x"] - r0["ref_x"]).abs().max() / r0["ref_x"].abs().max()
     assert err <= 1e-2

@@ -111,12 +111,15 @@ class TPDecodeEngine:
 
     ``model`` is the full synthetic model dict (``synth.random_model``); the
     rank keeps its shard.  ``group`` is an initialised NCCL process group of
-    ``tp`` ranks.  All ``B`` rows run on every rank (replicated residual
-    stream); the collectives are issued on the current stream in eager mode.
+    ``tp`` ranks (the default group when None).  All ``B`` rows run on every
+    rank (replicated residual stream).  With ``use_graph`` the step -- NCCL
+    all-reduces and gathers included -- is captured once in a CUDA graph
+    (every rank captures the same sequence); ``release()`` drops the graphs,
+    which must happen before the process group is destroyed.
     """
 
     def __init__(self, cfg, model: dict, batch: int, max_ctx: int, tp: int, rank: int, group=None,
-                 device="cuda"):
+                 device="cuda", use_graph: bool = False):
         import torch.distributed as dist
         from . import _lib
         from . import weights as W
@@ -169,6 +172,9 @@ class TPDecodeEngine:
         }
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
         self._lib, self._W = _lib, W
+        self.use_graph, self.graph, self._step_graph = use_graph, None, None
+        self.vals = [torch.zeros(B, dtype=f32, device=dev) for _ in range(tp)]
+        self.idxs = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(tp)]
         torch.cuda.synchronize(dev)
 
     def _ws(self, k):
@@ -224,23 +230,50 @@ class TPDecodeEngine:
         lib.check("t2b_argmax_rows", L.t2b_argmax_rows(p(self.logits), 2, B, self.v_local, self.v_local,
                                                        p(self.local_idx), *self._ws("argmax"), st))
         val = self.logits.gather(1, self.local_idx.long()[:, None])[:, 0].contiguous()
-        vals = [torch.empty_like(val) for _ in range(self.tp)]
-        idxs = [torch.empty_like(self.local_idx) for _ in range(self.tp)]
-        self.dist.all_gather(vals, val, group=self.group)
-        self.dist.all_gather(idxs, self.local_idx, group=self.group)
-        self.next_tokens.copy_(merge_argmax(torch.stack(vals), torch.stack(idxs), self.v_local))
+        self.dist.all_gather(self.vals, val, group=self.group)
+        self.dist.all_gather(self.idxs, self.local_idx, group=self.group)
+        self.next_tokens.copy_(merge_argmax(torch.stack(self.vals), torch.stack(self.idxs), self.v_local))
 
     def kernels_per_step(self) -> int:
         """Launches of this library's kernels per step (lm_head GEMM, NCCL and gathers excluded)."""
         return 1 + 7 * self.cfg.n_layers + 2
 
+    def capture(self) -> None:
+        """Capture ``step`` and ``step + (tokens <- next, pos += 1)`` as CUDA graphs."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):   # NCCL communicators, cuBLAS and lazy init outside the capture
+                self.enqueue_step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.enqueue_step()
+        self._step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._step_graph):
+            self.enqueue_step()
+            self.tokens.copy_(self.next_tokens)
+            self.pos.add_(1)
+        torch.cuda.synchronize(self.device)
+
     def run_step(self) -> None:
-        self.enqueue_step()
+        if self.use_graph:
+            if self.graph is None:
+                self.capture()
+            self.graph.replay()
+        else:
+            self.enqueue_step()
 
     def advance(self) -> None:
-        self.enqueue_step()
-        self.tokens.copy_(self.next_tokens)
-        self.pos.add_(1)
+        if self.use_graph:
+            if self._step_graph is None:
+                self.capture()
+            self._step_graph.replay()
+        else:
+            self.enqueue_step()
+            self.tokens.copy_(self.next_tokens)
+            self.pos.add_(1)
 
     def prefill(self, prompts: torch.Tensor) -> None:
         P = prompts.shape[1]
@@ -253,4 +286,7 @@ class TPDecodeEngine:
         self.pos.fill_(P)
 
     def release(self) -> None:
-        pass
+        """Drop the captured graphs (before destroying the process group)."""
+        torch.cuda.synchronize(self.device)
+        self.graph = None
+        self._step_graph = None
