@@ -18,10 +18,14 @@
  * must be complete -- synchronize the stream -- before the first call that
  * reads them.
  *
- * Weight layout "T2B" (T2B_WFMT_T2B) for an [N, K] linear, group 128:
- *   qw   uint8  [N][K/2]  byte k/2 of row n: low nibble q[n,k even], high q[n,k odd]
- *                          (unsigned AutoGPTQ nibbles, 0..15)
- *   meta uint32 [N][K/128] bits 0-15 fp16 scale, bits 16-20 zero point (1..16)
+ * Weight layout "T2B" (T2B_WFMT_T2B) for an [N, K] linear, group 128, built
+ * by t2b_repack_autogptq (N % 128 == 0, K % 256 == 0):
+ *   qw   N*K/2 bytes of 8 KB blocks, block (n/128, k/128) at ((n/128)*(K/128) + k/128) * 8192;
+ *        inside it, the 16 bytes of row n%128 for k 32p..32p+31 sit at p*2048 + (n%128)*16,
+ *        as 4 words of 8 unsigned nibbles (0..15) with the even k first: nibble
+ *        slot t < 4 holds k 8j+2t, slot t >= 4 holds k 8j+2(t-4)+1 (word j)
+ *   meta N*K/128 uint32 in 128-entry blocks in the same order: bits 0-15 fp16
+ *        scale, bits 16-20 zero point (1..16)
  *   W[n,k] = (q[n,k] - zero[n,k/128]) * scale[n,k/128]
  * Weight layout "QPARAM" (T2B_WFMT_QPARAM) is the reference's runtime row
  * format (src/models/quantized_qwen3/packed_format.py:195-205): row n is
