@@ -296,7 +296,9 @@ def kernel_profile(eng, steps):
             rec("down_residual", lambda: L.t2b_down_residual(
                 p(lw.down.qw), p(lw.down.meta), p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(li)), p(eng.xw), B, H, cfg.hidden_dim,
                 *eng._ws("down"), st))
-        rec("lm_head(cublas)", lambda: torch.mm(eng.xn, eng.lm_head.t(), out_dtype=torch.float32, out=eng.logits))
+        rec("lm_head_argmax", lambda: L.t2b_lm_head_argmax(
+            p(eng.xn), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
+            *eng._ws("lm"), st))
     torch.cuda.synchronize()
     for name, a, b in evs:
         times[name] += a.elapsed_time(b)
@@ -319,7 +321,7 @@ def run_t2b(args, cfg):
     B, P = args.batch, args.prompt
     max_ctx = ((P + args.warmup + args.steps + 1 + 63) // 64) * 64
     model = synth.random_model(cfg, seed=args.seed, device="cuda")
-    eng = DecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, use_graph=True)
+    eng = DecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, use_graph=True, keep_logits=False)
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=g)
     eng.prefill(prompts)
@@ -401,7 +403,7 @@ def run_t2b(args, cfg):
             "oproj_residual": l0.o_proj.nbytes_algorithmic + B * cfg.q_dim * 2 + 2 * B * cfg.emb_dim * 4,
             "upgate_swiglu": l0.gate_up.nbytes_algorithmic + B * cfg.emb_dim * 4 + B * cfg.hidden_dim * 2,
             "down_residual": l0.down.nbytes_algorithmic + B * cfg.hidden_dim * 2 + 2 * B * cfg.emb_dim * 4,
-            "lm_head(cublas)": eng.lm_head.numel() * 2 + B * cfg.vocab_size * 4,
+            "lm_head_argmax": eng.lm_head.numel() * 2 + B * cfg.emb_dim * 2 + B * 4,
         }
         dur_ms = prof[dom][0]
         achieved = kernel_bytes[dom] / (dur_ms * 1e-3) / 1e9

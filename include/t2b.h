@@ -235,6 +235,20 @@ T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint
 T2B_API int t2b_residual_norm_input(const float* y, float* x_resid, float* ssq_out, const uint16_t* next_norm_w,
                                     uint16_t* xw_out, int M, int H, void* stream);
 
+/*
+ * Greedy lm_head: idx[m] = argmax_v (xn[m] . lm_head[v]) over V rows of a bf16
+ * [V][H] table (tied embedding or untied head), fp32 accumulation; ties to
+ * the lowest index (torch.argmax).  max_logit [M] (may be NULL) receives the
+ * maximum, logits fp32 [M][V] (may be NULL) the full rows.  xn bf16 [M][H],
+ * M <= 256, H % 64 == 0.  Workspace: t2b_lm_head_argmax_workspace_bytes(M),
+ * zeroed once (re-armed by the kernel).  Replaces the lm_head DenseLinear +
+ * host argmax (model.py:409-420, 477; qwen_npu.py:321).
+ */
+T2B_API size_t t2b_lm_head_argmax_workspace_bytes(int M);
+T2B_API int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* lm_head, int M, int H, int V, int32_t* idx,
+                               float* max_logit, float* logits, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
 T2B_API size_t t2b_argmax_workspace_bytes(int M, int V);
 T2B_API int t2b_argmax_rows(const void* logits, int dtype, int M, int V, int ld, int32_t* idx, void* workspace,
                     size_t workspace_bytes, void* stream);

@@ -282,3 +282,34 @@ def test_argmax_rows_vs_torch(M, V, dtype):
         _lib.call("t2b_argmax_rows", _lib.ptr(lg), code, M, V, V, _lib.ptr(out), _lib.ptr(ws), n, _lib.stream())
         torch.cuda.synchronize()
         assert torch.equal(out.cpu().long(), torch.argmax(logits.float(), dim=1))
+
+
+@pytest.mark.parametrize("M,H,V", [
+    (1, 1024, 151936),     # Qwen3 tied head, batch 1
+    (64, 1024, 151936),    # bench batch
+    (3, 2048, 128256),     # Llama
+    (17, 4096, 18992),     # Qwen3-8B vocab shard at TP8: last 128-row tile partly outside
+    (200, 1024, 5000),
+])
+def test_lm_head_argmax_vs_torch(M, H, V):
+    g = torch.Generator().manual_seed(M * 7 + V)
+    xn = torch.randn(M, H, generator=g).to(torch.bfloat16).cuda()
+    lm = (torch.randn(V, H, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    ref = xn.float() @ lm.float().t()
+    L = _lib.lib()
+    n = L.t2b_lm_head_argmax_workspace_bytes(M)
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    idx = torch.empty(M, dtype=torch.int32, device="cuda")
+    mx = torch.empty(M, dtype=torch.float32, device="cuda")
+    logits = torch.empty(M, V, dtype=torch.float32, device="cuda")
+    for with_logits in (True, False):       # the keys and ticket re-arm between calls
+        _lib.call("t2b_lm_head_argmax", _lib.ptr(xn), _lib.ptr(lm), M, H, V, _lib.ptr(idx), _lib.ptr(mx),
+                  _lib.ptr(logits) if with_logits else None, _lib.ptr(ws), n, _lib.stream())
+        torch.cuda.synchronize()
+        if with_logits:
+            assert max_abs(logits, ref) <= 1e-3 * ref.abs().max().item()
+            assert torch.equal(idx.long(), logits.argmax(dim=1))       # exactly the kernel's own logits
+        # against the fp32 reference: the picked logit is the maximum up to rounding
+        picked = ref.gather(1, idx.long()[:, None])[:, 0]
+        assert torch.all(picked >= ref.max(dim=1).values - 1e-3)
+        assert max_abs(mx, picked) <= 1e-3

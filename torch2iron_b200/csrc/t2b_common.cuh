@@ -142,6 +142,16 @@ T2B_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
       : "memory");
 }
 
+// 2-D tiled TMA load of one box at element coordinates (x, y); no multicast.
+// x * element size must be a multiple of 16 bytes.
+T2B_DEV void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 3-D tiled TMA load of one box at element coordinates (x, y, z) of the
 // tensor map `tmap` (a __grid_constant__ kernel parameter); no multicast.
 // x * element size must be a multiple of 16 bytes.

@@ -13,8 +13,8 @@ as 5 fused launches per layer:
       upgate_swiglu                 RMSNorm, [gate|up] GEMV, silu(g)*u
       down_residual                 x += down(h)          (+ sum of squares)
     rms_norm_rows                   final norm -> bf16
-    lm_head                         bf16 logits GEMM (fp32 out)
-    argmax_rows                     greedy token
+    lm_head_argmax                  bf16 lm_head GEMM with the greedy argmax fused in
+                                    (logits written only with keep_logits)
 
 The whole step is captured once in a CUDA graph and replayed; the kernels
 chain with programmatic dependent launch.  The residual stream is fp32; the
@@ -80,12 +80,12 @@ class DecodeEngine:
     """
 
     def __init__(self, cfg: QuantizedQwenConfig, model: dict, batch: int, max_ctx: int, device="cuda",
-                 use_graph: bool = True):
+                 use_graph: bool = True, keep_logits: bool = True):
         cfg.validate()
         if max_ctx % 64:
             raise ValueError("max_ctx must be a multiple of 64")
         self.cfg, self.B, self.max_ctx, self.device = cfg, batch, max_ctx, torch.device(device)
-        self.use_graph = use_graph
+        self.use_graph, self.keep_logits = use_graph, keep_logits
         dev = self.device
         self.layers = [load_layer(l, cfg, dev) for l in model["layers"]]
         if len(self.layers) != cfg.n_layers:
@@ -122,7 +122,7 @@ class DecodeEngine:
             "o": L.t2b_oproj_residual_workspace_bytes(B, H, cfg.q_dim),
             "ug": L.t2b_upgate_swiglu_workspace_bytes(B, H, cfg.hidden_dim),
             "down": L.t2b_down_residual_workspace_bytes(B, H, cfg.hidden_dim),
-            "argmax": L.t2b_argmax_workspace_bytes(B, cfg.vocab_size),
+            "lm": L.t2b_lm_head_argmax_workspace_bytes(B),
         }
         # one workspace per op kind: consecutive ops never share counters
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
@@ -192,9 +192,9 @@ class DecodeEngine:
             self.enqueue_layer(li, st)
         _lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
                                                             cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
-        torch.mm(self.xn, self.lm_head.t(), out_dtype=torch.float32, out=self.logits)
-        _lib.check("t2b_argmax_rows", L.t2b_argmax_rows(p(self.logits), 2, B, cfg.vocab_size, cfg.vocab_size,
-                                                        p(self.next_tokens), *self._ws("argmax"), st))
+        _lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
+            p(self.xn), p(self.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(self.next_tokens), None,
+            p(self.logits) if self.keep_logits else None, *self._ws("lm"), st))
 
     def set_hidden(self, x: torch.Tensor) -> None:
         """Load a residual-stream state (fp32 [B, H]) and its split norm input for layer 0."""
@@ -203,7 +203,7 @@ class DecodeEngine:
         self.xw.copy_((self.x * self.layers[0].input_layernorm.float()).to(torch.bfloat16))
 
     def kernels_per_step(self) -> int:
-        """Launches of this library's kernels per step (the lm_head GEMM is cuBLAS)."""
+        """Launches of this library's kernels per step (embed, 5 per layer, final norm, lm_head + argmax)."""
         return 1 + 5 * self.cfg.n_layers + 1 + 1
 
     # -- graph capture -------------------------------------------------------

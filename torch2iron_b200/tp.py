@@ -152,7 +152,7 @@ class TPDecodeEngine:
         self.attn = torch.zeros(B, lc.q_dim, dtype=bf, device=dev)
         self.h = torch.zeros(B, lc.hidden_dim, dtype=bf, device=dev)
         self.xn = torch.zeros(B, H, dtype=bf, device=dev)
-        self.logits = torch.zeros(B, self.v_local, dtype=f32, device=dev)
+        self.local_max = torch.zeros(B, dtype=f32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.local_idx = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -168,7 +168,7 @@ class TPDecodeEngine:
             "o": L.t2b_w4a16_gemm_workspace_bytes(B, H, lc.q_dim),
             "ug": L.t2b_upgate_swiglu_workspace_bytes(B, H, lc.hidden_dim),
             "down": L.t2b_w4a16_gemm_workspace_bytes(B, H, lc.hidden_dim),
-            "argmax": L.t2b_argmax_workspace_bytes(B, self.v_local),
+            "lm": L.t2b_lm_head_argmax_workspace_bytes(B),
         }
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
         self._lib, self._W = _lib, W
@@ -226,16 +226,15 @@ class TPDecodeEngine:
             self.enqueue_layer(li)
         lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
                                                            cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
-        torch.mm(self.xn, self.lm_head.t(), out_dtype=torch.float32, out=self.logits)
-        lib.check("t2b_argmax_rows", L.t2b_argmax_rows(p(self.logits), 2, B, self.v_local, self.v_local,
-                                                       p(self.local_idx), *self._ws("argmax"), st))
-        val = self.logits.gather(1, self.local_idx.long()[:, None])[:, 0].contiguous()
-        self.dist.all_gather(self.vals, val, group=self.group)
+        lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
+            p(self.xn), p(self.lm_head), B, cfg.emb_dim, self.v_local, p(self.local_idx), p(self.local_max), None,
+            *self._ws("lm"), st))
+        self.dist.all_gather(self.vals, self.local_max, group=self.group)
         self.dist.all_gather(self.idxs, self.local_idx, group=self.group)
         self.next_tokens.copy_(merge_argmax(torch.stack(self.vals), torch.stack(self.idxs), self.v_local))
 
     def kernels_per_step(self) -> int:
-        """Launches of this library's kernels per step (lm_head GEMM, NCCL and gathers excluded)."""
+        """Launches of this library's kernels per step (NCCL collectives and the final merge excluded)."""
         return 1 + 7 * self.cfg.n_layers + 2
 
     def capture(self) -> None:
