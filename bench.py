@@ -170,7 +170,8 @@ def arm_config(args, world):
     """The workload description both arms report (identical for the reference arm)."""
     c0 = args.prompt + args.warmup + 1
     c1 = c0 + args.steps - 1
-    return {"workload": f"config2 {args.model} greedy decode, {args.batch} rows/GPU, prompt {args.prompt}, "
+    cfg_no = {"qwen3-0.6b": 2, "llama-3.2-1b": 3, "qwen3-8b": 4}.get(args.model, 2)   # BASELINE.json configs[n]
+    return {"workload": f"config{cfg_no} {args.model} greedy decode, {args.batch} rows/GPU, prompt {args.prompt}, "
                         f"timed ctx {c0}..{c1}",
             "model": args.model, "global_batch": world * args.batch, "seq_len": c1, "parallelism": f"dp{world}"}
 

@@ -27,6 +27,8 @@
 // mbarrier wait is time-bounded; on timeout the CTA records T2B_ERR_TIMEOUT,
 // frees its TMEM, still passes its cluster barriers, and skips its epilogue.
 
+#include <algorithm>
+
 #include "linear_common.cuh"
 #include "launch.cuh"
 #include "tmap.cuh"
@@ -446,6 +448,29 @@ static TcPlan tc_plan(int M, int N, int K) {
   }
   pl.ok = pl.S > 0 && N % TILE_N == 0;
   if (!pl.ok) return pl;
+  // A grid of more than one wave (resident CTAs: shared memory and TMEM, at
+  // most 2 per SM) takes more groups per CTA where they fit: fewer, longer CTAs.
+  {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+    const int mb = (M + pl.BP - 1) / pl.BP;
+    auto waves = [&](int s_) {
+      const long bytes = TcLayout(pl.BP, s_, G / s_).bytes;
+      int per_sm = (int)((228L * 1024) / (bytes + 1024));
+      per_sm = std::min(per_sm, (int)(512u / tc_tmem_cols(pl.BP, s_)));
+      per_sm = std::max(1, std::min(per_sm, 2));
+      const long ctas = (long)tiles * (G / s_) * mb;
+      return (ctas + (long)sms * per_sm - 1) / ((long)sms * per_sm);
+    };
+    int best = pl.S;
+    if (waves(best) > 1)
+      for (int s_ = pl.S + 1; s_ <= G; ++s_) {
+        if (G % s_ || G / s_ > 8 || G / s_ > pl.BP || !fits(pl.BP, s_)) continue;
+        if (waves(s_) < waves(best)) best = s_;
+      }
+    pl.S = best;
+  }
   pl.KS = G / pl.S;
   pl.mblocks = (M + pl.BP - 1) / pl.BP;
   pl.smem = (size_t)TcLayout(pl.BP, pl.S, pl.KS).bytes;
