@@ -491,14 +491,26 @@ def run_tp(args, cfg):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    # a step far slower than the byte floor (e.g. a collective stalling) would make
+    # the timed loop run for minutes on every GPU: time one step first and cut
+    # the loop to ~10 s (every rank takes the same decision: max over ranks)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    eng.advance()
+    p1.record()
+    torch.cuda.synchronize()
+    probe = torch.tensor([p0.elapsed_time(p1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(probe, op=dist.ReduceOp.MAX)
+    steps = max(1, min(args.steps, int(10_000 / max(float(probe.item()), 1e-3))))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             eng.advance()
         e1.record()
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    ms = e0.elapsed_time(e1) * args.steps / steps
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -526,7 +538,8 @@ def run_tp(args, cfg):
                        "l2": f"working set > L2 every step (~{gpu_bytes / 1e9:.2f} GB/step/GPU)"},
             "hbm": {"algorithmic_bytes_per_step_per_gpu": int(gpu_bytes), "achieved_gbs_per_gpu": round(per_gpu_gbs, 1),
                     "frac_of_peak": round(per_gpu_gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_kind},
-            "gpu_launches": eng.kernels_per_step() * args.steps,
+            "gpu_launches": eng.kernels_per_step() * steps,
+            "timed_steps": steps,
             "collectives_per_step": 2 * cfg.n_layers + 2,
             "clocks": clocks.summary(),
         }
