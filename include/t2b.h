@@ -72,6 +72,20 @@ extern "C" {
 T2B_API int t2b_version(void);
 T2B_API const char* t2b_status_string(int status);
 
+/*
+ * Device status word (int32, device memory, zeroed by the caller): every
+ * kernel launched after this call records T2B_ERR_TIMEOUT there when one of
+ * its time-bounded waits (0.5 s) gives up -- the kernel then skips its output
+ * instead of hanging.  One word per process; NULL stops recording.
+ */
+T2B_API int t2b_set_error_word(int32_t* word);
+
+/*
+ * Self-test of that path: a kernel waits (at most limit_us) on a barrier no
+ * copy completes and records T2B_ERR_TIMEOUT in `word`; the stream stays usable.
+ */
+T2B_API int t2b_selftest_bounded_wait(int32_t* word, int limit_us, void* stream);
+
 /* Zero a workspace (cudaMemsetAsync) before its first use. */
 T2B_API int t2b_workspace_init(void* workspace, size_t bytes, void* stream);
 

@@ -313,3 +313,22 @@ def test_lm_head_argmax_vs_torch(M, H, V):
         picked = ref.gather(1, idx.long()[:, None])[:, 0]
         assert torch.all(picked >= ref.max(dim=1).values - 1e-3)
         assert max_abs(mx, picked) <= 1e-3
+
+
+def test_bounded_wait_selftest_records_timeout_and_stream_stays_usable():
+    """A device wait that nothing completes gives up after its limit, records
+    T2B_ERR_TIMEOUT in the status word, and the next kernels run normally."""
+    word = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.call("t2b_selftest_bounded_wait", _lib.ptr(word), 2000, _lib.stream())
+    torch.cuda.synchronize()
+    assert int(word.item()) == 4          # T2B_ERR_TIMEOUT
+    test_argmax_rows_vs_torch(2, 5000, torch.float32)
+
+
+def test_status_word_stays_clear_over_decode_steps():
+    cfg = SMALL.scaled(n_layers=2)
+    model = synth.random_model(cfg, seed=31)
+    eng = DecodeEngine(cfg, model, batch=4, max_ctx=64, use_graph=True)
+    prompts = torch.randint(0, cfg.vocab_size, (4, 5), generator=torch.Generator().manual_seed(32))
+    eng.generate(prompts, 4)              # raises if any kernel recorded a timeout
+    assert int(eng.err.item()) == 0

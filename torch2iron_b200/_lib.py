@@ -48,6 +48,8 @@ SIGNATURES = {
     "t2b_down_residual": (I, [P, P, P, P, P, P, P, I, I, I, P, Z, P]),
     "t2b_embed_rows": (I, [P, P, P, P, P, P, I, I, I, P]),
     "t2b_rms_norm_rows": (I, [P, P, P, F, P, I, I, P]),
+    "t2b_set_error_word": (I, [P]),
+    "t2b_selftest_bounded_wait": (I, [P, I, P]),
     "t2b_residual_norm_input": (I, [P, P, P, P, P, I, I, P]),
     "t2b_lm_head_argmax_workspace_bytes": (Z, [I]),
     "t2b_lm_head_argmax": (I, [P, P, I, I, I, P, P, P, P, Z, P]),

@@ -152,6 +152,22 @@ __global__ void __launch_bounds__(256) residual_norm_input_kernel(const float* _
   }
 }
 
+static int* g_error_word = nullptr;
+int* error_word() { return g_error_word; }
+
+// Exercises the bounded-wait path end to end without a fault: one thread arms
+// an mbarrier for bytes no copy will deliver (nothing is issued, so nothing
+// can land after the kernel ends), waits for at most limit_ns, and the
+// timeout is recorded in `word` like any kernel's would be.
+__global__ void selftest_bounded_wait_kernel(int* word, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  mbar_arrive_expect_tx(&bar, 16);
+  mbar_wait_bounded(&bar, 0, word, limit_ns);
+}
+
 int residual_norm_input(const float* y, float* x, float* ssq, const uint16_t* w, uint16_t* xw, int M, int H,
                         cudaStream_t st) {
   if (M < 1 || H < 4 || H % 4) return T2B_ERR_SHAPE;
@@ -487,6 +503,17 @@ extern "C" int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const u
                                  int M, int H, void* stream) {
   if (!x_resid || !ssq || !w || !out) return T2B_ERR_ARG;
   return rms_norm_rows(x_resid, ssq, w, eps, out, M, H, S_(stream));
+}
+
+extern "C" int t2b_set_error_word(int32_t* word) {
+  g_error_word = word;
+  return T2B_OK;
+}
+
+extern "C" int t2b_selftest_bounded_wait(int32_t* word, int limit_us, void* stream) {
+  if (!word || limit_us < 1 || limit_us > 1000000) return T2B_ERR_ARG;
+  selftest_bounded_wait_kernel<<<1, 32, 0, S_(stream)>>>(word, 1000ull * (unsigned long long)limit_us);
+  return cudaGetLastError() == cudaSuccess ? T2B_OK : T2B_ERR_LAUNCH;
 }
 
 extern "C" int t2b_residual_norm_input(const float* y, float* x_resid, float* ssq_out, const uint16_t* next_norm_w,

@@ -370,6 +370,7 @@ size_t linear_workspace_bytes(int M, int N, int K) {
 }
 
 int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st) {
+  p.err = error_word();
   if (p.M < 1 || p.N <= 0 || p.K <= 0) return T2B_ERR_SHAPE;
   if (p.N % TILE_N || p.K % 256) return T2B_ERR_SHAPE;
   p.G = p.K / GROUP;

@@ -126,6 +126,9 @@ class DecodeEngine:
         }
         # one workspace per op kind: consecutive ops never share counters
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
+        # device status word: kernels record a timed-out wait here (t2b_set_error_word)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.check("t2b_set_error_word", L.t2b_set_error_word(_lib.ptr(self.err)))
         torch.cuda.synchronize(dev)   # repacked weights complete before any PDL launch reads them
         self.graph = None
         self._step_graph = None
@@ -245,13 +248,22 @@ class DecodeEngine:
             self.tokens.copy_(self.next_tokens)
             self.pos.add_(1)
 
+    def check_device_errors(self) -> None:
+        """Raise (and clear) the status a kernel recorded for a timed-out device wait."""
+        code = int(self.err.item())
+        if code:
+            self.err.zero_()
+            raise _lib.T2BError("a decode-step kernel (device status word)", code)
+
     # -- host-facing API (the reference runner's decode_step, qwen_npu.py:166-236) --
     def decode_step(self, tokens, positions) -> torch.Tensor:
         """tokens / positions: host sequences of length B -> next greedy tokens (host int32 [B])."""
         self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32), non_blocking=True)
         self.pos.copy_(torch.as_tensor(positions, dtype=torch.int32), non_blocking=True)
         self.run_step()
-        return self.next_tokens.cpu()
+        out = self.next_tokens.cpu()
+        self.check_device_errors()
+        return out
 
     def prefill(self, prompts: torch.Tensor) -> None:
         """Fill the KV caches by stepping through ``prompts [B, P]`` (teacher forcing).
@@ -275,8 +287,20 @@ class DecodeEngine:
         for _ in range(new_tokens - 1):
             self.advance()
             out.append(self.next_tokens.clone())
+        self.check_device_errors()
         return torch.stack(out, dim=1)
 
     def release(self) -> None:
         self.graph = None
         self._step_graph = None
+        self._drop_error_word()
+
+    def _drop_error_word(self) -> None:
+        """Stop kernels writing to this engine's status word (it is about to be freed)."""
+        try:
+            _lib.load().t2b_set_error_word(None)
+        except Exception:
+            pass
+
+    def __del__(self):
+        self._drop_error_word()

@@ -172,6 +172,8 @@ class TPDecodeEngine:
         }
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
         self._lib, self._W = _lib, W
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.check("t2b_set_error_word", L.t2b_set_error_word(_lib.ptr(self.err)))
         self.use_graph, self.graph, self._step_graph = use_graph, None, None
         self.vals = [torch.zeros(B, dtype=f32, device=dev) for _ in range(tp)]
         self.idxs = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(tp)]
@@ -289,3 +291,4 @@ class TPDecodeEngine:
         torch.cuda.synchronize(self.device)
         self.graph = None
         self._step_graph = None
+        self._lib.load().t2b_set_error_word(None)
