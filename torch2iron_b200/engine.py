@@ -188,6 +188,7 @@ class DecodeEngine:
         L = _lib.lib()
         st = _lib.stream()
         p = _lib.ptr
+        L.t2b_set_error_word(p(self.err))   # this engine's word for every launch below (engines may coexist)
         _lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a),
                                                       p(self.layers[0].input_layernorm), p(self.xw), B,
                                                       cfg.emb_dim, cfg.vocab_size, st))

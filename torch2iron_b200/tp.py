@@ -221,6 +221,7 @@ class TPDecodeEngine:
         cfg, B = self.cfg, self.B
         lib = self._lib
         L, p, st = lib.lib(), lib.ptr, lib.stream()
+        L.t2b_set_error_word(p(self.err))
         lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a),
                                                      p(self.layers[0].input_layernorm), p(self.xw), B, cfg.emb_dim,
                                                      cfg.vocab_size, st))
