@@ -1,0 +1,47 @@
+"""bench.py's JSON contract on the host (no GPU): the reference arm prints one
+line with every key the driver reads, and both arms describe the workload with
+the same `config`."""
+
+import argparse
+import io
+import json
+from contextlib import redirect_stdout
+
+import bench
+from torch2iron_b200.config import QuantizedQwenConfig
+
+TINY = QuantizedQwenConfig(vocab_size=512, emb_dim=256, n_layers=1, n_heads=4, n_kv_groups=2, head_dim=64,
+                           hidden_dim=512, rms_norm_eps=1e-6, rope_base=1e6)
+
+
+def _args(**kw):
+    a = dict(gpus=1, steps=2, warmup=3, impl="reference", batch=2, prompt=8, model="qwen3-0.6b", seed=0,
+             cpu_sample_steps=1, no_cpu_baseline=False, no_gemv=True, tp=0, ctx=4096)
+    a.update(kw)
+    return argparse.Namespace(**a)
+
+
+def test_reference_arm_line_has_the_contract_keys():
+    out = io.StringIO()
+    with redirect_stdout(out):
+        bench.run_reference(_args(), TINY)
+    line = json.loads(out.getvalue().strip().splitlines()[-1])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
+        assert k in line, k
+    assert line["impl"] == "reference" and line["value"] > 0 and line["higher_is_better"] is True
+    assert line["metric"] == bench.METRIC and line["unit"] == "tokens/s"
+    assert {"value", "unit", "cores", "kind", "sample"} <= set(line["cpu_baseline"])
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_both_arms_share_the_workload_description():
+    a = _args()
+    ref_cfg = bench.arm_config(a, a.gpus)
+    assert ref_cfg["workload"].startswith("config2 qwen3-0.6b greedy decode")
+    assert ref_cfg["global_batch"] == a.batch and ref_cfg["parallelism"] == "dp1"
+    assert ref_cfg["seq_len"] == a.prompt + a.warmup + a.steps          # last timed context
+    assert bench.arm_config(_args(model="llama-3.2-1b"), 1)["workload"].startswith("config3")
+    assert bench.arm_config(_args(gpus=8), 8)["global_batch"] == 8 * a.batch
