@@ -53,6 +53,7 @@ def parse():
                     help="tensor-parallel ranks (config 4: --model qwen3-8b --tp 8 under torchrun); "
                          "the batch is then the global batch")
     ap.add_argument("--ctx", type=int, default=4096, help="--tp: KV cache pre-filled to this many positions")
+    ap.add_argument("--tp-eager", action="store_true", help="--tp: launch every step eagerly (no CUDA graph)")
     return ap.parse_args()
 
 
@@ -205,31 +206,47 @@ NCU_ATTN = {"dram_bytes": 38_076_672 + 4_096, "units": 64 * 8, "keys_loaded": 14
             "source": "ncu capture, profiles/decode_attention_qwen3_0.6b_bs64_ctx133.md, scaled by keys loaded"}
 
 
-def gemv_batch1(eng, peak):
+def gemv_batch1(eng, peak, n_streams: int = 1):
     """Batch-1 GEMV sweep over every linear of the model (qkv, o, gate_up, down per
-    layer) captured in one CUDA graph; the working set (~229 MB) exceeds L2."""
+    layer) captured in one CUDA graph; the working set (~229 MB) exceeds L2.
+
+    n_streams = 1: one stream, so each GEMV waits for the previous one (the
+    dependent-chain cost).  n_streams > 1: the GEMVs are dealt round-robin to
+    that many streams forked inside the graph, each with its own output and
+    workspace, so independent projections overlap (the streaming cost)."""
     L = _lib.lib()
     cfg = eng.cfg
     ws_n = 1 << 20
-    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    wss = [torch.zeros(ws_n, dtype=torch.uint8, device="cuda") for _ in range(n_streams)]
     x = torch.randn(1, max(cfg.emb_dim, cfg.hidden_dim, cfg.q_dim), device="cuda").to(torch.bfloat16)
-    y = torch.empty(1, 2 * cfg.hidden_dim + cfg.q_dim + 2 * cfg.kv_dim, dtype=torch.bfloat16, device="cuda")
+    ys = [torch.empty(1, 2 * cfg.hidden_dim + cfg.q_dim + 2 * cfg.kv_dim, dtype=torch.bfloat16, device="cuda")
+          for _ in range(n_streams)]
     ws_used = max(L.t2b_w4a16_gemm_workspace_bytes(1, w.out_features, w.in_features)
                   for l in eng.layers for w in (l.qkv, l.o_proj, l.gate_up, l.down))
     assert ws_used <= ws_n
-    ws_ptr = _lib.ptr(ws)
+    linears = [w for l in eng.layers for w in (l.qkv, l.o_proj, l.gate_up, l.down)]
+    streams = [torch.cuda.Stream() for _ in range(n_streams)]
+
+    def launch(w, i):
+        _lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
+            _lib.ptr(w.qw), _lib.ptr(w.meta), 0, _lib.ptr(x), 0, _lib.ptr(ys[i]), 0, 1, w.out_features,
+            w.in_features, 128, _lib.ptr(wss[i]), ws_n, _lib.stream()))
 
     def seq():
-        st = _lib.stream()
-        for l in eng.layers:
-            for w in (l.qkv, l.o_proj, l.gate_up, l.down):
-                _lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-                    _lib.ptr(w.qw), _lib.ptr(w.meta), 0, _lib.ptr(x), 0, _lib.ptr(y), 0, 1, w.out_features,
-                    w.in_features, 128, ws_ptr, ws_n, st))
+        if n_streams == 1:
+            for w in linears:
+                launch(w, 0)
+            return
+        main = torch.cuda.current_stream()
+        for st in streams:
+            st.wait_stream(main)
+        for j, w in enumerate(linears):
+            with torch.cuda.stream(streams[j % n_streams]):
+                launch(w, j % n_streams)
+        for st in streams:
+            main.wait_stream(st)
 
-    nbytes = sum(w.nbytes_algorithmic + 2 * w.in_features + 2 * w.out_features
-                 for l in eng.layers for w in (l.qkv, l.o_proj, l.gate_up, l.down))
-    launches = 4 * len(eng.layers)
+    nbytes = sum(w.nbytes_algorithmic + 2 * w.in_features + 2 * w.out_features for w in linears)
     seq()
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
@@ -252,9 +269,11 @@ def gemv_batch1(eng, peak):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000 / reps
     gbs = nbytes / (us * 1e-6) / 1e9
-    return {"workload": f"{launches} batch-1 GEMVs (all linears of {cfg.n_layers} layers) in one CUDA graph",
+    how = "one stream (each waits for the previous)" if n_streams == 1 else \
+        f"{n_streams} streams forked in the graph (independent GEMVs overlap)"
+    return {"workload": f"{len(linears)} batch-1 GEMVs (all linears of {cfg.n_layers} layers) in one CUDA graph, {how}",
             "bytes": nbytes, "us": round(us, 2), "achieved_gbs": round(gbs, 1), "peak_gbs": peak,
-            "frac": round(gbs / peak, 4), "launches": launches}
+            "frac": round(gbs / peak, 4), "launches": len(linears)}
 
 
 def kernel_profile(eng, steps):
@@ -440,6 +459,7 @@ def run_t2b(args, cfg):
         }
         if not args.no_gemv:
             line["gemv_b1"] = gemv_batch1(eng, peak)
+            line["gemv_b1_streams"] = gemv_batch1(eng, peak, n_streams=4)
         if not args.no_cpu_baseline and world == 1:   # host-core baseline: rank 0 at N=1 only
             mcpu = model_to_cpu(model)
             rate, dt, cores = cpu_decode_rate(cfg, mcpu, B, mid_ctx, args.cpu_sample_steps, args.seed)
@@ -476,7 +496,7 @@ def run_tp(args, cfg):
     B, C = args.batch, args.ctx
     max_ctx = ((C + args.warmup + args.steps + 1 + 63) // 64) * 64
     model = synth.random_model(cfg, seed=args.seed, device="cuda")
-    eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank, use_graph=True)
+    eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank, use_graph=not args.tp_eager)
     del model
     torch.cuda.empty_cache()
     g = torch.Generator(device="cuda").manual_seed(args.seed * 1000 + 7 + rank)

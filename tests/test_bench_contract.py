@@ -16,7 +16,7 @@ TINY = QuantizedQwenConfig(vocab_size=512, emb_dim=256, n_layers=1, n_heads=4, n
 
 def _args(**kw):
     a = dict(gpus=1, steps=2, warmup=3, impl="reference", batch=2, prompt=8, model="qwen3-0.6b", seed=0,
-             cpu_sample_steps=1, no_cpu_baseline=False, no_gemv=True, tp=0, ctx=4096)
+             cpu_sample_steps=1, no_cpu_baseline=False, no_gemv=True, tp=0, ctx=4096, tp_eager=False)
     a.update(kw)
     return argparse.Namespace(**a)
 
