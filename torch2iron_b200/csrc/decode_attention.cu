@@ -5,8 +5,12 @@
 // GQA group (q[m, h*qpg .. +qpg], so each K/V byte is read once) over keys
 // 0..pos[m], cut into 64-key tiles.  All tiles of all units form one list
 // (row-major units); the grid (the CTAs resident at once) splits the list into
-// equal contiguous ranges, so every CTA streams the same number of KV bytes in
-// a single wave whatever the context lengths.
+// equal contiguous ranges, so every CTA streams about the same number of KV
+// bytes in a single wave whatever the context lengths.  A range boundary that
+// falls inside a short unit moves to the nearer unit edge (short units are
+// never cut, so short-context batches need no cross-CTA merge).  The
+// after-kvwrite entry point builds the list and issues the loads of every
+// tile older than a unit's newest key before the dependency wait.
 //
 // Data movement: K and V tiles arrive by 3-D TMA boxes (64 dims x 64 keys, or
 // 64 dims x 16 keys for a tile that ends inside the context, so at most 15
@@ -26,7 +30,8 @@
 //   O^T [HD x 8 heads]      += V_w^T . P^T                HD/16 MMAs
 // At a unit's end the four warps' (o, max, sum) are combined in shared memory.
 // A unit cut between CTAs leaves one normalised partial (o, max, sum) per CTA;
-// the last CTA to finish it (ticket counter, re-armed) merges them.
+// after its last tile each CTA takes one ticket per cut unit, and the last
+// CTA to arrive (ticket counter, re-armed) merges the unit's partials.
 //
 // The same kernel reads the reference's packet cache
 // ([group][chunk][K 64*hd | V 64*hd | mask 64], decode_packet_cache.py:11-43):

@@ -15,17 +15,21 @@
 //     128-byte swizzle, straight into the UMMA K-major layout; rows past M
 //     are zero-filled by the copy.
 //   * One fp32 TMEM accumulator of Bp columns collects all groups.
-//   * Raw int4 blocks (8 KB + 512 B of meta per 128x128 tile-group) arrive by
-//     1-D TMA bulk copies issued BEFORE the programmatic-dependent-launch
-//     wait, so weight streaming overlaps the previous kernel's tail.
-//   * The k-splits of a tile form a thread-block cluster; partial tiles are
-//     summed through distributed shared memory, each CTA finishing Bp/KS rows.
+//   * Everything that does not depend on the previous kernel runs BEFORE the
+//     programmatic-dependent-launch wait: the raw int4 blocks (8 KB + 512 B
+//     of meta per 128x128 tile-group) arrive by 1-D bulk copies, TMEM is
+//     allocated, and the first A stages are dequantised; dependents are
+//     released once the CTA holds its TMEM.
+//   * The k-splits of a tile form a thread-block cluster; each CTA pushes the
+//     rows a peer finishes into that peer's shared memory with one bulk
+//     copy and finishes Bp/KS rows itself.
 //
 // Roles (256 threads): warps 0-3 own TMEM lane quarters 0-3 (weight rows
-// 32w..32w+31) and produce A; warp 4 allocates TMEM and one lane issues the
-// MMAs; warps 5-7 stage the epilogue inputs; all 8 warps drain TMEM.  Every
-// mbarrier wait is time-bounded; on timeout the CTA records T2B_ERR_TIMEOUT,
-// frees its TMEM, still passes its cluster barriers, and skips its epilogue.
+// 32w..32w+31) and produce A; warp 4 allocates TMEM, issues the activation
+// TMA and (one lane) the MMAs; warps 5-7 compute the row scales and stage the
+// epilogue inputs; all 8 warps drain TMEM.  Every mbarrier wait is
+// time-bounded; on timeout the CTA records T2B_ERR_TIMEOUT, frees its TMEM,
+// still passes its cluster barriers, and skips its epilogue.
 
 #include <algorithm>
 
