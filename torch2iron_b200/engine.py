@@ -15,6 +15,9 @@ as 5 fused launches per layer:
     rms_norm_rows                   final norm -> bf16
     lm_head_argmax                  bf16 lm_head GEMM with the greedy argmax fused in
                                     (logits written only with keep_logits)
+  or, for a W4A16 head (the packed artifact's quantized ``lm_head`` linear,
+  ``model.py:410-414``):
+    w4a16_gemm + argmax_rows        fp32 logits, then the greedy argmax
 
 The whole step is captured once in a CUDA graph and replayed; the kernels
 chain with programmatic dependent launch.  The residual stream is fp32; the
@@ -34,6 +37,7 @@ from . import _lib
 from . import weights as W
 from .config import QuantizedQwenConfig
 from .rope import rope_angles
+from .synth import AutoGPTQLinear
 
 
 @dataclass
@@ -75,8 +79,9 @@ def load_layer(layer: dict, cfg: QuantizedQwenConfig, device="cuda") -> LayerWei
 class DecodeEngine:
     """Greedy batch decoder over device-resident W4A16 weights.
 
-    ``model`` is the dict produced by ``synth.random_model`` (AutoGPTQ linears
-    per layer, bf16 ``embed``, ``final_norm``, optional untied ``lm_head``).
+    ``model`` is the dict produced by ``synth.random_model`` or ``loaders``
+    (AutoGPTQ linears per layer, bf16 ``embed``, ``final_norm``, and
+    ``lm_head``: ``None`` when tied, bf16 ``[V, H]``, or an ``AutoGPTQLinear``).
     """
 
     def __init__(self, cfg: QuantizedQwenConfig, model: dict, batch: int, max_ctx: int, device="cuda",
@@ -92,7 +97,14 @@ class DecodeEngine:
             raise ValueError("layer count does not match the config")
         self.embed = model["embed"].to(dev, torch.bfloat16).contiguous()
         lm = model.get("lm_head")
-        self.lm_head = self.embed if lm is None else lm.to(dev, torch.bfloat16).contiguous()
+        self.lm_w4: W.W4Weight | None = None          # W4A16 head (a packed artifact's ``lm_head`` linear)
+        if isinstance(lm, AutoGPTQLinear):
+            if (lm.out_features, lm.in_features) != (cfg.vocab_size, cfg.emb_dim):
+                raise ValueError("lm_head shape does not match the config")
+            self.lm_w4 = W.from_autogptq(lm, dev)
+            self.lm_head = None
+        else:
+            self.lm_head = self.embed if lm is None else lm.to(dev, torch.bfloat16).contiguous()
         self.final_norm = model["final_norm"].to(dev, torch.bfloat16).contiguous()
         self.angles = rope_angles(cfg.head_dim, max_ctx, cfg.rope_base).to(dev)
 
@@ -122,8 +134,12 @@ class DecodeEngine:
             "o": L.t2b_oproj_residual_workspace_bytes(B, H, cfg.q_dim),
             "ug": L.t2b_upgate_swiglu_workspace_bytes(B, H, cfg.hidden_dim),
             "down": L.t2b_down_residual_workspace_bytes(B, H, cfg.hidden_dim),
-            "lm": L.t2b_lm_head_argmax_workspace_bytes(B),
         }
+        if self.lm_w4 is None:
+            sizes["lm"] = L.t2b_lm_head_argmax_workspace_bytes(B)
+        else:
+            sizes["lm"] = L.t2b_w4a16_gemm_workspace_bytes(B, cfg.vocab_size, H)
+            sizes["am"] = L.t2b_argmax_workspace_bytes(B, cfg.vocab_size)
         # one workspace per op kind: consecutive ops never share counters
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
         # device status word: kernels record a timed-out wait here (t2b_set_error_word)
@@ -136,8 +152,11 @@ class DecodeEngine:
     # -- byte accounting (algorithmic, for the roofline) ---------------------
     def weight_bytes(self) -> int:
         b = sum(l.algorithmic_bytes for l in self.layers)
-        b += self.lm_head.numel() * 2 + self.final_norm.numel() * 2
+        b += self.lm_head_bytes() + self.final_norm.numel() * 2
         return b
+
+    def lm_head_bytes(self) -> int:
+        return self.lm_w4.nbytes_algorithmic if self.lm_w4 is not None else self.lm_head.numel() * 2
 
     def step_bytes(self, ctx_lens: list[int] | None = None) -> int:
         """Algorithmic HBM bytes of one decode step with per-row context lengths (keys attended)."""
@@ -196,9 +215,18 @@ class DecodeEngine:
             self.enqueue_layer(li, st)
         _lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
                                                             cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
-        _lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
-            p(self.xn), p(self.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(self.next_tokens), None,
-            p(self.logits) if self.keep_logits else None, *self._ws("lm"), st))
+        if self.lm_w4 is None:
+            _lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
+                p(self.xn), p(self.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(self.next_tokens), None,
+                p(self.logits) if self.keep_logits else None, *self._ws("lm"), st))
+        else:
+            _lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
+                p(self.lm_w4.qw), p(self.lm_w4.meta), _lib.WFMT_T2B, p(self.xn), _lib.DTYPE[torch.bfloat16],
+                p(self.logits), _lib.DTYPE[torch.float32], B, cfg.vocab_size, cfg.emb_dim, cfg.group_size,
+                *self._ws("lm"), st))
+            _lib.check("t2b_argmax_rows", L.t2b_argmax_rows(
+                p(self.logits), _lib.DTYPE[torch.float32], B, cfg.vocab_size, cfg.vocab_size, p(self.next_tokens),
+                *self._ws("am"), st))
 
     def set_hidden(self, x: torch.Tensor) -> None:
         """Load a residual-stream state (fp32 [B, H]) and its split norm input for layer 0."""
@@ -208,7 +236,7 @@ class DecodeEngine:
 
     def kernels_per_step(self) -> int:
         """Launches of this library's kernels per step (embed, 5 per layer, final norm, lm_head + argmax)."""
-        return 1 + 5 * self.cfg.n_layers + 1 + 1
+        return 1 + 5 * self.cfg.n_layers + 1 + (1 if self.lm_w4 is None else 2)
 
     # -- graph capture -------------------------------------------------------
     def capture(self) -> None:

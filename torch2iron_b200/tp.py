@@ -135,6 +135,9 @@ class TPDecodeEngine:
         self.layers = [load_layer(shard_layer(l, cfg, tp, rank), lc, dev) for l in model["layers"]]
         self.embed = model["embed"].to(dev, torch.bfloat16).contiguous()
         lm = model.get("lm_head")
+        if lm is not None and not isinstance(lm, torch.Tensor):
+            raise NotImplementedError("tensor-parallel decode takes a bf16 lm_head (tied or untied); "
+                                      "a W4A16 head runs on the single-GPU engine")
         full_lm = model["embed"] if lm is None else lm
         v0, v1 = vocab_slice(cfg, tp, rank)
         self.v_local = v1 - v0
