@@ -1,12 +1,15 @@
 """Golden fixture for the artifact loaders, made by the reference itself.
 
 Writes a tiny seeded symmetric AutoGPTQ Qwen3 checkpoint (config.json +
-model.safetensors), packs it with the reference's own writer
-(``write_packed_inference_artifact``, src/models/quantized_qwen3/packed_format.py:405-655)
-into ``tests/golden/packed_tiny/`` (config.json + qwen3_w4a16_packed/), keeps
-the AutoGPTQ checkpoint there too, and records the reference model's logits
-and greedy tokens over a prompt (``QuantizedQwenForCausalLM`` on that artifact,
-model.py:360-480, fp32) in ``tests/golden/packed_tiny.npz``.
+model.safetensors, untied dense head; weights N(0, 0.02) and norm weights
+N(1, 0.02), the value distribution of the benchmark configurations), packs it
+with the reference's own writer (``write_packed_inference_artifact``,
+src/models/quantized_qwen3/packed_format.py:405-655) into
+``tests/golden/packed_tiny/`` (config.json + qwen3_w4a16_packed/, the
+checkpoint kept beside it), and records in ``tests/golden/packed_tiny.npz``
+the reference model's logits over a prompt, its greedy tokens and the logits
+each token was picked from (``QuantizedQwenForCausalLM`` on that artifact,
+model.py:360-480, fp32).
 
 Run once, in a container where the reference is mounted:
     python tests/golden/make_packed_artifact.py <reference root>
@@ -27,7 +30,7 @@ OUT = HERE / "packed_tiny"
 CFG = {"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "vocab_size": 512, "hidden_size": 256,
        "num_hidden_layers": 2, "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 64,
        "intermediate_size": 512, "rms_norm_eps": 1e-6, "rope_theta": 1000000.0, "max_position_embeddings": 256,
-       "tie_word_embeddings": True, "bos_token_id": 1, "eos_token_id": 2,
+       "tie_word_embeddings": False, "bos_token_id": 1, "eos_token_id": 2,
        "quantization_config": {"bits": 4, "group_size": 128, "sym": True, "quant_method": "gptq"}}
 
 
@@ -59,13 +62,15 @@ def main(ref_root: str) -> None:
     for i in range(CFG["num_hidden_layers"]):
         p = f"model.layers.{i}"
         for name, (n, k) in shapes.items():
-            qw, qz, sc = sym_autogptq(torch.randn(n, k, generator=gen) * 0.05)
+            qw, qz, sc = sym_autogptq(torch.randn(n, k, generator=gen) * 0.02)
             t[f"{p}.{name}.qweight"], t[f"{p}.{name}.qzeros"], t[f"{p}.{name}.scales"] = qw, qz, sc
         for nrm, size in (("input_layernorm", h), ("post_attention_layernorm", h), ("self_attn.q_norm", hd),
                           ("self_attn.k_norm", hd)):
-            t[f"{p}.{nrm}.weight"] = (1.0 + 0.05 * torch.randn(size, generator=gen)).to(torch.bfloat16)
-    t["model.embed_tokens.weight"] = (torch.randn(v, h, generator=gen) * 0.05).to(torch.bfloat16)
-    t["model.norm.weight"] = (1.0 + 0.05 * torch.randn(h, generator=gen)).to(torch.bfloat16)
+            t[f"{p}.{nrm}.weight"] = (1.0 + 0.02 * torch.randn(size, generator=gen)).to(torch.bfloat16)
+    t["model.embed_tokens.weight"] = (torch.randn(v, h, generator=gen) * 0.02).to(torch.bfloat16)
+    t["model.norm.weight"] = (1.0 + 0.02 * torch.randn(h, generator=gen)).to(torch.bfloat16)
+    # untied dense head: the packer quantizes it into the artifact's synthetic W4 lm_head
+    t["lm_head.weight"] = (torch.randn(v, h, generator=gen) * 0.02).to(torch.bfloat16)
 
     if OUT.exists():
         shutil.rmtree(OUT)
@@ -84,14 +89,16 @@ def main(ref_root: str) -> None:
                                      compute_dtype=torch.float32).eval()
     prompt = torch.randint(0, v, (1, 12), generator=gen)
     logits, past = model(prompt)
-    toks, last = [], logits[:, -1]
+    toks, gen_logits, last = [], [], logits[:, -1]
     for _ in range(6):
         nxt = torch.argmax(last, dim=-1)
         toks.append(int(nxt))
+        gen_logits.append(last[0].clone())
         lg, past = model(nxt.view(1, 1), past)
         last = lg[:, -1]
+    # gen_logits[i]: the logits greedy token i was picked from (teacher-forced checks)
     np.savez_compressed(HERE / "packed_tiny.npz", prompt=prompt.numpy(), logits=logits[0].numpy(),
-                        greedy=np.array(toks, dtype=np.int64))
+                        greedy=np.array(toks, dtype=np.int64), gen_logits=torch.stack(gen_logits).numpy())
     print("wrote", OUT, "and packed_tiny.npz;", len(toks), "greedy tokens:", toks)
 
 

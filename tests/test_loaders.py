@@ -52,7 +52,7 @@ def test_packed_artifact_config_and_heads():
             cfg.hidden_dim) == (512, 256, 2, 4, 2, 64, 512)
     assert cfg.qk_norm and cfg.rope_base == 1e6 and cfg.rms_norm_eps == 1e-6
     cfg.validate()
-    # the packer quantized the tied embedding into a synthetic W4A16 head (packed_format.py:583-648)
+    # the packer quantized the dense head into a synthetic W4A16 head (packed_format.py:583-648)
     assert isinstance(model["lm_head"], AutoGPTQLinear)
     assert model["lm_head"].scales.dtype == torch.float16
     assert model["embed"].dtype == torch.bfloat16 and model["embed"].shape == (512, 256)
@@ -76,16 +76,21 @@ def test_qparam_conversion_is_the_reference_dequant():
 
 def test_packed_artifact_matches_reference_logits():
     """The oracle decoder over the loaded weights reproduces the reference
-    model's logits (fp32 KV: 1e-4; the GPU's bf16 KV cache: 2e-2) and greedy tokens."""
+    model's logits (fp32 KV: 1e-4; the GPU's bf16 KV cache: 2e-2), its greedy
+    tokens and the logits along them."""
     cfg, model = LD.load_packed_artifact(MODEL_DIR)
     g = _golden()
     prompt, ref = torch.from_numpy(g["prompt"]), torch.from_numpy(g["logits"])
+    P = prompt.shape[1]
     for kv, tol in ((torch.float32, 1e-4), (torch.bfloat16, 2e-2)):
         dec = _oracle_decoder(cfg, model, kv)
-        lg = torch.stack([dec.step(prompt[:, p], torch.tensor([p]))[0] for p in range(prompt.shape[1])])
+        lg = torch.stack([dec.step(prompt[:, p], torch.tensor([p]))[0] for p in range(P)])
         assert (lg - ref).abs().max().item() <= tol
-        toks = _oracle_decoder(cfg, model, kv).generate(prompt, len(g["greedy"]))
-        assert toks[0].tolist() == g["greedy"].tolist()
+        for i, tok in enumerate(g["greedy"][:-1]):           # teacher-forced along the reference's tokens
+            lg = dec.step(torch.tensor([int(tok)]), torch.tensor([P + i]))[0]
+            assert (lg - torch.from_numpy(g["gen_logits"][i + 1])).abs().max().item() <= tol
+    toks = _oracle_decoder(cfg, model, torch.float32).generate(prompt, len(g["greedy"]))
+    assert toks[0].tolist() == g["greedy"].tolist()
 
 
 def test_checkpoint_with_reference_numerics_equals_packed():
@@ -103,13 +108,23 @@ def test_checkpoint_with_reference_numerics_equals_packed():
     assert torch.equal(ckpt["embed"], packed["embed"]) and torch.equal(ckpt["final_norm"], packed["final_norm"])
 
 
-def test_checkpoint_numerics_keeps_fp16_scales_and_tied_head():
+def test_checkpoint_numerics_keeps_fp16_scales_and_dense_head(tmp_path):
     cfg, model = LD.load_autogptq_checkpoint(MODEL_DIR, numerics="checkpoint")
     t = load_file(str(MODEL_DIR / "model.safetensors"))
     lin = model["layers"][1]["down_proj"]
     assert torch.equal(lin.scales, t["model.layers.1.mlp.down_proj.scales"])
     assert torch.equal(lin.qweight, t["model.layers.1.mlp.down_proj.qweight"])
+    assert torch.equal(model["lm_head"], t["lm_head.weight"]) and not cfg.tie_word_embeddings
+    # without a head tensor: tied to the embedding (checkpoint numerics) or the
+    # embedding quantized, as the packer does (reference numerics)
+    del t["lm_head.weight"]
+    save_file(t, str(tmp_path / "model.safetensors"))
+    shutil.copy(MODEL_DIR / "config.json", tmp_path)
+    cfg, model = LD.load_autogptq_checkpoint(tmp_path, numerics="checkpoint")
     assert model["lm_head"] is None and cfg.tie_word_embeddings
+    _, model = LD.load_autogptq_checkpoint(tmp_path)
+    q = LD.quantize_head_w4(t["model.embed_tokens.weight"])
+    assert torch.equal(model["lm_head"].qweight, q.qweight) and torch.equal(model["lm_head"].scales, q.scales)
     with pytest.raises(ValueError, match="numerics"):
         LD.load_autogptq_checkpoint(MODEL_DIR, numerics="fp8")
 
@@ -211,10 +226,10 @@ def test_bf16_scales_outside_fp16_are_rejected_unless_the_group_is_zero():
 
 
 def test_head_quantizer_is_the_packer_rtn():
-    """``quantize_head_w4`` on the fixture's embedding gives the artifact's synthetic head."""
+    """``quantize_head_w4`` on the fixture's dense head gives the artifact's synthetic head."""
     art = LD.PackedArtifact(PACKED_DIR)
     _, qp = art.qparam("lm_head")
-    embed = art.dense("model.embed_tokens.weight")
-    mine = LD.quantize_head_w4(embed)
+    assert art.manifest["linears"]["lm_head"]["qparam"]["source"] == "lm_head.weight"
+    mine = LD.quantize_head_w4(art.dense("lm_head.weight"))
     ref = LD.qparam_to_autogptq(qp, 256, 512)
     assert torch.equal(mine.qweight, ref.qweight) and torch.equal(mine.scales, ref.scales)
