@@ -401,6 +401,7 @@ def run_t2b(args, cfg):
         t = torch.tensor([ms_e2e], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_e2e = float(t.item())
+    fail_on_device_status(eng, world)
 
     peak, peak_kind = peaks()
     result = None
@@ -475,6 +476,30 @@ def run_t2b(args, cfg):
         print(json.dumps(result), flush=True)
 
 
+def device_status(eng, world: int) -> int:
+    """The largest device status word over the ranks (0: no kernel timed out a
+    wait); every rank takes this collective at the same point."""
+    code = eng.err.to(torch.int32).clone()
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(code, op=dist.ReduceOp.MAX)
+    return int(code.item())
+
+
+def fail_on_device_status(eng, world: int) -> None:
+    """Exit non-zero (after releasing graphs and the process group) when a kernel
+    recorded a timed-out wait: its outputs, and so this run's numbers, are void."""
+    code = device_status(eng, world)
+    if code == 0:
+        return
+    eng.release()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    raise SystemExit(f"a decode kernel recorded status {code} "
+                     f"({_lib.load().t2b_status_string(code).decode()}): measurement void")
+
+
 def run_tp(args, cfg):
     """Config 4: one model split over the torchrun ranks (tensor parallel), B rows
     in total, the KV cache pre-filled with N(0,1) bf16 to --ctx positions; K timed
@@ -536,6 +561,7 @@ def run_tp(args, cfg):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
+    fail_on_device_status(eng, world)
     # bytes one GPU must move per step: its weight shard, lm_head slice, KV of its kv heads
     lc = eng.lcfg
     c_mid = C + args.warmup + 1 + args.steps // 2

@@ -110,6 +110,18 @@ T2B_API int t2b_repack_autogptq(const int32_t* qweight, const int32_t* qzeros, c
  * kernel.cc:29-133) and the W4A16GEMM family (w4a16_gemm/op.py:22-399).
  */
 T2B_API size_t t2b_w4a16_gemm_workspace_bytes(int M, int N, int K);
+
+/*
+ * The launch plan every W4A16 linear of shape [M,N,K] takes (host only, no
+ * device work): path 0 = CUDA-core GEMV (rows_per_cta batch rows per CTA,
+ * groups_per_cta k-groups of 128 per CTA), 1 = tcgen05 (rows_per_cta = the
+ * padded batch tile Bp, groups_per_cta = S); ksplit = k-slices of a 128-row
+ * tile (a thread-block cluster when <= 8).  On the tcgen05 path ksplit
+ * divides rows_per_cta.  No counterpart in the reference (its tiling is fixed
+ * at NPU compile time, w4a16_gemm/design.py); exported so callers and tests
+ * can check a shape's decomposition without a GPU.
+ */
+T2B_API int t2b_linear_plan(int M, int N, int K, int* path, int* rows_per_cta, int* groups_per_cta, int* ksplit);
 T2B_API int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype, void* y,
                    int y_dtype, int M, int N, int K, int group_size, void* workspace, size_t workspace_bytes,
                    void* stream);

@@ -14,8 +14,9 @@ import oracle
 from tests import golden_io as gio
 from tests.gpu_util import max_abs, oracle_decoder, rel_err
 from torch2iron_b200 import _lib, synth
-from torch2iron_b200.config import QWEN3_0_6B, LLAMA_3_2_1B, QuantizedQwenConfig
+from torch2iron_b200.config import QWEN3_0_6B, QWEN3_8B, LLAMA_3_2_1B, QuantizedQwenConfig
 from torch2iron_b200.engine import DecodeEngine
+from torch2iron_b200.tp import local_config
 from torch2iron_b200.operators import (CopyPresentPacketKV, LlamaChunkedAttention, ResidualAddRMSNorm, RMSNormRoPE,
                                        SiLUMul)
 
@@ -175,10 +176,13 @@ def _run_engine_layer(eng, x, pos):
     (QWEN3_0_6B.scaled(n_layers=1), 64, 256, [200] * 64),         # bs 64, tcgen05 path
     (QWEN3_0_6B.scaled(n_layers=1), 8, 576, [512] * 8),
     (LLAMA_3_2_1B.scaled(n_layers=1, vocab_size=512), 3, 128, [5, 64, 127]),
+    # one rank of Qwen3-8B at TP8 (4 q heads, 1 kv head, intermediate 1536)
+    (local_config(QWEN3_8B.scaled(n_layers=1, vocab_size=512), 8), 64, 128, list(range(40, 104))),
 ])
 def test_decoder_layer_vs_oracle(cfg, batch, ctx, pos_list):
     eng, dec, x, pos = _one_layer(cfg, batch, ctx, pos_list, seed=1608560892)
     y = _run_engine_layer(eng, x, pos)
+    assert int(eng.err.item()) == 0       # no kernel timed out a wait
     ref = dec.layer_step(0, x, pos.long())
     # residual stream: bf16 activations into each linear -> compare at bf16 level
     assert rel_err(y, ref) <= 1e-2

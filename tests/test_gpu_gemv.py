@@ -68,7 +68,8 @@ def test_golden_gemv_batches(M):
     assert rel_err(y, torch.from_numpy(d["y"])[:M]) <= 1e-5
 
 
-@pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 3072), (6144, 1024), (1024, 2048), (256, 512), (128, 256)])
+@pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 3072), (6144, 1024), (1024, 2048), (256, 512), (128, 256),
+                                 (512, 1536)])   # K = 12 groups: cluster split 4 x 3 groups (Qwen3-8B down at TP8)
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 13, 16, 17, 33, 64, 100, 128, 200])
 def test_gemm_shapes_vs_oracle(N, K, M):
     g = torch.Generator().manual_seed(N * 7 + K + M)

@@ -42,7 +42,7 @@ def _rank(rank, world, port, batch, out_q):
             for _ in range(3):
                 eng.advance()
                 toks.append(eng.next_tokens.cpu().clone())
-            res[mode] = {"tokens": torch.stack(toks, 1), "x": eng.x.cpu().clone()}
+            res[mode] = {"tokens": torch.stack(toks, 1), "x": eng.x.cpu().clone(), "status": int(eng.err.item())}
             eng.release()
         res.update(res["eager"])
         if rank == 0:
@@ -74,6 +74,8 @@ def test_tp2_engine_matches_single_gpu(batch):
         p.join(timeout=120)
         assert p.exitcode == 0
     r0, r1 = res[0], res[1]
+    for r in (r0, r1):
+        assert r["eager"]["status"] == 0 and r["graph"]["status"] == 0   # no kernel timed out a wait
     assert torch.equal(r0["tokens"], r1["tokens"])            # replicated greedy picks
     assert torch.equal(r0["x"], r1["x"])                      # replicated residual stream
     assert torch.equal(r0["tokens"], r0["ref_tokens"])

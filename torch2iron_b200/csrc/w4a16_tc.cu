@@ -430,8 +430,11 @@ static TcPlan tc_plan(int M, int N, int K) {
   pl.BP = bp;
   pl.S = 0;
   auto fits = [&](int bp_, int s_) { return TcLayout(bp_, s_, G / s_).bytes <= 210 * 1024; };
+  // KS must divide BP: each CTA of a cluster finishes BP/KS rows, and its
+  // receive barrier expects the (KS-1) * BP/KS rows its peers push.
+  auto splits = [&](int bp_, int s_) { return G % s_ == 0 && G / s_ <= 8 && bp_ % (G / s_) == 0; };
   for (int s_ : {4, 3, 2, 1}) {
-    if (G % s_ || G / s_ > 8 || G / s_ > bp) continue;
+    if (!splits(bp, s_)) continue;
     if (!fits(bp, s_)) continue;
     const long ctas = (long)tiles * (G / s_) * ((M + bp - 1) / bp);
     if (ctas >= 64 || s_ == 1) {
@@ -444,13 +447,13 @@ static TcPlan tc_plan(int M, int N, int K) {
       if (G % s_) continue;
       int b = bp;
       while (b > 16 && !fits(b, s_)) b >>= 1;
-      if (fits(b, s_) && G / s_ <= b) {
+      if (fits(b, s_) && splits(b, s_)) {
         pl.S = s_;
         pl.BP = b;
       }
     }
   }
-  pl.ok = pl.S > 0 && N % TILE_N == 0;
+  pl.ok = pl.S > 0 && N % TILE_N == 0 && splits(pl.BP, pl.S);
   if (!pl.ok) return pl;
   // A grid of more than one wave (resident CTAs: shared memory and TMEM, at
   // most 2 per SM) takes more groups per CTA where they fit: fewer, longer CTAs.
@@ -470,7 +473,7 @@ static TcPlan tc_plan(int M, int N, int K) {
     int best = pl.S;
     if (waves(best) > 1)
       for (int s_ = pl.S + 1; s_ <= G; ++s_) {
-        if (G % s_ || G / s_ > 8 || G / s_ > pl.BP || !fits(pl.BP, s_)) continue;
+        if (!splits(pl.BP, s_) || !fits(pl.BP, s_)) continue;
         if (waves(s_) < waves(best)) best = s_;
       }
     pl.S = best;
@@ -490,6 +493,14 @@ static TcPlan tc_plan(int M, int N, int K) {
 size_t tc_ws_bytes(int, int, int) { return 0; }  // split-K stays on chip (cluster DSMEM)
 
 bool tc_supported(int M, int N, int K) { return tc_plan(M, N, K).ok; }
+
+bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks) {
+  const TcPlan pl = tc_plan(M, N, K);
+  *bp = pl.BP;
+  *s = pl.S;
+  *ks = pl.KS;
+  return pl.ok;
+}
 
 template <int BP, int PRO, int EPI>
 static int tc_launch_t(LinearParams& p, const TcPlan& pl, cudaStream_t st) {

@@ -290,6 +290,13 @@ class TPDecodeEngine:
         self.tokens.copy_(self.next_tokens)
         self.pos.fill_(P)
 
+    def check_device_errors(self) -> None:
+        """Raise (and clear) the status a kernel of this rank recorded for a timed-out device wait."""
+        code = int(self.err.item())
+        if code:
+            self.err.zero_()
+            raise self._lib.T2BError("a decode-step kernel (device status word)", code)
+
     def release(self) -> None:
         """Drop the captured graphs (before destroying the process group)."""
         torch.cuda.synchronize(self.device)
