@@ -157,6 +157,15 @@ T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int
  * 2x RMSNormRoPE + CopyPresentPacketKV (batch_decode_fused.py:426-474).
  */
 T2B_API size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, int head_dim);
+/* Same, with row m writing its K/V into cache sequence row_seq[m] (a prefill
+ * chunk: rows b*C + i of B sequences, pos[m] = p0 + i) instead of sequence m. */
+T2B_API int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
+                                          const float* ssq, float eps, const uint16_t* q_norm_w,
+                                          const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
+                                          const int32_t* row_seq, uint16_t* q_out, uint16_t* k_cache,
+                                          uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
+                                          int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
+                                          void* stream);
 T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq,
                                       float eps, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                                       const float* angles, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
@@ -186,6 +195,20 @@ T2B_API int t2b_decode_attention_after_kvwrite(const uint16_t* q, const uint16_t
                                                const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv,
                                                int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
                                                void* stream);
+
+/*
+ * Causal GQA attention of a prefill chunk: C tokens (positions p0..p0+C-1) of
+ * each of B sequences, whose K/V rows are already in the cache:
+ *   out[b*C + i, h] = softmax(q[b*C + i, h] . K[b, h/qpg, 0..p0+i]^T / sqrt(hd)) . V
+ * q, out bf16 [B*C][n_heads*hd]; caches bf16 [B][n_kv][max_ctx][hd];
+ * p0 + C <= max_ctx; 64 % (n_heads / n_kv) == 0.  No workspace.
+ * Replaces LlamaChunkedPrefillAttention
+ * (src/torch2iron/operators/llama_chunked_prefill_attention/op.py:21-197) as
+ * driven by prefill_forward_pass (src/models/quantized_qwen3/prefill_runtime.py:95-164).
+ */
+T2B_API int t2b_prefill_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
+                                  int B, int C, int p0, int n_heads, int n_kv, int head_dim, int max_ctx,
+                                  void* stream);
 
 /*
  * Attention over the reference's packet cache

@@ -1,0 +1,110 @@
+"""Chunked prefill: the causal prefill attention kernel against an fp32 torch
+reference, and the engine's chunked prefill (every linear over all B x chunk
+prompt tokens at once) against the one-token-per-step prefill, the oracle and
+the reference model's golden logits."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from tests.gpu_util import max_abs, oracle_decoder
+from torch2iron_b200 import _lib, synth
+from torch2iron_b200 import loaders as LD
+from torch2iron_b200.config import QuantizedQwenConfig
+from torch2iron_b200.engine import DecodeEngine
+
+pytestmark = pytest.mark.gpu
+
+SMALL = QuantizedQwenConfig(vocab_size=512, emb_dim=256, n_layers=2, n_heads=4, n_kv_groups=2, head_dim=64,
+                            hidden_dim=512, rms_norm_eps=1e-6, rope_base=1e6)
+
+
+def _ref_prefill_attention(q, kc, vc, C, p0, nq, nkv, hd):
+    B = kc.shape[0]
+    qpg = nq // nkv
+    q = q.float().view(B, C, nq, hd)
+    out = torch.empty(B, C, nq, hd)
+    for b in range(B):
+        for i in range(C):
+            n = p0 + i + 1
+            k = kc[b, :, :n].float().repeat_interleave(qpg, 0)          # [nq, n, hd]
+            v = vc[b, :, :n].float().repeat_interleave(qpg, 0)
+            w = torch.softmax(torch.einsum("hd,hnd->hn", q[b, i], k) / hd ** 0.5, -1)
+            out[b, i] = torch.einsum("hn,hnd->hd", w, v)
+    return out.view(B * C, nq * hd)
+
+
+# attention operands N(0, 1): P is rounded to bf16 for the PV product (as in
+# flash attention), so the bar is 2e-2 max-abs on outputs of magnitude ~1
+@pytest.mark.parametrize("B,C,p0,nq,nkv,hd,max_ctx", [
+    (2, 40, 0, 4, 2, 64, 128),       # one chunk from position 0, partial CTA
+    (1, 37, 70, 4, 1, 128, 128),     # a later chunk: keys before and inside it
+    (3, 64, 64, 16, 8, 128, 192),    # Qwen3-0.6B heads
+    (2, 16, 5, 32, 8, 64, 64),       # Llama-3.2-1B heads (qpg 4)
+    (1, 1, 0, 2, 1, 128, 64),        # a single token
+])
+def test_prefill_attention_vs_torch(B, C, p0, nq, nkv, hd, max_ctx):
+    g = torch.Generator().manual_seed(B * 1000 + C + p0)
+    q = torch.randn(B * C, nq * hd, generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, nkv, max_ctx, hd, generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, nkv, max_ctx, hd, generator=g).to(torch.bfloat16)
+    out = torch.full((B * C, nq * hd), float("nan"), dtype=torch.bfloat16, device="cuda")
+    qd, kd, vd = q.cuda(), kc.cuda(), vc.cuda()
+    _lib.call("t2b_prefill_attention", _lib.ptr(qd), _lib.ptr(kd), _lib.ptr(vd), _lib.ptr(out), B, C, p0, nq, nkv,
+              hd, max_ctx, _lib.stream())
+    torch.cuda.synchronize()
+    ref = _ref_prefill_attention(q, kc, vc, C, p0, nq, nkv, hd)
+    assert not torch.isnan(out.float()).any()
+    assert max_abs(out, ref) <= 2e-2
+
+
+def test_prefill_attention_rejects_bad_shapes():
+    t = torch.zeros(64, dtype=torch.bfloat16, device="cuda")
+    L = _lib.lib()
+    p = _lib.ptr(t)
+    assert L.t2b_prefill_attention(p, p, p, p, 1, 8, 60, 4, 2, 64, 64, None) != 0     # p0 + C > max_ctx
+    assert L.t2b_prefill_attention(p, p, p, p, 1, 8, 0, 4, 2, 96, 64, None) != 0      # head_dim
+    assert L.t2b_prefill_attention(p, p, p, p, 1, 8, 0, 6, 4, 64, 64, None) != 0      # heads not a multiple
+
+
+@pytest.mark.parametrize("chunk", [None, 16])
+def test_chunked_prefill_matches_stepwise_and_oracle(chunk):
+    cfg = SMALL
+    model = synth.random_model(cfg, seed=41)
+    B, P = 3, 37
+    prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(42))
+    a = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
+    a.prefill_chunked(prompts, chunk=chunk)
+    b = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
+    b.prefill(prompts)
+    torch.cuda.synchronize()
+    assert int(a.err.item()) == 0
+    for li in range(cfg.n_layers):
+        assert max_abs(a.k_cache[li][:, :, :P], b.k_cache[li][:, :, :P]) <= 5e-2
+        assert max_abs(a.v_cache[li][:, :, :P], b.v_cache[li][:, :, :P]) <= 5e-2
+        assert a.k_cache[li][:, :, P:].abs().max().item() == 0          # nothing written past the prompt
+    assert max_abs(a.logits, b.logits) <= 2e-2
+    ref = oracle_decoder(cfg, model, B, 64).prefill(prompts)
+    assert max_abs(a.logits, ref) <= 2e-2
+    top = torch.topk(ref, 2, dim=-1).values
+    sure = (top[:, 0] - top[:, 1]) > 4e-2
+    assert torch.equal(a.next_tokens.cpu().long()[sure], ref.argmax(-1)[sure])
+    # decoding continues from the chunked prefill exactly as from the stepwise one
+    a.advance()
+    b.advance()
+    assert max_abs(a.logits, b.logits) <= 2e-2
+
+
+def test_chunked_prefill_on_reference_artifact():
+    """The packed artifact's model: logits after the prompt against the reference model's."""
+    model_dir = Path(__file__).resolve().parent / "golden" / "packed_tiny"
+    cfg, model = LD.load_packed_artifact(model_dir)
+    g = np.load(model_dir.parent / "packed_tiny.npz")
+    prompt = torch.from_numpy(g["prompt"])
+    eng = DecodeEngine(cfg, model, batch=1, max_ctx=64, use_graph=True)
+    eng.prefill_chunked(prompt, chunk=5)
+    torch.cuda.synchronize()
+    assert max_abs(eng.logits[0], torch.from_numpy(g["logits"][-1])) <= 2e-2
+    eng.check_device_errors()

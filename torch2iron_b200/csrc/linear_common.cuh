@@ -52,6 +52,7 @@ struct LinearParams {
   const __nv_bfloat16* kn_w;
   const float* angles;
   const int* pos;
+  const int* row_seq;     // EPI_QKV: cache sequence of each row (nullptr: row m writes sequence m)
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
   int n_heads, n_kv, head_dim, max_ctx;
@@ -140,9 +141,10 @@ T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile
     for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const int pos = ec.pos ? ec.pos[b] : p.pos[m];
     const bool in_cache = pos >= 0 && pos < p.max_ctx;   // a bad position writes no cache entry
+    const size_t cm = p.row_seq ? (size_t)__ldg(p.row_seq + m) : (size_t)m;   // cache sequence of row m
     if (is_v) {  // value head: stored as projected (model.py:250,263)
       if (in_cache)
-        *reinterpret_cast<uint2*>(&p.v_cache[(((size_t)m * nkv + (head - nq - nkv)) * p.max_ctx + pos) * HD + d0]) =
+        *reinterpret_cast<uint2*>(&p.v_cache[((cm * nkv + (head - nq - nkv)) * p.max_ctx + pos) * HD + d0]) =
             pack_bf16x4(x.x, x.y, x.z, x.w);
       continue;
     }
@@ -157,7 +159,7 @@ T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile
     if (is_q)
       *reinterpret_cast<uint2*>(&q_out[(size_t)m * p.y_ld + head * HD + d0]) = o;
     else
-      *reinterpret_cast<uint2*>(&p.k_cache[(((size_t)m * nkv + (head - nq)) * p.max_ctx + pos) * HD + d0]) = o;
+      *reinterpret_cast<uint2*>(&p.k_cache[((cm * nkv + (head - nq)) * p.max_ctx + pos) * HD + d0]) = o;
   }
 }
 

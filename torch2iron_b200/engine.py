@@ -213,6 +213,13 @@ class DecodeEngine:
                                                       cfg.emb_dim, cfg.vocab_size, st))
         for li in range(cfg.n_layers):
             self.enqueue_layer(li, st)
+        self._enqueue_head(st)
+
+    def _enqueue_head(self, st) -> None:
+        """Final RMSNorm of ``x`` (with ``ssq_a``) and the greedy lm_head into ``next_tokens``."""
+        cfg, B = self.cfg, self.B
+        L = _lib.lib()
+        p = _lib.ptr
         _lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
                                                             cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
         if self.lm_w4 is None:
@@ -294,8 +301,108 @@ class DecodeEngine:
         self.check_device_errors()
         return out
 
+    # -- chunked prefill (prefill_runtime.py:95-164, for B sequences at once) --
+    PREFILL_ROWS = 8192      # prompt tokens (all sequences) per chunk by default
+
+    def _prefill_buffers(self, rows: int) -> dict:
+        """Activations and workspaces for a chunk of ``rows`` prompt tokens (kept for reuse)."""
+        pf = getattr(self, "_pf", None)
+        if pf is not None and pf["rows"] >= rows:
+            return pf
+        cfg, dev = self.cfg, self.device
+        H, f32, bf, i32 = cfg.emb_dim, torch.float32, torch.bfloat16, torch.int32
+        L = _lib.load()
+        nq, nkv, hd = cfg.n_heads, cfg.n_kv_groups, cfg.head_dim
+        sizes = {"qkv": L.t2b_qkv_workspace_bytes(rows, H, nq, nkv, hd),
+                 "o": L.t2b_oproj_residual_workspace_bytes(rows, H, cfg.q_dim),
+                 "ug": L.t2b_upgate_swiglu_workspace_bytes(rows, H, cfg.hidden_dim),
+                 "down": L.t2b_down_residual_workspace_bytes(rows, H, cfg.hidden_dim)}
+        pf = {"rows": rows,
+              "x": torch.zeros(rows, H, dtype=f32, device=dev), "xw": torch.zeros(rows, H, dtype=bf, device=dev),
+              "ssq_a": torch.zeros(rows, dtype=f32, device=dev), "ssq_b": torch.zeros(rows, dtype=f32, device=dev),
+              "q": torch.zeros(rows, cfg.q_dim, dtype=bf, device=dev),
+              "attn": torch.zeros(rows, cfg.q_dim, dtype=bf, device=dev),
+              "h": torch.zeros(rows, cfg.hidden_dim, dtype=bf, device=dev),
+              "tokens": torch.zeros(rows, dtype=i32, device=dev), "pos": torch.zeros(rows, dtype=i32, device=dev),
+              "seq": torch.zeros(rows, dtype=i32, device=dev),
+              "ws": {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256))
+                     for k, v in sizes.items()}}
+        self._pf = pf
+        return pf
+
+    def enqueue_prefill_chunk(self, pf: dict, n: int, c0: int, st) -> None:
+        """One chunk: tokens ``c0 .. c0+n-1`` of every sequence (rows ``b*n + i``
+        of ``pf``, already holding tokens / pos / seq) through all layers."""
+        cfg, B = self.cfg, self.B
+        M = B * n
+        H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
+        L = _lib.lib()
+        p = _lib.ptr
+
+        def ws(k):
+            t, nb = pf["ws"][k]
+            return p(t), nb
+
+        x, xw, sa, sb = pf["x"], pf["xw"], pf["ssq_a"], pf["ssq_b"]
+        _lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(pf["tokens"]), p(x), p(sa),
+                                                      p(self.layers[0].input_layernorm), p(xw), M, H,
+                                                      cfg.vocab_size, st))
+        for li, lw in enumerate(self.layers):
+            _lib.check("t2b_qkv_norm_rope_kvwrite_seq", L.t2b_qkv_norm_rope_kvwrite_seq(
+                p(lw.qkv.qw), p(lw.qkv.meta), p(xw), p(sa), cfg.rms_norm_eps, p(lw.q_norm), p(lw.k_norm),
+                p(self.angles), p(pf["pos"]), p(pf["seq"]), p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]),
+                p(sb), M, H, nq, nkv, hd, self.max_ctx, *ws("qkv"), st))
+            _lib.check("t2b_prefill_attention", L.t2b_prefill_attention(
+                p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]), p(pf["attn"]), B, n, c0, nq, nkv, hd,
+                self.max_ctx, st))
+            _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
+                p(lw.o_proj.qw), p(lw.o_proj.meta), p(pf["attn"]), p(x), p(sb), p(lw.post_attention_layernorm),
+                p(xw), M, H, cfg.q_dim, *ws("o"), st))
+            _lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
+                p(lw.gate_up.qw), p(lw.gate_up.meta), p(xw), p(sb), cfg.rms_norm_eps, p(pf["h"]), p(sa), M, H,
+                cfg.hidden_dim, *ws("ug"), st))
+            _lib.check("t2b_down_residual", L.t2b_down_residual(
+                p(lw.down.qw), p(lw.down.meta), p(pf["h"]), p(x), p(sa), p(self.next_norm_weight(li)), p(xw), M,
+                H, cfg.hidden_dim, *ws("down"), st))
+
+    def prefill_chunked(self, prompts: torch.Tensor, chunk: int | None = None) -> None:
+        """Fill the KV caches from ``prompts [B, P]`` in chunks of ``chunk`` tokens per
+        sequence: every linear runs over all ``B * chunk`` tokens at once and
+        attention is causal within and before the chunk (``t2b_prefill_attention``).
+
+        Leaves ``next_tokens`` = the greedy token after the prompt (``logits`` for
+        it with ``keep_logits``), and ``tokens``/``pos`` ready for ``advance()``.
+        """
+        B, P = prompts.shape
+        if B != self.B:
+            raise ValueError(f"prompts hold {B} sequences, the engine {self.B}")
+        if P < 1 or P > self.max_ctx:
+            raise ValueError(f"prompt length {P} outside 1..{self.max_ctx}")
+        C = chunk or max(1, min(P, self.PREFILL_ROWS // B))
+        pf = self._prefill_buffers(B * min(C, P))
+        prompts = prompts.to(self.device, torch.int32)
+        st = _lib.stream()
+        _lib.lib().t2b_set_error_word(_lib.ptr(self.err))
+        dev = self.device
+        seq_all = torch.arange(B, dtype=torch.int32, device=dev)
+        for c0 in range(0, P, C):
+            n = min(C, P - c0)
+            M = B * n
+            pf["tokens"][:M].copy_(prompts[:, c0:c0 + n].reshape(-1))
+            pf["pos"][:M].copy_((torch.arange(n, dtype=torch.int32, device=dev) + c0).repeat(B))
+            pf["seq"][:M].copy_(seq_all.repeat_interleave(n))
+            self.enqueue_prefill_chunk(pf, n, c0, st)
+        # the last prompt token of every sequence feeds the greedy head
+        last = seq_all.to(torch.int64) * n + (n - 1)
+        self.x.copy_(pf["x"].index_select(0, last))
+        self.ssq_a.copy_(pf["ssq_a"].index_select(0, last))
+        self._enqueue_head(st)
+        self.tokens.copy_(self.next_tokens)
+        self.pos.fill_(P)
+
     def prefill(self, prompts: torch.Tensor) -> None:
-        """Fill the KV caches by stepping through ``prompts [B, P]`` (teacher forcing).
+        """Fill the KV caches by stepping through ``prompts [B, P]`` one position at a
+        time with the decode step (teacher forcing).
 
         Leaves ``next_tokens`` = the greedy token after the prompt, and
         ``tokens``/``pos`` ready for ``advance()``.
