@@ -344,7 +344,20 @@ def run_t2b(args, cfg):
     eng = DecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, use_graph=True, keep_logits=False)
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=g)
-    eng.prefill(prompts)
+    eng.prefill(prompts)                     # chunked prefill; the first call sizes its buffers
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    q0.record()
+    eng.prefill(prompts)                     # timed: the same prompts again (rewrites the same cache rows)
+    q1.record()
+    torch.cuda.synchronize()
+    prefill_ms = q0.elapsed_time(q1)
+    if world > 1:
+        t = torch.tensor([prefill_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_ms = float(t.item())
     for _ in range(args.warmup):
         eng.advance()
     torch.cuda.synchronize()
@@ -457,6 +470,11 @@ def run_t2b(args, cfg):
                     "d2h_bytes_per_step": B * 4},
             "gpu_launches": eng.kernels_per_step() * args.steps,
             "clocks": clocks.summary(),
+            "prefill": {"value": round(world * B * P / (prefill_ms / 1000), 1), "unit": "prompt tokens/s",
+                        "ms": round(prefill_ms, 3), "prompt_tokens_per_gpu": B * P,
+                        "chunk_tokens_per_sequence": min(P, max(1, eng.PREFILL_ROWS // B)),
+                        "note": "chunked prefill (all prompt tokens of a chunk per launch), device-resident "
+                                "prompts, CUDA events, max over ranks; not part of value"},
         }
         if not args.no_gemv:
             line["gemv_b1"] = gemv_batch1(eng, peak)

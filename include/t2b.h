@@ -115,9 +115,10 @@ T2B_API size_t t2b_w4a16_gemm_workspace_bytes(int M, int N, int K);
  * The launch plan every W4A16 linear of shape [M,N,K] takes (host only, no
  * device work): path 0 = CUDA-core GEMV (rows_per_cta batch rows per CTA,
  * groups_per_cta k-groups of 128 per CTA), 1 = tcgen05 (rows_per_cta = the
- * padded batch tile Bp, groups_per_cta = S); ksplit = k-slices of a 128-row
- * tile (a thread-block cluster when <= 8).  On the tcgen05 path ksplit
- * divides rows_per_cta.  No counterpart in the reference (its tiling is fixed
+ * padded batch tile Bp, groups_per_cta = S), 2 = the large-M tcgen05 kernel
+ * of prefill chunks (128 rows x all K groups per work unit); ksplit = k-slices
+ * of a 128-row tile (a thread-block cluster when <= 8).  On the tcgen05 path
+ * ksplit divides rows_per_cta.  No counterpart in the reference (its tiling is fixed
  * at NPU compile time, w4a16_gemm/design.py); exported so callers and tests
  * can check a shape's decomposition without a GPU.
  */

@@ -227,8 +227,11 @@ def test_tiny_model_matches_reference_generate():
     eng.prefill(prompt)
     torch.cuda.synchronize()
     assert max_abs(eng.logits[0], torch.from_numpy(d["logits_last"])) <= 2e-2
+    # exact tokens through the batch-1 decode path (the first pick has a 0.011
+    # top-2 margin, below the logit bar, so only the fp32-exact GEMV path that
+    # one-token steps take is held to equality)
     eng2 = DecodeEngine(cfg, model, batch=1, max_ctx=64, use_graph=True)
-    gen = eng2.generate(prompt, 8).cpu()
+    gen = eng2.generate(prompt, 8, stepwise_prefill=True).cpu()
     assert torch.equal(gen[0].long(), torch.from_numpy(d["generated"]).long())
 
 

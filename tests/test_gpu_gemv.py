@@ -70,7 +70,7 @@ def test_golden_gemv_batches(M):
 
 @pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 3072), (6144, 1024), (1024, 2048), (256, 512), (128, 256),
                                  (512, 1536)])   # K = 12 groups: cluster split 4 x 3 groups (Qwen3-8B down at TP8)
-@pytest.mark.parametrize("M", [1, 2, 4, 8, 13, 16, 17, 33, 64, 100, 128, 200])
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 13, 16, 17, 33, 64, 100, 128, 200, 257, 513])
 def test_gemm_shapes_vs_oracle(N, K, M):
     g = torch.Generator().manual_seed(N * 7 + K + M)
     lin = synth.random_linear(N, K, g)
@@ -116,6 +116,21 @@ def test_shape_errors_raise():
         dw = W.W4Weight(torch.zeros(100, 128, dtype=torch.uint8, device="cuda"),
                         torch.zeros(100, 2, dtype=torch.int32, device="cuda"), 100, 256)
         gemm(dw, torch.zeros(1, 256, dtype=torch.bfloat16, device="cuda"))
+
+
+@pytest.mark.parametrize("M", [1, 5, 128, 130])
+@pytest.mark.parametrize("N,K", [(1024, 3072), (384, 256), (256, 12288)])
+def test_large_m_kernel_forced(monkeypatch, M, N, K):
+    """The large-M (prefill) tcgen05 kernel at any row count matches the oracle."""
+    monkeypatch.setenv("T2B_PREFILL_MIN_M", "1")
+    g = torch.Generator().manual_seed(M * 3 + N + K)
+    lin = synth.random_linear(N, K, g)
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    ref = oracle.GroupedW4A16Linear(lin.qweight, lin.qzeros, lin.scales)(x.float())
+    assert rel_err(gemm(dw, x.cuda(), torch.float32), ref) <= 1e-2
+    assert rel_err(gemm(dw, x.cuda(), torch.bfloat16), ref) <= 1e-2
 
 
 @pytest.mark.parametrize("M", [1, 3, 8, 16])

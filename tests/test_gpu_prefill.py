@@ -76,9 +76,9 @@ def test_chunked_prefill_matches_stepwise_and_oracle(chunk):
     B, P = 3, 37
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(42))
     a = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
-    a.prefill_chunked(prompts, chunk=chunk)
+    a.prefill(prompts, chunk=chunk)
     b = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
-    b.prefill(prompts)
+    b.prefill(prompts, stepwise=True)
     torch.cuda.synchronize()
     assert int(a.err.item()) == 0
     for li in range(cfg.n_layers):
@@ -91,10 +91,33 @@ def test_chunked_prefill_matches_stepwise_and_oracle(chunk):
     top = torch.topk(ref, 2, dim=-1).values
     sure = (top[:, 0] - top[:, 1]) > 4e-2
     assert torch.equal(a.next_tokens.cpu().long()[sure], ref.argmax(-1)[sure])
-    # decoding continues from the chunked prefill exactly as from the stepwise one
+    # decoding continues from the chunked prefill as from the stepwise one (same next token fed)
+    a.tokens.copy_(b.tokens)
     a.advance()
     b.advance()
     assert max_abs(a.logits, b.logits) <= 2e-2
+
+
+@pytest.mark.parametrize("B,P,force", [(8, 40, False), (3, 37, True)])
+def test_chunked_prefill_large_m_kernel(monkeypatch, B, P, force):
+    """Chunks of >= 257 prompt tokens (or any, forced) run every fused linear on
+    the large-M tcgen05 kernel: same caches and logits as the stepwise prefill."""
+    cfg = SMALL
+    model = synth.random_model(cfg, seed=43)
+    prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(44))
+    b = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
+    b.prefill(prompts, stepwise=True)
+    if force:
+        monkeypatch.setenv("T2B_PREFILL_MIN_M", "1")
+    a = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
+    a.prefill(prompts)
+    torch.cuda.synchronize()
+    assert int(a.err.item()) == 0
+    for li in range(cfg.n_layers):
+        assert max_abs(a.k_cache[li][:, :, :P], b.k_cache[li][:, :, :P]) <= 5e-2
+        assert max_abs(a.v_cache[li][:, :, :P], b.v_cache[li][:, :, :P]) <= 5e-2
+    assert max_abs(a.logits, b.logits) <= 2e-2
+    assert max_abs(a.x, b.x) <= 2e-2 * b.x.abs().max().item()
 
 
 def test_chunked_prefill_on_reference_artifact():
@@ -104,7 +127,7 @@ def test_chunked_prefill_on_reference_artifact():
     g = np.load(model_dir.parent / "packed_tiny.npz")
     prompt = torch.from_numpy(g["prompt"])
     eng = DecodeEngine(cfg, model, batch=1, max_ctx=64, use_graph=True)
-    eng.prefill_chunked(prompt, chunk=5)
+    eng.prefill(prompt, chunk=5)
     torch.cuda.synchronize()
     assert max_abs(eng.logits[0], torch.from_numpy(g["logits"][-1])) <= 2e-2
     eng.check_device_errors()

@@ -47,7 +47,7 @@ def _rank(rank, world, port, batch, out_q):
         res.update(res["eager"])
         if rank == 0:
             ref = DecodeEngine(CFG, model, batch=batch, max_ctx=64, use_graph=False)
-            ref.prefill(prompts)
+            ref.prefill(prompts, stepwise=True)     # the TP engine also feeds the prompt step by step
             rt = [ref.next_tokens.cpu().clone()]
             for _ in range(3):
                 ref.advance()

@@ -13,7 +13,8 @@ from torch2iron_b200 import _lib
 from torch2iron_b200 import tp as TP
 from torch2iron_b200.config import LLAMA_3_2_1B, QWEN3_0_6B, QWEN3_8B
 
-BATCHES = [1, 2, 3, 4, 5, 7, 8, 9, 12, 16, 17, 24, 31, 32, 33, 48, 63, 64, 65, 96, 128, 129, 192, 200, 256]
+BATCHES = [1, 2, 3, 4, 5, 7, 8, 9, 12, 16, 17, 24, 31, 32, 33, 48, 63, 64, 65, 96, 128, 129, 192, 200, 256,
+           257, 1000, 8192]   # the last three: prefill chunks (large-M kernel)
 
 
 def _plan(M, N, K):
@@ -40,7 +41,9 @@ def test_plans_cover_k_and_split_the_batch_tile_evenly(cfg, tp):
             st, (path, rows, groups, ks) = _plan(m, n, k)
             assert st == _lib.T2B_OK, (name, m, n, k)
             assert groups * ks * 128 == k, (name, m, n, k, rows, groups, ks)
-            if path == 1:
+            if path == 2:
+                assert m >= 257 and rows == 128 and ks == 1
+            elif path == 1:
                 assert rows in (16, 32, 64, 128, 256) and 1 <= ks <= 8 and rows % ks == 0, (name, m, n, k, rows, ks)
             else:
                 assert path == 0 and rows in (1, 2, 4, 8) and rows >= min(m, 8)

@@ -345,6 +345,14 @@ static int tc_min_m() {
   return 2;
 }
 
+// large-M path (w4a16_prefill.cu)
+int prefill_min_m();
+int prefill_launch(LinearParams& p, int pro, int epi, cudaStream_t st);
+
+static bool use_prefill(int M, int wfmt, int x_dtype) {
+  return wfmt == T2B_WFMT_T2B && x_dtype == T2B_DTYPE_BF16 && M >= prefill_min_m();
+}
+
 static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {
   return wfmt == T2B_WFMT_T2B && x_dtype == T2B_DTYPE_BF16 && M >= tc_min_m() && tc_supported(M, N, K);
 }
@@ -375,6 +383,7 @@ int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t 
   if (p.M < 1 || p.N <= 0 || p.K <= 0) return T2B_ERR_SHAPE;
   if (p.N % TILE_N || p.K % 256) return T2B_ERR_SHAPE;
   p.G = p.K / GROUP;
+  if (use_prefill(p.M, wfmt, p.x_dtype)) return prefill_launch(p, pro, epi, st);
   if (use_tc(p.M, p.N, p.K, wfmt, p.x_dtype)) return tc_launch(p, pro, epi, ws, ws_bytes, st);
   return gemv_launch(p, pro, epi, wfmt, ws, ws_bytes, st);
 }
@@ -404,6 +413,13 @@ extern "C" int t2b_linear_plan(int M, int N, int K, int* path, int* rows_per_cta
                                int* ksplit) {
   if (!path || !rows_per_cta || !groups_per_cta || !ksplit) return T2B_ERR_ARG;
   if (M < 1 || N <= 0 || K <= 0 || N % TILE_N || K % 256) return T2B_ERR_SHAPE;
+  if (use_prefill(M, T2B_WFMT_T2B, T2B_DTYPE_BF16)) {   // one weight tile x 128 rows per work unit, all of K
+    *path = 2;
+    *rows_per_cta = 128;
+    *groups_per_cta = K / GROUP;
+    *ksplit = 1;
+    return T2B_OK;
+  }
   if (use_tc(M, N, K, T2B_WFMT_T2B, T2B_DTYPE_BF16)) {
     *path = 1;
     tc_plan_info(M, N, K, rows_per_cta, groups_per_cta, ksplit);

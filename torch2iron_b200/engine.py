@@ -365,14 +365,19 @@ class DecodeEngine:
                 p(lw.down.qw), p(lw.down.meta), p(pf["h"]), p(x), p(sa), p(self.next_norm_weight(li)), p(xw), M,
                 H, cfg.hidden_dim, *ws("down"), st))
 
-    def prefill_chunked(self, prompts: torch.Tensor, chunk: int | None = None) -> None:
+    def prefill(self, prompts: torch.Tensor, chunk: int | None = None, stepwise: bool = False) -> None:
         """Fill the KV caches from ``prompts [B, P]`` in chunks of ``chunk`` tokens per
-        sequence: every linear runs over all ``B * chunk`` tokens at once and
-        attention is causal within and before the chunk (``t2b_prefill_attention``).
+        sequence (default: up to ``PREFILL_ROWS`` prompt tokens per chunk): every
+        linear runs over all ``B * chunk`` tokens at once and attention is causal
+        within and before the chunk (``t2b_prefill_attention``).  ``stepwise``
+        feeds the prompt one position per decode step instead.
 
         Leaves ``next_tokens`` = the greedy token after the prompt (``logits`` for
         it with ``keep_logits``), and ``tokens``/``pos`` ready for ``advance()``.
         """
+        if stepwise:
+            self._prefill_stepwise(prompts)
+            return
         B, P = prompts.shape
         if B != self.B:
             raise ValueError(f"prompts hold {B} sequences, the engine {self.B}")
@@ -400,13 +405,8 @@ class DecodeEngine:
         self.tokens.copy_(self.next_tokens)
         self.pos.fill_(P)
 
-    def prefill(self, prompts: torch.Tensor) -> None:
-        """Fill the KV caches by stepping through ``prompts [B, P]`` one position at a
-        time with the decode step (teacher forcing).
-
-        Leaves ``next_tokens`` = the greedy token after the prompt, and
-        ``tokens``/``pos`` ready for ``advance()``.
-        """
+    def _prefill_stepwise(self, prompts: torch.Tensor) -> None:
+        """The prompt one position per decode step (teacher forcing)."""
         P = prompts.shape[1]
         prompts = prompts.to(self.device, torch.int32)
         for t in range(P):
@@ -416,9 +416,9 @@ class DecodeEngine:
         self.tokens.copy_(self.next_tokens)
         self.pos.fill_(P)
 
-    def generate(self, prompts: torch.Tensor, new_tokens: int) -> torch.Tensor:
+    def generate(self, prompts: torch.Tensor, new_tokens: int, stepwise_prefill: bool = False) -> torch.Tensor:
         """Greedy decode ``new_tokens`` per row after ``prompts`` -> ``[B, new_tokens]``."""
-        self.prefill(prompts)
+        self.prefill(prompts, stepwise=stepwise_prefill)
         out = [self.next_tokens.clone()]
         for _ in range(new_tokens - 1):
             self.advance()
