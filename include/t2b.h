@@ -158,12 +158,15 @@ T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int
  * 2x RMSNormRoPE + CopyPresentPacketKV (batch_decode_fused.py:426-474).
  */
 T2B_API size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, int head_dim);
-/* Same, with row m writing its K/V into cache sequence row_seq[m] (a prefill
- * chunk: rows b*C + i of B sequences, pos[m] = p0 + i) instead of sequence m. */
+/* Same, with row m writing its K/V into cache sequence row_seq[m] of n_seq
+ * (a prefill chunk: rows b*C + i of B sequences, pos[m] = p0 + i) instead of
+ * sequence m; caches bf16 [n_seq][n_kv][max_ctx][head_dim].  A row whose
+ * sequence is outside [0, n_seq) or position outside [0, max_ctx) writes no
+ * cache entry. */
 T2B_API int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
                                           const float* ssq, float eps, const uint16_t* q_norm_w,
                                           const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
-                                          const int32_t* row_seq, uint16_t* q_out, uint16_t* k_cache,
+                                          const int32_t* row_seq, int n_seq, uint16_t* q_out, uint16_t* k_cache,
                                           uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
                                           int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
                                           void* stream);

@@ -37,7 +37,7 @@ SIGNATURES = {
     "t2b_w4a16_gemm_noalloc": (I, [P, P, I, P, I, P, I, I, I, I, I, P]),
     "t2b_qkv_workspace_bytes": (Z, [I, I, I, I, I]),
     "t2b_qkv_norm_rope_kvwrite": (I, [P, P, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
-    "t2b_qkv_norm_rope_kvwrite_seq": (I, [P, P, P, P, F, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_qkv_norm_rope_kvwrite_seq": (I, [P, P, P, P, F, P, P, P, P, P, I, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_prefill_attention": (I, [P, P, P, P, I, I, I, I, I, I, I, P]),
     "t2b_decode_attention_workspace_bytes": (Z, [I, I, I, I, I]),
     "t2b_decode_attention": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),

@@ -53,6 +53,7 @@ struct LinearParams {
   const float* angles;
   const int* pos;
   const int* row_seq;     // EPI_QKV: cache sequence of each row (nullptr: row m writes sequence m)
+  int n_seq;              // EPI_QKV with row_seq: sequences in the cache (others write nothing)
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
   int n_heads, n_kv, head_dim, max_ctx;
@@ -120,10 +121,11 @@ T2B_DEV float4 unpack_bf16x4(uint2 v) {
 }
 
 template <int HD>
-T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile, int m0, int MB, const EpiCache& ec) {
+T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile, int m0, int MB, const EpiCache& ec,
+                          int t, int nt) {
   constexpr int HPT = TILE_N / HD;    // heads per tile
   constexpr int LPH = HD / 4;         // lanes per head
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = t >> 5, lane = t & 31, nwarps = nt >> 5;
   const int hl = lane / LPH, d0 = (lane % LPH) * 4;
   const int head = tile * HPT + hl;
   const int nq = p.n_heads, nkv = p.n_kv;
@@ -132,7 +134,7 @@ T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile
   if (is_v) nw = nullptr;
   const float4 w = nw ? unpack_bf16x4(*reinterpret_cast<const uint2*>(nw + d0)) : make_float4(1.f, 1.f, 1.f, 1.f);
   __nv_bfloat16* q_out = reinterpret_cast<__nv_bfloat16*>(p.y);
-  for (int b = warp; b < MB; b += 8) {
+  for (int b = warp; b < MB; b += nwarps) {
     const int m = m0 + b;
     if (m >= p.M) break;  // warp-uniform
     const float4 x = *reinterpret_cast<const float4*>(tile_acc + b * TILE_N + lane * 4);
@@ -140,8 +142,11 @@ T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile
 #pragma unroll
     for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const int pos = ec.pos ? ec.pos[b] : p.pos[m];
-    const bool in_cache = pos >= 0 && pos < p.max_ctx;   // a bad position writes no cache entry
-    const size_t cm = p.row_seq ? (size_t)__ldg(p.row_seq + m) : (size_t)m;   // cache sequence of row m
+    const int sq = p.row_seq ? __ldg(p.row_seq + m) : m;   // cache sequence of row m
+    // a bad position or sequence writes no cache entry
+    const bool pos_ok = pos >= 0 && pos < p.max_ctx;
+    const bool in_cache = pos_ok && (!p.row_seq || (sq >= 0 && sq < p.n_seq));
+    const size_t cm = (size_t)sq;
     if (is_v) {  // value head: stored as projected (model.py:250,263)
       if (in_cache)
         *reinterpret_cast<uint2*>(&p.v_cache[((cm * nkv + (head - nq - nkv)) * p.max_ctx + pos) * HD + d0]) =
@@ -153,7 +158,7 @@ T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile
     const float x0 = x.x * rs * w.x, x1 = x.y * rs * w.y, x2 = x.z * rs * w.z, x3 = x.w * rs * w.w;
     // interleaved RoPE (model.py:184-196): (x0, x1) -> (x0 c - x1 s, x1 c + x0 s)
     const float4 cs = *reinterpret_cast<const float4*>(
-        ec.angles ? ec.angles + (size_t)b * HD + d0 : p.angles + (size_t)(in_cache ? pos : 0) * HD + d0);
+        ec.angles ? ec.angles + (size_t)b * HD + d0 : p.angles + (size_t)(pos_ok ? pos : 0) * HD + d0);
     const uint2 o = pack_bf16x4(x0 * cs.x - x1 * cs.y, x1 * cs.x + x0 * cs.y, x2 * cs.z - x3 * cs.w,
                                 x3 * cs.z + x2 * cs.w);
     if (is_q)
@@ -169,14 +174,16 @@ T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile
 // takes 4 consecutive outputs (the residual stream and h are 16- / 8-byte
 // aligned with row strides of multiples of 4, checked at the C ABI).
 // ---------------------------------------------------------------------------
+// Threads t = 0..nt-1 (whole warps; default: the CTA's 256 threads) share the work.
 template <int EPI>
 T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* scratch, int tile, int m0, int MB,
-                           const EpiCache& ec = EpiCache{}) {
-  constexpr int NT = 256;
-  const int lane = threadIdx.x & 31;
+                           const EpiCache& ec = EpiCache{}, int t = -1, int nt = 256) {
+  if (t < 0) t = threadIdx.x;
+  const int NT = nt;
+  const int lane = t & 31;
   const int row0 = tile * TILE_N;
   if (EPI == EPI_STORE) {
-    for (int idx = threadIdx.x; idx < MB * TILE_N; idx += NT) {
+    for (int idx = t; idx < MB * TILE_N; idx += NT) {
       const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
       if (m < p.M) store_act(p.y, p.y_dtype, (size_t)m * p.y_ld + row0 + lr, tile_acc[idx]);
     }
@@ -184,7 +191,7 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
     // x += y ; sum of squares for the next RMSNorm ; bf16(x * w_next) for its GEMM.
     // A warp's 128 elements are one batch row of the tile -> one atomic per warp per pass.
     for (int base = 0; base < MB * TILE_N; base += NT * 4) {
-      const int idx = base + threadIdx.x * 4;
+      const int idx = base + t * 4;
       const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
       const bool live = idx < MB * TILE_N && m < p.M;
       float sq = 0.f;
@@ -207,7 +214,7 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
   } else if (EPI == EPI_SWIGLU) {
     // tile = 64 gate rows then the matching 64 up rows (model.py:215-216)
     __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.y);
-    for (int idx = threadIdx.x * 4; idx < MB * 64; idx += NT * 4) {
+    for (int idx = t * 4; idx < MB * 64; idx += NT * 4) {
       const int b = idx >> 6, t = idx & 63, m = m0 + b;
       if (m < p.M) {
         const float4 g = *reinterpret_cast<const float4*>(tile_acc + b * TILE_N + t);
@@ -218,8 +225,8 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
       }
     }
   } else {  // EPI_QKV
-    if (p.head_dim == 128) qkv_epilogue<128>(p, tile_acc, tile, m0, MB, ec);
-    else qkv_epilogue<64>(p, tile_acc, tile, m0, MB, ec);
+    if (p.head_dim == 128) qkv_epilogue<128>(p, tile_acc, tile, m0, MB, ec, t, nt);
+    else qkv_epilogue<64>(p, tile_acc, tile, m0, MB, ec, t, nt);
   }
 }
 

@@ -472,9 +472,9 @@ extern "C" size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, i
 
 static int qkv_impl(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq, float eps,
                     const uint16_t* q_norm_w, const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
-                    const int32_t* row_seq, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, float* ssq_clear,
-                    int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws, size_t ws_bytes,
-                    void* stream) {
+                    const int32_t* row_seq, int n_seq, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
+                    float* ssq_clear, int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
+                    size_t ws_bytes, void* stream) {
   if (head_dim != 64 && head_dim != 128) return T2B_ERR_SHAPE;
   if (n_kv < 1 || n_heads % n_kv || max_ctx < 1) return T2B_ERR_SHAPE;
   if (!qw || !meta || !xw || !ssq || !angles || !pos || !q_out || !k_cache || !v_cache) return T2B_ERR_ARG;
@@ -498,6 +498,7 @@ static int qkv_impl(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
   p.angles = angles;
   p.pos = pos;
   p.row_seq = row_seq;
+  p.n_seq = n_seq;
   p.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache);
   p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache);
   p.n_heads = n_heads;
@@ -513,19 +514,20 @@ extern "C" int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta
                                          uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, float* ssq_clear,
                                          int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
                                          size_t ws_bytes, void* stream) {
-  return qkv_impl(qw, meta, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, nullptr, q_out, k_cache, v_cache,
+  return qkv_impl(qw, meta, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, nullptr, M, q_out, k_cache, v_cache,
                   ssq_clear, M, H, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes, stream);
 }
 
 extern "C" int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
                                              const float* ssq, float eps, const uint16_t* q_norm_w,
                                              const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
-                                             const int32_t* row_seq, uint16_t* q_out, uint16_t* k_cache,
-                                             uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads,
-                                             int n_kv, int head_dim, int max_ctx, void* ws, size_t ws_bytes,
-                                             void* stream) {
+                                             const int32_t* row_seq, int n_seq, uint16_t* q_out,
+                                             uint16_t* k_cache, uint16_t* v_cache, float* ssq_clear, int M, int H,
+                                             int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
+                                             size_t ws_bytes, void* stream) {
   if (!row_seq) return T2B_ERR_ARG;
-  return qkv_impl(qw, meta, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, row_seq, q_out, k_cache, v_cache,
+  if (n_seq < 1) return T2B_ERR_SHAPE;
+  return qkv_impl(qw, meta, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, row_seq, n_seq, q_out, k_cache, v_cache,
                   ssq_clear, M, H, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes, stream);
 }
 

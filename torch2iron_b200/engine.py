@@ -350,7 +350,7 @@ class DecodeEngine:
         for li, lw in enumerate(self.layers):
             _lib.check("t2b_qkv_norm_rope_kvwrite_seq", L.t2b_qkv_norm_rope_kvwrite_seq(
                 p(lw.qkv.qw), p(lw.qkv.meta), p(xw), p(sa), cfg.rms_norm_eps, p(lw.q_norm), p(lw.k_norm),
-                p(self.angles), p(pf["pos"]), p(pf["seq"]), p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]),
+                p(self.angles), p(pf["pos"]), p(pf["seq"]), B, p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]),
                 p(sb), M, H, nq, nkv, hd, self.max_ctx, *ws("qkv"), st))
             _lib.check("t2b_prefill_attention", L.t2b_prefill_attention(
                 p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]), p(pf["attn"]), B, n, c0, nq, nkv, hd,
