@@ -54,6 +54,8 @@ def parse():
                          "the batch is then the global batch")
     ap.add_argument("--ctx", type=int, default=4096, help="--tp: KV cache pre-filled to this many positions")
     ap.add_argument("--tp-eager", action="store_true", help="--tp: launch every step eagerly (no CUDA graph)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="one GPU: time the chunked prefill of --batch x --prompt tokens only (profiling case)")
     return ap.parse_args()
 
 
@@ -623,7 +625,35 @@ def main():
     if args.tp:
         run_tp(args, cfg)
         return
+    if args.prefill_only:
+        run_prefill_only(args, cfg)
+        return
     run_t2b(args, cfg)
+
+
+def run_prefill_only(args, cfg):
+    """The chunked prefill alone (no decode, no CPU baseline): one untimed call,
+    then --steps timed calls; prints one JSON line."""
+    from torch2iron_b200.engine import DecodeEngine
+
+    B, P = args.batch, args.prompt
+    max_ctx = ((P + 63) // 64) * 64
+    model = synth.random_model(cfg, seed=args.seed, device="cuda")
+    eng = DecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, use_graph=False, keep_logits=False)
+    prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(args.seed))
+    eng.prefill(prompts)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        eng.prefill(prompts)
+    e1.record()
+    torch.cuda.synchronize()
+    eng.check_device_errors()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"metric": "prefill prompt tokens/s", "value": round(B * P / (ms / 1000), 1),
+                      "unit": "prompt tokens/s", "ms": round(ms, 3), "model": args.model, "batch": B, "prompt": P,
+                      "steps": args.steps}), flush=True)
 
 
 if __name__ == "__main__":

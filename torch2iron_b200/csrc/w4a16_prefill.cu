@@ -4,20 +4,21 @@
 // Work unit: one 128-row weight tile (n) x one block of BM = 128 activation
 // rows (m), over all K.  Persistent CTAs (one per SM) walk the units with the
 // weight tile fastest, so the CTAs running at once share an activation block.
-// Warp roles (320 threads), each a pipeline stage joined by mbarriers:
-//   * warp 10, weights: one bulk copy per group of the tile's raw int4 block
+// Warp roles (480 threads), each a pipeline stage joined by mbarriers:
+//   * warp 14, weights: one bulk copy per group of the tile's raw int4 block
 //     (8 KB) and meta (512 B) into a ring of NR shared-memory stages
 //     (constant data: this runs ahead of the dependency wait);
-//   * warps 0-3, producers: thread = TMEM lane = weight row; per group they
-//     read the row's nibbles and meta from the raw stage, dequantise to bf16
-//     (q - z) * s pairs (the decode kernel's arithmetic) and tcgen05.st them
-//     into a ring of NA TMEM A stages;
-//   * warp 8, TMA: the activations of each group (two 64-k x BM-row boxes,
+//   * warps 0-7, producers: warp w covers TMEM lane quarter w % 4 (weight
+//     rows) and the 64-k half w / 4 of each group: it reads its rows' nibbles
+//     and meta from the raw stage, dequantises to bf16 (q - z) * s pairs (the
+//     decode kernel's arithmetic) and tcgen05.st's them into a ring of NA
+//     TMEM A stages (two warps per scheduler hide the dequant latency);
+//   * warp 12, TMA: the activations of each group (two 64-k x BM-row boxes,
 //     128-byte swizzle = the UMMA K-major layout) into a ring of NX stages;
-//   * warp 9, MMA: 8 tcgen05.mma (M 128, N BM, K 16, A from TMEM) per group
+//   * warp 13, MMA: 8 tcgen05.mma (M 128, N BM, K 16, A from TMEM) per group
 //     into one of two fp32 TMEM accumulators, freeing A and X stages by
 //     tcgen05.commit;
-//   * warps 4-7, epilogue: drain the other accumulator (times the RMSNorm row
+//   * warps 8-11, epilogue: drain the other accumulator (times the RMSNorm row
 //     scale) into shared memory and run the decode path's fused epilogue
 //     (linear_common.cuh) on the [BM][128] tile, while the MMAs of the next
 //     unit run.
@@ -41,8 +42,8 @@ constexpr int PF_NX = 3;                 // activation stages
 constexpr int PF_NA = 4;                 // TMEM A stages (64 columns each)
 constexpr int PF_NR = 4;                 // raw weight stages
 constexpr int PF_RAW = BLOCK_BYTES + TILE_N * 4;   // int4 block + meta of one (tile, group)
-constexpr int PF_GT = 352;               // threads: 4 producer, 4 epilogue, TMA, MMA, weight warps
-constexpr int PF_EPI_T0 = 128;           // first epilogue thread
+constexpr int PF_GT = 480;               // threads: 8 producer, 4 epilogue, TMA, MMA, weight warps
+constexpr int PF_EPI_T0 = 256;           // first epilogue thread
 constexpr uint32_t PF_TMEM_COLS = 512;   // accumulators [0, 2*BM), A stages from column 2*BM
 constexpr uint32_t PF_A0 = 2 * PF_BM;
 
@@ -213,12 +214,12 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       mbar_init(&x_empty[i], 1);
     }
     for (int i = 0; i < PF_NA; ++i) {
-      mbar_init(&a_full[i], 4);     // one arrival per producer warp
+      mbar_init(&a_full[i], 8);     // one arrival per producer warp
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < PF_NR; ++i) {
       mbar_init(&w_full[i], 1);
-      mbar_init(&w_empty[i], 4);    // one arrival per producer warp
+      mbar_init(&w_empty[i], 8);    // one arrival per producer warp
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
@@ -239,10 +240,12 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
   const uint32_t tbase = *tmem_slot;
   grid_dep_launch();   // this CTA holds its TMEM: dependents may start
 
-  if (warp < 4) {
-    // ---- producers: weight row r of each group -> TMEM A stage (column c = k 2c, 2c+1) ----
-    const int r = warp * 32 + lane;
-    const uint32_t lane_base = tbase + ((uint32_t)(warp * 32) << 16);
+  if (warp < 8) {
+    // ---- producers: weight row r, pieces 2h and 2h+1 of each group -> TMEM A stage
+    //      (column c = k 2c, 2c+1) ----
+    const int q4 = warp & 3, h = warp >> 2;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     for (int it = 0; it < total; ++it) {
       const int sr = it % PF_NR, sa = it % PF_NA;
       bool ok = *abort_flag == 0 && mbar_wait_bounded(&w_full[sr], (it / PF_NR) & 1, p.err);
@@ -251,9 +254,9 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
         break;
       }
       const uint8_t* raw = sm + L::OFF_RAW + sr * PF_RAW;
-      uint4 v[4];
+      uint4 v[2];
 #pragma unroll
-      for (int pc = 0; pc < 4; ++pc) v[pc] = *reinterpret_cast<const uint4*>(raw + pc * 2048 + r * 16);
+      for (int j = 0; j < 2; ++j) v[j] = *reinterpret_cast<const uint4*>(raw + (2 * h + j) * 2048 + r * 16);
       const uint32_t mw = *reinterpret_cast<const uint32_t*>(raw + BLOCK_BYTES + r * 4);
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_empty[sr]);   // this warp is done with the raw stage
@@ -267,8 +270,9 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       const __nv_bfloat162 s2 = __halves2bfloat162(sb, sb);
       const __nv_bfloat162 z2 = __halves2bfloat162(zb, zb);
 #pragma unroll
-      for (int pc = 0; pc < 4; ++pc) {
-        const uint32_t w[4] = {v[pc].x, v[pc].y, v[pc].z, v[pc].w};
+      for (int j = 0; j < 2; ++j) {
+        const int pc = 2 * h + j;
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
         uint32_t cols[16];
 #pragma unroll
         for (int jw = 0; jw < 4; ++jw)
@@ -287,7 +291,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[sa]);
     }
-  } else if (warp == 8) {
+  } else if (warp == 12) {
     // ---- TMA: the activations of every group, NX stages ahead of the MMAs ----
     grid_dep_wait();   // x comes from the preceding kernel
     if (lane == 0) {
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       for (int it = std::max(0, issued - PF_NX); it < issued; ++it)
         mbar_wait_bounded(&x_full[it % PF_NX], (it / PF_NX) & 1, p.err);
     }
-  } else if (warp == 10) {
+  } else if (warp == 14) {
     // ---- raw weight blocks (constant: no dependency wait), NR stages ahead ----
     if (lane == 0) {
       int issued = 0;
@@ -331,7 +335,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       for (int it = std::max(0, issued - PF_NR); it < issued; ++it)
         mbar_wait_bounded(&w_full[it % PF_NR], (it / PF_NR) & 1, p.err);
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ---- MMA issuer ----
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_bf16(TILE_N, PF_BM);
@@ -364,7 +368,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       mbar_wait_bounded(done, 0, p.err);
     }
   } else {
-    // ---- epilogue warps 4-7: drain accumulator j&1, fused epilogue on the tile ----
+    // ---- epilogue warps 8-11: drain accumulator j&1, fused epilogue on the tile ----
     const int t = threadIdx.x - PF_EPI_T0;              // 0..127
     const int q4 = warp & 3;                            // TMEM lane quarter
     const int r = q4 * 32 + lane;                       // weight row
@@ -406,8 +410,8 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&acc_empty[buf]);   // the MMAs of unit j+2 may overwrite it
       epi_sync();                                    // the whole tile is in shared memory
       if (EPI == EPI_QKV) {
-        if (p.head_dim == 128) pf_qkv_epilogue<128, 8>(p, tile_acc, tile, m0, PF_BM, t, 128);
-        else pf_qkv_epilogue<64, 8>(p, tile_acc, tile, m0, PF_BM, t, 128);
+        if (p.head_dim == 128) pf_qkv_epilogue<128, 4>(p, tile_acc, tile, m0, PF_BM, t, 128);
+        else pf_qkv_epilogue<64, 4>(p, tile_acc, tile, m0, PF_BM, t, 128);
       } else if (EPI == EPI_RESIDUAL) {
         pf_residual_epilogue<8>(p, tile_acc, tile, m0, PF_BM, t, 128);
       } else {
