@@ -405,6 +405,49 @@ class OracleDecoder:
             x = self.layer_step(li, x, pos)
         return rms_norm(x, self.final_norm, self.shape.rms_norm_eps) @ self._lm.t()   # model.py:477
 
+    def prefill_chunked(self, prompts: torch.Tensor, chunk: int) -> torch.Tensor:
+        """Chunked prefill of ``prompts [B, P]``: every chunk of ``chunk`` tokens per
+        row goes through each layer at once, its K/V written into the cache
+        first and each token attending keys ``0..its position`` -- the causal
+        rule of the reference's chunked prefill (``prefill_runtime.py:95-164``,
+        ``llama_chunked_prefill_attention/op.py:21-50``) and of the full-prompt
+        forward (``model.py:453-478`` with a causal mask).  Returns the logits of
+        every prompt token ``[B, P, V]``."""
+        s = self.shape
+        B, P = prompts.shape
+        out = []
+        for c0 in range(0, P, chunk):
+            n = min(chunk, P - c0)
+            pos = torch.arange(c0, c0 + n)
+            x = self.embed[prompts[:, c0:c0 + n]].to(torch.float32)            # [B, n, H]
+            for li in range(s.n_layers):
+                layer = self.layers[li]
+                xn = rms_norm(x, layer.input_layernorm, s.rms_norm_eps).reshape(B * n, s.emb_dim)
+                q = layer.q_proj(xn).view(B, n, s.n_heads, s.head_dim)
+                k = layer.k_proj(xn).view(B, n, s.n_kv_groups, s.head_dim)
+                v = layer.v_proj(xn).view(B, n, s.n_kv_groups, s.head_dim)
+                if s.qk_norm:
+                    q = rms_norm(q, layer.q_norm, s.rms_norm_eps)
+                    k = rms_norm(k, layer.k_norm, s.rms_norm_eps)
+                ang = self.angles[pos]                                         # [n, hd]
+                q = apply_rope_rows(q.reshape(B * n, s.n_heads, s.head_dim), ang.repeat(B, 1)).view(q.shape)
+                k = apply_rope_rows(k.reshape(B * n, s.n_kv_groups, s.head_dim), ang.repeat(B, 1)).view(k.shape)
+                kc, vc = self.k_cache[li], self.v_cache[li]
+                kc[:, :, c0:c0 + n] = k.permute(0, 2, 1, 3).to(self.kv_dtype)
+                vc[:, :, c0:c0 + n] = v.permute(0, 2, 1, 3).to(self.kv_dtype)
+                qpg = s.q_heads_per_group
+                keys = kc[:, :, :c0 + n].to(torch.float32).repeat_interleave(qpg, dim=1)   # [B, nq, c0+n, hd]
+                vals = vc[:, :, :c0 + n].to(torch.float32).repeat_interleave(qpg, dim=1)
+                scores = torch.einsum("bihd,bhjd->bhij", q.to(torch.float32), keys) * s.head_dim ** -0.5
+                mask = torch.arange(c0 + n)[None, :] > pos[:, None]           # key after the token
+                scores = scores.masked_fill(mask[None, None], float("-inf"))
+                ctx = torch.einsum("bhij,bhjd->bihd", torch.softmax(scores, dim=-1), vals)
+                x = x + layer.o_proj(ctx.reshape(B * n, s.n_heads * s.head_dim)).view(B, n, s.emb_dim)
+                h = rms_norm(x, layer.post_attention_layernorm, s.rms_norm_eps).reshape(B * n, s.emb_dim)
+                x = x + layer.down_proj(F.silu(layer.gate_proj(h)) * layer.up_proj(h)).view(B, n, s.emb_dim)
+            out.append(rms_norm(x, self.final_norm, s.rms_norm_eps) @ self._lm.t())
+        return torch.cat(out, dim=1)
+
     def prefill(self, prompts: torch.Tensor) -> torch.Tensor:
         """Feed ``prompts [B, P]`` one position at a time; returns the last logits."""
         logits = None

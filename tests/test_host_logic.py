@@ -58,3 +58,25 @@ def test_synth_recipe_properties():
     assert lin.qzeros.shape == (4, 32) and lin.scales.shape == (4, 256) and lin.scales.dtype == torch.float16
     z = oracle.unpack_autogptq_qzeros(lin.qzeros, 256)
     assert 1 <= int(z.min()) and int(z.max()) <= 15
+
+
+def test_oracle_chunked_prefill_equals_stepwise():
+    """Several sequences, a chunk that does not divide the prompt: the chunked
+    restatement equals feeding one position per step (logits and KV caches)."""
+    from tests.gpu_util import oracle_layer, oracle_shape
+    from torch2iron_b200.config import QuantizedQwenConfig
+    cfg = QuantizedQwenConfig(vocab_size=512, emb_dim=256, n_layers=2, n_heads=4, n_kv_groups=2, head_dim=64,
+                              hidden_dim=512, rms_norm_eps=1e-6, rope_base=1e6)
+    model = synth.random_model(cfg, seed=12)
+    prompts = torch.randint(0, cfg.vocab_size, (3, 13), generator=torch.Generator().manual_seed(13))
+    def dec():   # fp32 caches: only the order of fp32 sums differs between the two forms
+        return oracle.OracleDecoder(oracle_shape(cfg), [oracle_layer(l, cfg) for l in model["layers"]],
+                                    embed=model["embed"], final_norm=model["final_norm"], lm_head=model["embed"],
+                                    max_ctx=64, batch=3, kv_dtype=torch.float32)
+    a, b = dec(), dec()
+    la = a.prefill_chunked(prompts, 4)[:, -1]
+    lb = b.prefill(prompts)
+    assert (la - lb).abs().max().item() <= 1e-5
+    for li in range(cfg.n_layers):
+        assert (a.k_cache[li] - b.k_cache[li]).abs().max().item() <= 1e-5
+        assert (a.v_cache[li] - b.v_cache[li]).abs().max().item() <= 1e-5

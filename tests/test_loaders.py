@@ -233,3 +233,16 @@ def test_head_quantizer_is_the_packer_rtn():
     mine = LD.quantize_head_w4(art.dense("lm_head.weight"))
     ref = LD.qparam_to_autogptq(qp, 256, 512)
     assert torch.equal(mine.qweight, ref.qweight) and torch.equal(mine.scales, ref.scales)
+
+
+@pytest.mark.parametrize("chunk", [12, 5, 1])
+def test_oracle_chunked_prefill_matches_reference_forward(chunk):
+    """The chunked-prefill restatement (the semantics the GPU prefill implements)
+    gives the reference model's full-prompt logits at every position."""
+    cfg, model = LD.load_packed_artifact(MODEL_DIR)
+    g = _golden()
+    prompt, ref = torch.from_numpy(g["prompt"]), torch.from_numpy(g["logits"])
+    dec = _oracle_decoder(cfg, model, torch.float32)
+    lg = dec.prefill_chunked(prompt, chunk)[0]
+    assert lg.shape == ref.shape
+    assert (lg - ref).abs().max().item() <= 1e-4
