@@ -50,3 +50,45 @@ def test_workspace_queries():
     assert lib.t2b_w4a16_gemm_workspace_bytes(1, 1024, 12288) > 0     # more than 8 k-slices: workspace
     assert lib.t2b_decode_attention_workspace_bytes(64, 16, 8, 128, 256) > 0   # tickets + partial records
     assert lib.t2b_decode_attention_workspace_bytes(1, 16, 8, 128, 4096) > 0
+
+
+def _header_prototypes():
+    """name -> (return type, [parameter types]) of every T2B_API declaration."""
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "t2b.h").read_text(), flags=re.S)
+    protos = {}
+    for m in re.finditer(r"T2B_API\s+([\w\s\*]+?)\s*\b(t2b_\w+)\s*\(([^)]*)\)\s*;", text):
+        ret, name, params = m.group(1).strip(), m.group(2), m.group(3).strip()
+        types = [] if params in ("", "void") else [p.strip().rsplit(" ", 1)[0] if not p.strip().endswith("*")
+                                                     else p.strip() for p in params.split(",")]
+        protos[name] = (ret, [p.replace(" ", "") if "*" in p else p for p in types])
+    return protos
+
+
+def _ctype(c_type):
+    import ctypes as C
+    t = " ".join(c_type.split())
+    if "*" in t:
+        return C.c_void_p
+    if t.endswith("size_t"):
+        return C.c_size_t
+    if t.endswith("float"):
+        return C.c_float
+    if t.endswith("int") or t.endswith("int32_t"):
+        return C.c_int
+    raise AssertionError(f"unmapped C type {c_type!r}")
+
+
+def test_binding_signatures_match_header_prototypes():
+    """Every ctypes declaration has the header's parameter count and kinds
+    (pointer / int / float / size_t) and return kind, so a changed C signature
+    cannot be called with a stale argument list."""
+    import ctypes as C
+    protos = _header_prototypes()
+    assert set(protos) == set(_lib.SIGNATURES)
+    for name, (ret, params) in protos.items():
+        res, args = _lib.SIGNATURES[name]
+        assert len(args) == len(params), (name, params)
+        for i, (a, p) in enumerate(zip(args, params)):
+            assert a == _ctype(p), (name, i, p)
+        want_ret = C.c_char_p if "char" in ret else _ctype(ret)
+        assert res == want_ret, (name, ret)
