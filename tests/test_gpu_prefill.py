@@ -131,3 +131,36 @@ def test_chunked_prefill_on_reference_artifact():
     torch.cuda.synchronize()
     assert max_abs(eng.logits[0], torch.from_numpy(g["logits"][-1])) <= 2e-2
     eng.check_device_errors()
+
+
+@pytest.mark.parametrize("force_large_m", [False, True])
+def test_ragged_prompts_match_per_sequence_oracle(monkeypatch, force_large_m):
+    """Right-padded prompts of lengths 5, 13 and 9: each row's greedy head and
+    its continued decode match the oracle run on that sequence alone (chunk
+    linears on the decode tcgen05 kernel, or forced onto the large-M kernel)."""
+    if force_large_m:
+        monkeypatch.setenv("T2B_PREFILL_MIN_M", "12")   # the 12-row chunks, not the 3-row decode step
+    cfg = SMALL
+    model = synth.random_model(cfg, seed=45)
+    lens = [5, 13, 9]
+    B, P = len(lens), max(lens)
+    prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(46))
+    eng = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
+    eng.prefill(prompts, chunk=4, lengths=lens)
+    torch.cuda.synchronize()
+    assert eng.pos.cpu().tolist() == lens
+    first = eng.logits.cpu().clone()
+    eng.tokens.copy_(torch.tensor([7, 8, 9], dtype=torch.int32))   # fixed next inputs for a decode step
+    eng.run_step()
+    second = eng.logits.cpu().clone()
+    eng.check_device_errors()
+    for b, n in enumerate(lens):
+        dec = oracle_decoder(cfg, model, 1, 64)
+        ref = dec.prefill(prompts[b:b + 1, :n])
+        assert max_abs(first[b], ref[0]) <= 2e-2, b
+        ref2 = dec.step(torch.tensor([7 + b]), torch.tensor([n]))
+        assert max_abs(second[b], ref2[0]) <= 2e-2, b
+    with pytest.raises(ValueError):
+        eng.prefill(prompts, lengths=[0, 13, 9])
+    with pytest.raises(ValueError):
+        eng.prefill(prompts, stepwise=True, lengths=lens)

@@ -365,17 +365,23 @@ class DecodeEngine:
                 p(lw.down.qw), p(lw.down.meta), p(pf["h"]), p(x), p(sa), p(self.next_norm_weight(li)), p(xw), M,
                 H, cfg.hidden_dim, *ws("down"), st))
 
-    def prefill(self, prompts: torch.Tensor, chunk: int | None = None, stepwise: bool = False) -> None:
+    def prefill(self, prompts: torch.Tensor, chunk: int | None = None, stepwise: bool = False,
+                lengths=None) -> None:
         """Fill the KV caches from ``prompts [B, P]`` in chunks of ``chunk`` tokens per
         sequence (default: up to ``PREFILL_ROWS`` prompt tokens per chunk): every
         linear runs over all ``B * chunk`` tokens at once and attention is causal
-        within and before the chunk (``t2b_prefill_attention``).  ``stepwise``
-        feeds the prompt one position per decode step instead.
+        within and before the chunk (``t2b_prefill_attention``).  ``lengths``
+        (B ints in 1..P) gives ragged prompts, right-padded in ``prompts``: a
+        padded position writes no cache entry and each row continues from its
+        own length.  ``stepwise`` feeds the prompt one position per decode step
+        instead (equal lengths only).
 
-        Leaves ``next_tokens`` = the greedy token after the prompt (``logits`` for
-        it with ``keep_logits``), and ``tokens``/``pos`` ready for ``advance()``.
+        Leaves ``next_tokens`` = the greedy token after each prompt (``logits``
+        for it with ``keep_logits``), and ``tokens``/``pos`` ready for ``advance()``.
         """
         if stepwise:
+            if lengths is not None:
+                raise ValueError("stepwise prefill takes prompts of equal length")
             self._prefill_stepwise(prompts)
             return
         B, P = prompts.shape
@@ -383,27 +389,38 @@ class DecodeEngine:
             raise ValueError(f"prompts hold {B} sequences, the engine {self.B}")
         if P < 1 or P > self.max_ctx:
             raise ValueError(f"prompt length {P} outside 1..{self.max_ctx}")
-        C = chunk or max(1, min(P, self.PREFILL_ROWS // B))
-        pf = self._prefill_buffers(B * min(C, P))
-        prompts = prompts.to(self.device, torch.int32)
+        lens = torch.full((B,), P, dtype=torch.int64) if lengths is None else \
+            torch.as_tensor(lengths, dtype=torch.int64).cpu()
+        if lens.shape != (B,) or int(lens.min()) < 1 or int(lens.max()) > P:
+            raise ValueError(f"lengths must be {B} values in 1..{P}")
+        Pmax = int(lens.max())
+        C = chunk or max(1, min(Pmax, self.PREFILL_ROWS // B))
+        pf = self._prefill_buffers(B * min(C, Pmax))
+        dev = self.device
+        valid = torch.arange(P)[None, :] < lens[:, None]                       # [B, P]
+        prompts = torch.where(valid, prompts.cpu().to(torch.int64), 0).to(dev, torch.int32)   # padding -> token 0
+        lens_d = lens.to(dev)
         st = _lib.stream()
         _lib.lib().t2b_set_error_word(_lib.ptr(self.err))
-        dev = self.device
-        seq_all = torch.arange(B, dtype=torch.int32, device=dev)
-        for c0 in range(0, P, C):
-            n = min(C, P - c0)
+        seq_all = torch.arange(B, dtype=torch.int64, device=dev)
+        for c0 in range(0, Pmax, C):
+            n = min(C, Pmax - c0)
             M = B * n
+            posm = torch.arange(c0, c0 + n, device=dev)[None, :].expand(B, n)
             pf["tokens"][:M].copy_(prompts[:, c0:c0 + n].reshape(-1))
-            pf["pos"][:M].copy_((torch.arange(n, dtype=torch.int32, device=dev) + c0).repeat(B))
+            pf["pos"][:M].copy_(torch.where(posm < lens_d[:, None], posm, -1).reshape(-1))   # -1: no cache write
             pf["seq"][:M].copy_(seq_all.repeat_interleave(n))
             self.enqueue_prefill_chunk(pf, n, c0, st)
-        # the last prompt token of every sequence feeds the greedy head
-        last = seq_all.to(torch.int64) * n + (n - 1)
-        self.x.copy_(pf["x"].index_select(0, last))
-        self.ssq_a.copy_(pf["ssq_a"].index_select(0, last))
+            # rows whose last prompt token is in this chunk: residual state for the head
+            ends = (lens_d - 1 >= c0) & (lens_d - 1 < c0 + n)
+            rows = seq_all[ends]
+            if rows.numel():
+                src = rows * n + (lens_d[ends] - 1 - c0)
+                self.x.index_copy_(0, rows, pf["x"].index_select(0, src))
+                self.ssq_a.index_copy_(0, rows, pf["ssq_a"].index_select(0, src))
         self._enqueue_head(st)
         self.tokens.copy_(self.next_tokens)
-        self.pos.fill_(P)
+        self.pos.copy_(lens_d.to(torch.int32))
 
     def _prefill_stepwise(self, prompts: torch.Tensor) -> None:
         """The prompt one position per decode step (teacher forcing)."""
@@ -416,9 +433,11 @@ class DecodeEngine:
         self.tokens.copy_(self.next_tokens)
         self.pos.fill_(P)
 
-    def generate(self, prompts: torch.Tensor, new_tokens: int, stepwise_prefill: bool = False) -> torch.Tensor:
-        """Greedy decode ``new_tokens`` per row after ``prompts`` -> ``[B, new_tokens]``."""
-        self.prefill(prompts, stepwise=stepwise_prefill)
+    def generate(self, prompts: torch.Tensor, new_tokens: int, stepwise_prefill: bool = False,
+                 lengths=None) -> torch.Tensor:
+        """Greedy decode ``new_tokens`` per row after ``prompts`` (right-padded to
+        ``lengths`` when given) -> ``[B, new_tokens]``."""
+        self.prefill(prompts, stepwise=stepwise_prefill, lengths=lengths)
         out = [self.next_tokens.clone()]
         for _ in range(new_tokens - 1):
             self.advance()
