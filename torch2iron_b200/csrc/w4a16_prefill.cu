@@ -60,6 +60,20 @@ struct PfLayout {
   static constexpr int BYTES = OFF_FLAG + 8 + 1024;                // + slack to 1024-align the base
 };
 
+// Trace build only (-DT2B_TRACE): SM cycles each role spends waiting, per CTA
+// record (t[1] MMA on A stages, t[2] MMA on activations, t[3] MMA on a free
+// accumulator, t[4] producers on raw weights, t[5] producers on a free A
+// stage, t[6] epilogue on a finished accumulator, t[7] the CTA's whole run).
+#ifdef T2B_TRACE
+#define PF_CLK(v) const long long v = clock64()
+#define PF_ADD(acc, t0) (acc) += clock64() - (t0)
+#define PF_PUT(slot, v) t2b::g_trace[t2b_trace_slot].t[(slot)] = (unsigned long long)(v)
+#else
+#define PF_CLK(v)
+#define PF_ADD(acc, t0)
+#define PF_PUT(slot, v)
+#endif
+
 // Named barrier among the four epilogue warps (id 1; 0 is __syncthreads).
 T2B_DEV void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -207,6 +221,8 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
   const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int total = my_units * G;   // groups this CTA runs, in order (global counter `it`)
   auto unit_of = [&](int j) { return (int)blockIdx.x + j * (int)gridDim.x; };
+  T2B_TRACE_BEGIN(30 + EPI, p.N);
+  PF_CLK(t_start);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < PF_NX; ++i) {
@@ -246,9 +262,14 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
     const int q4 = warp & 3, h = warp >> 2;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
+    long long w_wait = 0, a_wait = 0;
+    (void)w_wait;
+    (void)a_wait;
     for (int it = 0; it < total; ++it) {
       const int sr = it % PF_NR, sa = it % PF_NA;
+      PF_CLK(tw0);
       bool ok = *abort_flag == 0 && mbar_wait_bounded(&w_full[sr], (it / PF_NR) & 1, p.err);
+      PF_ADD(w_wait, tw0);
       if (!__all_sync(0xffffffffu, ok)) {
         *abort_flag = 1;
         break;
@@ -260,7 +281,9 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       const uint32_t mw = *reinterpret_cast<const uint32_t*>(raw + BLOCK_BYTES + r * 4);
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_empty[sr]);   // this warp is done with the raw stage
+      PF_CLK(ta0);
       if (it >= PF_NA) ok = mbar_wait_bounded(&a_empty[sa], ((it / PF_NA) - 1) & 1, p.err);
+      PF_ADD(a_wait, ta0);
       if (!__all_sync(0xffffffffu, ok)) {   // the warp takes the same branch before tcgen05.st
         *abort_flag = 1;
         break;
@@ -290,6 +313,10 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[sa]);
+    }
+    if (threadIdx.x == 0) {
+      PF_PUT(4, w_wait);
+      PF_PUT(5, a_wait);
     }
   } else if (warp == 12) {
     // ---- TMA: the activations of every group, NX stages ahead of the MMAs ----
@@ -340,14 +367,24 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_bf16(TILE_N, PF_BM);
       bool ok = true;
+      long long wa = 0, wx = 0, we = 0;
+      (void)wa;
+      (void)wx;
+      (void)we;
       for (int j = 0; j < my_units && ok; ++j) {
         const int buf = j & 1;
+        PF_CLK(te0);
         if (j >= 2) ok = mbar_wait_bounded(&acc_empty[buf], ((j >> 1) - 1) & 1, p.err);
+        PF_ADD(we, te0);
         tc_fence_after();
         for (int g = 0; g < G && ok; ++g) {
           const int it = j * G + g, sa = it % PF_NA, sx = it % PF_NX;
-          ok = *abort_flag == 0 && mbar_wait_bounded(&a_full[sa], (it / PF_NA) & 1, p.err) &&
-               mbar_wait_bounded(&x_full[sx], (it / PF_NX) & 1, p.err);
+          PF_CLK(ta0);
+          ok = *abort_flag == 0 && mbar_wait_bounded(&a_full[sa], (it / PF_NA) & 1, p.err);
+          PF_ADD(wa, ta0);
+          PF_CLK(tx0);
+          ok = ok && mbar_wait_bounded(&x_full[sx], (it / PF_NX) & 1, p.err);
+          PF_ADD(wx, tx0);
           if (!ok) break;
           tc_fence_after();
           const uint32_t xa = smem_u32(sm + sx * L::X_STAGE);
@@ -366,6 +403,9 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       // every MMA issued here has retired before TMEM is released
       mma_commit(done);
       mbar_wait_bounded(done, 0, p.err);
+      PF_PUT(1, wa);
+      PF_PUT(2, wx);
+      PF_PUT(3, we);
     }
   } else {
     // ---- epilogue warps 8-11: drain accumulator j&1, fused epilogue on the tile ----
@@ -375,6 +415,8 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     grid_dep_wait();   // row sums, residual rows, positions come from earlier kernels
     maybe_clear_ssq(p, blockIdx.x == 0, t, 128);
+    long long wf = 0;
+    (void)wf;
     for (int j = 0; j < my_units; ++j) {
       const int buf = j & 1;
       const int u = unit_of(j);
@@ -384,7 +426,9 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
         rowscale[t] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;   // model.py:179-180
       }
       epi_sync();   // row scales written; the previous unit's epilogue is done with tile_acc
+      PF_CLK(tf0);
       const bool ok = __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, p.err));
+      PF_ADD(wf, tf0);
       if (!ok && lane == 0) *epi_abort = 1;
       epi_sync();
       if (*epi_abort) {   // the same value in every epilogue warp: no warp is left at a named barrier
@@ -418,6 +462,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
         tile_epilogue<EPI>(p, tile_acc, scratch, tile, m0, PF_BM, EpiCache{}, t, 128);
       }
     }
+    if (t == 0) PF_PUT(6, wf);
   }
   tc_fence_before();
   __syncthreads();
@@ -425,6 +470,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
     tc_fence_after();
     tmem_dealloc(tbase, PF_TMEM_COLS);
   }
+  if (threadIdx.x == 0) PF_PUT(7, clock64() - t_start);
 }
 
 // ---------------------------------------------------------------------------
@@ -481,3 +527,5 @@ int prefill_launch(LinearParams& p, int pro, int epi, cudaStream_t st) {
 }
 
 }  // namespace t2b
+
+T2B_TRACE_DUMP_FN(t2b_trace_dump_prefill)
