@@ -33,6 +33,7 @@ __all__ = [
     "rope_two_halves",
     "compute_rope_angles",
     "chunked_attention_packet",
+    "gqa_attention",
     "OracleShape",
     "OracleLayer",
     "OracleDecoder",
@@ -291,6 +292,17 @@ def chunked_attention_packet(queries: torch.Tensor, packet: torch.Tensor, packet
 # Decoder layer and model
 # ---------------------------------------------------------------------------
 
+def gqa_attention(q: torch.Tensor, keys: torch.Tensor, vals: torch.Tensor) -> torch.Tensor:
+    """One query token: q ``[n_heads, hd]`` over ``keys``/``vals`` ``[n_kv, n, hd]``,
+    q head h reading kv head ``h // (n_heads / n_kv)``; fp32 softmax(q k^T /
+    sqrt(hd)) v (``model.py:266-279``, ``kv_plane_reference.py:122-187``)."""
+    qpg = q.shape[0] // keys.shape[0]
+    k = keys.to(torch.float32).repeat_interleave(qpg, dim=0)
+    v = vals.to(torch.float32).repeat_interleave(qpg, dim=0)
+    scores = torch.einsum("hd,hnd->hn", q.to(torch.float32), k) * q.shape[-1] ** -0.5
+    return torch.einsum("hn,hnd->hd", torch.softmax(scores, dim=-1), v)
+
+
 @dataclass(frozen=True)
 class OracleShape:
     """Field-for-field subset of ``QuantizedQwenConfig`` (``model.py:330-348``) plus ``qk_norm``."""
@@ -378,14 +390,9 @@ class OracleDecoder:
             kc[r, :, int(pos[r])] = k[r].to(self.kv_dtype)
             vc[r, :, int(pos[r])] = v[r].to(self.kv_dtype)
         ctx = torch.empty(b, s.n_heads, s.head_dim)
-        scale = s.head_dim ** -0.5
         for r in range(b):
             n = int(pos[r]) + 1
-            keys = kc[r, :, :n].to(torch.float32).repeat_interleave(s.q_heads_per_group, dim=0)
-            vals = vc[r, :, :n].to(torch.float32).repeat_interleave(s.q_heads_per_group, dim=0)
-            scores = torch.einsum("hd,hnd->hn", q[r].to(torch.float32), keys) * scale
-            w = torch.softmax(scores, dim=-1)
-            ctx[r] = torch.einsum("hn,hnd->hd", w, vals)
+            ctx[r] = gqa_attention(q[r], kc[r, :, :n], vc[r, :, :n])
         return layer.o_proj(ctx.reshape(b, s.n_heads * s.head_dim))
 
     def layer_step(self, li: int, x: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:

@@ -71,6 +71,19 @@ def test_decode_attention_vs_oracle(B, nq, nkv, hd, ctx, positions):
         assert max_abs(out[r], ref) <= 1e-2
 
 
+@pytest.mark.parametrize("case", [0, 1])
+def test_decode_attention_matches_kv_plane_reference(case):
+    """The decode attention kernel on the reference's own KV-plane golden
+    (``kv_plane_reference.py:122-187``), planes read into this library's cache
+    layout; the reference output is rounded to bf16, hence 2e-2."""
+    d = gio.load("kv_plane_attention.npz")
+    ctx = 128
+    q, k, v, attend, ref, qpg, hd = gio.kv_plane_case(d, case, max_ctx=ctx)
+    pos = torch.tensor([attend - 1], dtype=torch.int32)
+    out = attention_call(q.cuda(), k.cuda(), v.cuda(), pos.cuda(), 8 * qpg, 8, hd, ctx)
+    assert max_abs(out[0], ref) <= 2e-2
+
+
 def test_packet_attention_matches_reference_golden():
     d = gio.load("attention_packet.npz")
     seq, chunk = int(d["seq"]), int(d["chunk"])

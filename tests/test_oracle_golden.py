@@ -3,6 +3,7 @@
 import hashlib
 
 import numpy as np
+import pytest
 import torch
 
 import oracle
@@ -123,3 +124,13 @@ def test_packet_attention_matches_reference():
                                           int(d["chunk"]))
     ref = gio.bf16(d["out"])
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_gqa_attention_matches_kv_plane_reference(case):
+    """The oracle's attention core against the reference's KV-plane attention
+    (``kv_plane_reference.py:122-187``), read through this library's cache layout."""
+    d = gio.load("kv_plane_attention.npz")
+    q, k, v, attend, out, qpg, hd = gio.kv_plane_case(d, case, max_ctx=80)
+    y = oracle.gqa_attention(q.view(8 * qpg, hd), k[0, :, :attend], v[0, :, :attend]).reshape(-1)
+    assert (y - out).abs().max().item() <= 8e-3        # the reference output is rounded to bf16
