@@ -2,8 +2,10 @@
 
 This package restates, in plain PyTorch-CPU fp32 arithmetic, the reference
 implementation of torch2iron's quantized Qwen3 decode path
-(``src/models/quantized_qwen3/model.py`` and
-``src/models/fast_qwen3/fast_packed_format.py``).  Every function cites the
+(``src/models/quantized_qwen3/model.py``,
+``src/models/fast_qwen3/fast_packed_format.py``, the attention references of
+``src/models/fast_qwen3/`` and the Q4NX layout of
+``src/models/fast_qwen3/q4nx_layout.py``).  Every function cites the
 reference file:line it follows.
 
 It is the checker, never the product:
@@ -14,8 +16,10 @@ It is the checker, never the product:
 
 Parity pin: ``tests/golden/make_golden.py`` imports the reference itself (in
 the build container, where it is mounted) and writes golden input/output
-vectors to ``tests/golden/*.npz``; ``tests/test_oracle_golden.py`` checks this
-restatement against them.
+vectors to ``tests/golden/*.npz`` (``make_packed_artifact.py``,
+``make_kv_plane.py`` and ``make_q4nx.py`` beside it cover the packed artifact,
+the KV-plane attention and the Q4NX layout); ``tests/test_oracle_golden.py``
+and ``tests/test_loaders.py`` check this restatement against them.
 """
 
 from .reference_port import *  # noqa: F401,F403

@@ -34,6 +34,14 @@ __all__ = [
     "compute_rope_angles",
     "chunked_attention_packet",
     "gqa_attention",
+    "Q4NX_GROUP",
+    "Q4NX_OUT_CHUNK",
+    "Q4NX_IN_CHUNK",
+    "Q4NX_PATCH_ROWS",
+    "Q4NX_CHUNK_BYTES",
+    "q4nx_unpack_chunk",
+    "q4nx_dequantize_linear",
+    "q4nx_linear",
     "OracleShape",
     "OracleLayer",
     "OracleDecoder",
@@ -291,6 +299,63 @@ def chunked_attention_packet(queries: torch.Tensor, packet: torch.Tensor, packet
 # ---------------------------------------------------------------------------
 # Decoder layer and model
 # ---------------------------------------------------------------------------
+
+# ---------------------------------------------------------------------------
+# Q4NX group-32 layout of the fast Qwen3 path (src/models/fast_qwen3/q4nx_layout.py)
+# ---------------------------------------------------------------------------
+Q4NX_GROUP = 32          # k per (scale, zero point)            q4nx_layout.py:30
+Q4NX_OUT_CHUNK = 32      # output rows per chunk                 :31
+Q4NX_IN_CHUNK = 256      # k per chunk                           :32
+Q4NX_PATCH_ROWS = 64     # output rows per patch (two chunks)    :33
+Q4NX_CHUNK_BYTES = 2 * 2 * Q4NX_OUT_CHUNK * (Q4NX_IN_CHUNK // Q4NX_GROUP) + Q4NX_OUT_CHUNK * Q4NX_IN_CHUNK // 2
+
+
+def q4nx_unpack_chunk(chunk) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """One 5120-byte chunk -> (q ``[32, 256]``, scale ``[32, 8]``, zero ``[32, 8]``):
+    bf16 scales, then bf16 zero points, then 4-bit values two per byte, low
+    nibble = even k (``q4nx_layout.py:92-113,159-174``)."""
+    b = torch.frombuffer(bytearray(bytes(chunk)), dtype=torch.uint8)
+    if b.numel() != Q4NX_CHUNK_BYTES:
+        raise ValueError(f"a Q4NX chunk is {Q4NX_CHUNK_BYTES} bytes, got {b.numel()}")
+    ng = Q4NX_OUT_CHUNK * (Q4NX_IN_CHUNK // Q4NX_GROUP)
+    scale = b[:2 * ng].view(torch.bfloat16).to(torch.float32).view(Q4NX_OUT_CHUNK, -1)
+    zero = b[2 * ng:4 * ng].view(torch.bfloat16).to(torch.float32).view(Q4NX_OUT_CHUNK, -1)
+    packed = b[4 * ng:].view(Q4NX_OUT_CHUNK, Q4NX_IN_CHUNK // 2)
+    q = torch.stack((packed & 0xF, packed >> 4), dim=-1).reshape(Q4NX_OUT_CHUNK, Q4NX_IN_CHUNK)
+    return q, scale, zero
+
+
+def q4nx_dequantize_linear(data, in_features: int, out_features: int) -> torch.Tensor:
+    """Dense fp32 ``[out, in]`` of a Q4NX linear: output rows padded to 64-row
+    patches, each patch stored K-chunk-major as (rows 0-31, rows 32-63) chunk
+    pairs; ``w = (q - zero) * scale`` per 32-k group in fp32
+    (``q4nx_layout.py:132-146,177-237``)."""
+    if in_features % Q4NX_IN_CHUNK:
+        raise ValueError(f"in_features must be a multiple of {Q4NX_IN_CHUNK}")
+    padded = -(-out_features // Q4NX_PATCH_ROWS) * Q4NX_PATCH_ROWS
+    raw = bytes(data)
+    n_chunks = padded // Q4NX_OUT_CHUNK * (in_features // Q4NX_IN_CHUNK)
+    if len(raw) != n_chunks * Q4NX_CHUNK_BYTES:
+        raise ValueError(f"expected {n_chunks * Q4NX_CHUNK_BYTES} bytes, got {len(raw)}")
+    w = torch.empty(padded, in_features, dtype=torch.float32)
+    i = 0
+    for r0 in range(0, padded, Q4NX_PATCH_ROWS):
+        for k0 in range(0, in_features, Q4NX_IN_CHUNK):
+            for half in (0, Q4NX_OUT_CHUNK):
+                q, scale, zero = q4nx_unpack_chunk(raw[i * Q4NX_CHUNK_BYTES:(i + 1) * Q4NX_CHUNK_BYTES])
+                i += 1
+                g = q.to(torch.float32).view(Q4NX_OUT_CHUNK, -1, Q4NX_GROUP)
+                w[r0 + half:r0 + half + Q4NX_OUT_CHUNK, k0:k0 + Q4NX_IN_CHUNK] = \
+                    ((g - zero[..., None]) * scale[..., None]).view(Q4NX_OUT_CHUNK, Q4NX_IN_CHUNK)
+    return w[:out_features]
+
+
+def q4nx_linear(x: torch.Tensor, data, in_features: int, out_features: int) -> torch.Tensor:
+    """fp32 ``x . W^T`` over the dense Q4NX weight (``q4nx_layout.py:292-303``
+    before its final bf16 rounding)."""
+    return x.to(torch.float32).reshape(-1, in_features) @ q4nx_dequantize_linear(data, in_features,
+                                                                                 out_features).t()
+
 
 def gqa_attention(q: torch.Tensor, keys: torch.Tensor, vals: torch.Tensor) -> torch.Tensor:
     """One query token: q ``[n_heads, hd]`` over ``keys``/``vals`` ``[n_kv, n, hd]``,

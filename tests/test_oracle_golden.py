@@ -134,3 +134,21 @@ def test_gqa_attention_matches_kv_plane_reference(case):
     q, k, v, attend, out, qpg, hd = gio.kv_plane_case(d, case, max_ctx=80)
     y = oracle.gqa_attention(q.view(8 * qpg, hd), k[0, :, :attend], v[0, :, :attend]).reshape(-1)
     assert (y - out).abs().max().item() <= 8e-3        # the reference output is rounded to bf16
+
+
+def test_q4nx_layout_matches_reference():
+    """The Q4NX group-32 restatement against the reference's own packing of a
+    96 x 512 weight (rows padded to a 64-row patch): dequantisation bit-exact,
+    the linear within the reference's final bf16 rounding."""
+    d = gio.load("q4nx_linear.npz")
+    out_f, in_f, padded = (int(v) for v in d["shape"])
+    assert (out_f, in_f, padded) == (96, 512, 128)
+    data = d["data"].tobytes()
+    assert len(data) == padded // oracle.Q4NX_OUT_CHUNK * (in_f // oracle.Q4NX_IN_CHUNK) * oracle.Q4NX_CHUNK_BYTES
+    dense = oracle.q4nx_dequantize_linear(data, in_f, out_f)
+    assert torch.equal(dense, torch.from_numpy(d["dense"]))
+    x = gio.bf16(d["x"])
+    y = oracle.q4nx_linear(x, data, in_f, out_f)
+    assert torch.equal(y.to(torch.bfloat16), gio.bf16(d["y"]))
+    with pytest.raises(ValueError):
+        oracle.q4nx_dequantize_linear(data[:-1], in_f, out_f)
