@@ -352,3 +352,28 @@ def test_status_word_stays_clear_over_decode_steps():
     prompts = torch.randint(0, cfg.vocab_size, (4, 5), generator=torch.Generator().manual_seed(32))
     eng.generate(prompts, 4)              # raises if any kernel recorded a timeout
     assert int(eng.err.item()) == 0
+
+
+def test_decode_step_host_api_and_input_checks():
+    """``decode_step`` (the reference runner's host-facing call, qwen_npu.py:166-236)
+    gives the same next tokens as the device-side ``advance``; bad host inputs
+    raise before any launch."""
+    cfg = SMALL.scaled(n_layers=2)
+    model = synth.random_model(cfg, seed=51)
+    prompts = torch.randint(0, cfg.vocab_size, (3, 5), generator=torch.Generator().manual_seed(52))
+    a = DecodeEngine(cfg, model, batch=3, max_ctx=64, use_graph=True)
+    a.prefill(prompts)
+    first = a.next_tokens.cpu().clone()
+    out = a.decode_step(first.tolist(), [5, 5, 5])
+    b = DecodeEngine(cfg, model, batch=3, max_ctx=64, use_graph=True)
+    b.prefill(prompts)
+    b.advance()
+    assert torch.equal(out, b.next_tokens.cpu())
+    with pytest.raises(ValueError):
+        a.decode_step([1, 2], [0, 0])                  # one row short
+    with pytest.raises(ValueError):
+        a.decode_step([1, 2, 3], [0, 0, 64])           # position past the cache
+    with pytest.raises(ValueError):
+        a.decode_step([1, 2, cfg.vocab_size], [0, 0, 0])
+    with pytest.raises(ValueError):
+        a.generate(prompts, 61)                        # 5 + 61 - 1 > 64

@@ -294,8 +294,16 @@ class DecodeEngine:
     # -- host-facing API (the reference runner's decode_step, qwen_npu.py:166-236) --
     def decode_step(self, tokens, positions) -> torch.Tensor:
         """tokens / positions: host sequences of length B -> next greedy tokens (host int32 [B])."""
-        self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32), non_blocking=True)
-        self.pos.copy_(torch.as_tensor(positions, dtype=torch.int32), non_blocking=True)
+        tok = torch.as_tensor(tokens, dtype=torch.int32)
+        pos = torch.as_tensor(positions, dtype=torch.int32)
+        if tok.shape != (self.B,) or pos.shape != (self.B,):
+            raise ValueError(f"decode_step takes {self.B} tokens and {self.B} positions")
+        if int(tok.min()) < 0 or int(tok.max()) >= self.cfg.vocab_size:
+            raise ValueError(f"token ids must be in [0, {self.cfg.vocab_size})")
+        if int(pos.min()) < 0 or int(pos.max()) >= self.max_ctx:
+            raise ValueError(f"positions must be in [0, {self.max_ctx}) (the KV cache length)")
+        self.tokens.copy_(tok, non_blocking=True)
+        self.pos.copy_(pos, non_blocking=True)
         self.run_step()
         out = self.next_tokens.cpu()
         self.check_device_errors()
@@ -437,6 +445,9 @@ class DecodeEngine:
                  lengths=None) -> torch.Tensor:
         """Greedy decode ``new_tokens`` per row after ``prompts`` (right-padded to
         ``lengths`` when given) -> ``[B, new_tokens]``."""
+        longest = prompts.shape[1] if lengths is None else max(int(n) for n in lengths)
+        if new_tokens < 1 or longest + new_tokens - 1 > self.max_ctx:
+            raise ValueError(f"{longest} prompt + {new_tokens} new tokens do not fit max_ctx {self.max_ctx}")
         self.prefill(prompts, stepwise=stepwise_prefill, lengths=lengths)
         out = [self.next_tokens.clone()]
         for _ in range(new_tokens - 1):
