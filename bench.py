@@ -1,6 +1,6 @@
-"""Decode throughput benchmark (BASELINE.json metric: decode tokens/s, Qwen3 W4A16).
+"""Decode throughput benchmark (decode tokens/s of Qwen3 W4A16 greedy decode).
 
-Workload (BASELINE config 2 at bs 64): Qwen3-0.6B shapes, 28 layers, tied
+Workload (benchmark configuration 2 at bs 64): Qwen3-0.6B shapes, 28 layers, tied
 bf16 embedding/lm_head, random N(0,0.02) weights quantized int4 g128
 (AutoGPTQ-v1 asymmetric RTN), 64 prompts of 128 uniform-random token ids
 per GPU, greedy decode.  The prompt is prefilled (untimed), ``--warmup``
@@ -173,7 +173,7 @@ def arm_config(args, world):
     """The workload description both arms report (identical for the reference arm)."""
     c0 = args.prompt + args.warmup + 1
     c1 = c0 + args.steps - 1
-    cfg_no = {"qwen3-0.6b": 2, "llama-3.2-1b": 3, "qwen3-8b": 4}.get(args.model, 2)   # BASELINE.json configs[n]
+    cfg_no = {"qwen3-0.6b": 2, "llama-3.2-1b": 3, "qwen3-8b": 4}.get(args.model, 2)   # benchmark configuration number
     return {"workload": f"config{cfg_no} {args.model} greedy decode, {args.batch} rows/GPU, prompt {args.prompt}, "
                         f"timed ctx {c0}..{c1}",
             "model": args.model, "global_batch": world * args.batch, "seq_len": c1, "parallelism": f"dp{world}"}

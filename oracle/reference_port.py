@@ -106,8 +106,8 @@ def autogptq_linear_to_dense(qweight: torch.Tensor, qzeros: torch.Tensor, scales
 
 def autogptq_gemv(x: torch.Tensor, qweight, qzeros, scales, group_size: int = 128) -> torch.Tensor:
     """``y = x . dequant(W)^T`` in fp32 (the config-0 reference computation:
-    ``_autogptq_linear_to_dense`` followed by an fp32 matmul, as the survey
-    probe of ``fast_packed_format.py:132-161`` ran it)."""
+    ``_autogptq_linear_to_dense`` of ``fast_packed_format.py:132-161``
+    followed by an fp32 matmul)."""
     w = autogptq_linear_to_dense(qweight, qzeros, scales, group_size)
     return x.to(torch.float32) @ w.t()
 
@@ -420,7 +420,7 @@ class OracleDecoder:
 
     shape: OracleShape
     layers: list
-    embed: torch.Tensor            # [V, H] (bf16 in BASELINE configs)
+    embed: torch.Tensor            # [V, H] (bf16 in the benchmark configurations)
     final_norm: torch.Tensor       # [H]
     lm_head: torch.Tensor          # [V, H] (tied -> same tensor as embed)
     max_ctx: int

@@ -20,7 +20,7 @@ unmodified:
 * ``write_decode_packet_slot`` / ``chunked_attention_reference``
   (``src/models/fast_qwen3/attention_reference.py:69-171``) -> attention_packet.npz
 
-Weights are the BASELINE recipe (``torch2iron_b200.synth``): asymmetric RTN
+Weights are the benchmark recipe (``torch2iron_b200.synth``): asymmetric RTN
 int4, AutoGPTQ-v1 packing.  The files are small; tests never need the
 reference at run time.
 """

@@ -1,6 +1,6 @@
 """Fused decode-layer kernels and the decode engine vs the oracle / reference goldens.
 
-Bars: decoder logits within 2e-2 max-abs of the torch
+Bars (the parity targets of the decode path): decoder logits within 2e-2 max-abs of the torch
 reference; greedy tokens agreeing >= 99 %.  Intermediate tensors are bf16 on
 the device, so per-op checks use bf16-level tolerances stated per test.
 """
@@ -187,7 +187,7 @@ def _run_engine_layer(eng, x, pos):
     (SMALL, 2, 64, [7, 7]),
     (SMALL, 20, 64, list(range(3, 63, 3))),                       # tcgen05 path, rows at different positions
     (QWEN3_0_6B.scaled(n_layers=1), 64, 256, [200] * 64),         # bs 64, tcgen05 path
-    (QWEN3_0_6B.scaled(n_layers=1), 8, 576, [512] * 8),
+    (QWEN3_0_6B.scaled(n_layers=1), 8, 576, [512] * 8),          # benchmark configuration 1
     (LLAMA_3_2_1B.scaled(n_layers=1, vocab_size=512), 3, 128, [5, 64, 127]),
     # one rank of Qwen3-8B at TP8 (4 q heads, 1 kv head, intermediate 1536)
     (local_config(QWEN3_8B.scaled(n_layers=1, vocab_size=512), 8), 64, 128, list(range(40, 104))),

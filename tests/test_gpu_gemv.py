@@ -1,6 +1,6 @@
 """W4A16 GEMV/GEMM parity through the C-ABI against the oracle and reference goldens.
 
-Bar: each GEMV/GEMM within 1e-2 relative error
+Bar (the parity target of the decode path): each GEMV/GEMM within 1e-2 relative error
 (max-abs error / max |ref|) of fp32-accumulated dequantized math.  The
 CUDA-core path (1 row, fp16/fp32 activations, reference qparam rows)
 dequantizes exactly in fp32, so its fp32 outputs are held to 1e-4; the

@@ -61,7 +61,7 @@ class QuantizedQwenConfig:
             raise ValueError("hidden_dim must be a multiple of 64")
 
 
-# BASELINE.json configs[1..4] model shapes.
+# Model shapes of the benchmark configurations (decode configs 1-4).
 QWEN3_0_6B = QuantizedQwenConfig(
     vocab_size=151936, emb_dim=1024, n_layers=28, n_heads=16, n_kv_groups=8, head_dim=128,
     hidden_dim=3072, rms_norm_eps=1e-6, rope_base=1e6, qk_norm=True, tie_word_embeddings=True)

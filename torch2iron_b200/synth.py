@@ -1,6 +1,6 @@
-"""Seeded synthetic AutoGPTQ-v1 W4A16 weights (the BASELINE.json inputs).
+"""Seeded synthetic AutoGPTQ-v1 W4A16 weights (the benchmark configurations' inputs).
 
-BASELINE configs quantize ``W ~ N(0, 0.02)`` with asymmetric round-to-nearest
+The benchmark configurations quantize ``W ~ N(0, 0.02)`` with asymmetric round-to-nearest
 int4 per group of 128 along K:
 
 * ``scale = (max - min) / 15`` (stored fp16),
