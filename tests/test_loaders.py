@@ -246,3 +246,57 @@ def test_oracle_chunked_prefill_matches_reference_forward(chunk):
     lg = dec.prefill_chunked(prompt, chunk)[0]
     assert lg.shape == ref.shape
     assert (lg - ref).abs().max().item() <= 1e-4
+
+
+# ---- fast Qwen3 artifact (Q4NX group-32) ------------------------------------
+FAST_DIR = MODEL_DIR / LD.FAST_DIRNAME
+
+
+def test_fast_artifact_linears_match_reference():
+    """Every Q4NX linear read by the loader dequantises to the reference's dense
+    weight (sha256 of its fp32 bytes) and gives the reference's output on a
+    seeded input, through the oracle's Q4NX restatement."""
+    import hashlib
+    cfg, model = LD.load_fast_qwen3_artifact(MODEL_DIR)
+    g = np.load(GOLD / "fast_tiny.npz")
+    assert LD.find_fast_dir(MODEL_DIR) == FAST_DIR
+    for li in range(cfg.n_layers):
+        for name in LINEAR_NAMES:
+            prefix = f"model.layers.{li}.{'self_attn' if name in ('q_proj', 'k_proj', 'v_proj', 'o_proj') else 'mlp'}.{name}"
+            lin = model["layers"][li][name]
+            assert isinstance(lin, LD.Q4NXLinear)
+            raw = lin.data.numpy().tobytes()
+            dense = oracle.q4nx_dequantize_linear(raw, lin.in_features, lin.out_features)
+            assert hashlib.sha256(dense.numpy().tobytes()).hexdigest() == str(g[f"{prefix}.sha256"]), prefix
+            x = torch.from_numpy(g[f"{prefix}.x"].view(np.int16)).view(torch.bfloat16)
+            y = oracle.q4nx_linear(x, raw, lin.in_features, lin.out_features).to(torch.bfloat16)
+            assert torch.equal(y, torch.from_numpy(g[f"{prefix}.y"].view(np.int16)).view(torch.bfloat16)), prefix
+
+
+def test_fast_artifact_dense_tensors_and_config():
+    cfg, fast = LD.load_fast_qwen3_artifact(MODEL_DIR)
+    _, packed = LD.load_packed_artifact(MODEL_DIR)
+    assert torch.equal(fast["embed"], packed["embed"]) and torch.equal(fast["final_norm"], packed["final_norm"])
+    for nrm in ("input_layernorm", "post_attention_layernorm", "q_norm", "k_norm"):
+        assert torch.equal(fast["layers"][1][nrm], packed["layers"][1][nrm])
+    assert fast["lm_head"].dtype == torch.bfloat16 and not cfg.tie_word_embeddings   # the dense head stays dense
+    assert (cfg.emb_dim, cfg.n_layers, cfg.head_dim) == (256, 2, 64)
+
+
+def test_fast_artifact_errors_and_engine_refusal(tmp_path):
+    d = tmp_path / "m"
+    shutil.copytree(MODEL_DIR, d)
+    mpath = d / LD.FAST_DIRNAME / "manifest.json"
+    man = json.loads(mpath.read_text())
+    bad = dict(man, format="fast_qwen3_q4nx_layer_v0")
+    mpath.write_text(json.dumps(bad))
+    with pytest.raises(RuntimeError, match="unsupported fast Qwen3 format"):
+        LD.FastArtifact(d / LD.FAST_DIRNAME)
+    man["linears"]["model.layers.0.mlp.down_proj"]["byte_length"] -= 16
+    mpath.write_text(json.dumps(man))
+    with pytest.raises(ValueError, match="layout needs"):
+        LD.load_fast_qwen3_artifact(d)
+    from torch2iron_b200.engine import DecodeEngine
+    cfg, model = LD.load_fast_qwen3_artifact(MODEL_DIR)
+    with pytest.raises(NotImplementedError, match="Q4NX"):
+        DecodeEngine(cfg, model, batch=1, max_ctx=64)

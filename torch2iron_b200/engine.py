@@ -61,6 +61,12 @@ class LayerWeights:
 
 
 def load_layer(layer: dict, cfg: QuantizedQwenConfig, device="cuda") -> LayerWeights:
+    for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+        if not isinstance(layer[name], AutoGPTQLinear):
+            raise NotImplementedError(
+                f"{name} is a {type(layer[name]).__name__}: the decode kernels take group-128 AutoGPTQ-derived "
+                "weights (the packed artifact or the checkpoint); Q4NX group-32 weights are not supported yet")
+
     def bf(t):
         return None if t is None else t.to(device=device, dtype=torch.bfloat16).contiguous()
 

@@ -1,6 +1,6 @@
 """Weight loaders: the reference's on-disk formats into this engine's model dict.
 
-Two sources, both producing ``(QuantizedQwenConfig, model)`` where ``model``
+Three sources, each producing ``(QuantizedQwenConfig, model)`` where ``model``
 has the layout ``synth.random_model`` returns (``layers`` of AutoGPTQ linears
 and bf16 norms, bf16 ``embed`` / ``final_norm``, and ``lm_head`` = ``None``
 (tied), a bf16 ``[V, H]`` tensor, or an ``AutoGPTQLinear`` for a W4A16 head):
@@ -23,7 +23,11 @@ and bf16 norms, bf16 ``embed`` / ``final_norm``, and ``lm_head`` = ``None``
   runs after packing (scales rounded to bf16 by ``make_qparam``; a dense or
   tied head quantized like ``quantize_dense_to_biased_int4``, :384-402);
   ``numerics="checkpoint"`` keeps the checkpoint's fp16 scales and its bf16
-  head.
+  head;
+* the fast Qwen3 artifact ``fast_qwen3_q4nx/`` (format
+  ``fast_qwen3_q4nx_layer_v1``, ``fast_qwen3/fast_packed_format.py:178-300``):
+  bf16 dense tensors and Q4NX group-32 linears (``Q4NXLinear``, bytes as
+  stored).  The decode engine does not run Q4NX weights yet.
 
 The T2B meta word stores an fp16 scale, so a bf16 scale is accepted only when
 fp16 holds it exactly (every bf16 value of magnitude >= 2**-17 does) or when
@@ -35,6 +39,7 @@ from __future__ import annotations
 
 import json
 import sys
+from dataclasses import dataclass
 from pathlib import Path
 
 import numpy as np
@@ -384,6 +389,113 @@ def load_autogptq_checkpoint(model_dir: str | Path, numerics: str = "reference")
     else:
         lm_head = dense("lm_head.weight") if "lm_head.weight" in t else None
     model = {"layers": layers, "embed": embed, "final_norm": dense("model.norm.weight"), "lm_head": lm_head}
+    cfg = config_from_hf(hf, qk_norm=qk_norm, tie_word_embeddings=lm_head is None)
+    _check_shapes(cfg, model)
+    return cfg, model
+
+
+# ---------------------------------------------------------------------------
+# fast Qwen3 artifact (Q4NX group-32 weights)
+# ---------------------------------------------------------------------------
+FAST_FORMAT = "fast_qwen3_q4nx_layer_v1"
+FAST_DIRNAME = "fast_qwen3_q4nx"
+Q4NX_CHUNK_BYTES = 5120   # 32 rows x 256 k: 256 bf16 scales, 256 bf16 zero points, 4096 bytes of 4-bit values
+
+
+@dataclass
+class Q4NXLinear:
+    """One linear of the fast Qwen3 artifact as stored: output rows padded to
+    64-row patches, each patch K-chunk-major as pairs of 32-row x 256-k chunks,
+    a chunk = bf16 scales and bf16 zero points per 32 k, then two 4-bit values
+    per byte (low nibble = even k); ``w = (q - zero) * scale``
+    (``fast_qwen3/q4nx_layout.py:14-38,115-237``).  ``data`` is uint8."""
+
+    data: torch.Tensor
+    in_features: int
+    out_features: int
+    padded_out_features: int
+    group_size: int = 32
+
+    @property
+    def n_chunks(self) -> int:
+        return self.padded_out_features // 32 * (self.in_features // 256)
+
+
+def find_fast_dir(path: str | Path) -> Path | None:
+    """The fast artifact directory for ``path`` (itself, ``path/fast_qwen3_q4nx``,
+    else the newest fast manifest below it), as ``find_fast_dir`` of
+    fast_packed_format.py:45-62 resolves it."""
+    def ok(m: Path) -> bool:
+        try:
+            return json.loads(m.read_text()).get("format") == FAST_FORMAT
+        except (OSError, ValueError):
+            return False
+
+    path = Path(path).expanduser().resolve()
+    for cand in (path, path / FAST_DIRNAME):
+        if ok(cand / PACKED_MANIFEST):
+            return cand
+    if not path.is_dir():
+        return None
+    found = [m.parent for m in path.rglob(PACKED_MANIFEST) if ok(m)]
+    found.sort(key=lambda d: (d / PACKED_MANIFEST).stat().st_mtime, reverse=True)
+    return found[0] if found else None
+
+
+class FastArtifact(PackedArtifact):
+    """Read-only view of a fast Qwen3 artifact (``FastQwen3Store``,
+    fast_packed_format.py:265-300): bf16 dense tensors and Q4NX linears."""
+
+    FORMAT = FAST_FORMAT
+
+    def __init__(self, fast_dir: str | Path):
+        self.dir = Path(fast_dir).expanduser().resolve()
+        mpath = self.dir / PACKED_MANIFEST
+        if not mpath.exists():
+            raise FileNotFoundError(f"missing fast Qwen3 manifest: {mpath}")
+        self.manifest = json.loads(mpath.read_text())
+        if self.manifest.get("format") != FAST_FORMAT:
+            raise RuntimeError(f"unsupported fast Qwen3 format {self.manifest.get('format')!r}")
+        self.data_path = self.dir / self.manifest["data_file"]
+        self._data = np.memmap(self.data_path, dtype=np.uint8, mode="r")
+
+    def linear(self, prefix: str) -> Q4NXLinear:
+        try:
+            e = self.manifest["linears"][prefix]
+        except KeyError as exc:
+            raise KeyError(f"missing Q4NX linear {prefix!r}") from exc
+        if int(e["group_size"]) != 32 or int(e["in_chunk"]) != 256 or int(e["out_chunk"]) != 32:
+            raise ValueError(f"{prefix}: not the Q4NX group-32 layout")
+        lin = Q4NXLinear(torch.empty(0, dtype=torch.uint8), int(e["in_features"]), int(e["out_features"]),
+                         int(e["padded_out_features"]))
+        want = lin.n_chunks * Q4NX_CHUNK_BYTES
+        if int(e["byte_length"]) != want:
+            raise ValueError(f"{prefix}: {e['byte_length']} bytes, the layout needs {want}")
+        lin.data = torch.from_numpy(np.array(self._bytes({"name": prefix, **e})))
+        return lin
+
+
+def load_fast_qwen3_artifact(path: str | Path, hf_config: dict | None = None) -> tuple[QuantizedQwenConfig, dict]:
+    """Load a ``fast_qwen3_q4nx`` artifact (or a model dir holding one): dense
+    tensors as bf16, the linears as ``Q4NXLinear``.  The decode engine does not
+    run Q4NX weights yet (its kernels take the group-128 T2B layout)."""
+    fdir = find_fast_dir(path)
+    if fdir is None:
+        raise FileNotFoundError(f"no {FAST_FORMAT} artifact under {path}")
+    art = FastArtifact(fdir)
+    hf = dict(hf_config) if hf_config is not None else _hf_config_near(fdir)
+    for key, val in art.manifest.get("model_config", {}).items():
+        if val is not None and key in hf and hf[key] is not None and float(hf[key]) != float(val):
+            raise ValueError(f"manifest model_config {key}={val} disagrees with config.json ({hf[key]})")
+    layers, qk_norm = _model_from(art.linear, art.dense, art.has_dense, int(hf["num_hidden_layers"]))
+    if art.has_linear("lm_head"):
+        lm_head = art.linear("lm_head")
+    elif art.has_dense("lm_head.weight"):
+        lm_head = art.dense("lm_head.weight")
+    else:
+        lm_head = None
+    model = {"layers": layers, "embed": art.dense("model.embed_tokens.weight"),
+             "final_norm": art.dense("model.norm.weight"), "lm_head": lm_head}
     cfg = config_from_hf(hf, qk_norm=qk_norm, tie_word_embeddings=lm_head is None)
     _check_shapes(cfg, model)
     return cfg, model
