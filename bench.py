@@ -44,11 +44,18 @@ def parse():
     ap.add_argument("--impl", default="t2b", choices=["t2b", "reference"])
     ap.add_argument("--batch", type=int, default=64, help="rows per GPU")
     ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--gen", type=int, default=128,
+                    help="tokens the configuration generates per sequence: the timed window is centred on "
+                         "the mean decode context prompt + gen/2")
     ap.add_argument("--model", default="qwen3-0.6b", choices=sorted(PRESETS))
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the batch sweep (config 2 at 1/8/32 rows) and the config 3 line (N=1 only)")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="skip the config 4 tensor-parallel run that N>1 bench lines carry under 'tp'")
     ap.add_argument("--tp", type=int, default=0,
                     help="tensor-parallel ranks (config 4: --model qwen3-8b --tp 8 under torchrun); "
                          "the batch is then the global batch")
@@ -137,24 +144,28 @@ def peaks():
 # ---------------------------------------------------------------------------
 # CPU side (oracle = the reference algorithm restated; checker / baseline only)
 # ---------------------------------------------------------------------------
-def cpu_decode_rate(cfg, model_cpu, batch, ctx_fill, steps, seed):
-    """Time ``steps`` oracle decode steps for ``batch`` rows at context ``ctx_fill`` on the host cores."""
+def cpu_decode_rate(cfg, model_cpu, batch, first_ctx, steps, seed, warmup=1):
+    """Time ``steps`` oracle decode steps for ``batch`` rows on the host cores,
+    step s attending ``first_ctx + s`` keys (positions before ``first_ctx - 1``
+    pre-filled with N(0,1) bf16); ``warmup`` untimed steps first."""
     import oracle
     from tests.gpu_util import oracle_decoder
 
     torch.set_num_threads(os.cpu_count() or 1)
-    dec = oracle_decoder(cfg, model_cpu, batch, ctx_fill + steps + 1)
+    fill = first_ctx - 1
+    dec = oracle_decoder(cfg, model_cpu, batch, first_ctx + steps)
     g = torch.Generator().manual_seed(seed)
     for li in range(cfg.n_layers):
-        dec.k_cache[li][:, :, :ctx_fill] = torch.randn(batch, cfg.n_kv_groups, ctx_fill, cfg.head_dim,
-                                                       generator=g).to(torch.bfloat16)
-        dec.v_cache[li][:, :, :ctx_fill] = torch.randn(batch, cfg.n_kv_groups, ctx_fill, cfg.head_dim,
-                                                       generator=g).to(torch.bfloat16)
+        dec.k_cache[li][:, :, :fill] = torch.randn(batch, cfg.n_kv_groups, fill, cfg.head_dim,
+                                                   generator=g).to(torch.bfloat16)
+        dec.v_cache[li][:, :, :fill] = torch.randn(batch, cfg.n_kv_groups, fill, cfg.head_dim,
+                                                   generator=g).to(torch.bfloat16)
     tok = torch.randint(0, cfg.vocab_size, (batch,), generator=g)
-    dec.step(tok, torch.full((batch,), ctx_fill, dtype=torch.long))       # warm (page-in)
+    for _ in range(max(1, warmup)):                                        # page-in; rewrites slot fill
+        dec.step(tok, torch.full((batch,), fill, dtype=torch.long))
     t0 = time.perf_counter()
     for s in range(steps):
-        logits = dec.step(tok, torch.full((batch,), ctx_fill + 1 + s, dtype=torch.long))
+        logits = dec.step(tok, torch.full((batch,), fill + s, dtype=torch.long))
         tok = torch.argmax(logits, -1)
     dt = time.perf_counter() - t0
     del oracle
@@ -169,32 +180,48 @@ def model_to_cpu(model):
     return out
 
 
+def timed_window(args) -> tuple[int, int]:
+    """Keys attended by the first and the last timed step.  The window of
+    ``--steps`` steps is centred on the configuration's mean decode context
+    (prompt + gen/2: 192 for 128 prompt + 128 generated tokens), and starts
+    after the prompt and the warm-up steps."""
+    first = max(args.prompt + args.warmup + 1, args.prompt + args.gen // 2 - args.steps // 2)
+    return first, first + args.steps - 1
+
+
+L2_NOTE = "inputs larger than L2 (126 MB): every step reads all weights, the lm_head and the KV cache once"
+
+
 def arm_config(args, world):
     """The workload description both arms report (identical for the reference arm)."""
-    c0 = args.prompt + args.warmup + 1
-    c1 = c0 + args.steps - 1
+    c0, c1 = timed_window(args)
     cfg_no = {"qwen3-0.6b": 2, "llama-3.2-1b": 3, "qwen3-8b": 4}.get(args.model, 2)   # benchmark configuration number
     return {"workload": f"config{cfg_no} {args.model} greedy decode, {args.batch} rows/GPU, prompt {args.prompt}, "
                         f"timed ctx {c0}..{c1}",
-            "model": args.model, "global_batch": world * args.batch, "seq_len": c1, "parallelism": f"dp{world}"}
+            "model": args.model, "global_batch": world * args.batch, "seq_len": c1, "parallelism": f"dp{world}",
+            "l2": L2_NOTE}
 
 
 def run_reference(args, cfg):
+    """The reference arm: the reference's CPU decode path (the oracle
+    restatement of ``model.py``) on the host cores, rank 0 only, every one of
+    the ``--steps`` timed steps run (``--warmup`` untimed steps first) on the
+    GPU arm's workload and timed window."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     model = synth.random_model(cfg, seed=args.seed, device="cpu")
-    ctx = args.prompt + args.warmup + 1
-    rate, dt, cores = cpu_decode_rate(cfg, model, args.batch, ctx, max(1, min(args.steps, args.cpu_sample_steps)),
-                                      args.seed)
+    c0, c1 = timed_window(args)
+    rate, dt, cores = cpu_decode_rate(cfg, model, args.batch, c0, args.steps, args.seed, warmup=args.warmup)
     line = {"metric": METRIC, "value": round(rate, 3), "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1000 * args.batch / rate, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4-weights/fp32-compute", "data": "synthetic",
             "impl": "reference",
-            "config": dict(arm_config(args, args.gpus), l2="host memory (CPU path)"),
+            "config": arm_config(args, args.gpus),
             "cpu_baseline": {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": f"{max(1, min(args.steps, args.cpu_sample_steps))} decode steps x {args.batch} "
-                                       f"rows at ctx {ctx} ({dt:.1f} s)"},
+                             "sample": f"all {args.steps} timed decode steps x {args.batch} rows, ctx {c0}..{c1} "
+                                       f"({dt:.1f} s), after {args.warmup} untimed steps; one host process "
+                                       "whatever the GPU count"},
             "e2e": {"value": round(rate, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -328,55 +355,59 @@ def kernel_profile(eng, steps):
     return {k: (times[k] / counts[k], counts[k]) for k in times}
 
 
-def kernel_profile_graph(eng, reps=20, rounds=5):
-    """Per-launch device time of each fused op: layer 0's op (and the lm_head)
-    captured as a CUDA graph of `reps` back-to-back launches -- chained by
-    programmatic dependent launch as in the decode step, so a launch's
-    constant-data prologue overlaps its predecessor -- replayed `rounds` times
-    between CUDA events on the capture stream.  Returns name -> (ms per
+def kernel_profile_graph(eng, rounds=5):
+    """Per-launch device time of each fused op: the op of every layer in turn
+    (layer 0, 1, ..., n_layers-1, so consecutive launches read different
+    weights and KV caches: at bs 64 the 28 KV caches of the attention launches
+    are ~1.4 GB, far above L2) captured as one CUDA graph of back-to-back
+    launches -- chained by programmatic dependent launch as in the decode
+    step, so a launch's constant-data prologue overlaps its predecessor --
+    replayed ``rounds`` times between CUDA events on the capture stream; the
+    lm_head 20 times (its 311 MB table exceeds L2).  Returns name -> (ms per
     launch, launches per decode step)."""
     L = _lib.lib()
     cfg, B = eng.cfg, eng.B
     p = _lib.ptr
-    lw = eng.layers[0]
     H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
     nl = cfg.n_layers
+    lw = eng.layers
     ops = {
-        "qkv_norm_rope_kvwrite": (nl, lambda st: L.t2b_qkv_norm_rope_kvwrite(
-            p(lw.qkv.qw), p(lw.qkv.meta), p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps, p(lw.q_norm), p(lw.k_norm),
-            p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[0]), p(eng.v_cache[0]), p(eng.ssq_b), B, H, nq, nkv,
-            hd, eng.max_ctx, *eng._ws("qkv"), st)),
-        "decode_attention": (nl, lambda st: L.t2b_decode_attention_after_kvwrite(
-            p(eng.q), p(eng.k_cache[0]), p(eng.v_cache[0]), p(eng.pos), p(eng.attn), B, nq, nkv, hd, eng.max_ctx,
+        "qkv_norm_rope_kvwrite": (nl, lambda st, i: L.t2b_qkv_norm_rope_kvwrite(
+            p(lw[i].qkv.qw), p(lw[i].qkv.meta), p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps, p(lw[i].q_norm),
+            p(lw[i].k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.ssq_b),
+            B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st)),
+        "decode_attention": (nl, lambda st, i: L.t2b_decode_attention_after_kvwrite(
+            p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.pos), p(eng.attn), B, nq, nkv, hd, eng.max_ctx,
             *eng._ws("attn"), st)),
-        "oproj_residual": (nl, lambda st: L.t2b_oproj_residual(
-            p(lw.o_proj.qw), p(lw.o_proj.meta), p(eng.attn), p(eng.x), p(eng.ssq_b), p(lw.post_attention_layernorm),
-            p(eng.xw), B, H, cfg.q_dim, *eng._ws("o"), st)),
-        "upgate_swiglu": (nl, lambda st: L.t2b_upgate_swiglu(
-            p(lw.gate_up.qw), p(lw.gate_up.meta), p(eng.xw), p(eng.ssq_b), cfg.rms_norm_eps, p(eng.h), p(eng.ssq_a),
-            B, H, cfg.hidden_dim, *eng._ws("ug"), st)),
-        "down_residual": (nl, lambda st: L.t2b_down_residual(
-            p(lw.down.qw), p(lw.down.meta), p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(0)), p(eng.xw),
-            B, H, cfg.hidden_dim, *eng._ws("down"), st)),
+        "oproj_residual": (nl, lambda st, i: L.t2b_oproj_residual(
+            p(lw[i].o_proj.qw), p(lw[i].o_proj.meta), p(eng.attn), p(eng.x), p(eng.ssq_b),
+            p(lw[i].post_attention_layernorm), p(eng.xw), B, H, cfg.q_dim, *eng._ws("o"), st)),
+        "upgate_swiglu": (nl, lambda st, i: L.t2b_upgate_swiglu(
+            p(lw[i].gate_up.qw), p(lw[i].gate_up.meta), p(eng.xw), p(eng.ssq_b), cfg.rms_norm_eps, p(eng.h),
+            p(eng.ssq_a), B, H, cfg.hidden_dim, *eng._ws("ug"), st)),
+        "down_residual": (nl, lambda st, i: L.t2b_down_residual(
+            p(lw[i].down.qw), p(lw[i].down.meta), p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(i)),
+            p(eng.xw), B, H, cfg.hidden_dim, *eng._ws("down"), st)),
     }
     if eng.lm_w4 is None:
-        ops["lm_head_argmax"] = (1, lambda st: L.t2b_lm_head_argmax(
+        ops["lm_head_argmax"] = (1, lambda st, i: L.t2b_lm_head_argmax(
             p(eng.xn), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
             *eng._ws("lm"), st))
     out = {}
     side = torch.cuda.Stream()
     for name, (per_step, fn) in ops.items():
+        reps = nl if per_step == nl else 20
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            for _ in range(2):
-                _lib.check(name, fn(side.cuda_stream))
+            for i in range(2):
+                _lib.check(name, fn(side.cuda_stream, i % nl))
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             st = torch.cuda.current_stream()
-            for _ in range(reps):
-                fn(st.cuda_stream)
+            for i in range(reps):
+                fn(st.cuda_stream, i % nl)
         g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -387,6 +418,64 @@ def kernel_profile_graph(eng, reps=20, rounds=5):
         torch.cuda.synchronize()
         out[name] = (e0.elapsed_time(e1) / (rounds * reps), per_step)
         del g
+    return out
+
+
+def advance_to(eng, first_ctx: int) -> None:
+    """Untimed greedy steps until the next step attends ``first_ctx`` keys."""
+    n = first_ctx - 1 - int(eng.pos[0].item())
+    if n < 0:
+        raise ValueError(f"the engine is already past context {first_ctx}")
+    for _ in range(n):
+        eng.advance()
+    torch.cuda.synchronize()
+
+
+def time_steps(eng, steps: int) -> float:
+    """Device time (ms, CUDA events on the replay stream) of ``steps`` greedy steps."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        eng.advance()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def decode_point(cfg, model, B, args, first_ctx, peak, seed, prefill=True) -> dict:
+    """tokens/s and byte-roofline fraction of B rows decoding from context
+    ``first_ctx`` (one GPU): the prompt prefilled (``prefill``) or the KV cache
+    filled with N(0,1) bf16 up to ``first_ctx - 1`` positions."""
+    from torch2iron_b200.engine import DecodeEngine
+
+    last = first_ctx + args.steps - 1
+    max_ctx = ((last + 63) // 64) * 64
+    eng = DecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, use_graph=True, keep_logits=False)
+    g = torch.Generator().manual_seed(seed)
+    if prefill:
+        eng.prefill(torch.randint(0, cfg.vocab_size, (B, args.prompt), generator=g))
+    else:
+        gd = torch.Generator(device="cuda").manual_seed(seed)
+        for kc, vc in zip(eng.k_cache, eng.v_cache):
+            kc[:, :, :first_ctx - 1].normal_(generator=gd)
+            vc[:, :, :first_ctx - 1].normal_(generator=gd)
+        eng.tokens.copy_(torch.randint(0, cfg.vocab_size, (B,), generator=g))
+        eng.pos.fill_(first_ctx - 1)
+        for _ in range(args.warmup):          # warm-up steps rewrite slot first_ctx - 1
+            eng.advance()
+            eng.pos.fill_(first_ctx - 1)
+    advance_to(eng, first_ctx)
+    ms = time_steps(eng, args.steps)
+    eng.check_device_errors()
+    avg = sum(eng.step_bytes([c] * B) for c in range(first_ctx, last + 1)) / args.steps
+    gbs = avg / (ms / args.steps * 1e-3) / 1e9
+    out = {"batch": B, "value": round(B * args.steps / (ms / 1000), 1), "unit": "tokens/s",
+           "ms_per_step": round(ms / args.steps, 4), "ctx": f"{first_ctx}..{last}",
+           "algorithmic_bytes_per_step": int(avg), "achieved_gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)}
+    eng.release()
+    del eng
+    torch.cuda.empty_cache()
     return out
 
 
@@ -403,7 +492,8 @@ def run_t2b(args, cfg):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     B, P = args.batch, args.prompt
-    max_ctx = ((P + args.warmup + args.steps + 1 + 63) // 64) * 64
+    first, last = timed_window(args)
+    max_ctx = ((last + 63) // 64) * 64
     model = synth.random_model(cfg, seed=args.seed, device="cuda")
     eng = DecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, use_graph=True, keep_logits=False)
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
@@ -422,13 +512,10 @@ def run_t2b(args, cfg):
         t = torch.tensor([prefill_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         prefill_ms = float(t.item())
-    for _ in range(args.warmup):
-        eng.advance()
-    torch.cuda.synchronize()
+    advance_to(eng, first)                   # the warm-up steps and the way to the window
     start_tokens = eng.tokens.clone()
     start_pos = eng.pos.clone()
-    ctx_lens = [P + args.warmup + 1 + s for s in range(args.steps)]
-    step_bytes = [eng.step_bytes([c] * B) for c in ctx_lens]
+    step_bytes = [eng.step_bytes([c] * B) for c in range(first, last + 1)]
 
     # ---- device-resident timed region -------------------------------------
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -450,12 +537,13 @@ def run_t2b(args, cfg):
         ms = float(t.item())
         dist.barrier()
 
-    # ---- end to end through the host API (pinned host tokens in / out) ------
+    # ---- end to end through the host API: DecodeEngine.decode_step ---------
+    # (pinned host tokens and positions in, next tokens and the status word out,
+    # one synchronisation per step)
     eng.tokens.copy_(start_tokens)
     eng.pos.copy_(start_pos)
     tok_h = torch.empty(B, dtype=torch.int32).pin_memory()
     pos_h = torch.empty(B, dtype=torch.int32).pin_memory()
-    out_h = torch.empty(B, dtype=torch.int32).pin_memory()
     tok_h.copy_(start_tokens.cpu())
     pos_h.copy_(start_pos.cpu())
     torch.cuda.synchronize()
@@ -464,12 +552,8 @@ def run_t2b(args, cfg):
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
     for _ in range(args.steps):
-        eng.tokens.copy_(tok_h, non_blocking=True)
-        eng.pos.copy_(pos_h, non_blocking=True)
-        eng.run_step()
-        out_h.copy_(eng.next_tokens, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        tok_h.copy_(out_h)
+        out = eng.decode_step(tok_h, pos_h)
+        tok_h.copy_(out)
         pos_h.add_(1)
     f1.record()
     torch.cuda.synchronize()
@@ -493,11 +577,11 @@ def run_t2b(args, cfg):
         eager = kernel_profile(eng, 2)
         prof = kernel_profile_graph(eng)
         dom = max(prof, key=lambda k: prof[k][0] * prof[k][1])   # device time per decode step
-        mid_ctx = P + args.warmup + 1
+        ctx0 = int(start_pos[0].item()) + 1                      # keys the profiled launches attend
         kv_tok = 2 * cfg.n_kv_groups * cfg.head_dim * 2
         l0 = eng.layers[0]
         kernel_bytes = {
-            "decode_attention": B * mid_ctx * kv_tok + 2 * B * cfg.q_dim * 2,
+            "decode_attention": B * ctx0 * kv_tok + 2 * B * cfg.q_dim * 2,
             "qkv_norm_rope_kvwrite": l0.qkv.nbytes_algorithmic + B * cfg.emb_dim * 4 + B * (cfg.q_dim + 2 * cfg.kv_dim) * 2,
             "oproj_residual": l0.o_proj.nbytes_algorithmic + B * cfg.q_dim * 2 + 2 * B * cfg.emb_dim * 4,
             "upgate_swiglu": l0.gate_up.nbytes_algorithmic + B * cfg.emb_dim * 4 + B * cfg.hidden_dim * 2,
@@ -510,7 +594,7 @@ def run_t2b(args, cfg):
         if dom == "decode_attention" and cfg.head_dim == NCU_ATTN["head_dim"]:
             # ncu DRAM bytes of one capture, scaled by the keys this launch loads
             # (tiles load whole 16-key boxes at the end of each unit)
-            loaded = 64 * (mid_ctx // 64) + 16 * -(-(mid_ctx % 64) // 16)
+            loaded = 64 * (ctx0 // 64) + 16 * -(-(ctx0 % 64) // 16)
             per_key = NCU_ATTN["dram_bytes"] / (NCU_ATTN["units"] * NCU_ATTN["keys_loaded"])
             traffic = int(per_key * B * cfg.n_kv_groups * loaded)
             traffic_src = NCU_ATTN["source"]
@@ -519,8 +603,7 @@ def run_t2b(args, cfg):
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4-weights/bf16-activations/fp32-accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
-            "config": dict(arm_config(args, world), l2="working set > L2 every step (weights+lm_head+KV "
-                                                           f"~{avg_bytes / 1e9:.2f} GB/step/GPU)"),
+            "config": arm_config(args, world),
             "hbm": {"algorithmic_bytes_per_step": int(avg_bytes),
                     "achieved_gbs": round(avg_bytes / (ms / args.steps * 1e-3) / 1e9, 1),
                     "frac_of_peak": round(avg_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4),
@@ -529,13 +612,16 @@ def run_t2b(args, cfg):
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                          "traffic_source": traffic_src,
                          "bytes_per_launch": kernel_bytes[dom], "avg_launch_us": round(dur_ms * 1000, 2),
-                         "peak_source": peak_kind,
-                         "timing": "per launch in a CUDA graph of 20 back-to-back launches of the op "
-                                   "(PDL-chained as in the step), 5 replays, CUDA events on the capture stream",
+                         "ctx": ctx0, "peak_source": peak_kind,
+                         "timing": "per launch in a CUDA graph of the op over all layers in turn (different "
+                                   "weights and KV caches each launch; PDL-chained as in the step), 5 replays, "
+                                   "CUDA events on the capture stream",
                          "kernel_avg_us": {k: round(v[0] * 1000, 2) for k, v in prof.items()},
                          "kernel_eager_us": {k: round(v[0] * 1000, 2) for k, v in eager.items()}},
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * B * 4,
-                    "d2h_bytes_per_step": B * 4},
+                    "d2h_bytes_per_step": B * 4 + 4,
+                    "how": "DecodeEngine.decode_step per step: pinned host tokens and positions in, next tokens "
+                           "and the status word out (one synchronisation)"},
             "gpu_launches": eng.kernels_per_step() * args.steps,
             "clocks": clocks.summary(),
             "prefill": {"value": round(world * B * P / (prefill_ms / 1000), 1), "unit": "prompt tokens/s",
@@ -547,14 +633,41 @@ def run_t2b(args, cfg):
         if not args.no_gemv:
             line["gemv_b1"] = gemv_batch1(eng, peak)
             line["gemv_b1_streams"] = gemv_batch1(eng, peak, n_streams=4)
-        if not args.no_cpu_baseline and world == 1:   # host-core baseline: rank 0 at N=1 only
-            mcpu = model_to_cpu(model)
-            rate, dt, cores = cpu_decode_rate(cfg, mcpu, B, mid_ctx, args.cpu_sample_steps, args.seed)
-            line["cpu_baseline"] = {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                                    "sample": f"{args.cpu_sample_steps} oracle decode steps x {B} rows at ctx "
-                                              f"{mid_ctx} ({dt:.1f} s)"}
         result = line
     eng.release()
+    del eng
+    torch.cuda.empty_cache()
+    if result is not None and world == 1:
+        if not args.no_cpu_baseline:            # host-core baseline: rank 0 at N=1 only
+            mcpu = model_to_cpu(model)
+            rate, dt, cores = cpu_decode_rate(cfg, mcpu, B, first, args.cpu_sample_steps, args.seed)
+            del mcpu
+            result["cpu_baseline"] = {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                      "sample": f"{args.cpu_sample_steps} oracle decode steps x {B} rows at ctx "
+                                                f"{first}..{first + args.cpu_sample_steps - 1} ({dt:.1f} s)"}
+        if not args.no_sweep and args.model == "qwen3-0.6b":
+            # the other batch sizes of configuration 2 (same weights, same timed window)
+            result["sweep"] = [decode_point(cfg, model, b, args, first, peak, seed=args.seed + b)
+                               for b in (1, 8, 32) if b != B]
+            # configuration 3: Llama-3.2-1B, 32 rows, KV cache pre-filled to a 2048-token context
+            del model
+            torch.cuda.empty_cache()
+            from torch2iron_b200.config import LLAMA_3_2_1B
+            m3 = synth.random_model(LLAMA_3_2_1B, seed=args.seed, device="cuda")
+            f3 = 2048 + args.gen // 2 - args.steps // 2
+            result["config3"] = dict(decode_point(LLAMA_3_2_1B, m3, 32, args, f3, peak, seed=args.seed + 3,
+                                                  prefill=False),
+                                     workload="config3 llama-3.2-1b greedy decode, 32 rows, KV cache "
+                                              "pre-filled N(0,1) bf16 to a 2048-token context")
+            del m3
+            torch.cuda.empty_cache()
+    if world > 1 and not args.no_tp and args.model == "qwen3-0.6b":
+        # configuration 4 on the same ranks: Qwen3-8B tensor parallel over all N GPUs
+        del model
+        torch.cuda.empty_cache()
+        tp_line = tp_measure(args, PRESETS["qwen3-8b"], world, rank, local, batch=64, ctx=4096)
+        if result is not None:
+            result["tp"] = tp_line
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -586,25 +699,18 @@ def fail_on_device_status(eng, world: int) -> None:
                      f"({_lib.load().t2b_status_string(code).decode()}): measurement void")
 
 
-def run_tp(args, cfg):
-    """Config 4: one model split over the torchrun ranks (tensor parallel), B rows
-    in total, the KV cache pre-filled with N(0,1) bf16 to --ctx positions; K timed
-    decode steps (one CUDA graph per step, the two NCCL all-reduces per layer
-    captured between the fused kernels)."""
+def tp_measure(args, cfg, world, rank, local, batch, ctx) -> dict | None:
+    """Config 4 on the initialised process group: one model split over the
+    ``world`` ranks (tensor parallel), ``batch`` rows in total, the KV cache
+    pre-filled with N(0,1) bf16 to ``ctx`` positions; ``--steps`` timed decode
+    steps (one CUDA graph per step, the two NCCL all-reduces per layer
+    captured between the fused kernels).  Returns rank 0's description (None
+    on the other ranks); every rank takes the same collective steps."""
     import torch.distributed as dist
-    from datetime import timedelta
 
     from torch2iron_b200.tp import TPDecodeEngine
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.tp:
-        raise SystemExit(f"--tp {args.tp} needs {args.tp} ranks (torchrun --nproc-per-node {args.tp}), got {world}")
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    B, C = args.batch, args.ctx
+    B, C = batch, ctx
     max_ctx = ((C + args.warmup + args.steps + 1 + 63) // 64) * 64
     model = synth.random_model(cfg, seed=args.seed, device="cuda")
     eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank, use_graph=not args.tp_eager)
@@ -634,6 +740,7 @@ def run_tp(args, cfg):
     if world > 1:
         dist.all_reduce(probe, op=dist.ReduceOp.MAX)
     steps = max(1, min(args.steps, int(10_000 / max(float(probe.item()), 1e-3))))
+    c_first = int(eng.pos[0].item()) + 1
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         e0.record()
@@ -641,45 +748,72 @@ def run_tp(args, cfg):
             eng.advance()
         e1.record()
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) * args.steps / steps
+    ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    fail_on_device_status(eng, world)
+    status = device_status(eng, world)
     # bytes one GPU must move per step: its weight shard, lm_head slice, KV of its kv heads
     lc = eng.lcfg
-    c_mid = C + args.warmup + 1 + args.steps // 2
+    c_mid = c_first + steps // 2
     kv_tok = 2 * lc.n_kv_groups * cfg.head_dim * 2
     w_bytes = sum(l.algorithmic_bytes for l in eng.layers) + eng.lm_head.numel() * 2
     gpu_bytes = w_bytes + B * c_mid * kv_tok * cfg.n_layers
     peak, peak_kind = peaks()
+    line = None
     if rank == 0:
-        value = B * args.steps / (ms / 1000)
-        per_gpu_gbs = gpu_bytes / (ms / args.steps * 1e-3) / 1e9
+        per_gpu_gbs = gpu_bytes / (ms / steps * 1e-3) / 1e9
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int4-weights/bf16-activations/fp32-accumulate",
-            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) bf16 KV pre-fill, uniform-random token ids)",
-            "config": {"workload": f"config4 {args.model} greedy decode, {B} rows, tensor parallel over {world} "
-                                   f"GPUs, ctx {C + args.warmup + 1}..{C + args.warmup + args.steps}",
-                       "model": args.model, "global_batch": B, "seq_len": C + args.warmup + args.steps,
-                       "parallelism": f"tp{world}",
-                       "l2": f"working set > L2 every step (~{gpu_bytes / 1e9:.2f} GB/step/GPU)"},
+            "metric": METRIC, "value": round(B * steps / (ms / 1000), 1) if status == 0 else None,
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / steps, 4), "scaling": "strong",
+            "config": {"workload": f"config4 {cfg_name(cfg)} greedy decode, {B} rows, tensor parallel over {world} "
+                                   f"GPUs, KV cache pre-filled N(0,1) bf16, ctx {c_first}..{c_first + steps - 1}",
+                       "model": cfg_name(cfg), "global_batch": B, "seq_len": c_first + steps - 1,
+                       "parallelism": f"tp{world}", "l2": L2_NOTE},
             "hbm": {"algorithmic_bytes_per_step_per_gpu": int(gpu_bytes), "achieved_gbs_per_gpu": round(per_gpu_gbs, 1),
                     "frac_of_peak": round(per_gpu_gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_kind},
             "gpu_launches": eng.kernels_per_step() * steps,
-            "timed_steps": steps,
             "collectives_per_step": 2 * cfg.n_layers + 2,
+            "allreduce_dtype": str(eng.partial_dtype).replace("torch.", ""),
+            "device_status": status,
             "clocks": clocks.summary(),
         }
-        print(json.dumps(line), flush=True)
     eng.release()   # graphs holding NCCL calls go before the process group
+    del eng
+    torch.cuda.empty_cache()
+    return line
+
+
+def cfg_name(cfg) -> str:
+    return next((k for k, v in PRESETS.items() if v == cfg), "custom")
+
+
+def run_tp(args, cfg):
+    """``--tp N`` under torchrun: config 4 alone (see tp_measure), one JSON line."""
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.tp:
+        raise SystemExit(f"--tp {args.tp} needs {args.tp} ranks (torchrun --nproc-per-node {args.tp}), got {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    line = tp_measure(args, cfg, world, rank, local, batch=args.batch, ctx=args.ctx)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if line is not None:
+        line.update(higher_is_better=True, vs_baseline=None, dtype="int4-weights/bf16-activations/fp32-accumulate",
+                    data="synthetic (seeded N(0,0.02) weights, N(0,1) bf16 KV pre-fill, uniform-random token ids)")
+        print(json.dumps(line), flush=True)
+        if line["device_status"]:
+            raise SystemExit(f"a decode kernel recorded status {line['device_status']}: measurement void")
 
 
 def main():

@@ -73,16 +73,26 @@ T2B_API int t2b_version(void);
 T2B_API const char* t2b_status_string(int status);
 
 /*
- * Device status word (int32, device memory, zeroed by the caller): every
- * kernel launched after this call records T2B_ERR_TIMEOUT there when one of
- * its time-bounded waits (0.5 s) gives up -- the kernel then skips its output
- * instead of hanging.  One word per process; NULL stops recording.
+ * Device status words (int32, device memory, zeroed by the caller): a kernel
+ * records T2B_ERR_TIMEOUT in its launch's word when one of its time-bounded
+ * waits (0.5 s) gives up -- it then skips its output instead of hanging.
+ * A launch on stream s uses the word bound to s by t2b_bind_error_word, else
+ * the word the calling host thread set with t2b_set_error_word (NULL: no
+ * record).  Bindings are per stream, defaults per host thread, so decoders
+ * on different streams or threads keep separate words.  A CUDA graph keeps
+ * the word its launches were captured with.  No counterpart in the reference
+ * (its NPU runs are synchronous and report through XRT, fusion.py:718-726).
  */
 T2B_API int t2b_set_error_word(int32_t* word);
+/* Bind `word` to `stream` (NULL removes the binding; the thread default applies again). */
+T2B_API int t2b_bind_error_word(void* stream, int32_t* word);
+/* The word a launch on `stream` from this thread would record into (host only, no device work). */
+T2B_API int t2b_error_word_for_stream(void* stream, int32_t** word);
 
 /*
  * Self-test of that path: a kernel waits (at most limit_us) on a barrier no
- * copy completes and records T2B_ERR_TIMEOUT in `word`; the stream stays usable.
+ * copy completes and records T2B_ERR_TIMEOUT in `word` (NULL: the stream's
+ * word as above); the stream stays usable.
  */
 T2B_API int t2b_selftest_bounded_wait(int32_t* word, int limit_us, void* stream);
 
@@ -134,9 +144,13 @@ T2B_API int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt, c
  * cudaMalloc/cudaFree could block).  No counterpart in the reference: it is
  * an addition of this library.  Scratch is a fixed array inside the library
  * (t2b_w4a16_gemm_noalloc_max_workspace() bytes, held on every GPU that loads
- * it); larger workspace needs return T2B_ERR_WORKSPACE.  All calls share
- * that array: calls that may overlap on the GPU race.  The first call on a
- * device resolves the array's address; issue it before any stream capture.
+ * it).  The call sizes its need from the path it takes (the tcgen05 and
+ * large-M paths need none; the CUDA-core split-K path needs its partials and
+ * tile counters) and returns T2B_ERR_WORKSPACE for more; every check runs
+ * before anything is enqueued.  All calls share that array: calls that may
+ * overlap on the GPU race.  The first call on a device resolves the array's
+ * address; issue it before any stream capture, and do not use this entry
+ * point on a device after cudaDeviceReset.
  */
 T2B_API size_t t2b_w4a16_gemm_noalloc_max_workspace(void);
 T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype,
@@ -279,14 +293,14 @@ T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint
  */
 /*
  * Tensor-parallel residual step: after the all-reduce of the row-parallel
- * o_proj / down partials y [M][H] (fp32), x_resid += y, ssq_out[m] =
+ * o_proj / down partials y [M][H] (y_dtype bf16 or fp32), x_resid += y, ssq_out[m] =
  * sum_n x_resid[m,n]^2 (overwritten) and xw_out = bf16(x_resid * next_norm_w)
  * (both NULL to skip).  Replaces ResidualAddRMSNorm
  * (src/torch2iron/operators/residual_add_rms_norm/kernel.cc:70-93) where the
  * GEMM before it is split over GPUs (batch_decode_fused.py:485-498, 529-539).
  */
-T2B_API int t2b_residual_norm_input(const float* y, float* x_resid, float* ssq_out, const uint16_t* next_norm_w,
-                                    uint16_t* xw_out, int M, int H, void* stream);
+T2B_API int t2b_residual_norm_input(const void* y, int y_dtype, float* x_resid, float* ssq_out,
+                                    const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, void* stream);
 
 /*
  * Greedy lm_head: idx[m] = argmax_v (xn[m] . lm_head[v]) over V rows of a bf16

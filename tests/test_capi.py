@@ -92,3 +92,35 @@ def test_binding_signatures_match_header_prototypes():
             assert a == _ctype(p), (name, i, p)
         want_ret = C.c_char_p if "char" in ret else _ctype(ret)
         assert res == want_ret, (name, ret)
+
+
+def test_status_word_bindings_are_per_stream_and_per_thread():
+    """Host-side table of the device status words (no device work): a stream's
+    binding wins over the thread's default; defaults are per host thread."""
+    import ctypes as C
+    import threading
+
+    lib = _lib.load()
+
+    def word_for(stream):
+        out = C.c_void_p()
+        assert lib.t2b_error_word_for_stream(stream, C.byref(out)) == 0
+        return out.value
+
+    s1, s2, w1, w2, wd = 0x1000, 0x2000, 0x10, 0x20, 0x30     # stand-in handles, never dereferenced
+    assert lib.t2b_set_error_word(wd) == 0
+    assert lib.t2b_bind_error_word(s1, w1) == 0
+    assert lib.t2b_bind_error_word(s2, w2) == 0
+    assert word_for(s1) == w1 and word_for(s2) == w2 and word_for(0x3000) == wd
+    assert lib.t2b_bind_error_word(s1, w2) == 0                # rebinding replaces
+    assert word_for(s1) == w2
+    seen = {}
+    t = threading.Thread(target=lambda: seen.update(other=word_for(0x3000), bound=word_for(s2)))
+    t.start()
+    t.join()
+    assert seen == {"other": None, "bound": w2}                # another thread: no default, same bindings
+    for s in (s1, s2):
+        assert lib.t2b_bind_error_word(s, None) == 0
+    assert word_for(s1) == wd
+    assert lib.t2b_set_error_word(None) == 0
+    assert word_for(s1) is None

@@ -133,11 +133,14 @@ def test_chunked_prefill_on_reference_artifact():
     eng.check_device_errors()
 
 
-@pytest.mark.parametrize("force_large_m", [False, True])
-def test_ragged_prompts_match_per_sequence_oracle(monkeypatch, force_large_m):
+@pytest.mark.parametrize("force_large_m,reuse", [(False, False), (True, False), (False, True)])
+def test_ragged_prompts_match_per_sequence_oracle(monkeypatch, force_large_m, reuse):
     """Right-padded prompts of lengths 5, 13 and 9: each row's greedy head and
     its continued decode match the oracle run on that sequence alone (chunk
-    linears on the decode tcgen05 kernel, or forced onto the large-M kernel)."""
+    linears on the decode tcgen05 kernel, or forced onto the large-M kernel).
+    ``reuse``: the engine first generates from other, full-length prompts, so
+    the cache slots past each ragged length hold that run's keys and values
+    (the padded positions read them, masked, and must not disturb the rows)."""
     if force_large_m:
         monkeypatch.setenv("T2B_PREFILL_MIN_M", "12")   # the 12-row chunks, not the 3-row decode step
     cfg = SMALL
@@ -146,6 +149,10 @@ def test_ragged_prompts_match_per_sequence_oracle(monkeypatch, force_large_m):
     B, P = len(lens), max(lens)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(46))
     eng = DecodeEngine(cfg, model, batch=B, max_ctx=64, use_graph=False)
+    if reuse:
+        other = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(47))
+        eng.generate(other, 8)
+        torch.cuda.synchronize()
     eng.prefill(prompts, chunk=4, lengths=lens)
     torch.cuda.synchronize()
     assert eng.pos.cpu().tolist() == lens

@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, batch, out_q):
+def _rank(rank, world, port, batch, partial, out_q):
     import torch.distributed as dist
     from torch2iron_b200 import synth
     from torch2iron_b200.engine import DecodeEngine
@@ -36,7 +36,8 @@ def _rank(rank, world, port, batch, out_q):
         prompts = torch.randint(0, CFG.vocab_size, (batch, 6), generator=torch.Generator().manual_seed(22))
         res = {}
         for mode in ("eager", "graph"):
-            eng = TPDecodeEngine(CFG, model, batch=batch, max_ctx=64, tp=world, rank=rank, use_graph=mode == "graph")
+            eng = TPDecodeEngine(CFG, model, batch=batch, max_ctx=64, tp=world, rank=rank, use_graph=mode == "graph",
+                                 partial_dtype=getattr(torch, partial))
             eng.prefill(prompts)
             toks = [eng.next_tokens.cpu().clone()]
             for _ in range(3):
@@ -59,14 +60,16 @@ def _rank(rank, world, port, batch, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("batch", [1, 5])
-def test_tp2_engine_matches_single_gpu(batch):
+@pytest.mark.parametrize("batch,partial", [(1, "bfloat16"), (5, "bfloat16"), (5, "float32")])
+def test_tp2_engine_matches_single_gpu(batch, partial):
+    """bf16 row-parallel partials (the default, half the all-reduce bytes) and
+    fp32 ones both hold the single-GPU engine's tokens and residual stream."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, partial, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))

@@ -300,3 +300,7 @@ def test_fast_artifact_errors_and_engine_refusal(tmp_path):
     cfg, model = LD.load_fast_qwen3_artifact(MODEL_DIR)
     with pytest.raises(NotImplementedError, match="Q4NX"):
         DecodeEngine(cfg, model, batch=1, max_ctx=64)
+    # the tensor-parallel engine refuses before sharding (which reads AutoGPTQ tensors)
+    from torch2iron_b200.tp import TPDecodeEngine
+    with pytest.raises(NotImplementedError, match="AutoGPTQ"):
+        TPDecodeEngine(cfg, model, batch=1, max_ctx=64, tp=1, rank=0)

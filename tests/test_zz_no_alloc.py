@@ -66,10 +66,39 @@ def test_noalloc_matches_allocating_entry_point(monkeypatch, M, N, K, needs_ws):
         assert rel_err(y, ref) <= 1e-4
 
 
-def test_noalloc_rejects_sizes_beyond_its_scratch():
+def test_noalloc_takes_the_tcgen05_path_without_scratch():
+    """Batch rows on the tcgen05 path need no scratch at any K: a Qwen3-8B down
+    projection at 64 rows (K = 12288, more than the CUDA-core path could hold)
+    runs and matches the allocating entry point."""
+    M, N, K = 64, 1024, 12288
+    L = _lib.lib()
+    import ctypes as C
+    path, rows, groups, ks = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+    assert L.t2b_linear_plan(M, N, K, C.byref(path), C.byref(rows), C.byref(groups), C.byref(ks)) == 0
+    assert path.value == 1
+    g = torch.Generator().manual_seed(77)
+    lin = synth.random_linear(N, K, g)
+    w = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    ref = _allocating(w, x)
+    for _ in range(2):
+        assert rel_err(_noalloc(w, x), ref) <= 1e-4
+
+
+def test_noalloc_rejects_sizes_beyond_its_scratch(monkeypatch):
+    import ctypes as C
+    monkeypatch.setenv("T2B_TC_MIN_M", "16")   # 8 rows on the CUDA-core split-K path
     L = _lib.lib()
     cap = L.t2b_w4a16_gemm_noalloc_max_workspace()
     M, N, K = 8, 65536, 16384         # needs more scratch than the library holds
+    path, rows, groups, ks = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+    assert L.t2b_linear_plan(M, N, K, C.byref(path), C.byref(rows), C.byref(groups), C.byref(ks)) == 0
+    assert path.value == 0
     assert L.t2b_w4a16_gemm_workspace_bytes(M, N, K) > cap
-    status = L.t2b_w4a16_gemm_noalloc(None, None, 0, None, 0, None, 0, M, N, K, 128, None)
+    # aligned stand-in pointers: the call must return before touching them
+    status = L.t2b_w4a16_gemm_noalloc(256, 256, 0, 256, 0, 256, 0, M, N, K, 128, None)
     assert status == 5   # T2B_ERR_WORKSPACE, returned before anything is enqueued
+    # argument errors come first, also before anything is enqueued
+    assert L.t2b_w4a16_gemm_noalloc(None, None, 0, None, 0, None, 0, M, N, K, 128, None) == 6
+    assert L.t2b_w4a16_gemm_noalloc(256, 256, 0, 256, 0, 256, 0, M, N, K, 64, None) == 1

@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+from contextlib import contextmanager
 from pathlib import Path
 
 import torch
@@ -52,8 +53,10 @@ SIGNATURES = {
     "t2b_embed_rows": (I, [P, P, P, P, P, P, I, I, I, P]),
     "t2b_rms_norm_rows": (I, [P, P, P, F, P, I, I, P]),
     "t2b_set_error_word": (I, [P]),
+    "t2b_bind_error_word": (I, [P, P]),
+    "t2b_error_word_for_stream": (I, [P, P]),
     "t2b_selftest_bounded_wait": (I, [P, I, P]),
-    "t2b_residual_norm_input": (I, [P, P, P, P, P, I, I, P]),
+    "t2b_residual_norm_input": (I, [P, I, P, P, P, P, I, I, P]),
     "t2b_lm_head_argmax_workspace_bytes": (Z, [I]),
     "t2b_lm_head_argmax": (I, [P, P, I, I, I, P, P, P, P, Z, P]),
     "t2b_argmax_workspace_bytes": (Z, [I, I]),
@@ -119,3 +122,23 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 def stream(s: torch.cuda.Stream | None = None) -> int:
     return (s or torch.cuda.current_stream()).cuda_stream
+
+
+@contextmanager
+def status_word(word: torch.Tensor, st: int):
+    """Launches on stream ``st`` inside this block record timed-out device waits
+    in ``word`` (int32 device tensor): the stream is bound to it
+    (``t2b_bind_error_word``) and unbound on exit.  A block nested in one
+    that already bound the same word leaves the binding alone."""
+    L = load()
+    mine = ptr(word)
+    cur = C.c_void_p()
+    check("t2b_error_word_for_stream", L.t2b_error_word_for_stream(st, C.byref(cur)))
+    if cur.value == mine:
+        yield
+        return
+    check("t2b_bind_error_word", L.t2b_bind_error_word(st, mine))
+    try:
+        yield
+    finally:
+        L.t2b_bind_error_word(st, None)

@@ -23,7 +23,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build"
 LIB = PKG / "libt2b.so"
-TRACE_LIB = PKG / "libt2b_trace.so"   # -DT2B_TRACE: device phase timestamps (diagnostics only)
+TRACE_LIB = BUILD / "libt2b_trace.so"   # -DT2B_TRACE: device phase timestamps (diagnostics only, kept out of the package)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",

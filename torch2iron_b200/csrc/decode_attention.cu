@@ -665,7 +665,7 @@ int attention_launch(AttnParams& P, int rows, int head_dim, int max_keys, void* 
   size_t part = (size_t)grid * 2 * qpg * (head_dim + 2) * sizeof(float);
   part = (part + 255) & ~size_t(255);
   P.ws = reinterpret_cast<float*>(ws);
-  P.err = error_word();
+  P.err = error_word(st);
   P.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + part);
   P.rows = rows;
   P.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);

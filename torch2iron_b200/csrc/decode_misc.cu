@@ -2,6 +2,9 @@
 // embedding gather, final RMSNorm, greedy argmax, and the standalone
 // element-wise reference operators.
 
+#include <mutex>
+#include <vector>
+
 #include "t2b_common.cuh"
 #include "launch.cuh"
 
@@ -116,7 +119,9 @@ __global__ void rms_norm_rows_kernel(const float* __restrict__ x, const float* _
 // residual_add_rms_norm/kernel.cc:70-93 in split form): x += y, then the row's
 // sum of squares (written, not accumulated) and xw = bf16(x * w) -- the input
 // the next linear normalises (model.py:179-181).  One CTA per row, float4.
-__global__ void __launch_bounds__(256) residual_norm_input_kernel(const float* __restrict__ y, float* __restrict__ x,
+// y: the all-reduced row-parallel partials, fp32 or bf16 (YBF16).
+template <bool YBF16>
+__global__ void __launch_bounds__(256) residual_norm_input_kernel(const void* __restrict__ yv, float* __restrict__ x,
                                                                   float* __restrict__ ssq,
                                                                   const __nv_bfloat16* __restrict__ w,
                                                                   __nv_bfloat16* __restrict__ xw, int H) {
@@ -127,7 +132,14 @@ __global__ void __launch_bounds__(256) residual_norm_input_kernel(const float* _
   for (int i = threadIdx.x * 4; i < H; i += 256 * 4) {
     const size_t o = (size_t)m * H + i;
     const float4 a = *reinterpret_cast<const float4*>(x + o);
-    const float4 b = *reinterpret_cast<const float4*>(y + o);
+    float4 b;
+    if (YBF16) {
+      const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(yv) + o);
+      b = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xffff0000u), __uint_as_float(r.y << 16),
+                      __uint_as_float(r.y & 0xffff0000u));
+    } else {
+      b = *reinterpret_cast<const float4*>(static_cast<const float*>(yv) + o);
+    }
     const float4 v = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
     *reinterpret_cast<float4*>(x + o) = v;
     sq += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
@@ -152,8 +164,26 @@ __global__ void __launch_bounds__(256) residual_norm_input_kernel(const float* _
   }
 }
 
-static int* g_error_word = nullptr;
-int* error_word() { return g_error_word; }
+// Status words: a per-stream binding table (t2b_bind_error_word) and a
+// per-host-thread default (t2b_set_error_word).  The table is only touched at
+// launch time on the host; a graph captured with a binding keeps the word
+// pointer it was captured with.
+struct ErrorBinding {
+  cudaStream_t stream;
+  int* word;
+};
+static std::mutex g_err_mu;
+static std::vector<ErrorBinding> g_err_bindings;
+static thread_local int* t_error_word = nullptr;
+
+int* error_word(cudaStream_t st) {
+  {
+    std::lock_guard<std::mutex> lock(g_err_mu);
+    for (const ErrorBinding& b : g_err_bindings)
+      if (b.stream == st) return b.word;
+  }
+  return t_error_word;
+}
 
 // Exercises the bounded-wait path end to end without a fault: one thread arms
 // an mbarrier for bytes no copy will deliver (nothing is issued, so nothing
@@ -168,12 +198,16 @@ __global__ void selftest_bounded_wait_kernel(int* word, unsigned long long limit
   mbar_wait_bounded(&bar, 0, word, limit_ns);
 }
 
-int residual_norm_input(const float* y, float* x, float* ssq, const uint16_t* w, uint16_t* xw, int M, int H,
-                        cudaStream_t st) {
+int residual_norm_input(const void* y, int y_dtype, float* x, float* ssq, const uint16_t* w, uint16_t* xw, int M,
+                        int H, cudaStream_t st) {
   if (M < 1 || H < 4 || H % 4) return T2B_ERR_SHAPE;
   const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(w);
   __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(xw);
-  return launch_pdl(residual_norm_input_kernel, dim3(M), dim3(256), 0, st, y, x, ssq, wp, op, H);
+  if (y_dtype == T2B_DTYPE_BF16)
+    return launch_pdl(residual_norm_input_kernel<true>, dim3(M), dim3(256), 0, st, y, x, ssq, wp, op, H);
+  if (y_dtype == T2B_DTYPE_F32)
+    return launch_pdl(residual_norm_input_kernel<false>, dim3(M), dim3(256), 0, st, y, x, ssq, wp, op, H);
+  return T2B_ERR_ARG;
 }
 
 // ---------------------------------------------------------------------------
@@ -506,24 +540,50 @@ extern "C" int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const u
 }
 
 extern "C" int t2b_set_error_word(int32_t* word) {
-  g_error_word = word;
+  t_error_word = word;
+  return T2B_OK;
+}
+
+extern "C" int t2b_bind_error_word(void* stream, int32_t* word) {
+  const cudaStream_t st = S_(stream);
+  std::lock_guard<std::mutex> lock(g_err_mu);
+  for (size_t i = 0; i < g_err_bindings.size(); ++i) {
+    if (g_err_bindings[i].stream != st) continue;
+    if (word) {
+      g_err_bindings[i].word = word;
+    } else {
+      g_err_bindings.erase(g_err_bindings.begin() + (long)i);
+    }
+    return T2B_OK;
+  }
+  if (word) g_err_bindings.push_back(ErrorBinding{st, word});
+  return T2B_OK;
+}
+
+extern "C" int t2b_error_word_for_stream(void* stream, int32_t** word) {
+  if (!word) return T2B_ERR_ARG;
+  *word = error_word(S_(stream));
   return T2B_OK;
 }
 
 extern "C" int t2b_selftest_bounded_wait(int32_t* word, int limit_us, void* stream) {
+  if (!word) word = error_word(S_(stream));   // the stream's (or thread's) status word
   if (!word || limit_us < 1 || limit_us > 1000000) return T2B_ERR_ARG;
   selftest_bounded_wait_kernel<<<1, 32, 0, S_(stream)>>>(word, 1000ull * (unsigned long long)limit_us);
   return cudaGetLastError() == cudaSuccess ? T2B_OK : T2B_ERR_LAUNCH;
 }
 
-extern "C" int t2b_residual_norm_input(const float* y, float* x_resid, float* ssq_out, const uint16_t* next_norm_w,
-                                       uint16_t* xw_out, int M, int H, void* stream) {
+extern "C" int t2b_residual_norm_input(const void* y, int y_dtype, float* x_resid, float* ssq_out,
+                                       const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, void* stream) {
   if (!y || !x_resid || !ssq_out) return T2B_ERR_ARG;
   if ((next_norm_w == nullptr) != (xw_out == nullptr)) return T2B_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(x_resid)) & 15) return T2B_ERR_ALIGN;
+  if (y_dtype != T2B_DTYPE_BF16 && y_dtype != T2B_DTYPE_F32) return T2B_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(y) & (y_dtype == T2B_DTYPE_BF16 ? 7 : 15)) ||
+      (reinterpret_cast<uintptr_t>(x_resid) & 15))
+    return T2B_ERR_ALIGN;
   if (xw_out && ((reinterpret_cast<uintptr_t>(xw_out) | reinterpret_cast<uintptr_t>(next_norm_w)) & 7))
     return T2B_ERR_ALIGN;
-  return residual_norm_input(y, x_resid, ssq_out, next_norm_w, xw_out, M, H, S_(stream));
+  return residual_norm_input(y, y_dtype, x_resid, ssq_out, next_norm_w, xw_out, M, H, S_(stream));
 }
 
 extern "C" size_t t2b_argmax_workspace_bytes(int M, int V) {

@@ -241,5 +241,10 @@ T2B_DEV void maybe_clear_ssq(const LinearParams& p, bool designated, int t, int 
 int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t linear_workspace_bytes(int M, int N, int K);
 void linear_workspace_layout(int M, int N, int K, size_t* partial_bytes, size_t* counter_bytes);
+// Plain GEMM entry split into host checks and launch (w4a16_gemv.cu).
+int gemm_params(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype, void* y,
+                int y_dtype, int M, int N, int K, int group_size, LinearParams* out);
+void gemm_path_workspace(const LinearParams& p, int wfmt, size_t* partial_bytes, size_t* counter_bytes);
+int gemm_launch(LinearParams& p, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st);
 
 }  // namespace t2b

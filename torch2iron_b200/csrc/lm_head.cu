@@ -323,7 +323,7 @@ int lm_head_argmax(const uint16_t* xn, const uint16_t* lm, int M, int H, int V, 
   p.logits = logits;
   p.keys = reinterpret_cast<unsigned long long*>(ws);
   p.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * 8 + 255) & ~size_t(255)));
-  p.err = error_word();
+  p.err = error_word(st);
   if (bp == 16) return lm_launch_t<16>(p, st);
   if (bp == 32) return lm_launch_t<32>(p, st);
   if (bp == 64) return lm_launch_t<64>(p, st);

@@ -81,10 +81,12 @@ T2B_DEV bool split_ticket(int* counter, int arrivals) {
 
 T2B_DEV float ldcg(const float* p) { return __ldcg(p); }
 
-// Process-wide device status word (t2b_set_error_word): every launch passes it
-// to its kernel, whose time-bounded waits record T2B_ERR_TIMEOUT there
-// (atomicCAS from 0, so the first error sticks).  nullptr = not recorded.
-int* error_word();
+// Device status word of a launch on stream `st`: the word bound to that
+// stream (t2b_bind_error_word), else the calling host thread's word
+// (t2b_set_error_word).  Every launch passes it to its kernel, whose
+// time-bounded waits record T2B_ERR_TIMEOUT there (atomicCAS from 0, so the
+// first error sticks).  nullptr = not recorded.
+int* error_word(cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // mbarrier + bulk async copy (TMA 1-D) with bounded waits.

@@ -379,7 +379,7 @@ size_t linear_workspace_bytes(int M, int N, int K) {
 }
 
 int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st) {
-  p.err = error_word();
+  p.err = error_word(st);
   if (p.M < 1 || p.N <= 0 || p.K <= 0) return T2B_ERR_SHAPE;
   if (p.N % TILE_N || p.K % 256) return T2B_ERR_SHAPE;
   p.G = p.K / GROUP;
@@ -438,12 +438,15 @@ extern "C" size_t t2b_w4a16_gemm_workspace_bytes(int M, int N, int K) {
   return linear_workspace_bytes(M, N, K);
 }
 
-extern "C" int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype,
-                              void* y, int y_dtype, int M, int N, int K, int group_size, void* ws, size_t ws_bytes,
-                              void* stream) {
+namespace t2b {
+
+// Host-side checks of a plain W4A16 GEMM call; fills the launch parameters.
+int gemm_params(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype, void* y,
+                int y_dtype, int M, int N, int K, int group_size, LinearParams* out) {
   if (group_size != 128) return T2B_ERR_SHAPE;
   if (!weight || !x || !y) return T2B_ERR_ARG;
   if (x_dtype < 0 || x_dtype > 2 || y_dtype < 0 || y_dtype > 2) return T2B_ERR_ARG;
+  if (M < 1 || N <= 0 || K <= 0 || N % TILE_N || K % 256) return T2B_ERR_SHAPE;
   int w_ld;
   if (wfmt == T2B_WFMT_T2B) {
     if (!meta) return T2B_ERR_ARG;
@@ -462,7 +465,33 @@ extern "C" int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt
   p.y = y;
   p.y_dtype = y_dtype;
   p.y_ld = N;
-  return linear_launch(p, PRO_ACT, EPI_STORE, wfmt, ws, ws_bytes, S_(stream));
+  *out = p;
+  return T2B_OK;
+}
+
+// Workspace the path this call takes needs: 0 on the tcgen05 and large-M
+// paths (their split-K stays on chip), the CUDA-core split-K partials and
+// tile counters otherwise (zero when its k-slices meet in a cluster).
+void gemm_path_workspace(const LinearParams& p, int wfmt, size_t* partial_bytes, size_t* counter_bytes) {
+  *partial_bytes = 0;
+  *counter_bytes = 0;
+  if (use_prefill(p.M, wfmt, p.x_dtype) || use_tc(p.M, p.N, p.K, wfmt, p.x_dtype)) return;
+  linear_workspace_layout(p.M, p.N, p.K, partial_bytes, counter_bytes);
+}
+
+int gemm_launch(LinearParams& p, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st) {
+  return linear_launch(p, PRO_ACT, EPI_STORE, wfmt, ws, ws_bytes, st);
+}
+
+}  // namespace t2b
+
+extern "C" int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype,
+                              void* y, int y_dtype, int M, int N, int K, int group_size, void* ws, size_t ws_bytes,
+                              void* stream) {
+  LinearParams p;
+  const int r = gemm_params(weight, meta, wfmt, x, x_dtype, y, y_dtype, M, N, K, group_size, &p);
+  if (r != T2B_OK) return r;
+  return gemm_launch(p, wfmt, ws, ws_bytes, S_(stream));
 }
 
 extern "C" size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, int head_dim) {

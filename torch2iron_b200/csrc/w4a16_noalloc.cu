@@ -18,8 +18,10 @@
 //     calls that can overlap on the GPU (different streams, no ordering)
 //     race on it and must not be issued;
 //   * the first call on a device resolves the array's device address
-//     (cudaGetSymbolAddress, with that device current); make that first call
-//     before any stream capture.
+//     (cudaGetSymbolAddress, with that device current) and keeps it for the
+//     life of the process; make that first call before any stream capture,
+//     and do not use this entry point on a device after cudaDeviceReset
+//     (the module, and with it the array's address, may change).
 // No cudaMalloc, cudaFree or allocating library routine is called here.
 #include <mutex>
 
@@ -59,19 +61,22 @@ extern "C" T2B_API size_t t2b_w4a16_gemm_noalloc_max_workspace(void) { return t2
 extern "C" T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int wfmt, const void* x,
                                               int x_dtype, void* y, int y_dtype, int M, int N, int K,
                                               int group_size, void* stream) {
-  const size_t need = t2b_w4a16_gemm_workspace_bytes(M, N, K);
-  if (need > t2b::NOALLOC_SCRATCH_BYTES) return T2B_ERR_WORKSPACE;
+  // every check first: a rejected call enqueues nothing
+  t2b::LinearParams p;
+  const int r = t2b::gemm_params(weight, meta, wfmt, x, x_dtype, y, y_dtype, M, N, K, group_size, &p);
+  if (r != T2B_OK) return r;
+  // scratch only for the path this call takes (the tcgen05 and large-M paths need none)
+  size_t partial_bytes = 0, counter_bytes = 0;
+  t2b::gemm_path_workspace(p, wfmt, &partial_bytes, &counter_bytes);
+  if (partial_bytes + counter_bytes > t2b::NOALLOC_SCRATCH_BYTES) return T2B_ERR_WORKSPACE;
   void* scratch = nullptr;
   const int st = t2b::scratch_on_current_device(&scratch);
   if (st != T2B_OK) return st;
-  size_t partial_bytes = 0, counter_bytes = 0;
-  t2b::linear_workspace_layout(M, N, K, &partial_bytes, &counter_bytes);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (counter_bytes) {
     // split-K tile counters must start at zero (an earlier aborted call may have left them armed)
-    if (cudaMemsetAsync(static_cast<char*>(scratch) + partial_bytes, 0, counter_bytes,
-                        reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+    if (cudaMemsetAsync(static_cast<char*>(scratch) + partial_bytes, 0, counter_bytes, s) != cudaSuccess)
       return T2B_ERR_LAUNCH;
   }
-  return t2b_w4a16_gemm(weight, meta, wfmt, x, x_dtype, y, y_dtype, M, N, K, group_size, scratch,
-                        t2b::NOALLOC_SCRATCH_BYTES, stream);
+  return t2b::gemm_launch(p, wfmt, scratch, t2b::NOALLOC_SCRATCH_BYTES, s);
 }

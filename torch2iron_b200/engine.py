@@ -148,9 +148,11 @@ class DecodeEngine:
             sizes["am"] = L.t2b_argmax_workspace_bytes(B, cfg.vocab_size)
         # one workspace per op kind: consecutive ops never share counters
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
-        # device status word: kernels record a timed-out wait here (t2b_set_error_word)
+        # device status word: this engine's kernels record a timed-out wait here (the
+        # launch stream is bound to it while the engine enqueues, t2b_bind_error_word)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        _lib.check("t2b_set_error_word", L.t2b_set_error_word(_lib.ptr(self.err)))
+        # decode_step reads the next tokens and the status word in one copy
+        self._host_out = torch.zeros(batch + 1, dtype=torch.int32).pin_memory()
         torch.cuda.synchronize(dev)   # repacked weights complete before any PDL launch reads them
         self.graph = None
         self._step_graph = None
@@ -185,6 +187,10 @@ class DecodeEngine:
         return self.layers[li + 1].input_layernorm if li + 1 < len(self.layers) else self.final_norm
 
     def enqueue_layer(self, li: int, st: int) -> None:
+        with _lib.status_word(self.err, st):
+            self._enqueue_layer(li, st)
+
+    def _enqueue_layer(self, li: int, st: int) -> None:
         cfg, B = self.cfg, self.B
         H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
         L = _lib.lib()
@@ -213,13 +219,13 @@ class DecodeEngine:
         L = _lib.lib()
         st = _lib.stream()
         p = _lib.ptr
-        L.t2b_set_error_word(p(self.err))   # this engine's word for every launch below (engines may coexist)
-        _lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a),
-                                                      p(self.layers[0].input_layernorm), p(self.xw), B,
-                                                      cfg.emb_dim, cfg.vocab_size, st))
-        for li in range(cfg.n_layers):
-            self.enqueue_layer(li, st)
-        self._enqueue_head(st)
+        with _lib.status_word(self.err, st):     # this engine's word for every launch below
+            _lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a),
+                                                          p(self.layers[0].input_layernorm), p(self.xw), B,
+                                                          cfg.emb_dim, cfg.vocab_size, st))
+            for li in range(cfg.n_layers):
+                self._enqueue_layer(li, st)
+            self._enqueue_head(st)
 
     def _enqueue_head(self, st) -> None:
         """Final RMSNorm of ``x`` (with ``ssq_a``) and the greedy lm_head into ``next_tokens``."""
@@ -311,9 +317,13 @@ class DecodeEngine:
         self.tokens.copy_(tok, non_blocking=True)
         self.pos.copy_(pos, non_blocking=True)
         self.run_step()
-        out = self.next_tokens.cpu()
-        self.check_device_errors()
-        return out
+        # one device->host read per step: the next tokens and the status word
+        self._host_out[:self.B].copy_(self.next_tokens, non_blocking=True)
+        self._host_out[self.B:].copy_(self.err, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        if int(self._host_out[self.B]):
+            self.check_device_errors()
+        return self._host_out[:self.B].clone()
 
     # -- chunked prefill (prefill_runtime.py:95-164, for B sequences at once) --
     PREFILL_ROWS = 8192      # prompt tokens (all sequences) per chunk by default
@@ -392,6 +402,13 @@ class DecodeEngine:
 
         Leaves ``next_tokens`` = the greedy token after each prompt (``logits``
         for it with ``keep_logits``), and ``tokens``/``pos`` ready for ``advance()``.
+
+        With ragged prompts, a chunk's padded query rows attend cache slots
+        this prefill does not write (whatever an earlier run left there).
+        Their outputs are discarded, and valid rows mask those keys out, but a
+        masked key still enters the P.V product with P = 0, so the caches
+        must hold finite values: they start zeroed and every write is a
+        kernel's finite bf16 output.
         """
         if stepwise:
             if lengths is not None:
@@ -415,7 +432,13 @@ class DecodeEngine:
         prompts = torch.where(valid, prompts.cpu().to(torch.int64), 0).to(dev, torch.int32)   # padding -> token 0
         lens_d = lens.to(dev)
         st = _lib.stream()
-        _lib.lib().t2b_set_error_word(_lib.ptr(self.err))
+        with _lib.status_word(self.err, st):
+            self._prefill_chunks(prompts, lens_d, pf, B, C, Pmax, st)
+        self.tokens.copy_(self.next_tokens)
+        self.pos.copy_(lens_d.to(torch.int32))
+
+    def _prefill_chunks(self, prompts, lens_d, pf, B, C, Pmax, st) -> None:
+        dev = self.device
         seq_all = torch.arange(B, dtype=torch.int64, device=dev)
         for c0 in range(0, Pmax, C):
             n = min(C, Pmax - c0)
@@ -433,8 +456,6 @@ class DecodeEngine:
                 self.x.index_copy_(0, rows, pf["x"].index_select(0, src))
                 self.ssq_a.index_copy_(0, rows, pf["ssq_a"].index_select(0, src))
         self._enqueue_head(st)
-        self.tokens.copy_(self.next_tokens)
-        self.pos.copy_(lens_d.to(torch.int32))
 
     def _prefill_stepwise(self, prompts: torch.Tensor) -> None:
         """The prompt one position per decode step (teacher forcing)."""
@@ -463,16 +484,6 @@ class DecodeEngine:
         return torch.stack(out, dim=1)
 
     def release(self) -> None:
+        """Drop the captured graphs (the engine's buffers stay usable for eager steps)."""
         self.graph = None
         self._step_graph = None
-        self._drop_error_word()
-
-    def _drop_error_word(self) -> None:
-        """Stop kernels writing to this engine's status word (it is about to be freed)."""
-        try:
-            _lib.load().t2b_set_error_word(None)
-        except Exception:
-            pass
-
-    def __del__(self):
-        self._drop_error_word()

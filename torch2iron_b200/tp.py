@@ -20,8 +20,10 @@ decoder layer (``model.py:240-327``):
 Every split falls on a 128-wide quantization group (``H/tp``, ``I/tp`` and
 the head blocks are multiples of 128), so no scale or zero point is split.
 The residual stream, embedding and norms are replicated.  The two row-parallel
-partials per layer meet in an NCCL all-reduce (fp32 sum) on the decode
-stream, followed by ``t2b_residual_norm_input``.
+partials per layer meet in an NCCL all-reduce on the decode stream (bf16
+partials by default, ``[B, H]`` = 512 KiB at 64 rows of Qwen3-8B; fp32 on
+request), followed by ``t2b_residual_norm_input``, which adds the sum into the
+fp32 residual stream.
 """
 
 from __future__ import annotations
@@ -119,7 +121,7 @@ class TPDecodeEngine:
     """
 
     def __init__(self, cfg, model: dict, batch: int, max_ctx: int, tp: int, rank: int, group=None,
-                 device="cuda", use_graph: bool = False):
+                 device="cuda", use_graph: bool = False, partial_dtype: torch.dtype = torch.bfloat16):
         import torch.distributed as dist
         from . import _lib
         from . import weights as W
@@ -129,9 +131,18 @@ class TPDecodeEngine:
         self.dist, self.group, self.tp, self.rank = dist, group, tp, rank
         self.cfg, self.lcfg = cfg, local_config(cfg, tp)
         self.B, self.max_ctx, self.device = batch, max_ctx, torch.device(device)
+        if partial_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("the row-parallel partials are bf16 or fp32")
+        self.partial_dtype = partial_dtype
         if max_ctx % 64:
             raise ValueError("max_ctx must be a multiple of 64")
         dev, lc = self.device, self.lcfg
+        for li, l in enumerate(model["layers"]):   # the sharding reads AutoGPTQ tensors (.qweight, ...)
+            for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+                if not isinstance(l[name], AutoGPTQLinear):
+                    raise NotImplementedError(
+                        f"layer {li} {name} is a {type(l[name]).__name__}: tensor-parallel decode shards "
+                        "group-128 AutoGPTQ-derived weights only")
         self.layers = [load_layer(shard_layer(l, cfg, tp, rank), lc, dev) for l in model["layers"]]
         self.embed = model["embed"].to(dev, torch.bfloat16).contiguous()
         lm = model.get("lm_head")
@@ -147,7 +158,7 @@ class TPDecodeEngine:
         B, H, hd = batch, cfg.emb_dim, cfg.head_dim
         f32, bf = torch.float32, torch.bfloat16
         self.x = torch.zeros(B, H, dtype=f32, device=dev)
-        self.y = torch.zeros(B, H, dtype=f32, device=dev)        # row-parallel partial, all-reduced in place
+        self.y = torch.zeros(B, H, dtype=partial_dtype, device=dev)   # row-parallel partial, all-reduced in place
         self.xw = torch.zeros(B, H, dtype=bf, device=dev)
         self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
         self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
@@ -175,8 +186,8 @@ class TPDecodeEngine:
         }
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
         self._lib, self._W = _lib, W
+        # this rank's status word; the launch stream is bound to it while the engine enqueues
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        _lib.check("t2b_set_error_word", L.t2b_set_error_word(_lib.ptr(self.err)))
         self.use_graph, self.graph, self._step_graph = use_graph, None, None
         self.vals = [torch.zeros(B, dtype=f32, device=dev) for _ in range(tp)]
         self.idxs = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(tp)]
@@ -193,7 +204,8 @@ class TPDecodeEngine:
         lib, p = self._lib, self._lib.ptr
         self.dist.all_reduce(self.y, group=self.group)
         lib.check("t2b_residual_norm_input", lib.lib().t2b_residual_norm_input(
-            p(self.y), p(self.x), p(ssq_out), p(next_w), p(self.xw), self.B, self.cfg.emb_dim, lib.stream()))
+            p(self.y), lib.DTYPE[self.partial_dtype], p(self.x), p(ssq_out), p(next_w), p(self.xw), self.B,
+            self.cfg.emb_dim, lib.stream()))
 
     def enqueue_layer(self, li: int) -> None:
         cfg, lc, B = self.cfg, self.lcfg, self.B
@@ -210,21 +222,24 @@ class TPDecodeEngine:
             self.max_ctx, *self._ws("attn"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
             p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[torch.bfloat16], p(self.y),
-            lib.DTYPE[torch.float32], B, H, lc.q_dim, 128, *self._ws("o"), st))
+            lib.DTYPE[self.partial_dtype], B, H, lc.q_dim, 128, *self._ws("o"), st))
         self._allreduce_residual(self.ssq_b, lw.post_attention_layernorm)
         lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
             p(lw.gate_up.qw), p(lw.gate_up.meta), p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
             p(self.ssq_a), B, H, lc.hidden_dim, *self._ws("ug"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
             p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[torch.bfloat16], p(self.y),
-            lib.DTYPE[torch.float32], B, H, lc.hidden_dim, 128, *self._ws("down"), st))
+            lib.DTYPE[self.partial_dtype], B, H, lc.hidden_dim, 128, *self._ws("down"), st))
         self._allreduce_residual(self.ssq_a, self.next_norm_weight(li))
 
     def enqueue_step(self) -> None:
+        with self._lib.status_word(self.err, self._lib.stream()):
+            self._enqueue_step()
+
+    def _enqueue_step(self) -> None:
         cfg, B = self.cfg, self.B
         lib = self._lib
         L, p, st = lib.lib(), lib.ptr, lib.stream()
-        L.t2b_set_error_word(p(self.err))
         lib.check("t2b_embed_rows", L.t2b_embed_rows(p(self.embed), p(self.tokens), p(self.x), p(self.ssq_a),
                                                      p(self.layers[0].input_layernorm), p(self.xw), B, cfg.emb_dim,
                                                      cfg.vocab_size, st))
@@ -302,4 +317,3 @@ class TPDecodeEngine:
         torch.cuda.synchronize(self.device)
         self.graph = None
         self._step_graph = None
-        self._lib.load().t2b_set_error_word(None)

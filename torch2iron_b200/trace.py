@@ -20,7 +20,7 @@ import os
 import sys
 from pathlib import Path
 
-TRACE_LIB = Path(__file__).resolve().parent / "libt2b_trace.so"
+TRACE_LIB = Path(__file__).resolve().parent.parent / "_build" / "libt2b_trace.so"
 _KINDS = {30: "store", 31: "residual (o, down)", 32: "swiglu (gate/up)", 33: "qkv"}
 _COLUMNS = [(1, "mma<-A"), (2, "mma<-X"), (3, "mma<-acc"), (4, "prod<-W"), (5, "prod<-Afree"), (6, "epi<-acc")]
 
