@@ -179,8 +179,20 @@ class GroupedW4A16Linear:
     def dense(self) -> torch.Tensor:
         return self.signed.to(torch.float32) * self.scales.repeat_interleave(self.group_size, dim=1)
 
+    def cache_dense(self) -> "GroupedW4A16Linear":
+        """Keep the dequantised fp32 matrix and contract in one matmul: the
+        same fp32 products, summed in one pass over K instead of one pass per
+        group (only the association of the fp32 sum differs).  For the
+        full-size model checks, where the per-group loop would re-dequantise
+        every weight at every step."""
+        self._dense = self.dense().contiguous()
+        return self
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x_flat = x.reshape(-1, self.in_features).to(torch.float32)
+        dense = getattr(self, "_dense", None)
+        if dense is not None:
+            return x_flat.matmul(dense.t()).reshape(*x.shape[:-1], self.out_features)
         out = torch.zeros((x_flat.shape[0], self.out_features), dtype=torch.float32)
         for g in range(self.scales.shape[1]):
             start = g * self.group_size
@@ -477,14 +489,15 @@ class OracleDecoder:
             x = self.layer_step(li, x, pos)
         return rms_norm(x, self.final_norm, self.shape.rms_norm_eps) @ self._lm.t()   # model.py:477
 
-    def prefill_chunked(self, prompts: torch.Tensor, chunk: int) -> torch.Tensor:
+    def prefill_chunked(self, prompts: torch.Tensor, chunk: int, last_only: bool = False) -> torch.Tensor:
         """Chunked prefill of ``prompts [B, P]``: every chunk of ``chunk`` tokens per
         row goes through each layer at once, its K/V written into the cache
         first and each token attending keys ``0..its position`` -- the causal
         rule of the reference's chunked prefill (``prefill_runtime.py:95-164``,
         ``llama_chunked_prefill_attention/op.py:21-50``) and of the full-prompt
         forward (``model.py:453-478`` with a causal mask).  Returns the logits of
-        every prompt token ``[B, P, V]``."""
+        every prompt token ``[B, P, V]``, or with ``last_only`` those of the last
+        one ``[B, V]`` (the only row a greedy decode needs)."""
         s = self.shape
         B, P = prompts.shape
         out = []
@@ -517,6 +530,10 @@ class OracleDecoder:
                 x = x + layer.o_proj(ctx.reshape(B * n, s.n_heads * s.head_dim)).view(B, n, s.emb_dim)
                 h = rms_norm(x, layer.post_attention_layernorm, s.rms_norm_eps).reshape(B * n, s.emb_dim)
                 x = x + layer.down_proj(F.silu(layer.gate_proj(h)) * layer.up_proj(h)).view(B, n, s.emb_dim)
+            if last_only:
+                if c0 + n == P:
+                    return rms_norm(x[:, -1], self.final_norm, s.rms_norm_eps) @ self._lm.t()
+                continue
             out.append(rms_norm(x, self.final_norm, s.rms_norm_eps) @ self._lm.t())
         return torch.cat(out, dim=1)
 

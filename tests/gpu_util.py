@@ -33,8 +33,14 @@ def oracle_shape(cfg) -> oracle.OracleShape:
                               qk_norm=cfg.qk_norm)
 
 
-def oracle_decoder(cfg, model: dict, batch: int, max_ctx: int) -> oracle.OracleDecoder:
+def oracle_decoder(cfg, model: dict, batch: int, max_ctx: int, dense: bool = False) -> oracle.OracleDecoder:
+    """The oracle model over ``model``'s weights (moved to the host); ``dense``
+    keeps each linear's dequantised fp32 matrix (full-size model checks)."""
     layers = [oracle_layer(l, cfg) for l in model["layers"]]
+    if dense:
+        for ol in layers:
+            for n in synth.LINEAR_NAMES:
+                getattr(ol, n).cache_dense()
     emb = model["embed"].cpu()
     lm = emb if model.get("lm_head") is None else model["lm_head"].cpu()
     return oracle.OracleDecoder(oracle_shape(cfg), layers, embed=emb, final_norm=model["final_norm"].cpu(),

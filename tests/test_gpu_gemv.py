@@ -111,6 +111,35 @@ def test_qparam_gemv_operator_matches_reference_runtime():
     assert rel_err(y, torch.from_numpy(d["y"])) <= 1e-2
 
 
+@pytest.mark.parametrize("M,batches,shared", [(256, 3, False), (200, 1, False), (72, 2, True), (300, 2, False)])
+def test_qparam_gemv_per_batch_and_ragged_rows(M, batches, shared):
+    """Per-batch qparam (``w4a16_gemv/op.py:115-126``: ``qparam_dim = (batch,)``
+    unless shared) and row counts that are not a multiple of the 128-row tile,
+    against the reference runtime linear restated by the oracle (fp32)."""
+    K = 512
+    g = torch.Generator().manual_seed(M * 7 + batches)
+    nq = 1 if shared else batches
+    qps, refs = [], []
+    x = torch.randn(batches, K, generator=g).to(torch.bfloat16)
+    for b in range(nq):
+        packed = torch.randint(0, 256, (M, K // 2), generator=g, dtype=torch.int64).to(torch.uint8)
+        scales = (torch.rand(M, K // 128, generator=g) * 0.01 + 1e-3).to(torch.bfloat16)
+        qps.append(torch.cat([packed, scales.view(torch.uint8)], dim=1))
+        refs.append((packed, scales))
+    qparam = torch.stack(qps) if not shared and batches > 1 else qps[0]
+    op = W4A16GEMV(M=M, K=K, num_batches=batches, shared_qparam=shared)
+    assert tuple(op.get_arg_spec()[0].shape) == tuple(qparam.shape)
+    y = torch.empty(batches, M, dtype=torch.bfloat16, device="cuda") if batches > 1 else \
+        torch.empty(M, dtype=torch.bfloat16, device="cuda")
+    op(qparam.cuda(), (x if batches > 1 else x[0]).cuda(), y)
+    torch.cuda.synchronize()
+    y = y.view(batches, M).float().cpu()
+    for b in range(batches):
+        packed, scales = refs[0 if shared else b]
+        ref = oracle.packed_w4a16_linear(x[b:b + 1].float(), packed, scales, K, M, 128)
+        assert rel_err(y[b:b + 1], ref) <= 1e-2
+
+
 def test_shape_errors_raise():
     with pytest.raises(_lib.T2BError):
         dw = W.W4Weight(torch.zeros(100, 128, dtype=torch.uint8, device="cuda"),

@@ -37,6 +37,10 @@ def test_arg_specs_follow_reference_shapes():
     spec = op.get_arg_spec()
     assert spec[0].shape == (3072, 1024 // 2 + 8 * 2) and spec[0].dtype == torch.uint8
     assert spec[1].shape == (1024,) and spec[2].shape == (3072,)
+    per_batch = W4A16GEMV(M=200, K=512, num_batches=3).get_arg_spec()     # ragged M, one qparam per batch row
+    assert per_batch[0].shape == (3, 200, 256 + 8) and per_batch[1].shape == (3, 512)
+    assert per_batch[2].shape == (3, 200)
+    assert W4A16GEMV(M=256, K=512, num_batches=3, shared_qparam=True).get_arg_spec()[0].shape == (256, 264)
     a = LlamaChunkedAttention(max_seq_len=512, num_kv_groups=8, q_heads_per_group=2, head_dim=128)
     assert a.get_arg_spec()[1].shape == (8 * 8 * (2 * 64 * 128 + 64),)
 

@@ -152,3 +152,22 @@ def test_q4nx_layout_matches_reference():
     assert torch.equal(y.to(torch.bfloat16), gio.bf16(d["y"]))
     with pytest.raises(ValueError):
         oracle.q4nx_dequantize_linear(data[:-1], in_f, out_f)
+
+
+def test_oracle_dense_cache_and_last_only_prefill_agree_with_the_plain_forms():
+    """The two shortcuts the full-size checks use: a linear contracting its
+    cached dequantised matrix in one matmul equals the per-group loop of
+    model.py:133-146 up to fp32 association, and the last-token prefill
+    logits are the last row of the all-token ones."""
+    from tests.gpu_util import oracle_decoder
+    from torch2iron_b200 import synth
+    from torch2iron_b200.config import QuantizedQwenConfig
+
+    cfg = QuantizedQwenConfig(vocab_size=300, emb_dim=256, n_layers=2, n_heads=4, n_kv_groups=2, head_dim=64,
+                              hidden_dim=512, rms_norm_eps=1e-6, rope_base=1e6)
+    model = synth.random_model(cfg, seed=8)
+    prompts = torch.randint(0, cfg.vocab_size, (3, 10), generator=torch.Generator().manual_seed(9))
+    full = oracle_decoder(cfg, model, 3, 64).prefill_chunked(prompts, chunk=4)
+    fast = oracle_decoder(cfg, model, 3, 64, dense=True).prefill_chunked(prompts, chunk=4, last_only=True)
+    assert full.shape == (3, 10, 300) and fast.shape == (3, 300)
+    assert torch.allclose(fast, full[:, -1], atol=1e-5, rtol=0)

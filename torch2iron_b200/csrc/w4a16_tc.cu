@@ -32,6 +32,7 @@
 // still passes its cluster barriers, and skips its epilogue.
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "linear_common.cuh"
 #include "launch.cuh"
@@ -281,6 +282,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     }
     T2B_TRACE_MARK(2);
     grid_dep_wait();
+    T2B_TRACE_MARK(3);
   } else if (warp == 4) {
     grid_dep_wait();
     // ---- activations (one 64-k x BP-row TMA box per group and 64-k atom, swizzled
@@ -332,7 +334,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     const bool ok = __all_sync(0xffffffffu, (*abort_flag == 0) && mbar_wait_bounded(acc_full, 0, p.err));
     if (!ok) *abort_flag = 1;
-    T2B_TRACE_MARK(3);
+    T2B_TRACE_MARK(4);
     tc_fence_after();
     constexpr int CB = HB < 32 ? HB : 32;  // columns per TMEM load round
 #pragma unroll 1
@@ -348,7 +350,6 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
         }
         tmem_ld_wait();
       }
-      if (c0 == 0) T2B_TRACE_MARK(4);
 #pragma unroll
       for (int e = 0; e < CB; ++e) {
         const int b = half * HB + c0 + e;
@@ -421,12 +422,25 @@ struct TcPlan {
 // largest S <= 4 that keeps KS <= 8 and the grid at >= 64 CTAs (or as many
 // as the shape allows).  Bp covers the batch up to 256 rows per CTA; shared
 // memory bounds S * Bp.
+// Largest batch tile (env T2B_TC_MAX_BP overrides, for experiments): a larger
+// batch than this runs as several row blocks, each CTA dequantising its
+// weight tile again (off the critical path, before the dependency wait).
+static int tc_max_bp() {
+  const char* e = getenv("T2B_TC_MAX_BP");
+  if (e && *e) {
+    const int v = atoi(e);
+    if (v == 16 || v == 32 || v == 64 || v == 128 || v == 256) return v;
+  }
+  return 256;
+}
+
 static TcPlan tc_plan(int M, int N, int K) {
   TcPlan pl{};
   const int G = K / GROUP;
   const int tiles = N / TILE_N;
+  const int max_bp = tc_max_bp();
   int bp = 16;
-  while (bp < M && bp < 256) bp <<= 1;
+  while (bp < M && bp < max_bp) bp <<= 1;
   pl.BP = bp;
   pl.S = 0;
   auto fits = [&](int bp_, int s_) { return TcLayout(bp_, s_, G / s_).bytes <= 210 * 1024; };

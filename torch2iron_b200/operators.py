@@ -55,9 +55,11 @@ def _check_shape(t: torch.Tensor, shape, name: str):
 
 @dataclass
 class W4A16GEMV:
-    """``y = x . W^T`` over the reference ``qparam`` rows (batch-1 GEMV, or
-    ``num_batches`` independent rows sharing one ``qparam`` when
-    ``shared_qparam``)."""
+    """``y = x . W^T`` over the reference ``qparam`` rows: a batch-1 GEMV, or
+    ``num_batches`` rows, sharing one ``qparam`` (``shared_qparam``, one
+    launch over all rows) or each with its own (one launch per row, as the
+    reference's per-batch arg spec lays them out).  ``M`` not a multiple of
+    the kernel's 128-row tile runs on a zero-padded copy of the rows."""
 
     M: int
     K: int
@@ -86,10 +88,8 @@ class W4A16GEMV:
         # B200 kernel constraints
         if self.group_size != 128:
             raise ValueError("the B200 kernel supports group_size=128")
-        if self.K % 256 or self.M % 128:
-            raise ValueError("the B200 kernel needs K % 256 == 0 and M % 128 == 0")
-        if self.num_batches > 1 and not self.shared_qparam:
-            raise ValueError("per-batch qparam is not supported; use shared_qparam=True")
+        if self.K % 256:
+            raise ValueError("the B200 kernel needs K % 256 == 0")
 
     @property
     def num_groups(self) -> int:
@@ -101,19 +101,36 @@ class W4A16GEMV:
 
     def get_arg_spec(self):
         batch_dim = (self.num_batches,) if self.num_batches > 1 else ()
-        return [ArgSpec("in", (self.M, self.qparam_row_bytes), torch.uint8),
+        qparam_dim = () if self.shared_qparam else batch_dim
+        return [ArgSpec("in", qparam_dim + (self.M, self.qparam_row_bytes), torch.uint8),
                 ArgSpec("in", batch_dim + (self.K,), torch.bfloat16),
                 ArgSpec("out", batch_dim + (self.M,), torch.bfloat16)]
 
     def __call__(self, qparam: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
         for t, spec, nm in zip((qparam, x, y), self.get_arg_spec(), ("qparam", "x", "y")):
             _check_shape(t, spec.shape, nm)
-        rows = self.num_batches
         L = _lib.lib()
-        ws, n = _ws(L.t2b_w4a16_gemm_workspace_bytes(rows, self.M, self.K), qparam.device)
-        _lib.call("t2b_w4a16_gemm", _lib.ptr(qparam), None, _lib.WFMT_QPARAM, _lib.ptr(x), _lib.DTYPE[x.dtype],
-                  _lib.ptr(y), _lib.DTYPE[y.dtype], rows, self.M, self.K, self.group_size, _lib.ptr(ws), n,
-                  _lib.stream())
+        rows = self.num_batches
+        n_pad = -(-self.M // 128) * 128
+        per_batch = rows > 1 and not self.shared_qparam
+        qp = qparam.reshape(rows if per_batch else 1, self.M, self.qparam_row_bytes)
+        if n_pad != self.M:                                   # rows past M: zero weights and scales
+            padded = torch.zeros(qp.shape[0], n_pad, self.qparam_row_bytes, dtype=torch.uint8, device=qp.device)
+            padded[:, :self.M].copy_(qp)
+            qp = padded
+            out = torch.empty(rows, n_pad, dtype=y.dtype, device=y.device)
+        else:
+            out = y.reshape(rows, self.M)
+        xr = x.reshape(rows, self.K)
+        ws, n = _ws(L.t2b_w4a16_gemm_workspace_bytes(1 if per_batch else rows, n_pad, self.K), qparam.device)
+        calls = [(qp[b], xr[b:b + 1], out[b:b + 1], 1) for b in range(rows)] if per_batch else \
+            [(qp[0], xr, out, rows)]
+        for w, xb, yb, m in calls:
+            _lib.call("t2b_w4a16_gemm", _lib.ptr(w), None, _lib.WFMT_QPARAM, _lib.ptr(xb), _lib.DTYPE[x.dtype],
+                      _lib.ptr(yb), _lib.DTYPE[y.dtype], m, n_pad, self.K, self.group_size, _lib.ptr(ws), n,
+                      _lib.stream())
+        if n_pad != self.M:
+            y.reshape(rows, self.M).copy_(out[:, :self.M])
         return y
 
 
