@@ -330,20 +330,20 @@ def kernel_profile(eng, steps):
             lw = eng.layers[li]
             H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
             rec("qkv_norm_rope_kvwrite", lambda: L.t2b_qkv_norm_rope_kvwrite(
-                p(lw.qkv.qw), p(lw.qkv.meta), p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps,
+                p(lw.qkv.qw), p(lw.qkv.meta), lw.qkv.fmt, p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps,
                 p(lw.q_norm), p(lw.k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[li]),
                 p(eng.v_cache[li]), p(eng.ssq_b), B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st))
             rec("decode_attention", lambda: L.t2b_decode_attention_after_kvwrite(
                 p(eng.q), p(eng.k_cache[li]), p(eng.v_cache[li]), p(eng.pos), p(eng.attn), B, nq, nkv, hd,
                 eng.max_ctx, *eng._ws("attn"), st))
             rec("oproj_residual", lambda: L.t2b_oproj_residual(
-                p(lw.o_proj.qw), p(lw.o_proj.meta), p(eng.attn), p(eng.x), p(eng.ssq_b), p(lw.post_attention_layernorm), p(eng.xw), B, H, cfg.q_dim,
+                p(lw.o_proj.qw), p(lw.o_proj.meta), lw.o_proj.fmt, p(eng.attn), p(eng.x), p(eng.ssq_b), p(lw.post_attention_layernorm), p(eng.xw), B, H, cfg.q_dim,
                 *eng._ws("o"), st))
             rec("upgate_swiglu", lambda: L.t2b_upgate_swiglu(
-                p(lw.gate_up.qw), p(lw.gate_up.meta), p(eng.xw), p(eng.ssq_b),
+                p(lw.gate_up.qw), p(lw.gate_up.meta), lw.gate_up.fmt, p(eng.xw), p(eng.ssq_b),
                 cfg.rms_norm_eps, p(eng.h), p(eng.ssq_a), B, H, cfg.hidden_dim, *eng._ws("ug"), st))
             rec("down_residual", lambda: L.t2b_down_residual(
-                p(lw.down.qw), p(lw.down.meta), p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(li)), p(eng.xw), B, H, cfg.hidden_dim,
+                p(lw.down.qw), p(lw.down.meta), lw.down.fmt, p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(li)), p(eng.xw), B, H, cfg.hidden_dim,
                 *eng._ws("down"), st))
         rec("lm_head_argmax", lambda: L.t2b_lm_head_argmax(
             p(eng.xn), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
@@ -373,20 +373,20 @@ def kernel_profile_graph(eng, rounds=5):
     lw = eng.layers
     ops = {
         "qkv_norm_rope_kvwrite": (nl, lambda st, i: L.t2b_qkv_norm_rope_kvwrite(
-            p(lw[i].qkv.qw), p(lw[i].qkv.meta), p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps, p(lw[i].q_norm),
+            p(lw[i].qkv.qw), p(lw[i].qkv.meta), lw[i].qkv.fmt, p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps, p(lw[i].q_norm),
             p(lw[i].k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.ssq_b),
             B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st)),
         "decode_attention": (nl, lambda st, i: L.t2b_decode_attention_after_kvwrite(
             p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.pos), p(eng.attn), B, nq, nkv, hd, eng.max_ctx,
             *eng._ws("attn"), st)),
         "oproj_residual": (nl, lambda st, i: L.t2b_oproj_residual(
-            p(lw[i].o_proj.qw), p(lw[i].o_proj.meta), p(eng.attn), p(eng.x), p(eng.ssq_b),
+            p(lw[i].o_proj.qw), p(lw[i].o_proj.meta), lw[i].o_proj.fmt, p(eng.attn), p(eng.x), p(eng.ssq_b),
             p(lw[i].post_attention_layernorm), p(eng.xw), B, H, cfg.q_dim, *eng._ws("o"), st)),
         "upgate_swiglu": (nl, lambda st, i: L.t2b_upgate_swiglu(
-            p(lw[i].gate_up.qw), p(lw[i].gate_up.meta), p(eng.xw), p(eng.ssq_b), cfg.rms_norm_eps, p(eng.h),
+            p(lw[i].gate_up.qw), p(lw[i].gate_up.meta), lw[i].gate_up.fmt, p(eng.xw), p(eng.ssq_b), cfg.rms_norm_eps, p(eng.h),
             p(eng.ssq_a), B, H, cfg.hidden_dim, *eng._ws("ug"), st)),
         "down_residual": (nl, lambda st, i: L.t2b_down_residual(
-            p(lw[i].down.qw), p(lw[i].down.meta), p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(i)),
+            p(lw[i].down.qw), p(lw[i].down.meta), lw[i].down.fmt, p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(i)),
             p(eng.xw), B, H, cfg.hidden_dim, *eng._ws("down"), st)),
     }
     if eng.lm_w4 is None:

@@ -30,6 +30,14 @@
  * Weight layout "QPARAM" (T2B_WFMT_QPARAM) is the reference's runtime row
  * format (src/models/quantized_qwen3/packed_format.py:195-205): row n is
  * K/2 bytes of biased int4 (zero 8) followed by K/128 bf16 scales.
+ * Weight layout "Q4NX" (T2B_WFMT_Q4NX) is the fast Qwen3 group-32 format
+ * (src/models/fast_qwen3/q4nx_layout.py:30-38,132-174) in T2B blocks: qw as
+ * above; meta N*K/32 uint32, block (n/128, k/128) at ((n/128)*(K/128) +
+ * k/128) * 512 holding [piece p][row r] words: bits 0-15 bf16 scale, bits
+ * 16-31 bf16 zero point of row r, k 32p..32p+31;
+ *   W[n,k] = (q[n,k] - zero[n,k/32]) * scale[n,k/32]   (fp32 on the CUDA-core
+ *   path, as the reference; rounded once to bf16 on the tcgen05 paths).
+ * The fused layer operations take wfmt T2B or Q4NX.
  */
 #ifndef T2B_H
 #define T2B_H
@@ -67,6 +75,7 @@ extern "C" {
 
 #define T2B_WFMT_T2B 0
 #define T2B_WFMT_QPARAM 1
+#define T2B_WFMT_Q4NX 2
 
 /* Library / ABI version and a short human-readable message for a status. */
 T2B_API int t2b_version(void);
@@ -114,8 +123,9 @@ T2B_API int t2b_repack_autogptq(const int32_t* qweight, const int32_t* qzeros, c
 
 /*
  * y[M,N] = x[M,K] . W^T  (fp32 accumulate of the exact dequantized weights).
- * x / y dtypes: T2B_DTYPE_*.  wfmt T2B (weight = qw, meta) or QPARAM (weight =
- * qparam rows, meta = NULL).  Any M >= 1; M <= 8 per CTA row-block.
+ * x / y dtypes: T2B_DTYPE_*.  wfmt T2B (weight = qw, meta; group_size 128),
+ * Q4NX (weight = qw, meta; group_size 32) or QPARAM (weight = qparam rows,
+ * meta = NULL; group_size 128).  Any M >= 1; M <= 8 per CTA row-block.
  * Replaces W4A16GEMV (src/models/quantized_qwen3/operators/w4a16_gemv/op.py:22-126,
  * kernel.cc:29-133) and the W4A16GEMM family (w4a16_gemm/op.py:22-399).
  */
@@ -177,14 +187,14 @@ T2B_API size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, int 
  * sequence m; caches bf16 [n_seq][n_kv][max_ctx][head_dim].  A row whose
  * sequence is outside [0, n_seq) or position outside [0, max_ctx) writes no
  * cache entry. */
-T2B_API int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
+T2B_API int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw,
                                           const float* ssq, float eps, const uint16_t* q_norm_w,
                                           const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
                                           const int32_t* row_seq, int n_seq, uint16_t* q_out, uint16_t* k_cache,
                                           uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
                                           int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
                                           void* stream);
-T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq,
+T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw, const float* ssq,
                                       float eps, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                                       const float* angles, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
                                       uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
@@ -247,7 +257,7 @@ T2B_API int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, uint
  * Replaces W4A16KGroupGEMM(o) + ResidualAddRMSNorm (batch_decode_fused.py:485-498).
  */
 T2B_API size_t t2b_oproj_residual_workspace_bytes(int M, int H, int K);
-T2B_API int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* attn, float* x_resid,
+T2B_API int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* attn, float* x_resid,
                                float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int K,
                                void* workspace, size_t workspace_bytes, void* stream);
 
@@ -259,7 +269,7 @@ T2B_API int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const ui
  * (batch_decode_fused.py:499-506, model.py:215-216).
  */
 T2B_API size_t t2b_upgate_swiglu_workspace_bytes(int M, int H, int I);
-T2B_API int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq,
+T2B_API int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw, const float* ssq,
                               float eps, uint16_t* h_out, float* ssq_clear, int M, int H, int I, void* workspace,
                               size_t workspace_bytes, void* stream);
 
@@ -268,7 +278,7 @@ T2B_API int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const uin
  * Replaces W4A16KGroupGEMM(down) + ResidualAddRMSNorm (batch_decode_fused.py:507-530).
  */
 T2B_API size_t t2b_down_residual_workspace_bytes(int M, int H, int I);
-T2B_API int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* h, float* x_resid,
+T2B_API int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* h, float* x_resid,
                               float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int I,
                               void* workspace, size_t workspace_bytes, void* stream);
 

@@ -16,6 +16,7 @@ from safetensors.torch import load_file, save_file
 import oracle
 from tests.gpu_util import oracle_layer, oracle_shape
 from torch2iron_b200 import loaders as LD
+from torch2iron_b200 import synth
 from torch2iron_b200.synth import LINEAR_NAMES, AutoGPTQLinear
 
 GOLD = Path(__file__).resolve().parent / "golden"
@@ -298,8 +299,11 @@ def test_fast_artifact_errors_and_engine_refusal(tmp_path):
         LD.load_fast_qwen3_artifact(d)
     from torch2iron_b200.engine import DecodeEngine
     cfg, model = LD.load_fast_qwen3_artifact(MODEL_DIR)
-    with pytest.raises(NotImplementedError, match="Q4NX"):
-        DecodeEngine(cfg, model, batch=1, max_ctx=64)
+    # one weight format per layer: a Q4NX layer with one AutoGPTQ linear is refused before any device work
+    mixed = dict(model, layers=[dict(model["layers"][0], o_proj=synth.random_linear(
+        cfg.emb_dim, cfg.q_dim, torch.Generator().manual_seed(0)))] + model["layers"][1:])
+    with pytest.raises(NotImplementedError, match="one format per layer"):
+        DecodeEngine(cfg, mixed, batch=1, max_ctx=64)
     # the tensor-parallel engine refuses before sharding (which reads AutoGPTQ tensors)
     from torch2iron_b200.tp import TPDecodeEngine
     with pytest.raises(NotImplementedError, match="AutoGPTQ"):

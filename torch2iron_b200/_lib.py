@@ -19,6 +19,7 @@ T2B_OK = 0
 DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 WFMT_T2B = 0
 WFMT_QPARAM = 1
+WFMT_Q4NX = 2
 
 P = C.c_void_p
 I = C.c_int
@@ -37,19 +38,19 @@ SIGNATURES = {
     "t2b_w4a16_gemm_noalloc_max_workspace": (Z, []),
     "t2b_w4a16_gemm_noalloc": (I, [P, P, I, P, I, P, I, I, I, I, I, P]),
     "t2b_qkv_workspace_bytes": (Z, [I, I, I, I, I]),
-    "t2b_qkv_norm_rope_kvwrite": (I, [P, P, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
-    "t2b_qkv_norm_rope_kvwrite_seq": (I, [P, P, P, P, F, P, P, P, P, P, I, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_qkv_norm_rope_kvwrite": (I, [P, P, I, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_qkv_norm_rope_kvwrite_seq": (I, [P, P, I, P, P, F, P, P, P, P, P, I, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_prefill_attention": (I, [P, P, P, P, I, I, I, I, I, I, I, P]),
     "t2b_decode_attention_workspace_bytes": (Z, [I, I, I, I, I]),
     "t2b_decode_attention": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_decode_attention_after_kvwrite": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_packet_attention": (I, [P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_oproj_residual_workspace_bytes": (Z, [I, I, I]),
-    "t2b_oproj_residual": (I, [P, P, P, P, P, P, P, I, I, I, P, Z, P]),
+    "t2b_oproj_residual": (I, [P, P, I, P, P, P, P, P, I, I, I, P, Z, P]),
     "t2b_upgate_swiglu_workspace_bytes": (Z, [I, I, I]),
-    "t2b_upgate_swiglu": (I, [P, P, P, P, F, P, P, I, I, I, P, Z, P]),
+    "t2b_upgate_swiglu": (I, [P, P, I, P, P, F, P, P, I, I, I, P, Z, P]),
     "t2b_down_residual_workspace_bytes": (Z, [I, I, I]),
-    "t2b_down_residual": (I, [P, P, P, P, P, P, P, I, I, I, P, Z, P]),
+    "t2b_down_residual": (I, [P, P, I, P, P, P, P, P, I, I, I, P, Z, P]),
     "t2b_embed_rows": (I, [P, P, P, P, P, P, I, I, I, P]),
     "t2b_rms_norm_rows": (I, [P, P, P, F, P, I, I, P]),
     "t2b_set_error_word": (I, [P]),

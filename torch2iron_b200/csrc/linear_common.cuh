@@ -58,10 +58,37 @@ struct LinearParams {
   __nv_bfloat16* v_cache;
   int n_heads, n_kv, head_dim, max_ctx;
   int* err;
+  int q4nx;               // 1: Q4NX meta (bf16 scale | bf16 zero per 32-k piece), 0: T2B (per 128-k group)
 };
 
 T2B_DEV size_t qw_block_offset(int nt, int g, int G) { return ((size_t)nt * G + g) * BLOCK_BYTES; }
 T2B_DEV size_t meta_block_offset(int nt, int g, int G) { return ((size_t)nt * G + g) * TILE_N; }
+// Q4NX meta: 4 pieces x 128 rows per block, piece-major
+constexpr int Q4NX_META_WORDS = 4 * TILE_N;
+T2B_DEV size_t meta_q4nx_offset(int nt, int g, int G) { return ((size_t)nt * G + g) * Q4NX_META_WORDS; }
+// Meta words of one (tile, group) block in either format.
+T2B_DEV int meta_block_words(bool q4nx) { return q4nx ? Q4NX_META_WORDS : TILE_N; }
+
+T2B_DEV float bf16_lo_f32(uint32_t w) { return __uint_as_float(w << 16); }
+T2B_DEV float bf16_hi_f32(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// One 16-byte piece (32 k of one row, T2B nibble order) of a Q4NX weight as
+// 16 bf16x2 words (k pairs in order): (q - zero) * scale in fp32, as the
+// reference computes it (q4nx_layout.py:132-146), rounded once to bf16.
+// 0x43000000 | q << 16 is the fp32 value 128 + q.
+T2B_DEV void dequant_piece_q4nx_bf16(const uint4 v, float s, float z, uint32_t cols[16]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t m = (w[j] >> (4 * t)) & 0x000F000Fu;
+      const float q0 = __uint_as_float(0x43000000u | (m << 16)) - 128.f;
+      const float q1 = __uint_as_float(0x43000000u | (m & 0xffff0000u)) - 128.f;
+      const __nv_bfloat162 d = __floats2bfloat162_rn(__fmul_rn(__fsub_rn(q0, z), s), __fmul_rn(__fsub_rn(q1, z), s));
+      cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d);
+    }
+}
 
 // ---------------------------------------------------------------------------
 // Split-K: publish this CTA's [MB][128] partial (already in `tile_acc`) and,

@@ -89,10 +89,13 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
     for (int i = 0; i < 4; ++i) {
       const int rr = warp * 16 + i * 4 + (lane >> 3);
       const int k = k0 + c * 256 + (lane & 7) * 32;
-      if (WFMT == T2B_WFMT_T2B) {
+      if (WFMT == T2B_WFMT_T2B || WFMT == T2B_WFMT_Q4NX) {
         const int g = k >> 7, pc = (k & 127) >> 5;
         wv[c][i] = ldg_stream(p.qw + qw_block_offset(tile, g, p.G) + pc * 2048 + rr * 16);
-        mt[c][i] = __ldg(p.meta + meta_block_offset(tile, g, p.G) + rr);
+        if (WFMT == T2B_WFMT_T2B)
+          mt[c][i] = __ldg(p.meta + meta_block_offset(tile, g, p.G) + rr);
+        else  // one Q4NX piece (32 k) per lane and chunk: its own scale and zero point
+          mt[c][i] = __ldg(p.meta + meta_q4nx_offset(tile, g, p.G) + pc * TILE_N + rr);
       } else {  // qparam rows are K/2 + 2G bytes: only 4-byte aligned
         const uint8_t* rowp = p.qw + (size_t)(row0 + rr) * p.w_ld;
         const uint32_t* w4 = reinterpret_cast<const uint32_t*>(rowp + (k >> 1));
@@ -152,6 +155,9 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
         sc[i] = __half2float(__ushort_as_half((unsigned short)(mt[c][i] & 0xffffu)));
         const float z = (float)((mt[c][i] >> 16) & 0x1fu);
         zc[i] = -(128.f + z) * sc[i];
+      } else if (WFMT == T2B_WFMT_Q4NX) {
+        sc[i] = bf16_lo_f32(mt[c][i]);
+        zc[i] = bf16_hi_f32(mt[c][i]);       // the zero point itself (not folded)
       } else {
         sc[i] = bf16_bits_to_f32(mt[c][i] & 0xffffu);
         zc[i] = -(128.f + 8.f) * sc[i];
@@ -166,7 +172,20 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
         const uint32_t w = wd == 0 ? wv[c][i].x : wd == 1 ? wv[c][i].y : wd == 2 ? wv[c][i].z : wv[c][i].w;
         const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
         // (128+q)*s - (128+z)*s is exact in fp32: (q - z) * s
-        if (WFMT == T2B_WFMT_T2B) {  // nibble slots hold k 0,2,4,6,1,3,5,7
+        if (WFMT == T2B_WFMT_Q4NX) {
+          // (q - zero) * scale in fp32 as the reference (q4nx_layout.py:132-146):
+          // nib_f - 128 is q exactly, then one rounded subtract and one multiply
+#define T2B_Q4(sel, src) __fmul_rn(__fsub_rn(nib_f(src, sel) - 128.f, zc[i]), sc[i])
+          wf[i][0] = T2B_Q4(0x7054, lo);
+          wf[i][2] = T2B_Q4(0x7054, hi);
+          wf[i][4] = T2B_Q4(0x7154, lo);
+          wf[i][6] = T2B_Q4(0x7154, hi);
+          wf[i][1] = T2B_Q4(0x7254, lo);
+          wf[i][3] = T2B_Q4(0x7254, hi);
+          wf[i][5] = T2B_Q4(0x7354, lo);
+          wf[i][7] = T2B_Q4(0x7354, hi);
+#undef T2B_Q4
+        } else if (WFMT == T2B_WFMT_T2B) {  // nibble slots hold k 0,2,4,6,1,3,5,7
           wf[i][0] = fmaf(nib_f(lo, 0x7054), sc[i], zc[i]);
           wf[i][2] = fmaf(nib_f(hi, 0x7054), sc[i], zc[i]);
           wf[i][4] = fmaf(nib_f(lo, 0x7154), sc[i], zc[i]);
@@ -317,6 +336,16 @@ static int gemv_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, si
     if (pro != PRO_ACT || epi != EPI_STORE) return T2B_ERR_ARG;
     return gemv_dispatch<PRO_ACT, EPI_STORE, T2B_WFMT_QPARAM>(p, MB, CH, grid, st);
   }
+  if (wfmt == T2B_WFMT_Q4NX) {
+    if (pro == PRO_ACT && epi == EPI_STORE) return gemv_dispatch<PRO_ACT, EPI_STORE, T2B_WFMT_Q4NX>(p, MB, CH, grid, st);
+    if (pro == PRO_ACT && epi == EPI_RESIDUAL)
+      return gemv_dispatch<PRO_ACT, EPI_RESIDUAL, T2B_WFMT_Q4NX>(p, MB, CH, grid, st);
+    if (pro == PRO_RMSNORM && epi == EPI_SWIGLU)
+      return gemv_dispatch<PRO_RMSNORM, EPI_SWIGLU, T2B_WFMT_Q4NX>(p, MB, CH, grid, st);
+    if (pro == PRO_RMSNORM && epi == EPI_QKV)
+      return gemv_dispatch<PRO_RMSNORM, EPI_QKV, T2B_WFMT_Q4NX>(p, MB, CH, grid, st);
+    return T2B_ERR_ARG;
+  }
   if (pro == PRO_ACT && epi == EPI_STORE) return gemv_dispatch<PRO_ACT, EPI_STORE, T2B_WFMT_T2B>(p, MB, CH, grid, st);
   if (pro == PRO_RMSNORM && epi == EPI_STORE)
     return gemv_dispatch<PRO_RMSNORM, EPI_STORE, T2B_WFMT_T2B>(p, MB, CH, grid, st);
@@ -332,7 +361,7 @@ static int gemv_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, si
 // tcgen05 path (w4a16_tc.cu)
 int tc_launch(LinearParams& p, int pro, int epi, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t tc_ws_bytes(int M, int N, int K);
-bool tc_supported(int M, int N, int K);
+bool tc_supported(int M, int N, int K, bool q4);
 bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks);
 
 // Rows at or above this count take the tcgen05 path (env T2B_TC_MIN_M overrides).
@@ -349,12 +378,15 @@ static int tc_min_m() {
 int prefill_min_m();
 int prefill_launch(LinearParams& p, int pro, int epi, cudaStream_t st);
 
+static bool tiled_wfmt(int wfmt) { return wfmt == T2B_WFMT_T2B || wfmt == T2B_WFMT_Q4NX; }
+
 static bool use_prefill(int M, int wfmt, int x_dtype) {
-  return wfmt == T2B_WFMT_T2B && x_dtype == T2B_DTYPE_BF16 && M >= prefill_min_m();
+  return tiled_wfmt(wfmt) && x_dtype == T2B_DTYPE_BF16 && M >= prefill_min_m();
 }
 
 static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {
-  return wfmt == T2B_WFMT_T2B && x_dtype == T2B_DTYPE_BF16 && M >= tc_min_m() && tc_supported(M, N, K);
+  return tiled_wfmt(wfmt) && x_dtype == T2B_DTYPE_BF16 && M >= tc_min_m() &&
+         tc_supported(M, N, K, wfmt == T2B_WFMT_Q4NX);
 }
 
 // Split of the CUDA-core path's workspace: fp32 partials, then the tile
@@ -380,6 +412,7 @@ size_t linear_workspace_bytes(int M, int N, int K) {
 
 int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t ws_bytes, cudaStream_t st) {
   p.err = error_word(st);
+  p.q4nx = wfmt == T2B_WFMT_Q4NX ? 1 : 0;
   if (p.M < 1 || p.N <= 0 || p.K <= 0) return T2B_ERR_SHAPE;
   if (p.N % TILE_N || p.K % 256) return T2B_ERR_SHAPE;
   p.G = p.K / GROUP;
@@ -443,12 +476,12 @@ namespace t2b {
 // Host-side checks of a plain W4A16 GEMM call; fills the launch parameters.
 int gemm_params(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype, void* y,
                 int y_dtype, int M, int N, int K, int group_size, LinearParams* out) {
-  if (group_size != 128) return T2B_ERR_SHAPE;
+  if (group_size != (wfmt == T2B_WFMT_Q4NX ? 32 : 128)) return T2B_ERR_SHAPE;
   if (!weight || !x || !y) return T2B_ERR_ARG;
   if (x_dtype < 0 || x_dtype > 2 || y_dtype < 0 || y_dtype > 2) return T2B_ERR_ARG;
   if (M < 1 || N <= 0 || K <= 0 || N % TILE_N || K % 256) return T2B_ERR_SHAPE;
   int w_ld;
-  if (wfmt == T2B_WFMT_T2B) {
+  if (tiled_wfmt(wfmt)) {
     if (!meta) return T2B_ERR_ARG;
     if (!al(weight, 16) || !al(meta, 4)) return T2B_ERR_ALIGN;
     w_ld = K / 2;
@@ -499,13 +532,14 @@ extern "C" size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, i
   return linear_workspace_bytes(M, (n_heads + 2 * n_kv) * head_dim, H);
 }
 
-static int qkv_impl(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq, float eps,
+static int qkv_impl(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw, const float* ssq, float eps,
                     const uint16_t* q_norm_w, const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
                     const int32_t* row_seq, int n_seq, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
                     float* ssq_clear, int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
                     size_t ws_bytes, void* stream) {
   if (head_dim != 64 && head_dim != 128) return T2B_ERR_SHAPE;
   if (n_kv < 1 || n_heads % n_kv || max_ctx < 1) return T2B_ERR_SHAPE;
+  if (!tiled_wfmt(wfmt)) return T2B_ERR_ARG;
   if (!qw || !meta || !xw || !ssq || !angles || !pos || !q_out || !k_cache || !v_cache) return T2B_ERR_ARG;
   if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return T2B_ERR_ARG;
   if (!al(qw, 16) || !al(xw, 16)) return T2B_ERR_ALIGN;
@@ -534,20 +568,20 @@ static int qkv_impl(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
   p.n_kv = n_kv;
   p.head_dim = head_dim;
   p.max_ctx = max_ctx;
-  return linear_launch(p, PRO_RMSNORM, EPI_QKV, T2B_WFMT_T2B, ws, ws_bytes, S_(stream));
+  return linear_launch(p, PRO_RMSNORM, EPI_QKV, wfmt, ws, ws_bytes, S_(stream));
 }
 
-extern "C" int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
+extern "C" int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw,
                                          const float* ssq, float eps, const uint16_t* q_norm_w,
                                          const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
                                          uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, float* ssq_clear,
                                          int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
                                          size_t ws_bytes, void* stream) {
-  return qkv_impl(qw, meta, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, nullptr, M, q_out, k_cache, v_cache,
+  return qkv_impl(qw, meta, wfmt, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, nullptr, M, q_out, k_cache, v_cache,
                   ssq_clear, M, H, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes, stream);
 }
 
-extern "C" int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw,
+extern "C" int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw,
                                              const float* ssq, float eps, const uint16_t* q_norm_w,
                                              const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
                                              const int32_t* row_seq, int n_seq, uint16_t* q_out,
@@ -556,7 +590,7 @@ extern "C" int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* 
                                              size_t ws_bytes, void* stream) {
   if (!row_seq) return T2B_ERR_ARG;
   if (n_seq < 1) return T2B_ERR_SHAPE;
-  return qkv_impl(qw, meta, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, row_seq, n_seq, q_out, k_cache, v_cache,
+  return qkv_impl(qw, meta, wfmt, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, row_seq, n_seq, q_out, k_cache, v_cache,
                   ssq_clear, M, H, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes, stream);
 }
 
@@ -565,10 +599,10 @@ extern "C" size_t t2b_oproj_residual_workspace_bytes(int M, int H, int K) {
   return linear_workspace_bytes(M, H, K);
 }
 
-extern "C" int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* attn, float* x_resid,
+extern "C" int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* attn, float* x_resid,
                                   float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int K,
                                   void* ws, size_t ws_bytes, void* stream) {
-  if (!qw || !meta || !attn || !x_resid || !ssq_out) return T2B_ERR_ARG;
+  if (!qw || !meta || !attn || !x_resid || !ssq_out || !tiled_wfmt(wfmt)) return T2B_ERR_ARG;
   if ((next_norm_w == nullptr) != (xw_out == nullptr)) return T2B_ERR_ARG;
   if (!al(qw, 16) || !al(attn, 16)) return T2B_ERR_ALIGN;
   // vectorised epilogue: float4 residual rows, 8-byte bf16 stores
@@ -582,7 +616,7 @@ extern "C" int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, const
   p.ssq_out = ssq_out;
   p.next_w = reinterpret_cast<const __nv_bfloat16*>(next_norm_w);
   p.xw_out = reinterpret_cast<__nv_bfloat16*>(xw_out);
-  return linear_launch(p, PRO_ACT, EPI_RESIDUAL, T2B_WFMT_T2B, ws, ws_bytes, S_(stream));
+  return linear_launch(p, PRO_ACT, EPI_RESIDUAL, wfmt, ws, ws_bytes, S_(stream));
 }
 
 extern "C" size_t t2b_upgate_swiglu_workspace_bytes(int M, int H, int I) {
@@ -590,11 +624,11 @@ extern "C" size_t t2b_upgate_swiglu_workspace_bytes(int M, int H, int I) {
   return linear_workspace_bytes(M, 2 * I, H);
 }
 
-extern "C" int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const uint16_t* xw, const float* ssq,
+extern "C" int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw, const float* ssq,
                                  float eps, uint16_t* h_out, float* ssq_clear, int M, int H, int I, void* ws,
                                  size_t ws_bytes, void* stream) {
   if (I % 64) return T2B_ERR_SHAPE;
-  if (!qw || !meta || !xw || !ssq || !h_out) return T2B_ERR_ARG;
+  if (!qw || !meta || !xw || !ssq || !h_out || !tiled_wfmt(wfmt)) return T2B_ERR_ARG;
   if (!al(qw, 16) || !al(xw, 16) || !al(h_out, 8)) return T2B_ERR_ALIGN;
   LinearParams p = gemv_base(qw, meta, H / 2, M, 2 * I, H);
   p.x = xw;
@@ -605,7 +639,7 @@ extern "C" int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, const 
   p.y = h_out;
   p.y_ld = I;
   p.ssq_clear = ssq_clear;
-  return linear_launch(p, PRO_RMSNORM, EPI_SWIGLU, T2B_WFMT_T2B, ws, ws_bytes, S_(stream));
+  return linear_launch(p, PRO_RMSNORM, EPI_SWIGLU, wfmt, ws, ws_bytes, S_(stream));
 }
 
 extern "C" size_t t2b_down_residual_workspace_bytes(int M, int H, int I) {
@@ -613,10 +647,10 @@ extern "C" size_t t2b_down_residual_workspace_bytes(int M, int H, int I) {
   return linear_workspace_bytes(M, H, I);
 }
 
-extern "C" int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, const uint16_t* h, float* x_resid,
+extern "C" int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* h, float* x_resid,
                                  float* ssq_out, const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, int I,
                                  void* ws, size_t ws_bytes, void* stream) {
-  return t2b_oproj_residual(qw, meta, h, x_resid, ssq_out, next_norm_w, xw_out, M, H, I, ws, ws_bytes, stream);
+  return t2b_oproj_residual(qw, meta, wfmt, h, x_resid, ssq_out, next_norm_w, xw_out, M, H, I, ws, ws_bytes, stream);
 }
 
 T2B_TRACE_DUMP_FN(t2b_trace_dump_gemv)

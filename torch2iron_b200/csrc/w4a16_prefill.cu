@@ -41,7 +41,7 @@ constexpr int PF_BM = 128;               // activation rows per unit (MMA N)
 constexpr int PF_NX = 3;                 // activation stages
 constexpr int PF_NA = 4;                 // TMEM A stages (64 columns each)
 constexpr int PF_NR = 4;                 // raw weight stages
-constexpr int PF_RAW = BLOCK_BYTES + TILE_N * 4;   // int4 block + meta of one (tile, group)
+constexpr int PF_RAW = BLOCK_BYTES + Q4NX_META_WORDS * 4;   // int4 block + meta of one (tile, group), either format
 constexpr int PF_GT = 480;               // threads: 8 producer, 4 epilogue, TMA, MMA, weight warps
 constexpr int PF_EPI_T0 = 256;           // first epilogue thread
 constexpr uint32_t PF_TMEM_COLS = 512;   // accumulators [0, 2*BM), A stages from column 2*BM
@@ -52,7 +52,7 @@ struct PfLayout {
   static constexpr int OFF_TILE = PF_NX * X_STAGE;                 // fp32 [BM][128]
   static constexpr int OFF_SCR = OFF_TILE + PF_BM * TILE_N * 4;    // fp32 [2*BM] epilogue scratch
   static constexpr int OFF_RS = OFF_SCR + 2 * PF_BM * 4;           // fp32 [BM] row scales
-  static constexpr int OFF_RAW = OFF_RS + PF_BM * 4;               // [NR][8 KB int4 | 512 B meta]
+  static constexpr int OFF_RAW = OFF_RS + PF_BM * 4;               // [NR][8 KB int4 | 512 B (T2B) or 2 KB (Q4NX) meta]
   static constexpr int N_BARS = 2 * PF_NX + 2 * PF_NA + 2 * PF_NR + 4 + 1;
   static constexpr int OFF_BAR = OFF_RAW + PF_NR * PF_RAW;
   static constexpr int OFF_TMEM = OFF_BAR + N_BARS * 8;
@@ -278,7 +278,13 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       uint4 v[2];
 #pragma unroll
       for (int j = 0; j < 2; ++j) v[j] = *reinterpret_cast<const uint4*>(raw + (2 * h + j) * 2048 + r * 16);
-      const uint32_t mw = *reinterpret_cast<const uint32_t*>(raw + BLOCK_BYTES + r * 4);
+      const uint32_t* rmeta = reinterpret_cast<const uint32_t*>(raw + BLOCK_BYTES);
+      const uint32_t mw = rmeta[r];
+      uint32_t mq[2] = {0u, 0u};                 // Q4NX: the words of pieces 2h, 2h+1
+      if (p.q4nx) {
+        mq[0] = rmeta[(2 * h) * TILE_N + r];
+        mq[1] = rmeta[(2 * h + 1) * TILE_N + r];
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_empty[sr]);   // this warp is done with the raw stage
       PF_CLK(ta0);
@@ -295,6 +301,12 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int pc = 2 * h + j;
+        if (p.q4nx) {
+          uint32_t cols[16];
+          dequant_piece_q4nx_bf16(v[j], bf16_lo_f32(mq[j]), bf16_hi_f32(mq[j]), cols);
+          tmem_st16(lane_base + PF_A0 + (uint32_t)(sa * 64 + pc * 16), cols);
+          continue;
+        }
         const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
         uint32_t cols[16];
 #pragma unroll
@@ -354,9 +366,11 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
         if (*abort_flag) break;
         const int tile = unit_of(it / G) % n_tiles, g = it % G;
         uint8_t* dst = sm + L::OFF_RAW + s * PF_RAW;
-        mbar_arrive_expect_tx(&w_full[s], (uint32_t)PF_RAW);
+        const int mwords = p.q4nx ? Q4NX_META_WORDS : TILE_N;
+        mbar_arrive_expect_tx(&w_full[s], (uint32_t)(BLOCK_BYTES + mwords * 4));
         bulk_g2s(dst, p.qw + qw_block_offset(tile, g, G), BLOCK_BYTES, &w_full[s]);
-        bulk_g2s(dst + BLOCK_BYTES, p.meta + meta_block_offset(tile, g, G), TILE_N * 4, &w_full[s]);
+        bulk_g2s(dst + BLOCK_BYTES, p.meta + (p.q4nx ? meta_q4nx_offset(tile, g, G) : meta_block_offset(tile, g, G)),
+                 (uint32_t)(mwords * 4), &w_full[s]);
         issued = it + 1;
       }
       for (int it = std::max(0, issued - PF_NR); it < issued; ++it)

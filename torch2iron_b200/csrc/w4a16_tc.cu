@@ -49,11 +49,12 @@ constexpr int EP_BYTES = EP_ROWS_BYTES + 256 + 1024;
 
 struct TcLayout {
   int x_group, off_raw, off_meta, off_tile, off_recv, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
-  __host__ __device__ TcLayout(int BP, int S, int KS) {
+  // q4: Q4NX meta (512 words per group: [piece 4][row 128]) instead of 128
+  __host__ __device__ TcLayout(int BP, int S, int KS, bool q4 = false) {
     x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group (TMA, 128B swizzle)
     off_raw = S * x_group;                   // [S][8 KB] raw int4 blocks
-    off_meta = off_raw + S * BLOCK_BYTES;    // [S][128] meta words
-    off_tile = off_meta + S * TILE_N * 4;    // fp32 [BP][128] partial tile
+    off_meta = off_raw + S * BLOCK_BYTES;    // [S][128 or 512] meta words
+    off_tile = off_meta + S * TILE_N * 4 * (q4 ? 4 : 1);   // fp32 [BP][128] partial tile
     off_recv = off_tile + BP * TILE_N * 4;   // fp32 [KS-1][BP/KS][128] peers' partials of this CTA's rows
     off_scr = off_recv + (BP - BP / KS) * TILE_N * 4;  // fp32 [8*BP] scratch (row scales, epilogue)
     off_ep = off_scr + 8 * BP * 4;           // epilogue inputs staged after the PDL wait
@@ -166,7 +167,9 @@ template <int BP, int PRO, int EPI>
 __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant__ LinearParams p) {
   const int S = p.kslice / GROUP;
   const int KS = p.ksplit;
-  const TcLayout L(BP, S, KS);
+  const bool q4 = p.q4nx != 0;
+  const TcLayout L(BP, S, KS, q4);
+  const int mwords = q4 ? Q4NX_META_WORDS : TILE_N;   // meta words per (tile, group)
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* xs = sm;
@@ -216,9 +219,11 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   // raw weight blocks of this CTA: constant data, fetched before the PDL wait
   if (threadIdx.x == 0) {
     for (int gl = 0; gl < S; ++gl) {
-      mbar_arrive_expect_tx(&raw_full[gl], BLOCK_BYTES + TILE_N * 4);
+      mbar_arrive_expect_tx(&raw_full[gl], (uint32_t)(BLOCK_BYTES + mwords * 4));
       bulk_g2s(raw + gl * BLOCK_BYTES, p.qw + qw_block_offset(tile, g0 + gl, p.G), BLOCK_BYTES, &raw_full[gl]);
-      bulk_g2s(sm + L.off_meta + gl * TILE_N * 4, p.meta + meta_block_offset(tile, g0 + gl, p.G), TILE_N * 4,
+      bulk_g2s(sm + L.off_meta + gl * mwords * 4,
+               p.meta + (q4 ? meta_q4nx_offset(tile, g0 + gl, p.G) : meta_block_offset(tile, g0 + gl, p.G)),
+               (uint32_t)(mwords * 4),
                &raw_full[gl]);
     }
   }
@@ -251,6 +256,21 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
       if (!ok) {  // the warp takes the same branch before tcgen05.st
         *abort_flag = 1;
         break;
+      }
+      if (q4) {  // Q4NX: a scale and zero point per 32-k piece, dequantised in fp32
+#pragma unroll 1
+        for (int pc = 0; pc < 4; ++pc) {
+          const uint4 v = *reinterpret_cast<const uint4*>(raw + gl * BLOCK_BYTES + pc * 2048 + r * 16);
+          const uint32_t mw = rmeta[gl * Q4NX_META_WORDS + pc * TILE_N + r];
+          uint32_t cols[16];
+          dequant_piece_q4nx_bf16(v, bf16_lo_f32(mw), bf16_hi_f32(mw), cols);
+          tmem_st16(lane_base + a0 + stage * 64 + pc * 16, cols);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[stage]);
+        continue;
       }
       const uint32_t mw = rmeta[gl * TILE_N + r];
       const __nv_bfloat16 sb = __float2bfloat16_rn(__half2float(__ushort_as_half((unsigned short)(mw & 0xffffu))));
@@ -434,7 +454,7 @@ static int tc_max_bp() {
   return 256;
 }
 
-static TcPlan tc_plan(int M, int N, int K) {
+static TcPlan tc_plan(int M, int N, int K, bool q4 = false) {
   TcPlan pl{};
   const int G = K / GROUP;
   const int tiles = N / TILE_N;
@@ -443,7 +463,7 @@ static TcPlan tc_plan(int M, int N, int K) {
   while (bp < M && bp < max_bp) bp <<= 1;
   pl.BP = bp;
   pl.S = 0;
-  auto fits = [&](int bp_, int s_) { return TcLayout(bp_, s_, G / s_).bytes <= 210 * 1024; };
+  auto fits = [&](int bp_, int s_) { return TcLayout(bp_, s_, G / s_, q4).bytes <= 210 * 1024; };
   // KS must divide BP: each CTA of a cluster finishes BP/KS rows, and its
   // receive barrier expects the (KS-1) * BP/KS rows its peers push.
   auto splits = [&](int bp_, int s_) { return G % s_ == 0 && G / s_ <= 8 && bp_ % (G / s_) == 0; };
@@ -477,7 +497,7 @@ static TcPlan tc_plan(int M, int N, int K) {
       sms = 148;
     const int mb = (M + pl.BP - 1) / pl.BP;
     auto waves = [&](int s_) {
-      const long bytes = TcLayout(pl.BP, s_, G / s_).bytes;
+      const long bytes = TcLayout(pl.BP, s_, G / s_, q4).bytes;
       int per_sm = (int)((228L * 1024) / (bytes + 1024));
       per_sm = std::min(per_sm, (int)(512u / tc_tmem_cols(pl.BP, s_)));
       per_sm = std::max(1, std::min(per_sm, 2));
@@ -494,7 +514,7 @@ static TcPlan tc_plan(int M, int N, int K) {
   }
   pl.KS = G / pl.S;
   pl.mblocks = (M + pl.BP - 1) / pl.BP;
-  pl.smem = (size_t)TcLayout(pl.BP, pl.S, pl.KS).bytes;
+  pl.smem = (size_t)TcLayout(pl.BP, pl.S, pl.KS, q4).bytes;
   // A CTA holding more than half of the SM's 512 TMEM columns runs alone on
   // its SM (more than half of the shared memory requested): a second one
   // there would only sit in tcgen05.alloc until the first frees its columns.
@@ -506,7 +526,7 @@ static TcPlan tc_plan(int M, int N, int K) {
 
 size_t tc_ws_bytes(int, int, int) { return 0; }  // split-K stays on chip (cluster DSMEM)
 
-bool tc_supported(int M, int N, int K) { return tc_plan(M, N, K).ok; }
+bool tc_supported(int M, int N, int K, bool q4) { return tc_plan(M, N, K, q4).ok; }
 
 bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks) {
   const TcPlan pl = tc_plan(M, N, K);
@@ -552,7 +572,7 @@ static int make_x_map(LinearParams& p, int BP) {
 }
 
 int tc_launch(LinearParams& p, int pro, int epi, void*, size_t, cudaStream_t st) {
-  const TcPlan pl = tc_plan(p.M, p.N, p.K);
+  const TcPlan pl = tc_plan(p.M, p.N, p.K, p.q4nx != 0);
   if (!pl.ok) return T2B_ERR_SHAPE;
   if (p.x_dtype != T2B_DTYPE_BF16) return T2B_ERR_ARG;
   const int mx = make_x_map(p, pl.BP);

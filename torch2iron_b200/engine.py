@@ -61,20 +61,29 @@ class LayerWeights:
 
 
 def load_layer(layer: dict, cfg: QuantizedQwenConfig, device="cuda") -> LayerWeights:
-    for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
-        if not isinstance(layer[name], AutoGPTQLinear):
-            raise NotImplementedError(
-                f"{name} is a {type(layer[name]).__name__}: the decode kernels take group-128 AutoGPTQ-derived "
-                "weights (the packed artifact or the checkpoint); Q4NX group-32 weights are not supported yet")
+    """One layer's device weights: group-128 AutoGPTQ-derived linears (the
+    packed artifact, checkpoints, synthetic models) into the T2B layout, or
+    the fast artifact's Q4NX group-32 linears into its group-32 variant; the
+    seven linears of a layer share one format."""
+    names = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+    kinds = {type(layer[n]) for n in names}
+    if kinds == {AutoGPTQLinear}:
+        concat, single, pair = W.concat_rows, W.from_autogptq, W.pair_blocks
+    elif len(kinds) == 1 and all(hasattr(layer[n], "padded_out_features") for n in names):
+        concat, single, pair = W.q4nx_concat_rows, W.from_q4nx, W.q4nx_pair_blocks
+    else:
+        raise NotImplementedError(
+            f"layer linears are {sorted(k.__name__ for k in kinds)}: the decode kernels take group-128 "
+            "AutoGPTQ-derived weights or Q4NX group-32 weights, one format per layer")
 
     def bf(t):
         return None if t is None else t.to(device=device, dtype=torch.bfloat16).contiguous()
 
     return LayerWeights(
-        qkv=W.concat_rows([layer["q_proj"], layer["k_proj"], layer["v_proj"]], device),
-        o_proj=W.from_autogptq(layer["o_proj"], device),
-        gate_up=W.pair_blocks(layer["gate_proj"], layer["up_proj"], device),
-        down=W.from_autogptq(layer["down_proj"], device),
+        qkv=concat([layer["q_proj"], layer["k_proj"], layer["v_proj"]], device),
+        o_proj=single(layer["o_proj"], device),
+        gate_up=pair(layer["gate_proj"], layer["up_proj"], device),
+        down=single(layer["down_proj"], device),
         input_layernorm=bf(layer["input_layernorm"]),
         post_attention_layernorm=bf(layer["post_attention_layernorm"]),
         q_norm=bf(layer.get("q_norm")) if cfg.qk_norm else None,
@@ -104,10 +113,10 @@ class DecodeEngine:
         self.embed = model["embed"].to(dev, torch.bfloat16).contiguous()
         lm = model.get("lm_head")
         self.lm_w4: W.W4Weight | None = None          # W4A16 head (a packed artifact's ``lm_head`` linear)
-        if isinstance(lm, AutoGPTQLinear):
+        if isinstance(lm, AutoGPTQLinear) or hasattr(lm, "padded_out_features"):
             if (lm.out_features, lm.in_features) != (cfg.vocab_size, cfg.emb_dim):
                 raise ValueError("lm_head shape does not match the config")
-            self.lm_w4 = W.from_autogptq(lm, dev)
+            self.lm_w4 = W.from_autogptq(lm, dev) if isinstance(lm, AutoGPTQLinear) else W.from_q4nx(lm, dev)
             self.lm_head = None
         else:
             self.lm_head = self.embed if lm is None else lm.to(dev, torch.bfloat16).contiguous()
@@ -197,20 +206,20 @@ class DecodeEngine:
         lw = self.layers[li]
         p = _lib.ptr
         _lib.check("t2b_qkv_norm_rope_kvwrite", L.t2b_qkv_norm_rope_kvwrite(
-            p(lw.qkv.qw), p(lw.qkv.meta), p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
+            p(lw.qkv.qw), p(lw.qkv.meta), lw.qkv.fmt, p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
             p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
         _lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
             p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), B, nq, nkv, hd,
             self.max_ctx, *self._ws("attn"), st))
         _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
-            p(lw.o_proj.qw), p(lw.o_proj.meta), p(self.attn), p(self.x), p(self.ssq_b),
+            p(lw.o_proj.qw), p(lw.o_proj.meta), lw.o_proj.fmt, p(self.attn), p(self.x), p(self.ssq_b),
             p(lw.post_attention_layernorm), p(self.xw), B, H, cfg.q_dim, *self._ws("o"), st))
         _lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
-            p(lw.gate_up.qw), p(lw.gate_up.meta), p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
+            p(lw.gate_up.qw), p(lw.gate_up.meta), lw.gate_up.fmt, p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
             p(self.ssq_a), B, H, cfg.hidden_dim, *self._ws("ug"), st))
         _lib.check("t2b_down_residual", L.t2b_down_residual(
-            p(lw.down.qw), p(lw.down.meta), p(self.h), p(self.x), p(self.ssq_a), p(self.next_norm_weight(li)),
+            p(lw.down.qw), p(lw.down.meta), lw.down.fmt, p(self.h), p(self.x), p(self.ssq_a), p(self.next_norm_weight(li)),
             p(self.xw), B, H, cfg.hidden_dim, *self._ws("down"), st))
 
     def enqueue_step(self) -> None:
@@ -240,9 +249,9 @@ class DecodeEngine:
                 p(self.logits) if self.keep_logits else None, *self._ws("lm"), st))
         else:
             _lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-                p(self.lm_w4.qw), p(self.lm_w4.meta), _lib.WFMT_T2B, p(self.xn), _lib.DTYPE[torch.bfloat16],
-                p(self.logits), _lib.DTYPE[torch.float32], B, cfg.vocab_size, cfg.emb_dim, cfg.group_size,
-                *self._ws("lm"), st))
+                p(self.lm_w4.qw), p(self.lm_w4.meta), self.lm_w4.fmt, p(self.xn), _lib.DTYPE[torch.bfloat16],
+                p(self.logits), _lib.DTYPE[torch.float32], B, cfg.vocab_size, cfg.emb_dim,
+                32 if self.lm_w4.fmt == W.WFMT_Q4NX else 128, *self._ws("lm"), st))
             _lib.check("t2b_argmax_rows", L.t2b_argmax_rows(
                 p(self.logits), _lib.DTYPE[torch.float32], B, cfg.vocab_size, cfg.vocab_size, p(self.next_tokens),
                 *self._ws("am"), st))
@@ -373,20 +382,20 @@ class DecodeEngine:
                                                       cfg.vocab_size, st))
         for li, lw in enumerate(self.layers):
             _lib.check("t2b_qkv_norm_rope_kvwrite_seq", L.t2b_qkv_norm_rope_kvwrite_seq(
-                p(lw.qkv.qw), p(lw.qkv.meta), p(xw), p(sa), cfg.rms_norm_eps, p(lw.q_norm), p(lw.k_norm),
+                p(lw.qkv.qw), p(lw.qkv.meta), lw.qkv.fmt, p(xw), p(sa), cfg.rms_norm_eps, p(lw.q_norm), p(lw.k_norm),
                 p(self.angles), p(pf["pos"]), p(pf["seq"]), B, p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]),
                 p(sb), M, H, nq, nkv, hd, self.max_ctx, *ws("qkv"), st))
             _lib.check("t2b_prefill_attention", L.t2b_prefill_attention(
                 p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]), p(pf["attn"]), B, n, c0, nq, nkv, hd,
                 self.max_ctx, st))
             _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
-                p(lw.o_proj.qw), p(lw.o_proj.meta), p(pf["attn"]), p(x), p(sb), p(lw.post_attention_layernorm),
+                p(lw.o_proj.qw), p(lw.o_proj.meta), lw.o_proj.fmt, p(pf["attn"]), p(x), p(sb), p(lw.post_attention_layernorm),
                 p(xw), M, H, cfg.q_dim, *ws("o"), st))
             _lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
-                p(lw.gate_up.qw), p(lw.gate_up.meta), p(xw), p(sb), cfg.rms_norm_eps, p(pf["h"]), p(sa), M, H,
+                p(lw.gate_up.qw), p(lw.gate_up.meta), lw.gate_up.fmt, p(xw), p(sb), cfg.rms_norm_eps, p(pf["h"]), p(sa), M, H,
                 cfg.hidden_dim, *ws("ug"), st))
             _lib.check("t2b_down_residual", L.t2b_down_residual(
-                p(lw.down.qw), p(lw.down.meta), p(pf["h"]), p(x), p(sa), p(self.next_norm_weight(li)), p(xw), M,
+                p(lw.down.qw), p(lw.down.meta), lw.down.fmt, p(pf["h"]), p(x), p(sa), p(self.next_norm_weight(li)), p(xw), M,
                 H, cfg.hidden_dim, *ws("down"), st))
 
     def prefill(self, prompts: torch.Tensor, chunk: int | None = None, stepwise: bool = False,

@@ -27,7 +27,8 @@ and bf16 norms, bf16 ``embed`` / ``final_norm``, and ``lm_head`` = ``None``
 * the fast Qwen3 artifact ``fast_qwen3_q4nx/`` (format
   ``fast_qwen3_q4nx_layer_v1``, ``fast_qwen3/fast_packed_format.py:178-300``):
   bf16 dense tensors and Q4NX group-32 linears (``Q4NXLinear``, bytes as
-  stored).  The decode engine does not run Q4NX weights yet.
+  stored), which the decode engine rearranges into its group-32 block
+  layout at load (``weights.from_q4nx``).
 
 The T2B meta word stores an fp16 scale, so a bf16 scale is accepted only when
 fp16 holds it exactly (every bf16 value of magnitude >= 2**-17 does) or when
@@ -477,8 +478,8 @@ class FastArtifact(PackedArtifact):
 
 def load_fast_qwen3_artifact(path: str | Path, hf_config: dict | None = None) -> tuple[QuantizedQwenConfig, dict]:
     """Load a ``fast_qwen3_q4nx`` artifact (or a model dir holding one): dense
-    tensors as bf16, the linears as ``Q4NXLinear``.  The decode engine does not
-    run Q4NX weights yet (its kernels take the group-128 T2B layout)."""
+    tensors as bf16, the linears as ``Q4NXLinear`` (run by the decode engine
+    in the group-32 variant of its block layout, ``WFMT_Q4NX``)."""
     fdir = find_fast_dir(path)
     if fdir is None:
         raise FileNotFoundError(f"no {FAST_FORMAT} artifact under {path}")

@@ -409,7 +409,7 @@ class QuantizedQwenLayer(nn.Module):
         ws = _ws(L.t2b_qkv_workspace_bytes(M, H, nq, nkv, hd), dev)
         if S == 1:
             pos = torch.full((B,), p0, dtype=torch.int32, device=dev)
-            _lib.call("t2b_qkv_norm_rope_kvwrite", p(f["qkv"].qw), p(f["qkv"].meta), p(xw), p(ssq_a), eps,
+            _lib.call("t2b_qkv_norm_rope_kvwrite", p(f["qkv"].qw), p(f["qkv"].meta), f["qkv"].fmt, p(xw), p(ssq_a), eps,
                       p(f["q_norm"]), p(f["k_norm"]), p(table), p(pos), p(q), p(cache.k), p(cache.v), p(ssq_b), B, H,
                       nq, nkv, hd, cache.max_ctx, p(ws[0]), ws[1], st)
             wa = _ws(L.t2b_decode_attention_workspace_bytes(B, nq, nkv, hd, cache.max_ctx), dev)
@@ -418,18 +418,18 @@ class QuantizedQwenLayer(nn.Module):
         else:
             pos = (p0 + torch.arange(S, device=dev, dtype=torch.int32)).repeat(B)
             seq = torch.arange(B, device=dev, dtype=torch.int32).repeat_interleave(S)
-            _lib.call("t2b_qkv_norm_rope_kvwrite_seq", p(f["qkv"].qw), p(f["qkv"].meta), p(xw), p(ssq_a), eps,
+            _lib.call("t2b_qkv_norm_rope_kvwrite_seq", p(f["qkv"].qw), p(f["qkv"].meta), f["qkv"].fmt, p(xw), p(ssq_a), eps,
                       p(f["q_norm"]), p(f["k_norm"]), p(table), p(pos), p(seq), B, p(q), p(cache.k), p(cache.v),
                       p(ssq_b), M, H, nq, nkv, hd, cache.max_ctx, p(ws[0]), ws[1], st)
             _lib.call("t2b_prefill_attention", p(q), p(cache.k), p(cache.v), p(attn), B, S, p0, nq, nkv, hd,
                       cache.max_ctx, st)
         wo = _ws(L.t2b_oproj_residual_workspace_bytes(M, H, nq * hd), dev)
-        _lib.call("t2b_oproj_residual", p(f["o"].qw), p(f["o"].meta), p(attn), p(xr), p(ssq_b),
+        _lib.call("t2b_oproj_residual", p(f["o"].qw), p(f["o"].meta), f["o"].fmt, p(attn), p(xr), p(ssq_b),
                   p(f["post_attention_layernorm"]), p(xw), M, H, nq * hd, p(wo[0]), wo[1], st)
         wu = _ws(L.t2b_upgate_swiglu_workspace_bytes(M, H, I), dev)
-        _lib.call("t2b_upgate_swiglu", p(f["gu"].qw), p(f["gu"].meta), p(xw), p(ssq_b), eps, p(h), p(ssq_a), M, H, I,
+        _lib.call("t2b_upgate_swiglu", p(f["gu"].qw), p(f["gu"].meta), f["gu"].fmt, p(xw), p(ssq_b), eps, p(h), p(ssq_a), M, H, I,
                   p(wu[0]), wu[1], st)
         wd = _ws(L.t2b_down_residual_workspace_bytes(M, H, I), dev)
-        _lib.call("t2b_down_residual", p(f["down"].qw), p(f["down"].meta), p(h), p(xr), p(ssq_a), None, None, M, H,
+        _lib.call("t2b_down_residual", p(f["down"].qw), p(f["down"].meta), f["down"].fmt, p(h), p(xr), p(ssq_a), None, None, M, H,
                   I, p(wd[0]), wd[1], st)
         return xr.view(B, S, H).to(self.compute_dtype)

@@ -214,7 +214,7 @@ class TPDecodeEngine:
         L, p, st = lib.lib(), lib.ptr, lib.stream()
         lw = self.layers[li]
         lib.check("t2b_qkv_norm_rope_kvwrite", L.t2b_qkv_norm_rope_kvwrite(
-            p(lw.qkv.qw), p(lw.qkv.meta), p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
+            p(lw.qkv.qw), p(lw.qkv.meta), lw.qkv.fmt, p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
             p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
         lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
@@ -225,7 +225,7 @@ class TPDecodeEngine:
             lib.DTYPE[self.partial_dtype], B, H, lc.q_dim, 128, *self._ws("o"), st))
         self._allreduce_residual(self.ssq_b, lw.post_attention_layernorm)
         lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
-            p(lw.gate_up.qw), p(lw.gate_up.meta), p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
+            p(lw.gate_up.qw), p(lw.gate_up.meta), lw.gate_up.fmt, p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
             p(self.ssq_a), B, H, lc.hidden_dim, *self._ws("ug"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
             p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[torch.bfloat16], p(self.y),
