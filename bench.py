@@ -334,7 +334,8 @@ def kernel_profile(eng, steps):
                 p(lw.q_norm), p(lw.k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[li]),
                 p(eng.v_cache[li]), p(eng.ssq_b), B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st))
             rec("decode_attention", lambda: L.t2b_decode_attention_after_kvwrite(
-                p(eng.q), p(eng.k_cache[li]), p(eng.v_cache[li]), p(eng.pos), p(eng.attn), B, nq, nkv, hd,
+                p(eng.q), p(eng.k_cache[li]), p(eng.v_cache[li]), p(eng.pos), p(eng.attn), _lib.DTYPE[_lib.ACT], B,
+                nq, nkv, hd,
                 eng.max_ctx, *eng._ws("attn"), st))
             rec("oproj_residual", lambda: L.t2b_oproj_residual(
                 p(lw.o_proj.qw), p(lw.o_proj.meta), lw.o_proj.fmt, p(eng.attn), p(eng.x), p(eng.ssq_b), p(lw.post_attention_layernorm), p(eng.xw), B, H, cfg.q_dim,
@@ -377,8 +378,8 @@ def kernel_profile_graph(eng, rounds=5):
             p(lw[i].k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.ssq_b),
             B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st)),
         "decode_attention": (nl, lambda st, i: L.t2b_decode_attention_after_kvwrite(
-            p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.pos), p(eng.attn), B, nq, nkv, hd, eng.max_ctx,
-            *eng._ws("attn"), st)),
+            p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.pos), p(eng.attn), _lib.DTYPE[_lib.ACT], B, nq, nkv,
+            hd, eng.max_ctx, *eng._ws("attn"), st)),
         "oproj_residual": (nl, lambda st, i: L.t2b_oproj_residual(
             p(lw[i].o_proj.qw), p(lw[i].o_proj.meta), lw[i].o_proj.fmt, p(eng.attn), p(eng.x), p(eng.ssq_b),
             p(lw[i].post_attention_layernorm), p(eng.xw), B, H, cfg.q_dim, *eng._ws("o"), st)),

@@ -38,6 +38,14 @@
  *   W[n,k] = (q[n,k] - zero[n,k/32]) * scale[n,k/32]   (fp32 on the CUDA-core
  *   path, as the reference; rounded once to bf16 on the tcgen05 paths).
  * The fused layer operations take wfmt T2B or Q4NX.
+ *
+ * Activations of the fused decode layer: the inputs of its linears (the
+ * split RMSNorm input xw, the attention output, the SwiGLU output h) are
+ * fp16, and the tensor-core paths dequantise the weights to fp16 for them
+ * (11-bit significands: 8x finer than bf16, which keeps a 28-layer decoder
+ * within the decoder-logit tolerance of the fp32 reference); values beyond
+ * fp16 range saturate at +-65504.  q and the KV cache are bf16, the residual
+ * stream fp32.  t2b_w4a16_gemm follows its x_dtype (bf16 or fp16 weights).
  */
 #ifndef T2B_H
 #define T2B_H
@@ -173,7 +181,7 @@ T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int
  *   q,k = RMSNorm_head(q|k; q_norm_w|k_norm_w, eps)    (model.py:252-253; skipped if NULL)
  *   q,k = interleaved RoPE(angles[pos[m]])             (model.py:184-196)
  *   q_out[m] = q ; k_cache/v_cache[m][kv][pos[m]] = k, v   (model.py:256-264)
- * The RMSNorm input arrives split: xw bf16 [M,H] = bf16(x * ln_w) (written by
+ * The RMSNorm input arrives split: xw fp16 [M,H] = fp16(x * ln_w) (written by
  * the producer of x: t2b_embed_rows / t2b_down_residual) and ssq fp32 [M] =
  * sum of x^2; the row scale is applied after the contraction.
  * angles fp32 [max_ctx, head_dim]; caches bf16 [M][n_kv][max_ctx][head_dim];
@@ -204,13 +212,14 @@ T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, i
 /*
  * GQA decode attention, one query token per row, over the bf16 cache:
  *   out[m, h] = softmax(q[m,h] . K[m, h/qpg, 0..pos[m]]^T / sqrt(hd)) . V  (model.py:266-279)
- * q bf16 [M][n_heads*hd]; caches bf16 [M][n_kv][max_ctx][hd]; out bf16 [M][n_heads*hd].
+ * q bf16 [M][n_heads*hd]; caches bf16 [M][n_kv][max_ctx][hd]; out [M][n_heads*hd] of out_dtype
+ * (T2B_DTYPE_BF16, or T2B_DTYPE_F16 for the fused layer's o_proj input).
  * Replaces LlamaChunkedAttention (src/torch2iron/operators/llama_chunked_attention/op.py:21-165).
  */
 T2B_API size_t t2b_decode_attention_workspace_bytes(int M, int n_heads, int n_kv, int head_dim, int max_ctx);
 T2B_API int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
-                         uint16_t* out, int M, int n_heads, int n_kv, int head_dim, int max_ctx, void* workspace,
-                         size_t workspace_bytes, void* stream);
+                         uint16_t* out, int out_dtype, int M, int n_heads, int n_kv, int head_dim, int max_ctx,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Same contract as t2b_decode_attention, for use directly after
@@ -220,23 +229,23 @@ T2B_API int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, con
  * preceding kernel may write only q and cache key pos[m] of each row.
  */
 T2B_API int t2b_decode_attention_after_kvwrite(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                               const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv,
-                                               int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
-                                               void* stream);
+                                               const int32_t* pos, uint16_t* out, int out_dtype, int M, int n_heads,
+                                               int n_kv, int head_dim, int max_ctx, void* workspace,
+                                               size_t workspace_bytes, void* stream);
 
 /*
  * Causal GQA attention of a prefill chunk: C tokens (positions p0..p0+C-1) of
  * each of B sequences, whose K/V rows are already in the cache:
  *   out[b*C + i, h] = softmax(q[b*C + i, h] . K[b, h/qpg, 0..p0+i]^T / sqrt(hd)) . V
- * q, out bf16 [B*C][n_heads*hd]; caches bf16 [B][n_kv][max_ctx][hd];
+ * q bf16, out (out_dtype: bf16 or fp16) [B*C][n_heads*hd]; caches bf16 [B][n_kv][max_ctx][hd];
  * p0 + C <= max_ctx; 64 % (n_heads / n_kv) == 0.  No workspace.
  * Replaces LlamaChunkedPrefillAttention
  * (src/torch2iron/operators/llama_chunked_prefill_attention/op.py:21-197) as
  * driven by prefill_forward_pass (src/models/quantized_qwen3/prefill_runtime.py:95-164).
  */
 T2B_API int t2b_prefill_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
-                                  int B, int C, int p0, int n_heads, int n_kv, int head_dim, int max_ctx,
-                                  void* stream);
+                                  int out_dtype, int B, int C, int p0, int n_heads, int n_kv, int head_dim,
+                                  int max_ctx, void* stream);
 
 /*
  * Attention over the reference's packet cache
@@ -251,7 +260,7 @@ T2B_API int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, uint
 
 /*
  * x_resid[M,H] += attn[M,K] . Wo^T ; ssq_out[m] += sum_n x_resid[m,n]^2 ;
- * xw_out = bf16(x_resid * next_norm_w) (both NULL to skip) -- the split
+ * xw_out = fp16(x_resid * next_norm_w) (both NULL to skip) -- the split
  * RMSNorm input of the following block.
  * ssq_out must be zero before the call (zeroed by the preceding block's ssq_clear).
  * Replaces W4A16KGroupGEMM(o) + ResidualAddRMSNorm (batch_decode_fused.py:485-498).
@@ -284,7 +293,7 @@ T2B_API int t2b_down_residual(const uint8_t* qw, const uint32_t* meta, int wfmt,
 
 /*
  * x_resid[m] = float(table[tokens[m]]) ; ssq_out[m] = sum x_resid[m]^2 ;
- * xw_out = bf16(x_resid * norm_w) (both NULL to skip).
+ * xw_out = fp16(x_resid * norm_w) (both NULL to skip).
  * Replaces the host-side embedding of qwen_npu.py:180-185 (model.py:469).
  */
 T2B_API int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* x_resid, float* ssq_out,
@@ -304,7 +313,7 @@ T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint
 /*
  * Tensor-parallel residual step: after the all-reduce of the row-parallel
  * o_proj / down partials y [M][H] (y_dtype bf16 or fp32), x_resid += y, ssq_out[m] =
- * sum_n x_resid[m,n]^2 (overwritten) and xw_out = bf16(x_resid * next_norm_w)
+ * sum_n x_resid[m,n]^2 (overwritten) and xw_out = fp16(x_resid * next_norm_w)
  * (both NULL to skip).  Replaces ResidualAddRMSNorm
  * (src/torch2iron/operators/residual_add_rms_norm/kernel.cc:70-93) where the
  * GEMM before it is split over GPUs (batch_decode_fused.py:485-498, 529-539).

@@ -38,7 +38,8 @@ def test_status_strings_and_host_side_errors():
     # host-side validation happens before any launch: no device needed
     assert lib.t2b_w4a16_gemm(None, None, 0, None, 0, None, 0, 1, 128, 256, 128, None, 0, None) == 6
     assert lib.t2b_w4a16_gemm(1, 1, 0, 1, 0, 1, 0, 1, 128, 256, 64, None, 0, None) == 1   # group 64
-    assert lib.t2b_decode_attention(16, 16, 16, 16, 16, 1, 16, 8, 128, 100, None, 0, None) == 1  # ctx % 8
+    assert lib.t2b_decode_attention(16, 16, 16, 16, 16, 0, 1, 16, 8, 128, 100, None, 0, None) == 1  # ctx % 8
+    assert lib.t2b_decode_attention(16, 16, 16, 16, 16, 2, 1, 16, 8, 128, 128, None, 0, None) == 6  # fp32 out
     assert lib.t2b_qkv_norm_rope_kvwrite(16, 16, 0, 16, 16, 1e-6, *([16] * 8), 1, 1024, 16, 8, 96, 64, None, 0,
                                          None) == 1   # head_dim 96
     assert lib.t2b_qkv_norm_rope_kvwrite(16, 16, 1, 16, 16, 1e-6, *([16] * 8), 1, 1024, 16, 8, 128, 64, None, 0,

@@ -26,13 +26,13 @@ SMALL = QuantizedQwenConfig(vocab_size=512, emb_dim=256, n_layers=1, n_heads=4, 
                             hidden_dim=512, rms_norm_eps=1e-6, rope_base=1e6)
 
 
-def attention_call(q, kc, vc, pos, n_heads, n_kv, hd, max_ctx, fn="t2b_decode_attention"):
+def attention_call(q, kc, vc, pos, n_heads, n_kv, hd, max_ctx, fn="t2b_decode_attention", out_dtype=torch.bfloat16):
     B = q.shape[0]
-    out = torch.empty_like(q)
+    out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
     L = _lib.lib()
     n = max(L.t2b_decode_attention_workspace_bytes(B, n_heads, n_kv, hd, max_ctx), 256)
     ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
-    _lib.call(fn, _lib.ptr(q), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pos), _lib.ptr(out), B,
+    _lib.call(fn, _lib.ptr(q), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pos), _lib.ptr(out), _lib.DTYPE[out_dtype], B,
               n_heads, n_kv, hd, max_ctx, _lib.ptr(ws), n, _lib.stream())
     torch.cuda.synchronize()
     return out
@@ -61,6 +61,8 @@ def test_decode_attention_vs_oracle(B, nq, nkv, hd, ctx, positions):
     early = attention_call(q.cuda(), kc.cuda(), vc.cuda(), pos.cuda(), nq, nkv, hd, ctx,
                            fn="t2b_decode_attention_after_kvwrite")
     assert torch.equal(out, early)   # same math; only the load order differs
+    half = attention_call(q.cuda(), kc.cuda(), vc.cuda(), pos.cuda(), nq, nkv, hd, ctx, out_dtype=torch.float16)
+    assert max_abs(half, out) <= 1e-2   # the fused layer's fp16 output: the same values, finer rounding
     qpg = nq // nkv
     for r in range(B):
         n = positions[r] + 1

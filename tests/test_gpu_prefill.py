@@ -50,23 +50,25 @@ def test_prefill_attention_vs_torch(B, C, p0, nq, nkv, hd, max_ctx):
     q = torch.randn(B * C, nq * hd, generator=g).to(torch.bfloat16)
     kc = torch.randn(B, nkv, max_ctx, hd, generator=g).to(torch.bfloat16)
     vc = torch.randn(B, nkv, max_ctx, hd, generator=g).to(torch.bfloat16)
-    out = torch.full((B * C, nq * hd), float("nan"), dtype=torch.bfloat16, device="cuda")
     qd, kd, vd = q.cuda(), kc.cuda(), vc.cuda()
-    _lib.call("t2b_prefill_attention", _lib.ptr(qd), _lib.ptr(kd), _lib.ptr(vd), _lib.ptr(out), B, C, p0, nq, nkv,
-              hd, max_ctx, _lib.stream())
-    torch.cuda.synchronize()
     ref = _ref_prefill_attention(q, kc, vc, C, p0, nq, nkv, hd)
-    assert not torch.isnan(out.float()).any()
-    assert max_abs(out, ref) <= 2e-2
+    for dt in (torch.bfloat16, torch.float16):      # reference-style bf16, and the fused layer's fp16
+        out = torch.full((B * C, nq * hd), float("nan"), dtype=dt, device="cuda")
+        _lib.call("t2b_prefill_attention", _lib.ptr(qd), _lib.ptr(kd), _lib.ptr(vd), _lib.ptr(out), _lib.DTYPE[dt], B,
+                  C, p0, nq, nkv, hd, max_ctx, _lib.stream())
+        torch.cuda.synchronize()
+        assert not torch.isnan(out.float()).any()
+        assert max_abs(out, ref) <= 2e-2
 
 
 def test_prefill_attention_rejects_bad_shapes():
     t = torch.zeros(64, dtype=torch.bfloat16, device="cuda")
     L = _lib.lib()
     p = _lib.ptr(t)
-    assert L.t2b_prefill_attention(p, p, p, p, 1, 8, 60, 4, 2, 64, 64, None) != 0     # p0 + C > max_ctx
-    assert L.t2b_prefill_attention(p, p, p, p, 1, 8, 0, 4, 2, 96, 64, None) != 0      # head_dim
-    assert L.t2b_prefill_attention(p, p, p, p, 1, 8, 0, 6, 4, 64, 64, None) != 0      # heads not a multiple
+    assert L.t2b_prefill_attention(p, p, p, p, 0, 1, 8, 60, 4, 2, 64, 64, None) != 0     # p0 + C > max_ctx
+    assert L.t2b_prefill_attention(p, p, p, p, 0, 1, 8, 0, 4, 2, 96, 64, None) != 0      # head_dim
+    assert L.t2b_prefill_attention(p, p, p, p, 0, 1, 8, 0, 6, 4, 64, 64, None) != 0      # heads not a multiple
+    assert L.t2b_prefill_attention(p, p, p, p, 2, 1, 8, 0, 4, 2, 64, 64, None) == 6      # fp32 output
 
 
 @pytest.mark.parametrize("chunk", [None, 16])

@@ -17,6 +17,7 @@ LIB_PATH = Path(os.environ.get("T2B_LIBRARY") or Path(__file__).resolve().parent
 
 T2B_OK = 0
 DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+ACT = torch.float16          # the fused decode layer's activations (linear inputs), see include/t2b.h
 WFMT_T2B = 0
 WFMT_QPARAM = 1
 WFMT_Q4NX = 2
@@ -40,10 +41,10 @@ SIGNATURES = {
     "t2b_qkv_workspace_bytes": (Z, [I, I, I, I, I]),
     "t2b_qkv_norm_rope_kvwrite": (I, [P, P, I, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_qkv_norm_rope_kvwrite_seq": (I, [P, P, I, P, P, F, P, P, P, P, P, I, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
-    "t2b_prefill_attention": (I, [P, P, P, P, I, I, I, I, I, I, I, P]),
+    "t2b_prefill_attention": (I, [P, P, P, P, I, I, I, I, I, I, I, I, P]),
     "t2b_decode_attention_workspace_bytes": (Z, [I, I, I, I, I]),
-    "t2b_decode_attention": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),
-    "t2b_decode_attention_after_kvwrite": (I, [P, P, P, P, P, I, I, I, I, I, P, Z, P]),
+    "t2b_decode_attention": (I, [P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_decode_attention_after_kvwrite": (I, [P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_packet_attention": (I, [P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_oproj_residual_workspace_bytes": (Z, [I, I, I]),
     "t2b_oproj_residual": (I, [P, P, I, P, P, P, P, P, I, I, I, P, Z, P]),

@@ -68,7 +68,8 @@ struct AttnParams {
   const int* pos;              // nullable: keys = pos[m] + 1 (clamped to [1, n_keys]), else n_keys
   int n_keys;                  // packet mode: keys per unit; cache mode: max_ctx
   int rows;
-  __nv_bfloat16* out;          // [rows][n_heads*hd]
+  __nv_bfloat16* out;          // [rows][n_heads*hd], bf16 or (out_f16) fp16
+  int out_f16;
   int n_heads, n_kv;
   float scale_log2;            // log2(e) / sqrt(hd)
   float* ws;                   // partial records [grid][2][qpg][hd + 2]
@@ -120,6 +121,15 @@ T2B_DEV int keys_of_row_global(const AttnParams& P, int m) {
   if (!P.pos) return P.n_keys;
   const int k = __ldcg(P.pos + m) + 1;
   return k < 1 ? 1 : (k > P.n_keys ? P.n_keys : k);
+}
+
+// Two adjacent outputs (element i even): bf16, or fp16 for the fused layer's o_proj input.
+T2B_DEV void store_out_pair(const AttnParams& P, size_t i, float a, float b) {
+  if (P.out_f16) {
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(P.out) + i) = f16x2_sat(a, b);
+  } else {
+    *reinterpret_cast<__nv_bfloat162*>(&P.out[i]) = __floats2bfloat162_rn(a, b);
+  }
 }
 
 template <class Aux>
@@ -488,7 +498,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         }
         const float inv = den > 0.f ? 1.f / den : 0.f;
         if (whole) {
-          *reinterpret_cast<__nv_bfloat162*>(&P.out[obase + hh * HD + d]) = __floats2bfloat162_rn(a0 * inv, a1 * inv);
+          store_out_pair(P, obase + hh * HD + d, a0 * inv, a1 * inv);
         } else {
           *reinterpret_cast<float2*>(&rec[hh * REC + d]) = make_float2(a0 * inv, a1 * inv);
           if (d == 0) *reinterpret_cast<float2*>(&rec[hh * REC + HD]) = make_float2(M, den);
@@ -580,8 +590,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
       const int e = tid + e2 * AT_THREADS;
       if (e < NPAIR) {
         const int hh = (2 * e) / HD, d = (2 * e) % HD;
-        *reinterpret_cast<__nv_bfloat162*>(&P.out[obase + hh * HD + d]) =
-            __floats2bfloat162_rn(acc[e2][0], acc[e2][1]);
+        store_out_pair(P, obase + hh * HD + d, acc[e2][0], acc[e2][1]);
       }
     }
   }
@@ -690,9 +699,10 @@ extern "C" size_t t2b_decode_attention_workspace_bytes(int M, int n_heads, int n
 }
 
 static int decode_attention_impl(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                 const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv, int head_dim,
-                                 int max_ctx, void* ws, size_t ws_bytes, void* stream, int kv_early) {
+                                 const int32_t* pos, uint16_t* out, int out_dtype, int M, int n_heads, int n_kv,
+                                 int head_dim, int max_ctx, void* ws, size_t ws_bytes, void* stream, int kv_early) {
   if (!q || !k_cache || !v_cache || !pos || !out) return T2B_ERR_ARG;
+  if (out_dtype != T2B_DTYPE_BF16 && out_dtype != T2B_DTYPE_F16) return T2B_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
        reinterpret_cast<uintptr_t>(q)) & 15)
     return T2B_ERR_ALIGN;
@@ -709,6 +719,7 @@ static int decode_attention_impl(const uint16_t* q, const uint16_t* k_cache, con
   P.pos = pos;
   P.n_keys = max_ctx;
   P.out = reinterpret_cast<__nv_bfloat16*>(out);
+  P.out_f16 = out_dtype == T2B_DTYPE_F16;
   P.n_heads = n_heads;
   P.n_kv = n_kv;
   P.kv_early = kv_early;
@@ -716,18 +727,18 @@ static int decode_attention_impl(const uint16_t* q, const uint16_t* k_cache, con
 }
 
 extern "C" int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                    const int32_t* pos, uint16_t* out, int M, int n_heads, int n_kv, int head_dim,
-                                    int max_ctx, void* ws, size_t ws_bytes, void* stream) {
-  return decode_attention_impl(q, k_cache, v_cache, pos, out, M, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes,
-                               stream, 0);
+                                    const int32_t* pos, uint16_t* out, int out_dtype, int M, int n_heads, int n_kv,
+                                    int head_dim, int max_ctx, void* ws, size_t ws_bytes, void* stream) {
+  return decode_attention_impl(q, k_cache, v_cache, pos, out, out_dtype, M, n_heads, n_kv, head_dim, max_ctx, ws,
+                               ws_bytes, stream, 0);
 }
 
 extern "C" int t2b_decode_attention_after_kvwrite(const uint16_t* q, const uint16_t* k_cache,
-                                                  const uint16_t* v_cache, const int32_t* pos, uint16_t* out, int M,
-                                                  int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
-                                                  size_t ws_bytes, void* stream) {
-  return decode_attention_impl(q, k_cache, v_cache, pos, out, M, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes,
-                               stream, 1);
+                                                  const uint16_t* v_cache, const int32_t* pos, uint16_t* out,
+                                                  int out_dtype, int M, int n_heads, int n_kv, int head_dim,
+                                                  int max_ctx, void* ws, size_t ws_bytes, void* stream) {
+  return decode_attention_impl(q, k_cache, v_cache, pos, out, out_dtype, M, n_heads, n_kv, head_dim, max_ctx, ws,
+                               ws_bytes, stream, 1);
 }
 
 extern "C" int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, uint16_t* out, int n_groups,

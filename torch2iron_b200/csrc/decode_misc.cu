@@ -76,7 +76,7 @@ int repack_autogptq(const int32_t* qweight, const int32_t* qzeros, const uint16_
 // ---------------------------------------------------------------------------
 __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ tokens,
                                   float* __restrict__ x, float* __restrict__ ssq,
-                                  const __nv_bfloat16* __restrict__ norm_w, __nv_bfloat16* __restrict__ xw, int H,
+                                  const __nv_bfloat16* __restrict__ norm_w, __half* __restrict__ xw, int H,
                                   int vocab, int* err) {
   grid_dep_wait();
   grid_dep_launch();
@@ -90,7 +90,7 @@ __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, const
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     const float v = __bfloat162float(table[(size_t)tok * H + i]);
     x[(size_t)m * H + i] = v;
-    if (xw) xw[(size_t)m * H + i] = __float2bfloat16_rn(v * __bfloat162float(norm_w[i]));
+    if (xw) xw[(size_t)m * H + i] = __float2half_rn(v * __bfloat162float(norm_w[i]));   // bf16 table * bf16 weight: in range
     s += v * v;
   }
   __shared__ float red[32];
@@ -124,7 +124,7 @@ template <bool YBF16>
 __global__ void __launch_bounds__(256) residual_norm_input_kernel(const void* __restrict__ yv, float* __restrict__ x,
                                                                   float* __restrict__ ssq,
                                                                   const __nv_bfloat16* __restrict__ w,
-                                                                  __nv_bfloat16* __restrict__ xw, int H) {
+                                                                  __half* __restrict__ xw, int H) {
   grid_dep_wait();
   grid_dep_launch();
   const int m = blockIdx.x;
@@ -145,12 +145,10 @@ __global__ void __launch_bounds__(256) residual_norm_input_kernel(const void* __
     sq += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     if (xw) {
       const uint2 wr = *reinterpret_cast<const uint2*>(w + i);
-      const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x * __uint_as_float(wr.x << 16),
-                                                      v.y * __uint_as_float(wr.x & 0xffff0000u));
-      const __nv_bfloat162 hi = __floats2bfloat162_rn(v.z * __uint_as_float(wr.y << 16),
-                                                      v.w * __uint_as_float(wr.y & 0xffff0000u));
+      // fp16 next-norm input, saturating like the fused epilogues
       *reinterpret_cast<uint2*>(xw + o) =
-          make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+          make_uint2(f16x2_sat(v.x * __uint_as_float(wr.x << 16), v.y * __uint_as_float(wr.x & 0xffff0000u)),
+                     f16x2_sat(v.z * __uint_as_float(wr.y << 16), v.w * __uint_as_float(wr.y & 0xffff0000u)));
     }
   }
   sq = warp_sum(sq);
@@ -202,7 +200,7 @@ int residual_norm_input(const void* y, int y_dtype, float* x, float* ssq, const 
                         int H, cudaStream_t st) {
   if (M < 1 || H < 4 || H % 4) return T2B_ERR_SHAPE;
   const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(w);
-  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(xw);
+  __half* op = reinterpret_cast<__half*>(xw);
   if (y_dtype == T2B_DTYPE_BF16)
     return launch_pdl(residual_norm_input_kernel<true>, dim3(M), dim3(256), 0, st, y, x, ssq, wp, op, H);
   if (y_dtype == T2B_DTYPE_F32)
@@ -327,7 +325,7 @@ int embed_rows(const uint16_t* table, const int* tokens, float* x, float* ssq, c
   if (M < 1 || H < 1) return T2B_ERR_SHAPE;
   const __nv_bfloat16* t = reinterpret_cast<const __nv_bfloat16*>(table);
   const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
-  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(xw);
+  __half* o = reinterpret_cast<__half*>(xw);
   return launch_pdl(embed_rows_kernel, dim3(M), dim3(256), 0, st, t, tokens, x, ssq, w, o, H, vocab, err);
 }
 

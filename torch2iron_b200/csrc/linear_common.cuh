@@ -46,7 +46,7 @@ struct LinearParams {
   float* resid;           // EPI_RESIDUAL fp32 [M][y_ld]
   float* ssq_out;
   const __nv_bfloat16* next_w;  // EPI_RESIDUAL: next RMSNorm weight [N] (nullable)
-  __nv_bfloat16* xw_out;        // EPI_RESIDUAL: bf16(resid * next_w) [M][y_ld] (nullable)
+  __half* xw_out;               // EPI_RESIDUAL: fp16(resid * next_w) [M][y_ld] (nullable)
   float* ssq_clear;
   const __nv_bfloat16* qn_w;
   const __nv_bfloat16* kn_w;
@@ -66,6 +66,52 @@ T2B_DEV size_t meta_block_offset(int nt, int g, int G) { return ((size_t)nt * G 
 // Q4NX meta: 4 pieces x 128 rows per block, piece-major
 constexpr int Q4NX_META_WORDS = 4 * TILE_N;
 T2B_DEV size_t meta_q4nx_offset(int nt, int g, int G) { return ((size_t)nt * G + g) * Q4NX_META_WORDS; }
+// One 16-byte piece of a T2B (group-128) weight as 16 bf16x2 / fp16x2 words:
+// the mask-or builds the pair (k, k+1) as 128+q (bf16) or 1024+q (fp16)
+// exactly, the subtraction of the equally biased zero point is exact, and
+// the multiplication by the group scale rounds once.  z2 = biased zero, s2 =
+// scale (bf16: the fp16 scale rounded; fp16: exact).
+template <bool F16>
+T2B_DEV void dequant_piece_t2b(const uint4 v, uint32_t z2, uint32_t s2, uint32_t cols[16]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t m = (w[j] >> (4 * t)) & 0x000F000Fu;
+      if (F16) {
+        const uint32_t b = m | 0x64006400u;
+        const __half2 d = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&b), *reinterpret_cast<const __half2*>(&z2)),
+                                  *reinterpret_cast<const __half2*>(&s2));
+        cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d);
+      } else {
+        const uint32_t b = m | 0x43004300u;
+        const __nv_bfloat162 d = __hmul2(__hsub2(*reinterpret_cast<const __nv_bfloat162*>(&b),
+                                                 *reinterpret_cast<const __nv_bfloat162*>(&z2)),
+                                         *reinterpret_cast<const __nv_bfloat162*>(&s2));
+        cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d);
+      }
+    }
+}
+
+// (biased zero, scale) pairs of a T2B meta word for dequant_piece_t2b.
+template <bool F16>
+T2B_DEV void t2b_meta_pairs(uint32_t mw, uint32_t& z2, uint32_t& s2) {
+  const unsigned short sh = (unsigned short)(mw & 0xffffu);
+  const float z = (float)((mw >> 16) & 0x1fu);
+  if (F16) {
+    const __half zb = __float2half_rn(1024.f + z), sb = __ushort_as_half(sh);
+    const __half2 z = __halves2half2(zb, zb), s = __halves2half2(sb, sb);
+    z2 = *reinterpret_cast<const uint32_t*>(&z);
+    s2 = *reinterpret_cast<const uint32_t*>(&s);
+  } else {
+    const __nv_bfloat16 zb = __float2bfloat16_rn(128.f + z), sb = __float2bfloat16_rn(__half2float(__ushort_as_half(sh)));
+    const __nv_bfloat162 z = __halves2bfloat162(zb, zb), s = __halves2bfloat162(sb, sb);
+    z2 = *reinterpret_cast<const uint32_t*>(&z);
+    s2 = *reinterpret_cast<const uint32_t*>(&s);
+  }
+}
+
 // Meta words of one (tile, group) block in either format.
 T2B_DEV int meta_block_words(bool q4nx) { return q4nx ? Q4NX_META_WORDS : TILE_N; }
 
@@ -73,10 +119,11 @@ T2B_DEV float bf16_lo_f32(uint32_t w) { return __uint_as_float(w << 16); }
 T2B_DEV float bf16_hi_f32(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
 // One 16-byte piece (32 k of one row, T2B nibble order) of a Q4NX weight as
-// 16 bf16x2 words (k pairs in order): (q - zero) * scale in fp32, as the
-// reference computes it (q4nx_layout.py:132-146), rounded once to bf16.
+// 16 bf16x2 or fp16x2 words (k pairs in order): (q - zero) * scale in fp32, as
+// the reference computes it (q4nx_layout.py:132-146), rounded once.
 // 0x43000000 | q << 16 is the fp32 value 128 + q.
-T2B_DEV void dequant_piece_q4nx_bf16(const uint4 v, float s, float z, uint32_t cols[16]) {
+template <bool F16>
+T2B_DEV void dequant_piece_q4nx(const uint4 v, float s, float z, uint32_t cols[16]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j)
@@ -85,8 +132,14 @@ T2B_DEV void dequant_piece_q4nx_bf16(const uint4 v, float s, float z, uint32_t c
       const uint32_t m = (w[j] >> (4 * t)) & 0x000F000Fu;
       const float q0 = __uint_as_float(0x43000000u | (m << 16)) - 128.f;
       const float q1 = __uint_as_float(0x43000000u | (m & 0xffff0000u)) - 128.f;
-      const __nv_bfloat162 d = __floats2bfloat162_rn(__fmul_rn(__fsub_rn(q0, z), s), __fmul_rn(__fsub_rn(q1, z), s));
-      cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d);
+      const float d0 = __fmul_rn(__fsub_rn(q0, z), s), d1 = __fmul_rn(__fsub_rn(q1, z), s);
+      if (F16) {
+        const __half2 d = __floats2half2_rn(d0, d1);
+        cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d);
+      } else {
+        const __nv_bfloat162 d = __floats2bfloat162_rn(d0, d1);
+        cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d);
+      }
     }
 }
 
@@ -146,6 +199,7 @@ T2B_DEV float4 unpack_bf16x4(uint2 v) {
   return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
                      __uint_as_float(v.y & 0xffff0000u));
 }
+T2B_DEV uint2 pack_f16x4(float a, float b, float c, float d) { return make_uint2(f16x2_sat(a, b), f16x2_sat(c, d)); }
 
 template <int HD>
 T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile, int m0, int MB, const EpiCache& ec,
@@ -232,23 +286,23 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
         if (p.xw_out) {
           const float4 w = unpack_bf16x4(
               *reinterpret_cast<const uint2*>(ec.next_w ? ec.next_w + lr : p.next_w + row0 + lr));
-          *reinterpret_cast<uint2*>(p.xw_out + o) = pack_bf16x4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
+          *reinterpret_cast<uint2*>(p.xw_out + o) = pack_f16x4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
         }
       }
       sq = warp_sum(sq);
       if (lane == 0 && live) atomicAdd(p.ssq_out + m, sq);
     }
   } else if (EPI == EPI_SWIGLU) {
-    // tile = 64 gate rows then the matching 64 up rows (model.py:215-216)
-    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.y);
+    // tile = 64 gate rows then the matching 64 up rows (model.py:215-216); h is fp16
+    __half* h = reinterpret_cast<__half*>(p.y);
     for (int idx = t * 4; idx < MB * 64; idx += NT * 4) {
       const int b = idx >> 6, t = idx & 63, m = m0 + b;
       if (m < p.M) {
         const float4 g = *reinterpret_cast<const float4*>(tile_acc + b * TILE_N + t);
         const float4 u = *reinterpret_cast<const float4*>(tile_acc + b * TILE_N + 64 + t);
         *reinterpret_cast<uint2*>(&h[(size_t)m * p.y_ld + tile * 64 + t]) =
-            pack_bf16x4(g.x / (1.f + expf(-g.x)) * u.x, g.y / (1.f + expf(-g.y)) * u.y,
-                        g.z / (1.f + expf(-g.z)) * u.z, g.w / (1.f + expf(-g.w)) * u.w);
+            pack_f16x4(g.x / (1.f + expf(-g.x)) * u.x, g.y / (1.f + expf(-g.y)) * u.y,
+                       g.z / (1.f + expf(-g.z)) * u.z, g.w / (1.f + expf(-g.w)) * u.w);
       }
     }
   } else {  // EPI_QKV

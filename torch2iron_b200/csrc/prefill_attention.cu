@@ -38,7 +38,8 @@ struct PrefillParams {
   const __nv_bfloat16* q;  // [B*C][n_heads*HD], row b*C + i
   const __nv_bfloat16* k;  // [B][n_kv][max_ctx][HD]
   const __nv_bfloat16* v;
-  __nv_bfloat16* out;      // [B*C][n_heads*HD]
+  __nv_bfloat16* out;      // [B*C][n_heads*HD], bf16 or (out_f16) fp16
+  int out_f16;
   int C, p0, n_heads, n_kv, qpg, max_ctx;
   float scale_log2;        // log2(e) / sqrt(HD)
 };
@@ -212,13 +213,15 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const Pre
     uint32_t* dst = reinterpret_cast<uint32_t*>(P.out + (size_t)(b * P.C + tok_a) * q_ld +
                                                 (size_t)(g * qpg + ra % qpg) * HD + dc);
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) dst[j * 4] = pack_bf16(o[j][0] * ia, o[j][1] * ia);
+    for (int j = 0; j < HD / 8; ++j)
+      dst[j * 4] = P.out_f16 ? f16x2_sat(o[j][0] * ia, o[j][1] * ia) : pack_bf16(o[j][0] * ia, o[j][1] * ia);
   }
   if (tok_b < P.C) {
     uint32_t* dst = reinterpret_cast<uint32_t*>(P.out + (size_t)(b * P.C + tok_b) * q_ld +
                                                 (size_t)(g * qpg + rb % qpg) * HD + dc);
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) dst[j * 4] = pack_bf16(o[j][2] * ib, o[j][3] * ib);
+    for (int j = 0; j < HD / 8; ++j)
+      dst[j * 4] = P.out_f16 ? f16x2_sat(o[j][2] * ib, o[j][3] * ib) : pack_bf16(o[j][2] * ib, o[j][3] * ib);
   }
 }
 
@@ -227,9 +230,10 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attention_kernel(const Pre
 using namespace t2b;
 
 extern "C" int t2b_prefill_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                     uint16_t* out, int B, int C, int p0, int n_heads, int n_kv, int head_dim,
-                                     int max_ctx, void* stream) {
+                                     uint16_t* out, int out_dtype, int B, int C, int p0, int n_heads, int n_kv,
+                                     int head_dim, int max_ctx, void* stream) {
   if (!q || !k_cache || !v_cache || !out) return T2B_ERR_ARG;
+  if (out_dtype != T2B_DTYPE_BF16 && out_dtype != T2B_DTYPE_F16) return T2B_ERR_ARG;
   if (head_dim != 64 && head_dim != 128) return T2B_ERR_SHAPE;
   if (B < 1 || B > 65535 || C < 1 || p0 < 0 || n_kv < 1 || n_kv > 65535 || n_heads % n_kv) return T2B_ERR_SHAPE;
   const int qpg = n_heads / n_kv;
@@ -243,6 +247,7 @@ extern "C" int t2b_prefill_attention(const uint16_t* q, const uint16_t* k_cache,
   P.k = reinterpret_cast<const __nv_bfloat16*>(k_cache);
   P.v = reinterpret_cast<const __nv_bfloat16*>(v_cache);
   P.out = reinterpret_cast<__nv_bfloat16*>(out);
+  P.out_f16 = out_dtype == T2B_DTYPE_F16;
   P.C = C;
   P.p0 = p0;
   P.n_heads = n_heads;

@@ -26,6 +26,15 @@ T2B_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;
 // Number formats
 // ---------------------------------------------------------------------------
 T2B_DEV float bf16_bits_to_f32(uint32_t lo16) { return __uint_as_float(lo16 << 16); }
+
+// The fused layer's fp16 activations (norm inputs, SwiGLU output): a in the
+// low half, b in the high half, round to nearest, saturating at +-65504
+// instead of overflowing to infinity.
+T2B_DEV uint32_t f16x2_sat(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
+  return r;
+}
 T2B_DEV float bf16_to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
 T2B_DEV float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 

@@ -71,6 +71,10 @@ T2B_DEV uint64_t sdesc_sw128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
+// Same with fp16 A and B (a_format = b_format = 0).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
 
 __host__ __device__ constexpr uint32_t pow2_cols(uint32_t n) {
   uint32_t c = 32;

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(GV_THREADS) w4a16_gemv_kernel(const LinearPara
     const int b = idx / (CH * 256), kk = idx - b * (CH * 256);
     const int m = m0 + b;
     float v = 0.f;
-    if (m < p.M) v = load_act(p.x, PRO == PRO_ACT ? p.x_dtype : (int)X_BF16, (size_t)m * p.x_ld + k0 + kk);
+    if (m < p.M) v = load_act(p.x, p.x_dtype, (size_t)m * p.x_ld + k0 + kk);
     xs[b * S::XS_LD + kk + (kk >> 5) * 4] = v;
   }
   maybe_clear_ssq(p, tile == 0 && split == 0 && mblk == 0, threadIdx.x, GV_THREADS);
@@ -379,13 +379,15 @@ int prefill_min_m();
 int prefill_launch(LinearParams& p, int pro, int epi, cudaStream_t st);
 
 static bool tiled_wfmt(int wfmt) { return wfmt == T2B_WFMT_T2B || wfmt == T2B_WFMT_Q4NX; }
+// 16-bit activations: the tensor-core paths dequantise the weights to the same type
+static bool half_act(int x_dtype) { return x_dtype == T2B_DTYPE_BF16 || x_dtype == T2B_DTYPE_F16; }
 
 static bool use_prefill(int M, int wfmt, int x_dtype) {
-  return tiled_wfmt(wfmt) && x_dtype == T2B_DTYPE_BF16 && M >= prefill_min_m();
+  return tiled_wfmt(wfmt) && half_act(x_dtype) && M >= prefill_min_m();
 }
 
 static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {
-  return tiled_wfmt(wfmt) && x_dtype == T2B_DTYPE_BF16 && M >= tc_min_m() &&
+  return tiled_wfmt(wfmt) && half_act(x_dtype) && M >= tc_min_m() &&
          tc_supported(M, N, K, wfmt == T2B_WFMT_Q4NX);
 }
 
@@ -549,7 +551,7 @@ static int qkv_impl(const uint8_t* qw, const uint32_t* meta, int wfmt, const uin
   const int N = (n_heads + 2 * n_kv) * head_dim;
   LinearParams p = gemv_base(qw, meta, H / 2, M, N, H);
   p.x = xw;
-  p.x_dtype = T2B_DTYPE_BF16;
+  p.x_dtype = T2B_DTYPE_F16;   // the fused layer's activations are fp16
   p.x_ld = H;
   p.ssq = ssq;
   p.eps = eps;
@@ -609,13 +611,13 @@ extern "C" int t2b_oproj_residual(const uint8_t* qw, const uint32_t* meta, int w
   if (!al(x_resid, 16) || (xw_out && (!al(xw_out, 8) || !al(next_norm_w, 8)))) return T2B_ERR_ALIGN;
   LinearParams p = gemv_base(qw, meta, K / 2, M, H, K);
   p.x = attn;
-  p.x_dtype = T2B_DTYPE_BF16;
+  p.x_dtype = T2B_DTYPE_F16;   // the fused layer's activations are fp16
   p.x_ld = K;
   p.resid = x_resid;
   p.y_ld = H;
   p.ssq_out = ssq_out;
   p.next_w = reinterpret_cast<const __nv_bfloat16*>(next_norm_w);
-  p.xw_out = reinterpret_cast<__nv_bfloat16*>(xw_out);
+  p.xw_out = reinterpret_cast<__half*>(xw_out);
   return linear_launch(p, PRO_ACT, EPI_RESIDUAL, wfmt, ws, ws_bytes, S_(stream));
 }
 
@@ -632,7 +634,7 @@ extern "C" int t2b_upgate_swiglu(const uint8_t* qw, const uint32_t* meta, int wf
   if (!al(qw, 16) || !al(xw, 16) || !al(h_out, 8)) return T2B_ERR_ALIGN;
   LinearParams p = gemv_base(qw, meta, H / 2, M, 2 * I, H);
   p.x = xw;
-  p.x_dtype = T2B_DTYPE_BF16;
+  p.x_dtype = T2B_DTYPE_F16;   // the fused layer's activations are fp16
   p.x_ld = H;
   p.ssq = ssq;
   p.eps = eps;

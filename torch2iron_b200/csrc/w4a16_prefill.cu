@@ -261,6 +261,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
     //      (column c = k 2c, 2c+1) ----
     const int q4 = warp & 3, h = warp >> 2;
     const int r = q4 * 32 + lane;
+    const bool f16 = p.x_dtype == T2B_DTYPE_F16;
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     long long w_wait = 0, a_wait = 0;
     (void)w_wait;
@@ -294,31 +295,21 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
         *abort_flag = 1;
         break;
       }
-      const __nv_bfloat16 sb = __float2bfloat16_rn(__half2float(__ushort_as_half((unsigned short)(mw & 0xffffu))));
-      const __nv_bfloat16 zb = __float2bfloat16_rn(128.f + (float)((mw >> 16) & 0x1fu));
-      const __nv_bfloat162 s2 = __halves2bfloat162(sb, sb);
-      const __nv_bfloat162 z2 = __halves2bfloat162(zb, zb);
+      uint32_t z2, s2;
+      if (f16) t2b_meta_pairs<true>(mw, z2, s2);
+      else t2b_meta_pairs<false>(mw, z2, s2);
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int pc = 2 * h + j;
-        if (p.q4nx) {
-          uint32_t cols[16];
-          dequant_piece_q4nx_bf16(v[j], bf16_lo_f32(mq[j]), bf16_hi_f32(mq[j]), cols);
-          tmem_st16(lane_base + PF_A0 + (uint32_t)(sa * 64 + pc * 16), cols);
-          continue;
-        }
-        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
         uint32_t cols[16];
-#pragma unroll
-        for (int jw = 0; jw < 4; ++jw)
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            // slot t holds k 2t, slot t+4 holds k 2t+1: the mask-or is the pair as 128+q
-            const uint32_t biased = ((w[jw] >> (4 * t)) & 0x000F000Fu) | 0x43004300u;
-            const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(&biased);
-            const __nv_bfloat162 d2 = __hmul2(__hsub2(q2, z2), s2);   // (q - z) exact, one rounding of * s
-            cols[4 * jw + t] = *reinterpret_cast<const uint32_t*>(&d2);
-          }
+        // weights in the activations' 16-bit type (T2B: slot t holds k 2t, slot t+4 k 2t+1)
+        if (p.q4nx) {
+          if (f16) dequant_piece_q4nx<true>(v[j], bf16_lo_f32(mq[j]), bf16_hi_f32(mq[j]), cols);
+          else dequant_piece_q4nx<false>(v[j], bf16_lo_f32(mq[j]), bf16_hi_f32(mq[j]), cols);
+        } else {
+          if (f16) dequant_piece_t2b<true>(v[j], z2, s2, cols);
+          else dequant_piece_t2b<false>(v[j], z2, s2, cols);
+        }
         tmem_st16(lane_base + PF_A0 + (uint32_t)(sa * 64 + pc * 16), cols);
       }
       tmem_st_wait();
@@ -379,7 +370,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
   } else if (warp == 13) {
     // ---- MMA issuer ----
     if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_bf16(TILE_N, PF_BM);
+      const uint32_t IDESC = p.x_dtype == T2B_DTYPE_F16 ? idesc_f16(TILE_N, PF_BM) : idesc_bf16(TILE_N, PF_BM);
       bool ok = true;
       long long wa = 0, wx = 0, we = 0;
       (void)wa;
@@ -515,7 +506,8 @@ static int pf_launch_t(LinearParams& p, cudaStream_t st) {
 }
 
 int prefill_launch(LinearParams& p, int pro, int epi, cudaStream_t st) {
-  if (p.x_dtype != T2B_DTYPE_BF16 || p.N % TILE_N || p.K % GROUP) return T2B_ERR_SHAPE;
+  if ((p.x_dtype != T2B_DTYPE_BF16 && p.x_dtype != T2B_DTYPE_F16) || p.N % TILE_N || p.K % GROUP)
+    return T2B_ERR_SHAPE;
   // bulk copies: weight blocks and meta 16-byte aligned; TMA base 16-byte aligned
   if ((reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.qw) | reinterpret_cast<uintptr_t>(p.meta)) & 15)
     return T2B_ERR_ALIGN;
@@ -526,7 +518,9 @@ int prefill_launch(LinearParams& p, int pro, int epi, cudaStream_t st) {
   cuuint32_t estr[2] = {1, 1};
   const EncodeTiledFn encode = encode_tiled();
   if (encode == nullptr) return T2B_ERR_LAUNCH;
-  if (encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p.x), dims, strides, box, estr,
+  const CUtensorMapDataType dt =
+      p.x_dtype == T2B_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (encode(&p.xmap, dt, 2, const_cast<void*>(p.x), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return T2B_ERR_ARG;

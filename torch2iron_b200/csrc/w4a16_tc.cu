@@ -237,7 +237,9 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   const uint32_t tbase = *tmem_slot;
   grid_dep_launch();  // this CTA holds its TMEM: dependents may start
   T2B_TRACE_MARK(1);
-  constexpr uint32_t IDESC = idesc_bf16(TILE_N, BP);
+  // weights are dequantised to the activations' 16-bit type (A and B of one MMA match)
+  const bool f16 = p.x_dtype == T2B_DTYPE_F16;
+  const uint32_t IDESC = f16 ? idesc_f16(TILE_N, BP) : idesc_bf16(TILE_N, BP);
 
   if (warp < 4) {
     // ---- producers: row r's nibbles -> bf16 (q - z) * s pairs -> TMEM lane r, A stage gl % NA ----
@@ -263,7 +265,8 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
           const uint4 v = *reinterpret_cast<const uint4*>(raw + gl * BLOCK_BYTES + pc * 2048 + r * 16);
           const uint32_t mw = rmeta[gl * Q4NX_META_WORDS + pc * TILE_N + r];
           uint32_t cols[16];
-          dequant_piece_q4nx_bf16(v, bf16_lo_f32(mw), bf16_hi_f32(mw), cols);
+          if (f16) dequant_piece_q4nx<true>(v, bf16_lo_f32(mw), bf16_hi_f32(mw), cols);
+          else dequant_piece_q4nx<false>(v, bf16_lo_f32(mw), bf16_hi_f32(mw), cols);
           tmem_st16(lane_base + a0 + stage * 64 + pc * 16, cols);
         }
         tmem_st_wait();
@@ -273,26 +276,16 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
         continue;
       }
       const uint32_t mw = rmeta[gl * TILE_N + r];
-      const __nv_bfloat16 sb = __float2bfloat16_rn(__half2float(__ushort_as_half((unsigned short)(mw & 0xffffu))));
-      const __nv_bfloat16 zb = __float2bfloat16_rn(128.f + (float)((mw >> 16) & 0x1fu));
-      const __nv_bfloat162 s2 = __halves2bfloat162(sb, sb);
-      const __nv_bfloat162 z2 = __halves2bfloat162(zb, zb);
+      uint32_t z2, s2;
+      if (f16) t2b_meta_pairs<true>(mw, z2, s2);
+      else t2b_meta_pairs<false>(mw, z2, s2);
 #pragma unroll
       for (int pc = 0; pc < 4; ++pc) {
         const uint4 v = *reinterpret_cast<const uint4*>(raw + gl * BLOCK_BYTES + pc * 2048 + r * 16);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t cols[16];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            // slot t holds k 2t, slot t+4 holds k 2t+1: the mask-or is the pair (2t, 2t+1) as 128+q
-            const uint32_t biased = ((w[j] >> (4 * t)) & 0x000F000Fu) | 0x43004300u;
-            const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(&biased);
-            const __nv_bfloat162 d2 = __hmul2(__hsub2(q2, z2), s2);   // (q - z) exact, one rounding of * s
-            cols[4 * j + t] = *reinterpret_cast<const uint32_t*>(&d2);
-          }
-        }
+        // slot t holds k 2t, slot t+4 holds k 2t+1: the mask-or is the pair (2t, 2t+1), biased
+        if (f16) dequant_piece_t2b<true>(v, z2, s2, cols);
+        else dequant_piece_t2b<false>(v, z2, s2, cols);
         tmem_st16(lane_base + a0 + stage * 64 + pc * 16, cols);
       }
       tmem_st_wait();
@@ -565,7 +558,9 @@ static int make_x_map(LinearParams& p, int BP) {
   cuuint32_t estr[2] = {1, 1};
   const EncodeTiledFn encode = encode_tiled();
   if (encode == nullptr) return T2B_ERR_LAUNCH;
-  CUresult r = encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p.x), dims,
+  const CUtensorMapDataType dt =
+      p.x_dtype == T2B_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = encode(&p.xmap, dt, 2, const_cast<void*>(p.x), dims,
                                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? T2B_OK : T2B_ERR_ARG;
@@ -574,7 +569,7 @@ static int make_x_map(LinearParams& p, int BP) {
 int tc_launch(LinearParams& p, int pro, int epi, void*, size_t, cudaStream_t st) {
   const TcPlan pl = tc_plan(p.M, p.N, p.K, p.q4nx != 0);
   if (!pl.ok) return T2B_ERR_SHAPE;
-  if (p.x_dtype != T2B_DTYPE_BF16) return T2B_ERR_ARG;
+  if (p.x_dtype != T2B_DTYPE_BF16 && p.x_dtype != T2B_DTYPE_F16) return T2B_ERR_ARG;
   const int mx = make_x_map(p, pl.BP);
   if (mx != T2B_OK) return mx;
   p.kslice = pl.S * GROUP;

@@ -126,12 +126,13 @@ class DecodeEngine:
         B, H, hd = batch, cfg.emb_dim, cfg.head_dim
         f32, bf = torch.float32, torch.bfloat16
         self.x = torch.zeros(B, H, dtype=f32, device=dev)
-        self.xw = torch.zeros(B, H, dtype=bf, device=dev)        # bf16(x * next norm weight)
+        act = _lib.ACT                                            # fp16 linear inputs (t2b.h)
+        self.xw = torch.zeros(B, H, dtype=act, device=dev)       # fp16(x * next norm weight)
         self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
         self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
         self.q = torch.zeros(B, cfg.q_dim, dtype=bf, device=dev)
-        self.attn = torch.zeros(B, cfg.q_dim, dtype=bf, device=dev)
-        self.h = torch.zeros(B, cfg.hidden_dim, dtype=bf, device=dev)
+        self.attn = torch.zeros(B, cfg.q_dim, dtype=act, device=dev)
+        self.h = torch.zeros(B, cfg.hidden_dim, dtype=act, device=dev)
         self.xn = torch.zeros(B, H, dtype=bf, device=dev)
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=f32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -210,8 +211,8 @@ class DecodeEngine:
             p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
         _lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
-            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), B, nq, nkv, hd,
-            self.max_ctx, *self._ws("attn"), st))
+            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), _lib.DTYPE[_lib.ACT], B,
+            nq, nkv, hd, self.max_ctx, *self._ws("attn"), st))
         _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
             p(lw.o_proj.qw), p(lw.o_proj.meta), lw.o_proj.fmt, p(self.attn), p(self.x), p(self.ssq_b),
             p(lw.post_attention_layernorm), p(self.xw), B, H, cfg.q_dim, *self._ws("o"), st))
@@ -260,7 +261,7 @@ class DecodeEngine:
         """Load a residual-stream state (fp32 [B, H]) and its split norm input for layer 0."""
         self.x.copy_(x.to(self.device, torch.float32))
         self.ssq_a.copy_((self.x.double() ** 2).sum(-1).float())
-        self.xw.copy_((self.x * self.layers[0].input_layernorm.float()).to(torch.bfloat16))
+        self.xw.copy_((self.x * self.layers[0].input_layernorm.float()).to(_lib.ACT))
 
     def kernels_per_step(self) -> int:
         """Launches of this library's kernels per step (embed, 5 per layer, final norm, lm_head + argmax)."""
@@ -351,11 +352,11 @@ class DecodeEngine:
                  "ug": L.t2b_upgate_swiglu_workspace_bytes(rows, H, cfg.hidden_dim),
                  "down": L.t2b_down_residual_workspace_bytes(rows, H, cfg.hidden_dim)}
         pf = {"rows": rows,
-              "x": torch.zeros(rows, H, dtype=f32, device=dev), "xw": torch.zeros(rows, H, dtype=bf, device=dev),
+              "x": torch.zeros(rows, H, dtype=f32, device=dev), "xw": torch.zeros(rows, H, dtype=_lib.ACT, device=dev),
               "ssq_a": torch.zeros(rows, dtype=f32, device=dev), "ssq_b": torch.zeros(rows, dtype=f32, device=dev),
               "q": torch.zeros(rows, cfg.q_dim, dtype=bf, device=dev),
-              "attn": torch.zeros(rows, cfg.q_dim, dtype=bf, device=dev),
-              "h": torch.zeros(rows, cfg.hidden_dim, dtype=bf, device=dev),
+              "attn": torch.zeros(rows, cfg.q_dim, dtype=_lib.ACT, device=dev),
+              "h": torch.zeros(rows, cfg.hidden_dim, dtype=_lib.ACT, device=dev),
               "tokens": torch.zeros(rows, dtype=i32, device=dev), "pos": torch.zeros(rows, dtype=i32, device=dev),
               "seq": torch.zeros(rows, dtype=i32, device=dev),
               "ws": {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256))
@@ -386,7 +387,8 @@ class DecodeEngine:
                 p(self.angles), p(pf["pos"]), p(pf["seq"]), B, p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]),
                 p(sb), M, H, nq, nkv, hd, self.max_ctx, *ws("qkv"), st))
             _lib.check("t2b_prefill_attention", L.t2b_prefill_attention(
-                p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]), p(pf["attn"]), B, n, c0, nq, nkv, hd,
+                p(pf["q"]), p(self.k_cache[li]), p(self.v_cache[li]), p(pf["attn"]), _lib.DTYPE[_lib.ACT], B, n, c0,
+                nq, nkv, hd,
                 self.max_ctx, st))
             _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
                 p(lw.o_proj.qw), p(lw.o_proj.meta), lw.o_proj.fmt, p(pf["attn"]), p(x), p(sb), p(lw.post_attention_layernorm),

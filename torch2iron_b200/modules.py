@@ -398,10 +398,11 @@ class QuantizedQwenLayer(nn.Module):
         xin = xin.contiguous()
         xr = torch.zeros(M, H, dtype=f32, device=dev)
         ssq_a, ssq_b = torch.zeros(M, dtype=f32, device=dev), torch.zeros(M, dtype=f32, device=dev)
-        xw = torch.empty(M, H, dtype=bf, device=dev)
+        act = _lib.ACT                                  # fp16 linear inputs (t2b.h)
+        xw = torch.empty(M, H, dtype=act, device=dev)
         q = torch.empty(M, nq * hd, dtype=bf, device=dev)
-        attn = torch.empty(M, nq * hd, dtype=bf, device=dev)
-        h = torch.empty(M, I, dtype=bf, device=dev)
+        attn = torch.empty(M, nq * hd, dtype=act, device=dev)
+        h = torch.empty(M, I, dtype=act, device=dev)
         eps = float(c.rms_norm_eps)
         # x -> residual stream + split norm input (bf16(x * ln1), sum of squares)
         _lib.call("t2b_residual_norm_input", p(xin), _lib.DTYPE[xin.dtype], p(xr), p(ssq_a), p(f["input_layernorm"]),
@@ -413,7 +414,8 @@ class QuantizedQwenLayer(nn.Module):
                       p(f["q_norm"]), p(f["k_norm"]), p(table), p(pos), p(q), p(cache.k), p(cache.v), p(ssq_b), B, H,
                       nq, nkv, hd, cache.max_ctx, p(ws[0]), ws[1], st)
             wa = _ws(L.t2b_decode_attention_workspace_bytes(B, nq, nkv, hd, cache.max_ctx), dev)
-            _lib.call("t2b_decode_attention_after_kvwrite", p(q), p(cache.k), p(cache.v), p(pos), p(attn), B, nq, nkv,
+            _lib.call("t2b_decode_attention_after_kvwrite", p(q), p(cache.k), p(cache.v), p(pos), p(attn),
+                      _lib.DTYPE[act], B, nq, nkv,
                       hd, cache.max_ctx, p(wa[0]), wa[1], st)
         else:
             pos = (p0 + torch.arange(S, device=dev, dtype=torch.int32)).repeat(B)
@@ -421,7 +423,8 @@ class QuantizedQwenLayer(nn.Module):
             _lib.call("t2b_qkv_norm_rope_kvwrite_seq", p(f["qkv"].qw), p(f["qkv"].meta), f["qkv"].fmt, p(xw), p(ssq_a), eps,
                       p(f["q_norm"]), p(f["k_norm"]), p(table), p(pos), p(seq), B, p(q), p(cache.k), p(cache.v),
                       p(ssq_b), M, H, nq, nkv, hd, cache.max_ctx, p(ws[0]), ws[1], st)
-            _lib.call("t2b_prefill_attention", p(q), p(cache.k), p(cache.v), p(attn), B, S, p0, nq, nkv, hd,
+            _lib.call("t2b_prefill_attention", p(q), p(cache.k), p(cache.v), p(attn), _lib.DTYPE[act], B, S, p0, nq,
+                      nkv, hd,
                       cache.max_ctx, st)
         wo = _ws(L.t2b_oproj_residual_workspace_bytes(M, H, nq * hd), dev)
         _lib.call("t2b_oproj_residual", p(f["o"].qw), p(f["o"].meta), f["o"].fmt, p(attn), p(xr), p(ssq_b),

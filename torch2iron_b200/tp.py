@@ -159,12 +159,13 @@ class TPDecodeEngine:
         f32, bf = torch.float32, torch.bfloat16
         self.x = torch.zeros(B, H, dtype=f32, device=dev)
         self.y = torch.zeros(B, H, dtype=partial_dtype, device=dev)   # row-parallel partial, all-reduced in place
-        self.xw = torch.zeros(B, H, dtype=bf, device=dev)
+        act = _lib.ACT                                            # fp16 linear inputs (t2b.h)
+        self.xw = torch.zeros(B, H, dtype=act, device=dev)
         self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
         self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
         self.q = torch.zeros(B, lc.q_dim, dtype=bf, device=dev)
-        self.attn = torch.zeros(B, lc.q_dim, dtype=bf, device=dev)
-        self.h = torch.zeros(B, lc.hidden_dim, dtype=bf, device=dev)
+        self.attn = torch.zeros(B, lc.q_dim, dtype=act, device=dev)
+        self.h = torch.zeros(B, lc.hidden_dim, dtype=act, device=dev)
         self.xn = torch.zeros(B, H, dtype=bf, device=dev)
         self.local_max = torch.zeros(B, dtype=f32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -218,17 +219,17 @@ class TPDecodeEngine:
             p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
         lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
-            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), B, nq, nkv, hd,
-            self.max_ctx, *self._ws("attn"), st))
+            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), lib.DTYPE[lib.ACT], B,
+            nq, nkv, hd, self.max_ctx, *self._ws("attn"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-            p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[torch.bfloat16], p(self.y),
+            p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[lib.ACT], p(self.y),
             lib.DTYPE[self.partial_dtype], B, H, lc.q_dim, 128, *self._ws("o"), st))
         self._allreduce_residual(self.ssq_b, lw.post_attention_layernorm)
         lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
             p(lw.gate_up.qw), p(lw.gate_up.meta), lw.gate_up.fmt, p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
             p(self.ssq_a), B, H, lc.hidden_dim, *self._ws("ug"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-            p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[torch.bfloat16], p(self.y),
+            p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[lib.ACT], p(self.y),
             lib.DTYPE[self.partial_dtype], B, H, lc.hidden_dim, 128, *self._ws("down"), st))
         self._allreduce_residual(self.ssq_a, self.next_norm_weight(li))
 
