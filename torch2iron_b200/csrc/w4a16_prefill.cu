@@ -157,7 +157,7 @@ T2B_DEV void pf_qkv_epilogue(const LinearParams& p, const float* tile_acc, int t
   }
 }
 
-// x += y; sum of squares for the next RMSNorm; bf16(x * w_next): R residual
+// x += y; sum of squares for the next RMSNorm; fp16(x * w_next): R residual
 // rows in flight per thread (a warp's 128 elements are one row of the tile).
 template <int R>
 T2B_DEV void pf_residual_epilogue(const LinearParams& p, const float* tile_acc, int tile, int m0, int MB, int t,
@@ -185,7 +185,7 @@ T2B_DEV void pf_residual_epilogue(const LinearParams& p, const float* tile_acc, 
       const float4 v = make_float4(rv[i].x + tv.x, rv[i].y + tv.y, rv[i].z + tv.z, rv[i].w + tv.w);
       *reinterpret_cast<float4*>(p.resid + o) = v;
       if (p.xw_out)
-        *reinterpret_cast<uint2*>(p.xw_out + o) = pack_bf16x4(v.x * wn.x, v.y * wn.y, v.z * wn.z, v.w * wn.w);
+        *reinterpret_cast<uint2*>(p.xw_out + o) = pack_f16x4(v.x * wn.x, v.y * wn.y, v.z * wn.z, v.w * wn.w);
       const float sq = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
       if (lane == 0) atomicAdd(p.ssq_out + m, sq);
     }
