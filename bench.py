@@ -331,10 +331,12 @@ def kernel_profile(eng, steps):
             H, hd, nq, nkv = cfg.emb_dim, cfg.head_dim, cfg.n_heads, cfg.n_kv_groups
             rec("qkv_norm_rope_kvwrite", lambda: L.t2b_qkv_norm_rope_kvwrite(
                 p(lw.qkv.qw), p(lw.qkv.meta), lw.qkv.fmt, p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps,
-                p(lw.q_norm), p(lw.k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[li]),
+                p(lw.q_norm), p(lw.k_norm), p(eng.angles), p(eng.pos), p(eng.q), _lib.DTYPE[eng.q.dtype],
+                p(eng.k_cache[li]),
                 p(eng.v_cache[li]), p(eng.ssq_b), B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st))
             rec("decode_attention", lambda: L.t2b_decode_attention_after_kvwrite(
-                p(eng.q), p(eng.k_cache[li]), p(eng.v_cache[li]), p(eng.pos), p(eng.attn), _lib.DTYPE[_lib.ACT], B,
+                p(eng.q), _lib.DTYPE[eng.q.dtype], p(eng.k_cache[li]), p(eng.v_cache[li]), p(eng.pos), p(eng.attn),
+                _lib.DTYPE[_lib.ACT], B,
                 nq, nkv, hd,
                 eng.max_ctx, *eng._ws("attn"), st))
             rec("oproj_residual", lambda: L.t2b_oproj_residual(
@@ -347,7 +349,7 @@ def kernel_profile(eng, steps):
                 p(lw.down.qw), p(lw.down.meta), lw.down.fmt, p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(li)), p(eng.xw), B, H, cfg.hidden_dim,
                 *eng._ws("down"), st))
         rec("lm_head_argmax", lambda: L.t2b_lm_head_argmax(
-            p(eng.xn), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
+            p(eng.xn), p(eng.xn_lo), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
             *eng._ws("lm"), st))
     torch.cuda.synchronize()
     for name, a, b in evs:
@@ -375,10 +377,12 @@ def kernel_profile_graph(eng, rounds=5):
     ops = {
         "qkv_norm_rope_kvwrite": (nl, lambda st, i: L.t2b_qkv_norm_rope_kvwrite(
             p(lw[i].qkv.qw), p(lw[i].qkv.meta), lw[i].qkv.fmt, p(eng.xw), p(eng.ssq_a), cfg.rms_norm_eps, p(lw[i].q_norm),
-            p(lw[i].k_norm), p(eng.angles), p(eng.pos), p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.ssq_b),
+            p(lw[i].k_norm), p(eng.angles), p(eng.pos), p(eng.q), _lib.DTYPE[eng.q.dtype], p(eng.k_cache[i]),
+            p(eng.v_cache[i]), p(eng.ssq_b),
             B, H, nq, nkv, hd, eng.max_ctx, *eng._ws("qkv"), st)),
         "decode_attention": (nl, lambda st, i: L.t2b_decode_attention_after_kvwrite(
-            p(eng.q), p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.pos), p(eng.attn), _lib.DTYPE[_lib.ACT], B, nq, nkv,
+            p(eng.q), _lib.DTYPE[eng.q.dtype], p(eng.k_cache[i]), p(eng.v_cache[i]), p(eng.pos), p(eng.attn),
+            _lib.DTYPE[_lib.ACT], B, nq, nkv,
             hd, eng.max_ctx, *eng._ws("attn"), st)),
         "oproj_residual": (nl, lambda st, i: L.t2b_oproj_residual(
             p(lw[i].o_proj.qw), p(lw[i].o_proj.meta), lw[i].o_proj.fmt, p(eng.attn), p(eng.x), p(eng.ssq_b),
@@ -392,7 +396,7 @@ def kernel_profile_graph(eng, rounds=5):
     }
     if eng.lm_w4 is None:
         ops["lm_head_argmax"] = (1, lambda st, i: L.t2b_lm_head_argmax(
-            p(eng.xn), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
+            p(eng.xn), p(eng.xn_lo), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
             *eng._ws("lm"), st))
     out = {}
     side = torch.cuda.Stream()

@@ -185,7 +185,9 @@ T2B_API int t2b_w4a16_gemm_noalloc(const void* weight, const uint32_t* meta, int
  * the producer of x: t2b_embed_rows / t2b_down_residual) and ssq fp32 [M] =
  * sum of x^2; the row scale is applied after the contraction.
  * angles fp32 [max_ctx, head_dim]; caches bf16 [M][n_kv][max_ctx][head_dim];
- * q_out bf16 [M][n_heads*head_dim].  ssq_clear (may be NULL): fp32 [M] zeroed.
+ * q_out [M][n_heads*head_dim] of q_dtype: T2B_DTYPE_F32 (the decode layer's
+ * input of t2b_decode_attention*) or T2B_DTYPE_BF16; the _seq form writes
+ * bf16 q (the prefill attention's input).  ssq_clear (may be NULL): fp32 [M] zeroed.
  * Replaces RMSNorm + W4A16KGroupGEMM(q) + W4A16PairedKGroupGEMM(k,v) +
  * 2x RMSNormRoPE + CopyPresentPacketKV (batch_decode_fused.py:426-474).
  */
@@ -204,22 +206,25 @@ T2B_API int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* met
                                           void* stream);
 T2B_API int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw, const float* ssq,
                                       float eps, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
-                                      const float* angles, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
-                                      uint16_t* v_cache, float* ssq_clear, int M, int H, int n_heads, int n_kv,
-                                      int head_dim, int max_ctx, void* workspace, size_t workspace_bytes,
-                                      void* stream);
+                                      const float* angles, const int32_t* pos, void* q_out, int q_dtype,
+                                      uint16_t* k_cache, uint16_t* v_cache, float* ssq_clear, int M, int H,
+                                      int n_heads, int n_kv, int head_dim, int max_ctx, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 /*
  * GQA decode attention, one query token per row, over the bf16 cache:
  *   out[m, h] = softmax(q[m,h] . K[m, h/qpg, 0..pos[m]]^T / sqrt(hd)) . V  (model.py:266-279)
- * q bf16 [M][n_heads*hd]; caches bf16 [M][n_kv][max_ctx][hd]; out [M][n_heads*hd] of out_dtype
- * (T2B_DTYPE_BF16, or T2B_DTYPE_F16 for the fused layer's o_proj input).
+ * q [M][n_heads*hd] of q_dtype (T2B_DTYPE_BF16, or T2B_DTYPE_F32: q enters
+ * the score MMAs as two bf16 terms, 16 significant bits); caches bf16
+ * [M][n_kv][max_ctx][hd]; out [M][n_heads*hd] of out_dtype (T2B_DTYPE_BF16,
+ * or T2B_DTYPE_F16 for the fused layer's o_proj input).  The probabilities
+ * enter the P.V MMAs as two bf16 terms as well.
  * Replaces LlamaChunkedAttention (src/torch2iron/operators/llama_chunked_attention/op.py:21-165).
  */
 T2B_API size_t t2b_decode_attention_workspace_bytes(int M, int n_heads, int n_kv, int head_dim, int max_ctx);
-T2B_API int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
-                         uint16_t* out, int out_dtype, int M, int n_heads, int n_kv, int head_dim, int max_ctx,
-                         void* workspace, size_t workspace_bytes, void* stream);
+T2B_API int t2b_decode_attention(const void* q, int q_dtype, const uint16_t* k_cache, const uint16_t* v_cache,
+                         const int32_t* pos, uint16_t* out, int out_dtype, int M, int n_heads, int n_kv, int head_dim,
+                         int max_ctx, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Same contract as t2b_decode_attention, for use directly after
@@ -228,10 +233,10 @@ T2B_API int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, con
  * newest key are read while that kernel is still running, so the stream's
  * preceding kernel may write only q and cache key pos[m] of each row.
  */
-T2B_API int t2b_decode_attention_after_kvwrite(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                                               const int32_t* pos, uint16_t* out, int out_dtype, int M, int n_heads,
-                                               int n_kv, int head_dim, int max_ctx, void* workspace,
-                                               size_t workspace_bytes, void* stream);
+T2B_API int t2b_decode_attention_after_kvwrite(const void* q, int q_dtype, const uint16_t* k_cache,
+                                               const uint16_t* v_cache, const int32_t* pos, uint16_t* out,
+                                               int out_dtype, int M, int n_heads, int n_kv, int head_dim, int max_ctx,
+                                               void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Causal GQA attention of a prefill chunk: C tokens (positions p0..p0+C-1) of
@@ -300,10 +305,12 @@ T2B_API int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* 
                            const uint16_t* norm_w, uint16_t* xw_out, int M, int H, int vocab, void* stream);
 
 /*
- * out[m] = bf16(RMSNorm(x_resid[m]; ssq, w, eps)) -- the final norm (model.py:409,477).
+ * out[m] = bf16(RMSNorm(x_resid[m]; ssq, w, eps)) -- the final norm (model.py:409,477);
+ * out_lo (may be NULL) = bf16 of what out does not hold: out + out_lo carries
+ * 16 significant bits (the lm_head's two-term input).
  */
 T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out,
-                              int M, int H, void* stream);
+                              uint16_t* out_lo, int M, int H, void* stream);
 
 /*
  * Greedy pick: idx[m] = argmax_v logits[m, v] (lowest index on ties), logits
@@ -326,14 +333,15 @@ T2B_API int t2b_residual_norm_input(const void* y, int y_dtype, float* x_resid, 
  * [V][H] table (tied embedding or untied head), fp32 accumulation; ties to
  * the lowest index (torch.argmax).  max_logit [M] (may be NULL) receives the
  * maximum, logits fp32 [M][V] (may be NULL) the full rows.  xn bf16 [M][H],
- * M <= 256, H % 64 == 0.  Workspace: t2b_lm_head_argmax_workspace_bytes(M),
+ * M <= 256, H % 64 == 0; xn_lo (may be NULL) its low bf16 terms
+ * (t2b_rms_norm_rows), multiplied in as a second MMA per k step.  Workspace: t2b_lm_head_argmax_workspace_bytes(M),
  * zeroed once (re-armed by the kernel).  Replaces the lm_head DenseLinear +
  * host argmax (model.py:409-420, 477; qwen_npu.py:321).
  */
 T2B_API size_t t2b_lm_head_argmax_workspace_bytes(int M);
-T2B_API int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* lm_head, int M, int H, int V, int32_t* idx,
-                               float* max_logit, float* logits, void* workspace, size_t workspace_bytes,
-                               void* stream);
+T2B_API int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* xn_lo, const uint16_t* lm_head, int M, int H,
+                               int V, int32_t* idx, float* max_logit, float* logits, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 T2B_API size_t t2b_argmax_workspace_bytes(int M, int V);
 T2B_API int t2b_argmax_rows(const void* logits, int dtype, int M, int V, int ld, int32_t* idx, void* workspace,

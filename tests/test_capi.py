@@ -38,11 +38,13 @@ def test_status_strings_and_host_side_errors():
     # host-side validation happens before any launch: no device needed
     assert lib.t2b_w4a16_gemm(None, None, 0, None, 0, None, 0, 1, 128, 256, 128, None, 0, None) == 6
     assert lib.t2b_w4a16_gemm(1, 1, 0, 1, 0, 1, 0, 1, 128, 256, 64, None, 0, None) == 1   # group 64
-    assert lib.t2b_decode_attention(16, 16, 16, 16, 16, 0, 1, 16, 8, 128, 100, None, 0, None) == 1  # ctx % 8
-    assert lib.t2b_decode_attention(16, 16, 16, 16, 16, 2, 1, 16, 8, 128, 128, None, 0, None) == 6  # fp32 out
-    assert lib.t2b_qkv_norm_rope_kvwrite(16, 16, 0, 16, 16, 1e-6, *([16] * 8), 1, 1024, 16, 8, 96, 64, None, 0,
+    assert lib.t2b_decode_attention(16, 0, 16, 16, 16, 16, 0, 1, 16, 8, 128, 100, None, 0, None) == 1  # ctx % 8
+    assert lib.t2b_decode_attention(16, 0, 16, 16, 16, 16, 2, 1, 16, 8, 128, 128, None, 0, None) == 6  # fp32 out
+    assert lib.t2b_decode_attention(16, 1, 16, 16, 16, 16, 0, 1, 16, 8, 128, 128, None, 0, None) == 6  # fp16 q
+    args = (1e-6, 16, 16, 16, 16, 16, 2, 16, 16, 16)       # eps, norms, angles, pos, q (fp32), caches, ssq_clear
+    assert lib.t2b_qkv_norm_rope_kvwrite(16, 16, 0, 16, 16, *args, 1, 1024, 16, 8, 96, 64, None, 0,
                                          None) == 1   # head_dim 96
-    assert lib.t2b_qkv_norm_rope_kvwrite(16, 16, 1, 16, 16, 1e-6, *([16] * 8), 1, 1024, 16, 8, 128, 64, None, 0,
+    assert lib.t2b_qkv_norm_rope_kvwrite(16, 16, 1, 16, 16, *args, 1, 1024, 16, 8, 128, 64, None, 0,
                                          None) == 6   # the fused ops take T2B or Q4NX weights, not qparam rows
     assert lib.t2b_w4a16_gemm(16, 16, 2, 16, 0, 16, 0, 1, 128, 256, 128, None, 0, None) == 1   # Q4NX is group 32
 

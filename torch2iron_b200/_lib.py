@@ -18,6 +18,7 @@ LIB_PATH = Path(os.environ.get("T2B_LIBRARY") or Path(__file__).resolve().parent
 T2B_OK = 0
 DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 ACT = torch.float16          # the fused decode layer's activations (linear inputs), see include/t2b.h
+QDT = torch.float32          # its q between the qkv kernel and the decode attention (two-term score MMAs)
 WFMT_T2B = 0
 WFMT_QPARAM = 1
 WFMT_Q4NX = 2
@@ -39,12 +40,12 @@ SIGNATURES = {
     "t2b_w4a16_gemm_noalloc_max_workspace": (Z, []),
     "t2b_w4a16_gemm_noalloc": (I, [P, P, I, P, I, P, I, I, I, I, I, P]),
     "t2b_qkv_workspace_bytes": (Z, [I, I, I, I, I]),
-    "t2b_qkv_norm_rope_kvwrite": (I, [P, P, I, P, P, F, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_qkv_norm_rope_kvwrite": (I, [P, P, I, P, P, F, P, P, P, P, P, I, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_qkv_norm_rope_kvwrite_seq": (I, [P, P, I, P, P, F, P, P, P, P, P, I, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_prefill_attention": (I, [P, P, P, P, I, I, I, I, I, I, I, I, P]),
     "t2b_decode_attention_workspace_bytes": (Z, [I, I, I, I, I]),
-    "t2b_decode_attention": (I, [P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
-    "t2b_decode_attention_after_kvwrite": (I, [P, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_decode_attention": (I, [P, I, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
+    "t2b_decode_attention_after_kvwrite": (I, [P, I, P, P, P, P, I, I, I, I, I, I, P, Z, P]),
     "t2b_packet_attention": (I, [P, P, P, I, I, I, I, I, P, Z, P]),
     "t2b_oproj_residual_workspace_bytes": (Z, [I, I, I]),
     "t2b_oproj_residual": (I, [P, P, I, P, P, P, P, P, I, I, I, P, Z, P]),
@@ -53,14 +54,14 @@ SIGNATURES = {
     "t2b_down_residual_workspace_bytes": (Z, [I, I, I]),
     "t2b_down_residual": (I, [P, P, I, P, P, P, P, P, I, I, I, P, Z, P]),
     "t2b_embed_rows": (I, [P, P, P, P, P, P, I, I, I, P]),
-    "t2b_rms_norm_rows": (I, [P, P, P, F, P, I, I, P]),
+    "t2b_rms_norm_rows": (I, [P, P, P, F, P, P, I, I, P]),
     "t2b_set_error_word": (I, [P]),
     "t2b_bind_error_word": (I, [P, P]),
     "t2b_error_word_for_stream": (I, [P, P]),
     "t2b_selftest_bounded_wait": (I, [P, I, P]),
     "t2b_residual_norm_input": (I, [P, I, P, P, P, P, I, I, P]),
     "t2b_lm_head_argmax_workspace_bytes": (Z, [I]),
-    "t2b_lm_head_argmax": (I, [P, P, I, I, I, P, P, P, P, Z, P]),
+    "t2b_lm_head_argmax": (I, [P, P, P, I, I, I, P, P, P, P, Z, P]),
     "t2b_argmax_workspace_bytes": (Z, [I, I]),
     "t2b_argmax_rows": (I, [P, I, I, I, I, P, P, Z, P]),
     "t2b_rms_norm_rope": (I, [P, P, P, P, I, I, I, F, I, P]),

@@ -61,7 +61,8 @@ struct AttnParams {
   CUtensorMap vmap_full;
   CUtensorMap kmap_sub;   // box: 64 dims x 16 keys
   CUtensorMap vmap_sub;
-  const __nv_bfloat16* q;      // [rows][n_heads*hd]
+  const void* q;               // [rows][n_heads*hd], bf16 or (q_f32) fp32
+  int q_f32;
   const __nv_bfloat16* mask0;  // nullable (packet mode): mask of (unit u, tile j) at mask0 + u*mask_unit + j*mask_tile
   long long mask_unit, mask_tile;
   int tile_y, unit_z, tile_z;  // TMA coordinates of (unit u, tile j): y = j*tile_y, z = u*unit_z + j*tile_z
@@ -92,7 +93,7 @@ struct AtGeom {
 template <int HD, int QPG>
 struct AttnAux {
   static constexpr int STAGES = AtGeom<HD>::STAGES;
-  __nv_bfloat16 qb[STAGES][QPG * HD];  // q heads of a unit, copied with the unit's first tile
+  float qb[STAGES][QPG * HD];          // q heads of a unit (fp32, or bf16 in the first half), copied with the unit's first tile
   __nv_bfloat16 msk[STAGES][AT_TILE];
   float ow[AT_WARPS][QPG][HD];         // per-warp (o, max, sum) at a unit's end
   float mw[AT_WARPS][QPG];
@@ -260,7 +261,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
     const int nk = tile_keys(r);
     const bool full = nk == AT_TILE;
     const uint32_t kv = full ? (uint32_t)G::KV_BYTES : (uint32_t)(G::HALVES * ((nk + AT_SUB - 1) / AT_SUB) * AT_SUB * 128);
-    const uint32_t qbytes = with_q(i, r) ? (uint32_t)(QPG * HD * 2) : 0u;
+    const uint32_t qbytes = with_q(i, r) ? (uint32_t)(QPG * HD * (P.q_f32 ? 4 : 2)) : 0u;
     const uint32_t mbytes = P.mask0 ? (uint32_t)(AT_TILE * 2) : 0u;
     mbar_arrive_expect_tx(&S.bar[i % STAGES], 2u * kv + qbytes + mbytes);
   };
@@ -287,8 +288,10 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
   };
   auto load_q = [&](int i, const TileRef& r) {
     if (with_q(i, r))
-      bulk_g2s(&S.qb[i % STAGES][0], P.q + (size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD,
-               (uint32_t)(QPG * HD * 2), &S.bar[i % STAGES]);
+      bulk_g2s(&S.qb[i % STAGES][0],
+               static_cast<const unsigned char*>(P.q) +
+                   ((size_t)r.m * P.n_heads * HD + (size_t)r.h * QPG * HD) * (P.q_f32 ? 4 : 2),
+               (uint32_t)(QPG * HD * (P.q_f32 ? 4 : 2)), &S.bar[i % STAGES]);
   };
   TileRef cur = locate(S, rows, t_lo);  // consumer position
   TileRef pro = cur;                    // producer position (thread 0)
@@ -324,7 +327,8 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
   const int kb = AT_SUB * warp;  // this warp's first key in a tile
   const int h0 = 2 * t4, h1 = h0 + 1;
   float o[NT16][4];
-  uint32_t qf[NT16][2];
+  uint32_t qf[NT16][2];   // q^T fragments: bf16(q) ...
+  uint32_t ql[NT16][2];   // ... and, for fp32 q, bf16(q - bf16(q)): the two terms carry 16 significant bits
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads h0, h1 (log2 domain)
   SplitUnit split[2];  // units of this range cut between CTAs: ticketed after the last tile
   int n_split = 0;
@@ -341,11 +345,26 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
     if (i == 0) T2B_TRACE_MARK(2);
     if (i == count - 1) T2B_TRACE_MARK(3);
     if (unit_begin) {  // new unit: B operand q^T (heads >= QPG are zero columns), fresh softmax state
-      const __nv_bfloat16* qs = &S.qb[st][0];
+      if (P.q_f32) {
+        const float* qs = &S.qb[st][0];
 #pragma unroll
-      for (int ks = 0; ks < NT16; ++ks) {
-        qf[ks][0] = g < QPG ? *reinterpret_cast<const uint32_t*>(qs + g * HD + ks * 16 + 2 * t4) : 0u;
-        qf[ks][1] = g < QPG ? *reinterpret_cast<const uint32_t*>(qs + g * HD + ks * 16 + 2 * t4 + 8) : 0u;
+        for (int ks = 0; ks < NT16; ++ks) {
+          float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+          if (g < QPG) {
+            a = *reinterpret_cast<const float2*>(qs + g * HD + ks * 16 + 2 * t4);
+            b = *reinterpret_cast<const float2*>(qs + g * HD + ks * 16 + 2 * t4 + 8);
+          }
+          split_bf16(a.x, a.y, qf[ks][0], ql[ks][0]);
+          split_bf16(b.x, b.y, qf[ks][1], ql[ks][1]);
+        }
+      } else {
+        const __nv_bfloat16* qs = reinterpret_cast<const __nv_bfloat16*>(&S.qb[st][0]);
+#pragma unroll
+        for (int ks = 0; ks < NT16; ++ks) {
+          qf[ks][0] = g < QPG ? *reinterpret_cast<const uint32_t*>(qs + g * HD + ks * 16 + 2 * t4) : 0u;
+          qf[ks][1] = g < QPG ? *reinterpret_cast<const uint32_t*>(qs + g * HD + ks * 16 + 2 * t4 + 8) : 0u;
+          ql[ks][0] = ql[ks][1] = 0u;
+        }
       }
 #pragma unroll
       for (int mt = 0; mt < NT16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
@@ -376,7 +395,12 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         const int ch = (ks & 3) * 2 + (lane >> 4);
         uint32_t a[4];
         ldsm_x4(a, kaddr + (ks >> 2) * G::HALF_BYTES + ((ch ^ (krow & 7)) << 4));
-        mma_bf16((ks & 1) ? sb : sa, a, qf[ks][0], qf[ks][1]);
+        if (P.q_f32) {   // the low terms of q in the second chain (warp-uniform branch)
+          mma_bf16(sa, a, qf[ks][0], qf[ks][1]);
+          mma_bf16(sb, a, ql[ks][0], ql[ks][1]);
+        } else {
+          mma_bf16((ks & 1) ? sb : sa, a, qf[ks][0], qf[ks][1]);
+        }
       }
       // online softmax over this warp's 16 keys (rows g, g+8; heads h0, h1)
       const int k0 = kb + g, k1 = k0 + 8;
@@ -413,9 +437,14 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         o[mt][2] *= c0;
         o[mt][3] *= c1;
       }
-      // P^T as the B operand: transpose the two 8x8 (key x head) blocks
-      const uint32_t b0 = movm_t(pack_bf16(p0, p1));
-      const uint32_t b1 = movm_t(pack_bf16(p2, p3));
+      // P^T as the B operand, split into bf16(P) + bf16(P - bf16(P)) so the
+      // probabilities enter O with 16 significant bits: transpose the 8x8
+      // (key x head) blocks of both terms
+      uint32_t ph0, pl0, ph1, pl1;
+      split_bf16(p0, p1, ph0, pl0);
+      split_bf16(p2, p3, ph1, pl1);
+      const uint32_t b0 = movm_t(ph0), b1 = movm_t(ph1);
+      const uint32_t bl0 = movm_t(pl0), bl1 = movm_t(pl1);
       // O^T += V_w^T . P^T
       const int vkey = kb + ((lane >> 4) << 3) + (lane & 7);
       const uint32_t vaddr = smem_u32(vst) + vkey * 128;
@@ -425,6 +454,7 @@ __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __gr
         uint32_t a[4];
         ldsm_x4_t(a, vaddr + (dch >> 3) * G::HALF_BYTES + (((dch & 7) ^ (vkey & 7)) << 4));
         mma_bf16(o[mt], a, b0, b1);
+        mma_bf16(o[mt], a, bl0, bl1);
       }
     }
     __syncthreads();  // stage consumed
@@ -698,11 +728,12 @@ extern "C" size_t t2b_decode_attention_workspace_bytes(int M, int n_heads, int n
   return attention_workspace_bytes(M, n_heads, n_kv, head_dim, max_ctx);
 }
 
-static int decode_attention_impl(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+static int decode_attention_impl(const void* q, int q_dtype, const uint16_t* k_cache, const uint16_t* v_cache,
                                  const int32_t* pos, uint16_t* out, int out_dtype, int M, int n_heads, int n_kv,
                                  int head_dim, int max_ctx, void* ws, size_t ws_bytes, void* stream, int kv_early) {
   if (!q || !k_cache || !v_cache || !pos || !out) return T2B_ERR_ARG;
   if (out_dtype != T2B_DTYPE_BF16 && out_dtype != T2B_DTYPE_F16) return T2B_ERR_ARG;
+  if (q_dtype != T2B_DTYPE_BF16 && q_dtype != T2B_DTYPE_F32) return T2B_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
        reinterpret_cast<uintptr_t>(q)) & 15)
     return T2B_ERR_ALIGN;
@@ -711,7 +742,8 @@ static int decode_attention_impl(const uint16_t* q, const uint16_t* k_cache, con
   const int mk = make_kv_maps(P, k_cache, v_cache, head_dim, max_ctx, (long long)M * n_kv, (long long)head_dim * 2,
                               (long long)max_ctx * head_dim * 2);
   if (mk != T2B_OK) return mk;
-  P.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  P.q = q;
+  P.q_f32 = q_dtype == T2B_DTYPE_F32;
   P.mask0 = nullptr;
   P.tile_y = AT_TILE;
   P.unit_z = 1;
@@ -726,19 +758,19 @@ static int decode_attention_impl(const uint16_t* q, const uint16_t* k_cache, con
   return attention_launch(P, M, head_dim, max_ctx, ws, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int t2b_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+extern "C" int t2b_decode_attention(const void* q, int q_dtype, const uint16_t* k_cache, const uint16_t* v_cache,
                                     const int32_t* pos, uint16_t* out, int out_dtype, int M, int n_heads, int n_kv,
                                     int head_dim, int max_ctx, void* ws, size_t ws_bytes, void* stream) {
-  return decode_attention_impl(q, k_cache, v_cache, pos, out, out_dtype, M, n_heads, n_kv, head_dim, max_ctx, ws,
-                               ws_bytes, stream, 0);
+  return decode_attention_impl(q, q_dtype, k_cache, v_cache, pos, out, out_dtype, M, n_heads, n_kv, head_dim,
+                               max_ctx, ws, ws_bytes, stream, 0);
 }
 
-extern "C" int t2b_decode_attention_after_kvwrite(const uint16_t* q, const uint16_t* k_cache,
+extern "C" int t2b_decode_attention_after_kvwrite(const void* q, int q_dtype, const uint16_t* k_cache,
                                                   const uint16_t* v_cache, const int32_t* pos, uint16_t* out,
                                                   int out_dtype, int M, int n_heads, int n_kv, int head_dim,
                                                   int max_ctx, void* ws, size_t ws_bytes, void* stream) {
-  return decode_attention_impl(q, k_cache, v_cache, pos, out, out_dtype, M, n_heads, n_kv, head_dim, max_ctx, ws,
-                               ws_bytes, stream, 1);
+  return decode_attention_impl(q, q_dtype, k_cache, v_cache, pos, out, out_dtype, M, n_heads, n_kv, head_dim,
+                               max_ctx, ws, ws_bytes, stream, 1);
 }
 
 extern "C" int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, uint16_t* out, int n_groups,
@@ -755,7 +787,8 @@ extern "C" int t2b_packet_attention(const uint16_t* q, const uint16_t* packet, u
   const int mk = make_kv_maps(P, base, base + (long long)chunk * head_dim, head_dim, chunk, n_groups * n_chunks,
                               (long long)head_dim * 2, chunk_el * 2);
   if (mk != T2B_OK) return mk;
-  P.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  P.q = q;
+  P.q_f32 = 0;
   P.mask0 = base + 2LL * chunk * head_dim;
   P.mask_unit = n_chunks * chunk_el;
   P.mask_tile = chunk_el;

@@ -104,15 +104,21 @@ __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, const
   }
 }
 
+// out = bf16(v) and, when out_lo is given, out_lo = bf16(v - out): the two
+// bf16 terms of the lm_head's split input.
 __global__ void rms_norm_rows_kernel(const float* __restrict__ x, const float* __restrict__ ssq,
                                      const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* __restrict__ out,
-                                     int H) {
+                                     __nv_bfloat16* __restrict__ out_lo, int H) {
   grid_dep_wait();
   grid_dep_launch();
   const int m = blockIdx.x;
   const float r = rsqrtf(ssq[m] / (float)H + eps);
-  for (int i = threadIdx.x; i < H; i += blockDim.x)
-    out[(size_t)m * H + i] = __float2bfloat16_rn((x[(size_t)m * H + i] * r) * __bfloat162float(w[i]));
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = (x[(size_t)m * H + i] * r) * __bfloat162float(w[i]);
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    out[(size_t)m * H + i] = hi;
+    if (out_lo) out_lo[(size_t)m * H + i] = __float2bfloat16_rn(v - __bfloat162float(hi));
+  }
 }
 
 // Residual add after a tensor-parallel all-reduce (the ResidualAddRMSNorm of
@@ -329,12 +335,13 @@ int embed_rows(const uint16_t* table, const int* tokens, float* x, float* ssq, c
   return launch_pdl(embed_rows_kernel, dim3(M), dim3(256), 0, st, t, tokens, x, ssq, w, o, H, vocab, err);
 }
 
-int rms_norm_rows(const float* x, const float* ssq, const uint16_t* w, float eps, uint16_t* out, int M, int H,
-                  cudaStream_t st) {
+int rms_norm_rows(const float* x, const float* ssq, const uint16_t* w, float eps, uint16_t* out, uint16_t* out_lo,
+                  int M, int H, cudaStream_t st) {
   if (M < 1 || H < 1) return T2B_ERR_SHAPE;
   const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(w);
   __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(out);
-  return launch_pdl(rms_norm_rows_kernel, dim3(M), dim3(256), 0, st, x, ssq, wp, eps, op, H);
+  __nv_bfloat16* ol = reinterpret_cast<__nv_bfloat16*>(out_lo);
+  return launch_pdl(rms_norm_rows_kernel, dim3(M), dim3(256), 0, st, x, ssq, wp, eps, op, ol, H);
 }
 
 // ---------------------------------------------------------------------------
@@ -532,9 +539,9 @@ extern "C" int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, floa
 }
 
 extern "C" int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out,
-                                 int M, int H, void* stream) {
+                                 uint16_t* out_lo, int M, int H, void* stream) {
   if (!x_resid || !ssq || !w || !out) return T2B_ERR_ARG;
-  return rms_norm_rows(x_resid, ssq, w, eps, out, M, H, S_(stream));
+  return rms_norm_rows(x_resid, ssq, w, eps, out, out_lo, M, H, S_(stream));
 }
 
 extern "C" int t2b_set_error_word(int32_t* word) {

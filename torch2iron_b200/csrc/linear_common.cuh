@@ -242,7 +242,10 @@ T2B_DEV void qkv_epilogue(const LinearParams& p, const float* tile_acc, int tile
         ec.angles ? ec.angles + (size_t)b * HD + d0 : p.angles + (size_t)(pos_ok ? pos : 0) * HD + d0);
     const uint2 o = pack_bf16x4(x0 * cs.x - x1 * cs.y, x1 * cs.x + x0 * cs.y, x2 * cs.z - x3 * cs.w,
                                 x3 * cs.z + x2 * cs.w);
-    if (is_q)
+    if (is_q && p.y_dtype == T2B_DTYPE_F32)   // fp32 q for the attention's two-term score MMAs
+      *reinterpret_cast<float4*>(static_cast<float*>(p.y) + (size_t)m * p.y_ld + head * HD + d0) =
+          make_float4(x0 * cs.x - x1 * cs.y, x1 * cs.x + x0 * cs.y, x2 * cs.z - x3 * cs.w, x3 * cs.z + x2 * cs.w);
+    else if (is_q)
       *reinterpret_cast<uint2*>(&q_out[(size_t)m * p.y_ld + head * HD + d0]) = o;
     else
       *reinterpret_cast<uint2*>(&p.k_cache[((cm * nkv + (head - nq)) * p.max_ctx + pos) * HD + d0]) = o;

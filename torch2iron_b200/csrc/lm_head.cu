@@ -5,6 +5,10 @@
 // Swap-AB on tcgen05: D[128 vocab rows, BP batch rows] = E_tile . xn^T, both
 // operands bf16 K-major in shared memory (2-D TMA boxes of 64 k with the
 // 128-byte swizzle = the UMMA canonical layout), fp32 accumulator in TMEM.
+// With SPLIT the normalised rows arrive as two bf16 terms (xn = hi + lo, 16
+// significant bits) and every k step issues one MMA per term into the same
+// accumulator, so the logits see xn almost exactly (the table is bf16 as
+// stored); the MMAs are far from the HBM bound either way.
 // Persistent CTAs (one per SM) walk the vocab tiles; the accumulator is
 // double-buffered so the drain of one tile overlaps the MMAs of the next.
 // Warp roles: 0-3 drain (thread = TMEM lane = vocab row), 4 TMA producer,
@@ -35,6 +39,7 @@ constexpr int LM_KB = 64;      // k per TMA box / pipeline stage
 struct LmParams {
   CUtensorMap emap;   // E [V][H] bf16, box 64 k x 128 rows
   CUtensorMap xmap;   // xn [M][H] bf16, box 64 k x BP rows (rows >= M read 0)
+  CUtensorMap xmap_lo;   // SPLIT: the low bf16 terms of xn, same shape
   int M, H, V, n_tiles;
   int32_t* idx;       // [M]
   float* vals;        // [M] maxima (nullable)
@@ -44,12 +49,15 @@ struct LmParams {
   int* err;
 };
 
-template <int BP>
+template <int BP, bool SPLIT = false>
 struct LmGeom {
   static constexpr int E_BYTES = LM_ROWS * LM_KB * 2;   // 16 KB
   static constexpr int X_BYTES = BP * LM_KB * 2;
-  static constexpr int STAGE = E_BYTES + X_BYTES;
-  static constexpr int STAGES = BP <= 64 ? 6 : (BP <= 128 ? 5 : 4);
+  static constexpr int STAGE = E_BYTES + X_BYTES * (SPLIT ? 2 : 1);
+  static constexpr int STAGES_FIT = (196 * 1024) / STAGE;
+  static constexpr int STAGES_PREF = BP <= 64 ? 6 : (BP <= 128 ? 5 : 4);
+  static constexpr int STAGES = STAGES_PREF < STAGES_FIT ? STAGES_PREF : STAGES_FIT;
+  static_assert(STAGES >= 2, "lm_head ring needs two stages");
   static constexpr int RING = STAGES * STAGE;
   static constexpr uint32_t TMEM_COLS = 2 * BP < 32 ? 32 : 2 * BP;   // two accumulators
   static constexpr int BEST = 4 * (BP < 32 ? 32 : BP) * 8;          // [4 warps][columns] keys
@@ -72,9 +80,9 @@ T2B_DEV unsigned long long shfl_xor_u64(unsigned long long x, int m) {
   return ((unsigned long long)hi << 32) | lo;
 }
 
-template <int BP>
+template <int BP, bool SPLIT>
 __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __grid_constant__ LmParams p) {
-  using G = LmGeom<BP>;
+  using G = LmGeom<BP, SPLIT>;
   constexpr int STG = G::STAGES;
   constexpr uint32_t IDESC = idesc_bf16(LM_ROWS, BP);
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
@@ -145,6 +153,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __g
             tma_load_2d(st, &p.emap, kc * LM_KB, t * LM_ROWS, &full[s]);
           }
           tma_load_2d(st + G::E_BYTES, &p.xmap, kc * LM_KB, 0, &full[s]);
+          if (SPLIT) tma_load_2d(st + G::E_BYTES + G::X_BYTES, &p.xmap_lo, kc * LM_KB, 0, &full[s]);
         }
     }
   } else if (warp == 5) {
@@ -168,9 +177,13 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __g
           tc_fence_after();
           const uint32_t ea = smem_u32(sm + s * G::STAGE), xa = ea + G::E_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < LM_KB / 16; ++ks)
+          for (int ks = 0; ks < LM_KB / 16; ++ks) {
             mma_ss(tbase + (uint32_t)(buf * BP), sdesc_sw128(ea + ks * 32), sdesc_sw128(xa + ks * 32), IDESC,
                    (kc > 0 || ks > 0) ? 1u : 0u);
+            if (SPLIT)
+              mma_ss(tbase + (uint32_t)(buf * BP), sdesc_sw128(ea + ks * 32),
+                     sdesc_sw128(xa + G::X_BYTES + ks * 32), IDESC, 1u);
+          }
           mma_commit(&empty[s]);
         }
         mma_commit(&acc_full[buf]);
@@ -280,10 +293,10 @@ static int lm_bp(int M) {
 
 size_t lm_head_workspace_bytes(int M) { return (((size_t)M * 8 + 255) & ~size_t(255)) + 256; }
 
-template <int BP>
+template <int BP, bool SPLIT>
 static int lm_launch_t(LmParams& p, cudaStream_t st) {
-  auto kern = lm_head_argmax_kernel<BP>;
-  const size_t smem = LmGeom<BP>::SMEM;
+  auto kern = lm_head_argmax_kernel<BP, SPLIT>;
+  const size_t smem = LmGeom<BP, SPLIT>::SMEM;
   if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -305,14 +318,15 @@ static int encode_2d(CUtensorMap* m, const void* base, int inner, int outer, int
   return r == CUDA_SUCCESS ? T2B_OK : T2B_ERR_ARG;
 }
 
-int lm_head_argmax(const uint16_t* xn, const uint16_t* lm, int M, int H, int V, int32_t* idx, float* vals,
-                   float* logits, void* ws, size_t ws_bytes, cudaStream_t st) {
+int lm_head_argmax(const uint16_t* xn, const uint16_t* xn_lo, const uint16_t* lm, int M, int H, int V, int32_t* idx,
+                   float* vals, float* logits, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (M < 1 || M > 256 || H < LM_KB || H % LM_KB || V < 1) return T2B_ERR_SHAPE;
   if (ws_bytes < lm_head_workspace_bytes(M) || !ws) return T2B_ERR_WORKSPACE;
   LmParams p{};
   const int bp = lm_bp(M);
   int r = encode_2d(&p.emap, lm, H, V, LM_ROWS);
   if (r == T2B_OK) r = encode_2d(&p.xmap, xn, H, M, bp);
+  if (r == T2B_OK && xn_lo) r = encode_2d(&p.xmap_lo, xn_lo, H, M, bp);
   if (r != T2B_OK) return r;
   p.M = M;
   p.H = H;
@@ -324,11 +338,18 @@ int lm_head_argmax(const uint16_t* xn, const uint16_t* lm, int M, int H, int V, 
   p.keys = reinterpret_cast<unsigned long long*>(ws);
   p.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * 8 + 255) & ~size_t(255)));
   p.err = error_word(st);
-  if (bp == 16) return lm_launch_t<16>(p, st);
-  if (bp == 32) return lm_launch_t<32>(p, st);
-  if (bp == 64) return lm_launch_t<64>(p, st);
-  if (bp == 128) return lm_launch_t<128>(p, st);
-  return lm_launch_t<256>(p, st);
+  if (xn_lo) {
+    if (bp == 16) return lm_launch_t<16, true>(p, st);
+    if (bp == 32) return lm_launch_t<32, true>(p, st);
+    if (bp == 64) return lm_launch_t<64, true>(p, st);
+    if (bp == 128) return lm_launch_t<128, true>(p, st);
+    return lm_launch_t<256, true>(p, st);
+  }
+  if (bp == 16) return lm_launch_t<16, false>(p, st);
+  if (bp == 32) return lm_launch_t<32, false>(p, st);
+  if (bp == 64) return lm_launch_t<64, false>(p, st);
+  if (bp == 128) return lm_launch_t<128, false>(p, st);
+  return lm_launch_t<256, false>(p, st);
 }
 
 }  // namespace t2b
@@ -340,10 +361,12 @@ extern "C" size_t t2b_lm_head_argmax_workspace_bytes(int M) {
   return lm_head_workspace_bytes(M);
 }
 
-extern "C" int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* lm_head, int M, int H, int V, int32_t* idx,
-                                  float* max_logit, float* logits, void* ws, size_t ws_bytes, void* stream) {
+extern "C" int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* xn_lo, const uint16_t* lm_head, int M, int H,
+                                  int V, int32_t* idx, float* max_logit, float* logits, void* ws, size_t ws_bytes,
+                                  void* stream) {
   if (!xn || !lm_head || !idx) return T2B_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(xn) | reinterpret_cast<uintptr_t>(lm_head)) & 15) return T2B_ERR_ALIGN;
-  return lm_head_argmax(xn, lm_head, M, H, V, idx, max_logit, logits, ws, ws_bytes,
+  if ((reinterpret_cast<uintptr_t>(xn) | reinterpret_cast<uintptr_t>(xn_lo) | reinterpret_cast<uintptr_t>(lm_head)) & 15)
+    return T2B_ERR_ALIGN;
+  return lm_head_argmax(xn, xn_lo, lm_head, M, H, V, idx, max_logit, logits, ws, ws_bytes,
                         reinterpret_cast<cudaStream_t>(stream));
 }

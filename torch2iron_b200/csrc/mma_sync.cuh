@@ -35,5 +35,12 @@ T2B_DEV uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
+// (a, b) as bf16 pairs hi = bf16(x) and lo = bf16(x - hi): hi + lo carries
+// 16 significant bits, so a bf16 MMA over both terms sees x almost exactly.
+T2B_DEV void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = pack_bf16(a - __low2float(h), b - __high2float(h));
+}
 
 }  // namespace t2b

@@ -534,14 +534,18 @@ extern "C" size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, i
   return linear_workspace_bytes(M, (n_heads + 2 * n_kv) * head_dim, H);
 }
 
-static int qkv_impl(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw, const float* ssq, float eps,
+static int qkv_impl(const uint8_t* qw, const uint32_t* meta, int wfmt, int q_dtype, const uint16_t* xw, const float* ssq,
+                    float eps,
                     const uint16_t* q_norm_w, const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
-                    const int32_t* row_seq, int n_seq, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
+                    const int32_t* row_seq, int n_seq, void* q_out, uint16_t* k_cache, uint16_t* v_cache,
                     float* ssq_clear, int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
                     size_t ws_bytes, void* stream) {
   if (head_dim != 64 && head_dim != 128) return T2B_ERR_SHAPE;
   if (n_kv < 1 || n_heads % n_kv || max_ctx < 1) return T2B_ERR_SHAPE;
   if (!tiled_wfmt(wfmt)) return T2B_ERR_ARG;
+  if (q_dtype != T2B_DTYPE_BF16 && q_dtype != T2B_DTYPE_F32) return T2B_ERR_ARG;
+  // fp32 q comes from the decode kernels' epilogue (rows <= 256, the attention's limit)
+  if (q_dtype == T2B_DTYPE_F32 && use_prefill(M, wfmt, T2B_DTYPE_F16)) return T2B_ERR_SHAPE;
   if (!qw || !meta || !xw || !ssq || !angles || !pos || !q_out || !k_cache || !v_cache) return T2B_ERR_ARG;
   if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return T2B_ERR_ARG;
   if (!al(qw, 16) || !al(xw, 16)) return T2B_ERR_ALIGN;
@@ -556,6 +560,7 @@ static int qkv_impl(const uint8_t* qw, const uint32_t* meta, int wfmt, const uin
   p.ssq = ssq;
   p.eps = eps;
   p.y = q_out;
+  p.y_dtype = q_dtype;
   p.y_ld = n_heads * head_dim;
   p.ssq_clear = ssq_clear;
   p.qn_w = reinterpret_cast<const __nv_bfloat16*>(q_norm_w);
@@ -576,10 +581,12 @@ static int qkv_impl(const uint8_t* qw, const uint32_t* meta, int wfmt, const uin
 extern "C" int t2b_qkv_norm_rope_kvwrite(const uint8_t* qw, const uint32_t* meta, int wfmt, const uint16_t* xw,
                                          const float* ssq, float eps, const uint16_t* q_norm_w,
                                          const uint16_t* k_norm_w, const float* angles, const int32_t* pos,
-                                         uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, float* ssq_clear,
+                                         void* q_out, int q_dtype, uint16_t* k_cache, uint16_t* v_cache,
+                                         float* ssq_clear,
                                          int M, int H, int n_heads, int n_kv, int head_dim, int max_ctx, void* ws,
                                          size_t ws_bytes, void* stream) {
-  return qkv_impl(qw, meta, wfmt, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, nullptr, M, q_out, k_cache, v_cache,
+  return qkv_impl(qw, meta, wfmt, q_dtype, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, nullptr, M, q_out, k_cache,
+                  v_cache,
                   ssq_clear, M, H, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes, stream);
 }
 
@@ -592,7 +599,8 @@ extern "C" int t2b_qkv_norm_rope_kvwrite_seq(const uint8_t* qw, const uint32_t* 
                                              size_t ws_bytes, void* stream) {
   if (!row_seq) return T2B_ERR_ARG;
   if (n_seq < 1) return T2B_ERR_SHAPE;
-  return qkv_impl(qw, meta, wfmt, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, row_seq, n_seq, q_out, k_cache, v_cache,
+  return qkv_impl(qw, meta, wfmt, T2B_DTYPE_BF16, xw, ssq, eps, q_norm_w, k_norm_w, angles, pos, row_seq, n_seq, q_out,
+                  k_cache, v_cache,
                   ssq_clear, M, H, n_heads, n_kv, head_dim, max_ctx, ws, ws_bytes, stream);
 }
 

@@ -130,10 +130,11 @@ class DecodeEngine:
         self.xw = torch.zeros(B, H, dtype=act, device=dev)       # fp16(x * next norm weight)
         self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
         self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
-        self.q = torch.zeros(B, cfg.q_dim, dtype=bf, device=dev)
+        self.q = torch.zeros(B, cfg.q_dim, dtype=_lib.QDT, device=dev)
         self.attn = torch.zeros(B, cfg.q_dim, dtype=act, device=dev)
         self.h = torch.zeros(B, cfg.hidden_dim, dtype=act, device=dev)
-        self.xn = torch.zeros(B, H, dtype=bf, device=dev)
+        self.xn = torch.zeros(B, H, dtype=bf, device=dev)        # final norm output, bf16 ...
+        self.xn_lo = torch.zeros(B, H, dtype=bf, device=dev)     # ... and its low bf16 terms (two-term lm_head)
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=f32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -208,10 +209,11 @@ class DecodeEngine:
         p = _lib.ptr
         _lib.check("t2b_qkv_norm_rope_kvwrite", L.t2b_qkv_norm_rope_kvwrite(
             p(lw.qkv.qw), p(lw.qkv.meta), lw.qkv.fmt, p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
-            p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
+            p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), _lib.DTYPE[_lib.QDT], p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
         _lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
-            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), _lib.DTYPE[_lib.ACT], B,
+            p(self.q), _lib.DTYPE[_lib.QDT], p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn),
+            _lib.DTYPE[_lib.ACT], B,
             nq, nkv, hd, self.max_ctx, *self._ws("attn"), st))
         _lib.check("t2b_oproj_residual", L.t2b_oproj_residual(
             p(lw.o_proj.qw), p(lw.o_proj.meta), lw.o_proj.fmt, p(self.attn), p(self.x), p(self.ssq_b),
@@ -242,11 +244,12 @@ class DecodeEngine:
         cfg, B = self.cfg, self.B
         L = _lib.lib()
         p = _lib.ptr
+        lo = self.xn_lo if self.lm_w4 is None else None
         _lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
-                                                            cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
+                                                            cfg.rms_norm_eps, p(self.xn), p(lo), B, cfg.emb_dim, st))
         if self.lm_w4 is None:
             _lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
-                p(self.xn), p(self.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(self.next_tokens), None,
+                p(self.xn), p(self.xn_lo), p(self.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(self.next_tokens), None,
                 p(self.logits) if self.keep_logits else None, *self._ws("lm"), st))
         else:
             _lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(

@@ -400,7 +400,7 @@ class QuantizedQwenLayer(nn.Module):
         ssq_a, ssq_b = torch.zeros(M, dtype=f32, device=dev), torch.zeros(M, dtype=f32, device=dev)
         act = _lib.ACT                                  # fp16 linear inputs (t2b.h)
         xw = torch.empty(M, H, dtype=act, device=dev)
-        q = torch.empty(M, nq * hd, dtype=bf, device=dev)
+        q = torch.empty(M, nq * hd, dtype=_lib.QDT if S == 1 else bf, device=dev)   # decode: fp32 q
         attn = torch.empty(M, nq * hd, dtype=act, device=dev)
         h = torch.empty(M, I, dtype=act, device=dev)
         eps = float(c.rms_norm_eps)
@@ -411,12 +411,11 @@ class QuantizedQwenLayer(nn.Module):
         if S == 1:
             pos = torch.full((B,), p0, dtype=torch.int32, device=dev)
             _lib.call("t2b_qkv_norm_rope_kvwrite", p(f["qkv"].qw), p(f["qkv"].meta), f["qkv"].fmt, p(xw), p(ssq_a), eps,
-                      p(f["q_norm"]), p(f["k_norm"]), p(table), p(pos), p(q), p(cache.k), p(cache.v), p(ssq_b), B, H,
-                      nq, nkv, hd, cache.max_ctx, p(ws[0]), ws[1], st)
+                      p(f["q_norm"]), p(f["k_norm"]), p(table), p(pos), p(q), _lib.DTYPE[q.dtype], p(cache.k),
+                      p(cache.v), p(ssq_b), B, H, nq, nkv, hd, cache.max_ctx, p(ws[0]), ws[1], st)
             wa = _ws(L.t2b_decode_attention_workspace_bytes(B, nq, nkv, hd, cache.max_ctx), dev)
-            _lib.call("t2b_decode_attention_after_kvwrite", p(q), p(cache.k), p(cache.v), p(pos), p(attn),
-                      _lib.DTYPE[act], B, nq, nkv,
-                      hd, cache.max_ctx, p(wa[0]), wa[1], st)
+            _lib.call("t2b_decode_attention_after_kvwrite", p(q), _lib.DTYPE[q.dtype], p(cache.k), p(cache.v), p(pos),
+                      p(attn), _lib.DTYPE[act], B, nq, nkv, hd, cache.max_ctx, p(wa[0]), wa[1], st)
         else:
             pos = (p0 + torch.arange(S, device=dev, dtype=torch.int32)).repeat(B)
             seq = torch.arange(B, device=dev, dtype=torch.int32).repeat_interleave(S)

@@ -163,10 +163,11 @@ class TPDecodeEngine:
         self.xw = torch.zeros(B, H, dtype=act, device=dev)
         self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
         self.ssq_b = torch.zeros(B, dtype=f32, device=dev)
-        self.q = torch.zeros(B, lc.q_dim, dtype=bf, device=dev)
+        self.q = torch.zeros(B, lc.q_dim, dtype=_lib.QDT, device=dev)
         self.attn = torch.zeros(B, lc.q_dim, dtype=act, device=dev)
         self.h = torch.zeros(B, lc.hidden_dim, dtype=act, device=dev)
         self.xn = torch.zeros(B, H, dtype=bf, device=dev)
+        self.xn_lo = torch.zeros(B, H, dtype=bf, device=dev)    # two-term lm_head input
         self.local_max = torch.zeros(B, dtype=f32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -216,10 +217,11 @@ class TPDecodeEngine:
         lw = self.layers[li]
         lib.check("t2b_qkv_norm_rope_kvwrite", L.t2b_qkv_norm_rope_kvwrite(
             p(lw.qkv.qw), p(lw.qkv.meta), lw.qkv.fmt, p(self.xw), p(self.ssq_a), cfg.rms_norm_eps,
-            p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), p(self.k_cache[li]),
+            p(lw.q_norm), p(lw.k_norm), p(self.angles), p(self.pos), p(self.q), lib.DTYPE[lib.QDT], p(self.k_cache[li]),
             p(self.v_cache[li]), p(self.ssq_b), B, H, nq, nkv, hd, self.max_ctx, *self._ws("qkv"), st))
         lib.check("t2b_decode_attention_after_kvwrite", L.t2b_decode_attention_after_kvwrite(
-            p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn), lib.DTYPE[lib.ACT], B,
+            p(self.q), lib.DTYPE[lib.QDT], p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn),
+            lib.DTYPE[lib.ACT], B,
             nq, nkv, hd, self.max_ctx, *self._ws("attn"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
             p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[lib.ACT], p(self.y),
@@ -247,10 +249,11 @@ class TPDecodeEngine:
         for li in range(cfg.n_layers):
             self.enqueue_layer(li)
         lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
-                                                           cfg.rms_norm_eps, p(self.xn), B, cfg.emb_dim, st))
+                                                           cfg.rms_norm_eps, p(self.xn), p(self.xn_lo), B, cfg.emb_dim,
+                                                           st))
         lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
-            p(self.xn), p(self.lm_head), B, cfg.emb_dim, self.v_local, p(self.local_idx), p(self.local_max), None,
-            *self._ws("lm"), st))
+            p(self.xn), p(self.xn_lo), p(self.lm_head), B, cfg.emb_dim, self.v_local, p(self.local_idx),
+            p(self.local_max), None, *self._ws("lm"), st))
         self.dist.all_gather(self.vals, self.local_max, group=self.group)
         self.dist.all_gather(self.idxs, self.local_idx, group=self.group)
         self.next_tokens.copy_(merge_argmax(torch.stack(self.vals), torch.stack(self.idxs), self.v_local))
