@@ -349,8 +349,8 @@ def kernel_profile(eng, steps):
                 p(lw.down.qw), p(lw.down.meta), lw.down.fmt, p(eng.h), p(eng.x), p(eng.ssq_a), p(eng.next_norm_weight(li)), p(eng.xw), B, H, cfg.hidden_dim,
                 *eng._ws("down"), st))
         rec("lm_head_argmax", lambda: L.t2b_lm_head_argmax(
-            p(eng.xn), p(eng.xn_lo), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
-            *eng._ws("lm"), st))
+            p(eng.xn), p(eng.lm_head), _lib.DTYPE[eng.lm_head.dtype], B, cfg.emb_dim, cfg.vocab_size,
+            p(eng.next_tokens), None, None, *eng._ws("lm"), st))
     torch.cuda.synchronize()
     for name, a, b in evs:
         times[name] += a.elapsed_time(b)
@@ -396,8 +396,8 @@ def kernel_profile_graph(eng, rounds=5):
     }
     if eng.lm_w4 is None:
         ops["lm_head_argmax"] = (1, lambda st, i: L.t2b_lm_head_argmax(
-            p(eng.xn), p(eng.xn_lo), p(eng.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(eng.next_tokens), None, None,
-            *eng._ws("lm"), st))
+            p(eng.xn), p(eng.lm_head), _lib.DTYPE[eng.lm_head.dtype], B, cfg.emb_dim, cfg.vocab_size,
+            p(eng.next_tokens), None, None, *eng._ws("lm"), st))
     out = {}
     side = torch.cuda.Stream()
     for name, (per_step, fn) in ops.items():

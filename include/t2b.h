@@ -305,12 +305,11 @@ T2B_API int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, float* 
                            const uint16_t* norm_w, uint16_t* xw_out, int M, int H, int vocab, void* stream);
 
 /*
- * out[m] = bf16(RMSNorm(x_resid[m]; ssq, w, eps)) -- the final norm (model.py:409,477);
- * out_lo (may be NULL) = bf16 of what out does not hold: out + out_lo carries
- * 16 significant bits (the lm_head's two-term input).
+ * out[m] = RMSNorm(x_resid[m]; ssq, w, eps) -- the final norm (model.py:409,477) --
+ * in out_dtype (T2B_DTYPE_BF16, or T2B_DTYPE_F16 for an fp16 lm_head).
  */
-T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out,
-                              uint16_t* out_lo, int M, int H, void* stream);
+T2B_API int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, void* out,
+                              int out_dtype, int M, int H, void* stream);
 
 /*
  * Greedy pick: idx[m] = argmax_v logits[m, v] (lowest index on ties), logits
@@ -332,15 +331,16 @@ T2B_API int t2b_residual_norm_input(const void* y, int y_dtype, float* x_resid, 
  * Greedy lm_head: idx[m] = argmax_v (xn[m] . lm_head[v]) over V rows of a bf16
  * [V][H] table (tied embedding or untied head), fp32 accumulation; ties to
  * the lowest index (torch.argmax).  max_logit [M] (may be NULL) receives the
- * maximum, logits fp32 [M][V] (may be NULL) the full rows.  xn bf16 [M][H],
- * M <= 256, H % 64 == 0; xn_lo (may be NULL) its low bf16 terms
- * (t2b_rms_norm_rows), multiplied in as a second MMA per k step.  Workspace: t2b_lm_head_argmax_workspace_bytes(M),
+ * maximum, logits fp32 [M][V] (may be NULL) the full rows.  xn [M][H] and the
+ * table share dtype: T2B_DTYPE_BF16, or T2B_DTYPE_F16 (the decode engines
+ * hold an fp16 copy of the head: xn then keeps 11 significant bits instead
+ * of 8); M <= 256, H % 64 == 0.  Workspace: t2b_lm_head_argmax_workspace_bytes(M),
  * zeroed once (re-armed by the kernel).  Replaces the lm_head DenseLinear +
  * host argmax (model.py:409-420, 477; qwen_npu.py:321).
  */
 T2B_API size_t t2b_lm_head_argmax_workspace_bytes(int M);
-T2B_API int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* xn_lo, const uint16_t* lm_head, int M, int H,
-                               int V, int32_t* idx, float* max_logit, float* logits, void* workspace,
+T2B_API int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* lm_head, int dtype, int M, int H, int V,
+                               int32_t* idx, float* max_logit, float* logits, void* workspace,
                                size_t workspace_bytes, void* stream);
 
 T2B_API size_t t2b_argmax_workspace_bytes(int M, int V);

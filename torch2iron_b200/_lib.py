@@ -54,14 +54,14 @@ SIGNATURES = {
     "t2b_down_residual_workspace_bytes": (Z, [I, I, I]),
     "t2b_down_residual": (I, [P, P, I, P, P, P, P, P, I, I, I, P, Z, P]),
     "t2b_embed_rows": (I, [P, P, P, P, P, P, I, I, I, P]),
-    "t2b_rms_norm_rows": (I, [P, P, P, F, P, P, I, I, P]),
+    "t2b_rms_norm_rows": (I, [P, P, P, F, P, I, I, I, P]),
     "t2b_set_error_word": (I, [P]),
     "t2b_bind_error_word": (I, [P, P]),
     "t2b_error_word_for_stream": (I, [P, P]),
     "t2b_selftest_bounded_wait": (I, [P, I, P]),
     "t2b_residual_norm_input": (I, [P, I, P, P, P, P, I, I, P]),
     "t2b_lm_head_argmax_workspace_bytes": (Z, [I]),
-    "t2b_lm_head_argmax": (I, [P, P, P, I, I, I, P, P, P, P, Z, P]),
+    "t2b_lm_head_argmax": (I, [P, P, I, I, I, I, P, P, P, P, Z, P]),
     "t2b_argmax_workspace_bytes": (Z, [I, I]),
     "t2b_argmax_rows": (I, [P, I, I, I, I, P, P, Z, P]),
     "t2b_rms_norm_rope": (I, [P, P, P, P, I, I, I, F, I, P]),

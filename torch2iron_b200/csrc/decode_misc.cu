@@ -104,20 +104,18 @@ __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, const
   }
 }
 
-// out = bf16(v) and, when out_lo is given, out_lo = bf16(v - out): the two
-// bf16 terms of the lm_head's split input.
+// out: bf16, or fp16 (F16) for an fp16 head.
+template <bool F16>
 __global__ void rms_norm_rows_kernel(const float* __restrict__ x, const float* __restrict__ ssq,
-                                     const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* __restrict__ out,
-                                     __nv_bfloat16* __restrict__ out_lo, int H) {
+                                     const __nv_bfloat16* __restrict__ w, float eps, void* __restrict__ out, int H) {
   grid_dep_wait();
   grid_dep_launch();
   const int m = blockIdx.x;
   const float r = rsqrtf(ssq[m] / (float)H + eps);
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     const float v = (x[(size_t)m * H + i] * r) * __bfloat162float(w[i]);
-    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    out[(size_t)m * H + i] = hi;
-    if (out_lo) out_lo[(size_t)m * H + i] = __float2bfloat16_rn(v - __bfloat162float(hi));
+    if (F16) static_cast<__half*>(out)[(size_t)m * H + i] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(out)[(size_t)m * H + i] = __float2bfloat16_rn(v);
   }
 }
 
@@ -335,13 +333,15 @@ int embed_rows(const uint16_t* table, const int* tokens, float* x, float* ssq, c
   return launch_pdl(embed_rows_kernel, dim3(M), dim3(256), 0, st, t, tokens, x, ssq, w, o, H, vocab, err);
 }
 
-int rms_norm_rows(const float* x, const float* ssq, const uint16_t* w, float eps, uint16_t* out, uint16_t* out_lo,
-                  int M, int H, cudaStream_t st) {
+int rms_norm_rows(const float* x, const float* ssq, const uint16_t* w, float eps, void* out, int out_dtype, int M,
+                  int H, cudaStream_t st) {
   if (M < 1 || H < 1) return T2B_ERR_SHAPE;
   const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(w);
-  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(out);
-  __nv_bfloat16* ol = reinterpret_cast<__nv_bfloat16*>(out_lo);
-  return launch_pdl(rms_norm_rows_kernel, dim3(M), dim3(256), 0, st, x, ssq, wp, eps, op, ol, H);
+  if (out_dtype == T2B_DTYPE_F16)
+    return launch_pdl(rms_norm_rows_kernel<true>, dim3(M), dim3(256), 0, st, x, ssq, wp, eps, out, H);
+  if (out_dtype == T2B_DTYPE_BF16)
+    return launch_pdl(rms_norm_rows_kernel<false>, dim3(M), dim3(256), 0, st, x, ssq, wp, eps, out, H);
+  return T2B_ERR_ARG;
 }
 
 // ---------------------------------------------------------------------------
@@ -538,10 +538,10 @@ extern "C" int t2b_embed_rows(const uint16_t* table, const int32_t* tokens, floa
   return embed_rows(table, tokens, x_resid, ssq_out, norm_w, xw_out, M, H, vocab, nullptr, S_(stream));
 }
 
-extern "C" int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, uint16_t* out,
-                                 uint16_t* out_lo, int M, int H, void* stream) {
+extern "C" int t2b_rms_norm_rows(const float* x_resid, const float* ssq, const uint16_t* w, float eps, void* out,
+                                 int out_dtype, int M, int H, void* stream) {
   if (!x_resid || !ssq || !w || !out) return T2B_ERR_ARG;
-  return rms_norm_rows(x_resid, ssq, w, eps, out, out_lo, M, H, S_(stream));
+  return rms_norm_rows(x_resid, ssq, w, eps, out, out_dtype, M, H, S_(stream));
 }
 
 extern "C" int t2b_set_error_word(int32_t* word) {

@@ -5,10 +5,9 @@
 // Swap-AB on tcgen05: D[128 vocab rows, BP batch rows] = E_tile . xn^T, both
 // operands bf16 K-major in shared memory (2-D TMA boxes of 64 k with the
 // 128-byte swizzle = the UMMA canonical layout), fp32 accumulator in TMEM.
-// With SPLIT the normalised rows arrive as two bf16 terms (xn = hi + lo, 16
-// significant bits) and every k step issues one MMA per term into the same
-// accumulator, so the logits see xn almost exactly (the table is bf16 as
-// stored); the MMAs are far from the HBM bound either way.
+// The table and the normalised rows share one 16-bit type: bf16, or fp16
+// (the decode engines keep an fp16 copy of the head, exact for every table
+// value in fp16 range, so xn enters with 11 significant bits instead of 8).
 // Persistent CTAs (one per SM) walk the vocab tiles; the accumulator is
 // double-buffered so the drain of one tile overlaps the MMAs of the next.
 // Warp roles: 0-3 drain (thread = TMEM lane = vocab row), 4 TMA producer,
@@ -39,7 +38,7 @@ constexpr int LM_KB = 64;      // k per TMA box / pipeline stage
 struct LmParams {
   CUtensorMap emap;   // E [V][H] bf16, box 64 k x 128 rows
   CUtensorMap xmap;   // xn [M][H] bf16, box 64 k x BP rows (rows >= M read 0)
-  CUtensorMap xmap_lo;   // SPLIT: the low bf16 terms of xn, same shape
+  int f16;            // table and xn are fp16 (else bf16)
   int M, H, V, n_tiles;
   int32_t* idx;       // [M]
   float* vals;        // [M] maxima (nullable)
@@ -49,15 +48,12 @@ struct LmParams {
   int* err;
 };
 
-template <int BP, bool SPLIT = false>
+template <int BP>
 struct LmGeom {
   static constexpr int E_BYTES = LM_ROWS * LM_KB * 2;   // 16 KB
   static constexpr int X_BYTES = BP * LM_KB * 2;
-  static constexpr int STAGE = E_BYTES + X_BYTES * (SPLIT ? 2 : 1);
-  static constexpr int STAGES_FIT = (196 * 1024) / STAGE;
-  static constexpr int STAGES_PREF = BP <= 64 ? 6 : (BP <= 128 ? 5 : 4);
-  static constexpr int STAGES = STAGES_PREF < STAGES_FIT ? STAGES_PREF : STAGES_FIT;
-  static_assert(STAGES >= 2, "lm_head ring needs two stages");
+  static constexpr int STAGE = E_BYTES + X_BYTES;
+  static constexpr int STAGES = BP <= 64 ? 6 : (BP <= 128 ? 5 : 4);
   static constexpr int RING = STAGES * STAGE;
   static constexpr uint32_t TMEM_COLS = 2 * BP < 32 ? 32 : 2 * BP;   // two accumulators
   static constexpr int BEST = 4 * (BP < 32 ? 32 : BP) * 8;          // [4 warps][columns] keys
@@ -80,11 +76,11 @@ T2B_DEV unsigned long long shfl_xor_u64(unsigned long long x, int m) {
   return ((unsigned long long)hi << 32) | lo;
 }
 
-template <int BP, bool SPLIT>
+template <int BP>
 __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __grid_constant__ LmParams p) {
-  using G = LmGeom<BP, SPLIT>;
+  using G = LmGeom<BP>;
   constexpr int STG = G::STAGES;
-  constexpr uint32_t IDESC = idesc_bf16(LM_ROWS, BP);
+  const uint32_t IDESC = p.f16 ? idesc_f16(LM_ROWS, BP) : idesc_bf16(LM_ROWS, BP);
   extern __shared__ __align__(1024) uint8_t smem_dyn[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   constexpr int NCOL = BP < 32 ? 32 : BP;                           // columns drained (padded to 32)
@@ -153,7 +149,6 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __g
             tma_load_2d(st, &p.emap, kc * LM_KB, t * LM_ROWS, &full[s]);
           }
           tma_load_2d(st + G::E_BYTES, &p.xmap, kc * LM_KB, 0, &full[s]);
-          if (SPLIT) tma_load_2d(st + G::E_BYTES + G::X_BYTES, &p.xmap_lo, kc * LM_KB, 0, &full[s]);
         }
     }
   } else if (warp == 5) {
@@ -177,13 +172,9 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __g
           tc_fence_after();
           const uint32_t ea = smem_u32(sm + s * G::STAGE), xa = ea + G::E_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < LM_KB / 16; ++ks) {
+          for (int ks = 0; ks < LM_KB / 16; ++ks)
             mma_ss(tbase + (uint32_t)(buf * BP), sdesc_sw128(ea + ks * 32), sdesc_sw128(xa + ks * 32), IDESC,
                    (kc > 0 || ks > 0) ? 1u : 0u);
-            if (SPLIT)
-              mma_ss(tbase + (uint32_t)(buf * BP), sdesc_sw128(ea + ks * 32),
-                     sdesc_sw128(xa + G::X_BYTES + ks * 32), IDESC, 1u);
-          }
           mma_commit(&empty[s]);
         }
         mma_commit(&acc_full[buf]);
@@ -293,10 +284,10 @@ static int lm_bp(int M) {
 
 size_t lm_head_workspace_bytes(int M) { return (((size_t)M * 8 + 255) & ~size_t(255)) + 256; }
 
-template <int BP, bool SPLIT>
+template <int BP>
 static int lm_launch_t(LmParams& p, cudaStream_t st) {
-  auto kern = lm_head_argmax_kernel<BP, SPLIT>;
-  const size_t smem = LmGeom<BP, SPLIT>::SMEM;
+  auto kern = lm_head_argmax_kernel<BP>;
+  const size_t smem = LmGeom<BP>::SMEM;
   if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -305,28 +296,30 @@ static int lm_launch_t(LmParams& p, cudaStream_t st) {
   return launch_pdl(kern, dim3(grid), dim3(LM_THREADS), smem, st, p);
 }
 
-static int encode_2d(CUtensorMap* m, const void* base, int inner, int outer, int box_outer) {
+static int encode_2d(CUtensorMap* m, const void* base, int inner, int outer, int box_outer, bool f16) {
   const EncodeTiledFn encode = encode_tiled();
   if (encode == nullptr) return T2B_ERR_LAUNCH;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
   cuuint32_t box[2] = {(cuuint32_t)LM_KB, (cuuint32_t)box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = encode(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                      const_cast<void*>(base), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? T2B_OK : T2B_ERR_ARG;
 }
 
-int lm_head_argmax(const uint16_t* xn, const uint16_t* xn_lo, const uint16_t* lm, int M, int H, int V, int32_t* idx,
+int lm_head_argmax(const uint16_t* xn, const uint16_t* lm, int dtype, int M, int H, int V, int32_t* idx,
                    float* vals, float* logits, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (M < 1 || M > 256 || H < LM_KB || H % LM_KB || V < 1) return T2B_ERR_SHAPE;
+  if (dtype != T2B_DTYPE_BF16 && dtype != T2B_DTYPE_F16) return T2B_ERR_ARG;
   if (ws_bytes < lm_head_workspace_bytes(M) || !ws) return T2B_ERR_WORKSPACE;
   LmParams p{};
   const int bp = lm_bp(M);
-  int r = encode_2d(&p.emap, lm, H, V, LM_ROWS);
-  if (r == T2B_OK) r = encode_2d(&p.xmap, xn, H, M, bp);
-  if (r == T2B_OK && xn_lo) r = encode_2d(&p.xmap_lo, xn_lo, H, M, bp);
+  p.f16 = dtype == T2B_DTYPE_F16;
+  int r = encode_2d(&p.emap, lm, H, V, LM_ROWS, p.f16);
+  if (r == T2B_OK) r = encode_2d(&p.xmap, xn, H, M, bp, p.f16);
   if (r != T2B_OK) return r;
   p.M = M;
   p.H = H;
@@ -338,18 +331,11 @@ int lm_head_argmax(const uint16_t* xn, const uint16_t* xn_lo, const uint16_t* lm
   p.keys = reinterpret_cast<unsigned long long*>(ws);
   p.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * 8 + 255) & ~size_t(255)));
   p.err = error_word(st);
-  if (xn_lo) {
-    if (bp == 16) return lm_launch_t<16, true>(p, st);
-    if (bp == 32) return lm_launch_t<32, true>(p, st);
-    if (bp == 64) return lm_launch_t<64, true>(p, st);
-    if (bp == 128) return lm_launch_t<128, true>(p, st);
-    return lm_launch_t<256, true>(p, st);
-  }
-  if (bp == 16) return lm_launch_t<16, false>(p, st);
-  if (bp == 32) return lm_launch_t<32, false>(p, st);
-  if (bp == 64) return lm_launch_t<64, false>(p, st);
-  if (bp == 128) return lm_launch_t<128, false>(p, st);
-  return lm_launch_t<256, false>(p, st);
+  if (bp == 16) return lm_launch_t<16>(p, st);
+  if (bp == 32) return lm_launch_t<32>(p, st);
+  if (bp == 64) return lm_launch_t<64>(p, st);
+  if (bp == 128) return lm_launch_t<128>(p, st);
+  return lm_launch_t<256>(p, st);
 }
 
 }  // namespace t2b
@@ -361,12 +347,11 @@ extern "C" size_t t2b_lm_head_argmax_workspace_bytes(int M) {
   return lm_head_workspace_bytes(M);
 }
 
-extern "C" int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* xn_lo, const uint16_t* lm_head, int M, int H,
-                                  int V, int32_t* idx, float* max_logit, float* logits, void* ws, size_t ws_bytes,
+extern "C" int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* lm_head, int dtype, int M, int H, int V,
+                                  int32_t* idx, float* max_logit, float* logits, void* ws, size_t ws_bytes,
                                   void* stream) {
   if (!xn || !lm_head || !idx) return T2B_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(xn) | reinterpret_cast<uintptr_t>(xn_lo) | reinterpret_cast<uintptr_t>(lm_head)) & 15)
-    return T2B_ERR_ALIGN;
-  return lm_head_argmax(xn, xn_lo, lm_head, M, H, V, idx, max_logit, logits, ws, ws_bytes,
+  if ((reinterpret_cast<uintptr_t>(xn) | reinterpret_cast<uintptr_t>(lm_head)) & 15) return T2B_ERR_ALIGN;
+  return lm_head_argmax(xn, lm_head, dtype, M, H, V, idx, max_logit, logits, ws, ws_bytes,
                         reinterpret_cast<cudaStream_t>(stream));
 }

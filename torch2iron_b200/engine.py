@@ -119,7 +119,9 @@ class DecodeEngine:
             self.lm_w4 = W.from_autogptq(lm, dev) if isinstance(lm, AutoGPTQLinear) else W.from_q4nx(lm, dev)
             self.lm_head = None
         else:
-            self.lm_head = self.embed if lm is None else lm.to(dev, torch.bfloat16).contiguous()
+            # the greedy head runs in fp16: an fp16 copy of the (bf16) table, exact for every value in fp16
+            # range, so the normalised rows keep 11 significant bits (t2b_lm_head_argmax)
+            self.lm_head = (self.embed if lm is None else lm).to(dev, torch.float16).contiguous()
         self.final_norm = model["final_norm"].to(dev, torch.bfloat16).contiguous()
         self.angles = rope_angles(cfg.head_dim, max_ctx, cfg.rope_base).to(dev)
 
@@ -133,8 +135,7 @@ class DecodeEngine:
         self.q = torch.zeros(B, cfg.q_dim, dtype=_lib.QDT, device=dev)
         self.attn = torch.zeros(B, cfg.q_dim, dtype=act, device=dev)
         self.h = torch.zeros(B, cfg.hidden_dim, dtype=act, device=dev)
-        self.xn = torch.zeros(B, H, dtype=bf, device=dev)        # final norm output, bf16 ...
-        self.xn_lo = torch.zeros(B, H, dtype=bf, device=dev)     # ... and its low bf16 terms (two-term lm_head)
+        self.xn = torch.zeros(B, H, dtype=torch.float16, device=dev)   # final norm output (fp16 head input)
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=f32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -244,16 +245,16 @@ class DecodeEngine:
         cfg, B = self.cfg, self.B
         L = _lib.lib()
         p = _lib.ptr
-        lo = self.xn_lo if self.lm_w4 is None else None
+        f16 = _lib.DTYPE[torch.float16]
         _lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
-                                                            cfg.rms_norm_eps, p(self.xn), p(lo), B, cfg.emb_dim, st))
+                                                            cfg.rms_norm_eps, p(self.xn), f16, B, cfg.emb_dim, st))
         if self.lm_w4 is None:
             _lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
-                p(self.xn), p(self.xn_lo), p(self.lm_head), B, cfg.emb_dim, cfg.vocab_size, p(self.next_tokens), None,
+                p(self.xn), p(self.lm_head), f16, B, cfg.emb_dim, cfg.vocab_size, p(self.next_tokens), None,
                 p(self.logits) if self.keep_logits else None, *self._ws("lm"), st))
         else:
             _lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-                p(self.lm_w4.qw), p(self.lm_w4.meta), self.lm_w4.fmt, p(self.xn), _lib.DTYPE[torch.bfloat16],
+                p(self.lm_w4.qw), p(self.lm_w4.meta), self.lm_w4.fmt, p(self.xn), f16,
                 p(self.logits), _lib.DTYPE[torch.float32], B, cfg.vocab_size, cfg.emb_dim,
                 32 if self.lm_w4.fmt == W.WFMT_Q4NX else 128, *self._ws("lm"), st))
             _lib.check("t2b_argmax_rows", L.t2b_argmax_rows(

@@ -152,7 +152,7 @@ class TPDecodeEngine:
         full_lm = model["embed"] if lm is None else lm
         v0, v1 = vocab_slice(cfg, tp, rank)
         self.v_local = v1 - v0
-        self.lm_head = full_lm[v0:v1].to(dev, torch.bfloat16).contiguous()
+        self.lm_head = full_lm[v0:v1].to(dev, torch.float16).contiguous()   # fp16 head (t2b_lm_head_argmax)
         self.final_norm = model["final_norm"].to(dev, torch.bfloat16).contiguous()
         self.angles = rope_angles(cfg.head_dim, max_ctx, cfg.rope_base).to(dev)
         B, H, hd = batch, cfg.emb_dim, cfg.head_dim
@@ -166,8 +166,7 @@ class TPDecodeEngine:
         self.q = torch.zeros(B, lc.q_dim, dtype=_lib.QDT, device=dev)
         self.attn = torch.zeros(B, lc.q_dim, dtype=act, device=dev)
         self.h = torch.zeros(B, lc.hidden_dim, dtype=act, device=dev)
-        self.xn = torch.zeros(B, H, dtype=bf, device=dev)
-        self.xn_lo = torch.zeros(B, H, dtype=bf, device=dev)    # two-term lm_head input
+        self.xn = torch.zeros(B, H, dtype=torch.float16, device=dev)
         self.local_max = torch.zeros(B, dtype=f32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -248,12 +247,12 @@ class TPDecodeEngine:
                                                      cfg.vocab_size, st))
         for li in range(cfg.n_layers):
             self.enqueue_layer(li)
+        f16 = lib.DTYPE[torch.float16]
         lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
-                                                           cfg.rms_norm_eps, p(self.xn), p(self.xn_lo), B, cfg.emb_dim,
-                                                           st))
+                                                           cfg.rms_norm_eps, p(self.xn), f16, B, cfg.emb_dim, st))
         lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
-            p(self.xn), p(self.xn_lo), p(self.lm_head), B, cfg.emb_dim, self.v_local, p(self.local_idx),
-            p(self.local_max), None, *self._ws("lm"), st))
+            p(self.xn), p(self.lm_head), f16, B, cfg.emb_dim, self.v_local, p(self.local_idx), p(self.local_max),
+            None, *self._ws("lm"), st))
         self.dist.all_gather(self.vals, self.local_max, group=self.group)
         self.dist.all_gather(self.idxs, self.local_idx, group=self.group)
         self.next_tokens.copy_(merge_argmax(torch.stack(self.vals), torch.stack(self.idxs), self.v_local))
