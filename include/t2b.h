@@ -44,8 +44,10 @@
  * fp16, and the tensor-core paths dequantise the weights to fp16 for them
  * (11-bit significands: 8x finer than bf16, which keeps a 28-layer decoder
  * within the decoder-logit tolerance of the fp32 reference); values beyond
- * fp16 range saturate at +-65504.  q and the KV cache are bf16, the residual
- * stream fp32.  t2b_w4a16_gemm follows its x_dtype (bf16 or fp16 weights).
+ * fp16 range saturate at +-65504.  The KV cache is bf16, q leaves the qkv
+ * operation in fp32 on the decode path (bf16 on the prefill path), the
+ * residual stream is fp32.  t2b_w4a16_gemm follows its x_dtype (bf16 or fp16
+ * weights).
  */
 #ifndef T2B_H
 #define T2B_H
