@@ -153,6 +153,12 @@ T2B_API size_t t2b_w4a16_gemm_workspace_bytes(int M, int N, int K);
  * can check a shape's decomposition without a GPU.
  */
 T2B_API int t2b_linear_plan(int M, int N, int K, int* path, int* rows_per_cta, int* groups_per_cta, int* ksplit);
+/* The plan the fused qkv operations (t2b_qkv_norm_rope_kvwrite[_seq]) take for the
+ * same shape: on the tcgen05 path each CTA finishes at most 8 batch rows where a
+ * grid of about one wave allows it, since the qkv epilogue's per-row work
+ * (QK-norm, RoPE, KV write) would otherwise dominate the launch. */
+T2B_API int t2b_linear_plan_qkv(int M, int N, int K, int* path, int* rows_per_cta, int* groups_per_cta,
+                                int* ksplit);
 T2B_API int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype, void* y,
                    int y_dtype, int M, int N, int K, int group_size, void* workspace, size_t workspace_bytes,
                    void* stream);

@@ -17,9 +17,10 @@ BATCHES = [1, 2, 3, 4, 5, 7, 8, 9, 12, 16, 17, 24, 31, 32, 33, 48, 63, 64, 65, 9
            257, 1000, 8192]   # the last three: prefill chunks (large-M kernel)
 
 
-def _plan(M, N, K):
+def _plan(M, N, K, qkv=False):
     out = [C.c_int() for _ in range(4)]
-    st = _lib.load().t2b_linear_plan(M, N, K, *[C.byref(v) for v in out])
+    f = _lib.load().t2b_linear_plan_qkv if qkv else _lib.load().t2b_linear_plan
+    st = f(M, N, K, *[C.byref(v) for v in out])
     return st, tuple(v.value for v in out)
 
 
@@ -36,9 +37,11 @@ CASES = [(c, t) for c, tps in ((QWEN3_0_6B, (1, 2)), (LLAMA_3_2_1B, (1, 2, 4, 8)
 
 @pytest.mark.parametrize("cfg,tp", CASES, ids=[f"{c.emb_dim}-{c.n_layers}-tp{t}" for c, t in CASES])
 def test_plans_cover_k_and_split_the_batch_tile_evenly(cfg, tp):
-    for name, (n, k) in _linears(cfg, tp).items():
+    plans = [(name, n, k, False) for name, (n, k) in _linears(cfg, tp).items()]
+    plans.append(("qkv (fused)",) + _linears(cfg, tp)["qkv"] + (True,))
+    for name, n, k, qkv in plans:
         for m in BATCHES:
-            st, (path, rows, groups, ks) = _plan(m, n, k)
+            st, (path, rows, groups, ks) = _plan(m, n, k, qkv)
             assert st == _lib.T2B_OK, (name, m, n, k)
             assert groups * ks * 128 == k, (name, m, n, k, rows, groups, ks)
             if path == 2:
@@ -52,6 +55,15 @@ def test_plans_cover_k_and_split_the_batch_tile_evenly(cfg, tp):
 def test_qwen3_8b_tp8_down_projection_plan():
     """K = 1536 (12 groups): 3 groups per CTA in clusters of 4, not 4 groups in clusters of 3."""
     assert _plan(64, 4096, 1536) == (_lib.T2B_OK, (1, 64, 3, 4))
+
+
+def test_qkv_plan_caps_rows_per_cta():
+    """The fused qkv launch of Qwen3-0.6B at 64 rows: 32-row tiles, 2 groups per CTA in
+    clusters of 4 (8 rows per CTA); the generic plan keeps 64-row tiles in clusters of 2."""
+    assert _plan(64, 4096, 1024, qkv=True) == (_lib.T2B_OK, (1, 32, 2, 4))
+    assert _plan(64, 4096, 1024) == (_lib.T2B_OK, (1, 64, 4, 2))
+    for m in (1, 8):   # the CUDA-core path is the same plan
+        assert _plan(m, 4096, 1024, qkv=True) == _plan(m, 4096, 1024)
 
 
 def test_plan_rejects_bad_shapes():

@@ -39,6 +39,7 @@
 // (attention_reference.py:153-154).
 
 #include <algorithm>
+#include <cstdlib>
 #include <math.h>
 
 #include "t2b_common.cuh"
@@ -689,7 +690,13 @@ static int attn_launch_t(AttnParams& P, int max_grid, cudaStream_t st) {
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, AT_THREADS, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   per_sm = std::min(per_sm, AT_MAX_CTAS_PER_SM);
-  const int grid = std::max(1, std::min(max_grid, sm_count() * per_sm));
+  int grid = std::max(1, std::min(max_grid, sm_count() * per_sm));
+  // env T2B_ATTN_GRID caps the grid (experiments: fewer CTAs, all resident
+  // beside the preceding kernel's)
+  if (const char* e = getenv("T2B_ATTN_GRID")) {
+    const int cap = atoi(e);
+    if (cap > 0) grid = std::min(grid, cap);
+  }
   return launch_pdl(kern, dim3(grid), dim3(AT_THREADS), smem, st, P);
 }
 

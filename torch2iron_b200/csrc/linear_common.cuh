@@ -23,6 +23,10 @@ namespace t2b {
 
 enum Prologue { PRO_ACT = 0, PRO_RMSNORM = 1 };
 enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+// Batch rows each CTA of the tcgen05 path finishes under the qkv epilogue, at
+// most (where a plan of about one wave allows it): its per-row work -- QK-norm,
+// RoPE, the KV-cache write -- then stays short beside the contraction.
+constexpr int QKV_MAX_ROWS_PER_CTA = 8;
 
 constexpr int TILE_N = 128;          // weight rows per output tile
 constexpr int GROUP = 128;           // quantization group along K

@@ -362,7 +362,7 @@ static int gemv_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, si
 int tc_launch(LinearParams& p, int pro, int epi, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t tc_ws_bytes(int M, int N, int K);
 bool tc_supported(int M, int N, int K, bool q4);
-bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks);
+bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks, int max_rows);
 
 // Rows at or above this count take the tcgen05 path (env T2B_TC_MIN_M overrides).
 static int tc_min_m() {
@@ -444,8 +444,8 @@ static LinearParams gemv_base(const void* weight, const uint32_t* meta, int w_ld
   return p;
 }
 
-extern "C" int t2b_linear_plan(int M, int N, int K, int* path, int* rows_per_cta, int* groups_per_cta,
-                               int* ksplit) {
+static int linear_plan(int M, int N, int K, int max_rows, int* path, int* rows_per_cta, int* groups_per_cta,
+                       int* ksplit) {
   if (!path || !rows_per_cta || !groups_per_cta || !ksplit) return T2B_ERR_ARG;
   if (M < 1 || N <= 0 || K <= 0 || N % TILE_N || K % 256) return T2B_ERR_SHAPE;
   if (use_prefill(M, T2B_WFMT_T2B, T2B_DTYPE_BF16)) {   // one weight tile x 128 rows per work unit, all of K
@@ -457,7 +457,7 @@ extern "C" int t2b_linear_plan(int M, int N, int K, int* path, int* rows_per_cta
   }
   if (use_tc(M, N, K, T2B_WFMT_T2B, T2B_DTYPE_BF16)) {
     *path = 1;
-    tc_plan_info(M, N, K, rows_per_cta, groups_per_cta, ksplit);
+    tc_plan_info(M, N, K, rows_per_cta, groups_per_cta, ksplit, max_rows);
     return T2B_OK;
   }
   *path = 0;
@@ -466,6 +466,16 @@ extern "C" int t2b_linear_plan(int M, int N, int K, int* path, int* rows_per_cta
   *groups_per_cta = kslice / GROUP;
   *ksplit = K / kslice;
   return T2B_OK;
+}
+
+extern "C" int t2b_linear_plan(int M, int N, int K, int* path, int* rows_per_cta, int* groups_per_cta,
+                               int* ksplit) {
+  return linear_plan(M, N, K, 0, path, rows_per_cta, groups_per_cta, ksplit);
+}
+
+extern "C" int t2b_linear_plan_qkv(int M, int N, int K, int* path, int* rows_per_cta, int* groups_per_cta,
+                                   int* ksplit) {
+  return linear_plan(M, N, K, QKV_MAX_ROWS_PER_CTA, path, rows_per_cta, groups_per_cta, ksplit);
 }
 
 extern "C" size_t t2b_w4a16_gemm_workspace_bytes(int M, int N, int K) {

@@ -32,6 +32,7 @@
 // still passes its cluster barriers, and skips its epilogue.
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 
 #include "linear_common.cuh"
@@ -42,13 +43,18 @@
 namespace t2b {
 
 // Shared-memory plan of one CTA (S groups, BP padded batch rows).
-// Staged epilogue inputs: EP_ROWS_BYTES of per-row data (angle rows or
-// residual rows), then 256 bytes of row positions, then 1 KB of weights.
-constexpr int EP_ROWS_BYTES = 32 * 1024;
-constexpr int EP_BYTES = EP_ROWS_BYTES + 256 + 1024;
+// Staged epilogue inputs: per-row data (angle rows or residual rows) of the
+// rows this CTA finishes, then 256 bytes of row positions, then 1 KB of
+// weights.  The per-row part is sized for those rows (at most 32 KB), so a
+// CTA that finishes few rows keeps its shared memory small and leaves room on
+// its SM for the neighbouring kernels' CTAs.
+constexpr int EP_ROWS_MAX = 32 * 1024;
+__host__ __device__ constexpr int tc_ep_rows_bytes(int BP, int KS) {
+  return (BP / KS) * TILE_N * 4 < EP_ROWS_MAX ? (BP / KS) * TILE_N * 4 : EP_ROWS_MAX;
+}
 
 struct TcLayout {
-  int x_group, off_raw, off_meta, off_tile, off_recv, off_scr, off_ep, off_bar, off_tmem, off_flag, bytes;
+  int x_group, off_raw, off_meta, off_tile, off_recv, off_scr, off_ep, ep_rows, off_bar, off_tmem, off_flag, bytes;
   // q4: Q4NX meta (512 words per group: [piece 4][row 128]) instead of 128
   __host__ __device__ TcLayout(int BP, int S, int KS, bool q4 = false) {
     x_group = BP * 256;                      // bf16 [2 atoms][BP][128 B] per group (TMA, 128B swizzle)
@@ -58,7 +64,8 @@ struct TcLayout {
     off_recv = off_tile + BP * TILE_N * 4;   // fp32 [KS-1][BP/KS][128] peers' partials of this CTA's rows
     off_scr = off_recv + (BP - BP / KS) * TILE_N * 4;  // fp32 [8*BP] scratch (row scales, epilogue)
     off_ep = off_scr + 8 * BP * 4;           // epilogue inputs staged after the PDL wait
-    off_bar = off_ep + EP_BYTES;             // raw_full[S], a_full[NA], a_empty[NA], acc_full, x_full, recv_full
+    ep_rows = tc_ep_rows_bytes(BP, KS);      // per-row part of the staged inputs
+    off_bar = off_ep + ep_rows + 256 + 1024; // raw_full[S], a_full[NA], a_empty[NA], acc_full, x_full, recv_full
     off_tmem = off_bar + (S + 17) * 8;       // (NA <= 7)
     off_flag = off_tmem + 8;
     bytes = off_flag + 8 + 1024;             // + slack to 1024-align the base
@@ -71,22 +78,23 @@ struct TcLayout {
 // touches no global memory it must wait for: for EPI_QKV the rows'
 // positions, their RoPE angle rows and the two QK-norm weights; for
 // EPI_RESIDUAL the residual rows of this tile and the next-norm weights.
-// Staged only when it fits EP_BYTES.
+// Staged only when it fits the per-row capacity `cap` (TcLayout::ep_rows).
 template <int EPI>
-T2B_DEV bool epilogue_staged(const LinearParams& p, int rows) {
-  if (EPI == EPI_QKV) return rows <= 64 && rows * p.head_dim * 4 <= EP_ROWS_BYTES;
-  if (EPI == EPI_RESIDUAL) return rows * TILE_N * 4 <= EP_ROWS_BYTES;
+T2B_DEV bool epilogue_staged(const LinearParams& p, int rows, int cap) {
+  if (EPI == EPI_QKV) return rows <= 64 && rows * p.head_dim * 4 <= cap;
+  if (EPI == EPI_RESIDUAL) return rows * TILE_N * 4 <= cap;
   return false;
 }
 
 template <int EPI>
-T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int tile, int m0, int rows, int t, int nt) {
-  if (!epilogue_staged<EPI>(p, rows)) return;
+T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int cap, int tile, int m0, int rows, int t,
+                                   int nt) {
+  if (!epilogue_staged<EPI>(p, rows, cap)) return;
   if (EPI == EPI_QKV) {
     const int hd = p.head_dim;
-    int* __restrict__ pos_s = reinterpret_cast<int*>(ep + EP_ROWS_BYTES);
+    int* __restrict__ pos_s = reinterpret_cast<int*>(ep + cap);
     float* __restrict__ ang = reinterpret_cast<float*>(ep);
-    __nv_bfloat16* __restrict__ qn = reinterpret_cast<__nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
+    __nv_bfloat16* __restrict__ qn = reinterpret_cast<__nv_bfloat16*>(ep + cap + 256);
     __nv_bfloat16* __restrict__ kn = qn + 256;
     // each thread takes whole 4-float chunks of an angle row: position and
     // angle loads of different chunks are independent and overlap
@@ -107,7 +115,7 @@ T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int tile,
       }
   } else if (EPI == EPI_RESIDUAL) {
     float* __restrict__ res = reinterpret_cast<float*>(ep);
-    __nv_bfloat16* __restrict__ nw = reinterpret_cast<__nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
+    __nv_bfloat16* __restrict__ nw = reinterpret_cast<__nv_bfloat16*>(ep + cap + 256);
     for (int i = t; i < rows * TILE_N / 4; i += nt) {
       const int b = (i * 4) / TILE_N, c = i * 4 - b * TILE_N, m = m0 + b;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -120,19 +128,19 @@ T2B_DEV void stage_epilogue_inputs(const LinearParams& p, uint8_t* ep, int tile,
 }
 
 template <int EPI>
-T2B_DEV EpiCache staged_epilogue_inputs(const LinearParams& p, uint8_t* ep, int rows) {
+T2B_DEV EpiCache staged_epilogue_inputs(const LinearParams& p, uint8_t* ep, int cap, int rows) {
   EpiCache c{};
-  if (!epilogue_staged<EPI>(p, rows)) return c;
+  if (!epilogue_staged<EPI>(p, rows, cap)) return c;
   if (EPI == EPI_QKV) {
     c.angles = reinterpret_cast<const float*>(ep);
-    c.pos = reinterpret_cast<const int*>(ep + EP_ROWS_BYTES);
+    c.pos = reinterpret_cast<const int*>(ep + cap);
     if (p.qn_w) {
-      c.qn = reinterpret_cast<const __nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
+      c.qn = reinterpret_cast<const __nv_bfloat16*>(ep + cap + 256);
       c.kn = c.qn + 256;
     }
   } else if (EPI == EPI_RESIDUAL) {
     c.resid = reinterpret_cast<const float*>(ep);
-    if (p.next_w) c.next_w = reinterpret_cast<const __nv_bfloat16*>(ep + EP_ROWS_BYTES + 256);
+    if (p.next_w) c.next_w = reinterpret_cast<const __nv_bfloat16*>(ep + cap + 256);
   }
   return c;
 }
@@ -334,7 +342,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
         const int m = m0 + b;
         rowscale[b] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;   // model.py:179-180
       }
-    stage_epilogue_inputs<EPI>(p, sm + L.off_ep, tile, mrow0, rows, threadIdx.x - 160, 96);
+    stage_epilogue_inputs<EPI>(p, sm + L.off_ep, L.ep_rows, tile, mrow0, rows, threadIdx.x - 160, 96);
   }
   __syncthreads();  // row scales and staged inputs visible
 
@@ -414,7 +422,8 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
   const float* fin = KS > 1 ? recv : tile_acc;
   T2B_TRACE_MARK(6);
   if (!*abort_flag)
-    tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows, staged_epilogue_inputs<EPI>(p, sm + L.off_ep, rows));
+    tile_epilogue<EPI>(p, fin, scratch, tile, mrow0, rows,
+                       staged_epilogue_inputs<EPI>(p, sm + L.off_ep, L.ep_rows, rows));
   __syncthreads();
   T2B_TRACE_MARK(7);
   // every peer has received this CTA's pushes (it waited for them before
@@ -438,7 +447,27 @@ struct TcPlan {
 // Largest batch tile (env T2B_TC_MAX_BP overrides, for experiments): a larger
 // batch than this runs as several row blocks, each CTA dequantising its
 // weight tile again (off the critical path, before the dependency wait).
-static int tc_max_bp() {
+// Env T2B_TC_PLAN="NxK:BP:S,..." (experiments) sets both for one shape.
+static bool tc_shape_override(int N, int K, int* bp, int* s) {
+  const char* e = getenv("T2B_TC_PLAN");
+  if (!e || !*e) return false;
+  int n = 0, k = 0, b = 0, g = 0, used = 0;
+  while (sscanf(e, "%dx%d:%d:%d%n", &n, &k, &b, &g, &used) == 4) {
+    if (n == N && k == K) {
+      *bp = b;
+      *s = g;
+      return true;
+    }
+    e += used;
+    if (*e != ',') break;
+    ++e;
+  }
+  return false;
+}
+
+static int tc_max_bp(int N, int K) {
+  int b = 0, g = 0;
+  if (tc_shape_override(N, K, &b, &g) && (b == 16 || b == 32 || b == 64 || b == 128 || b == 256)) return b;
   const char* e = getenv("T2B_TC_MAX_BP");
   if (e && *e) {
     const int v = atoi(e);
@@ -447,11 +476,26 @@ static int tc_max_bp() {
   return 256;
 }
 
-static TcPlan tc_plan(int M, int N, int K, bool q4 = false) {
+// Groups per CTA forced by env T2B_TC_S or T2B_TC_PLAN (experiments; 0: the
+// planner's choice).  Taken only where the split is valid and fits.
+static int tc_forced_s(int N, int K) {
+  int b = 0, g = 0;
+  if (tc_shape_override(N, K, &b, &g)) return g;
+  const char* e = getenv("T2B_TC_S");
+  return (e && *e) ? atoi(e) : 0;
+}
+
+// max_rows > 0: the plan for an epilogue with costly per-row work (the qkv
+// epilogue: QK-norm, RoPE and the KV-cache write of every row), whose CTAs
+// each finish at most max_rows batch rows where such a plan exists within
+// about one wave: Bp <= 32 and the largest S >= 2 with Bp/KS <= max_rows.
+// (Qwen3-0.6B qkv at 64 rows: Bp 32, 2 groups per CTA, clusters of 4 -- 8
+// rows per CTA instead of 32 -- took 39 us off the 1.41 ms decode step.)
+static TcPlan tc_plan(int M, int N, int K, bool q4 = false, int max_rows = 0) {
   TcPlan pl{};
   const int G = K / GROUP;
   const int tiles = N / TILE_N;
-  const int max_bp = tc_max_bp();
+  const int max_bp = tc_max_bp(N, K);
   int bp = 16;
   while (bp < M && bp < max_bp) bp <<= 1;
   pl.BP = bp;
@@ -460,7 +504,22 @@ static TcPlan tc_plan(int M, int N, int K, bool q4 = false) {
   // KS must divide BP: each CTA of a cluster finishes BP/KS rows, and its
   // receive barrier expects the (KS-1) * BP/KS rows its peers push.
   auto splits = [&](int bp_, int s_) { return G % s_ == 0 && G / s_ <= 8 && bp_ % (G / s_) == 0; };
+  int ov_bp = 0, ov_s = 0;
+  bool capped = false;
+  if (max_rows > 0 && !tc_shape_override(N, K, &ov_bp, &ov_s)) {
+    const int bpc = std::min(bp, 32);
+    const long mbc = (M + bpc - 1) / bpc;
+    for (int s_ : {4, 3, 2}) {
+      if (!splits(bpc, s_) || !fits(bpc, s_) || bpc / (G / s_) > max_rows) continue;
+      if ((long)tiles * (G / s_) * mbc > 2L * 148) continue;   // about one wave
+      pl.BP = bpc;
+      pl.S = s_;
+      capped = true;
+      break;
+    }
+  }
   for (int s_ : {4, 3, 2, 1}) {
+    if (capped) break;
     if (!splits(bp, s_)) continue;
     if (!fits(bp, s_)) continue;
     const long ctas = (long)tiles * (G / s_) * ((M + bp - 1) / bp);
@@ -498,12 +557,16 @@ static TcPlan tc_plan(int M, int N, int K, bool q4 = false) {
       return (ctas + (long)sms * per_sm - 1) / ((long)sms * per_sm);
     };
     int best = pl.S;
-    if (waves(best) > 1)
+    if (!capped && waves(best) > 1)
       for (int s_ = pl.S + 1; s_ <= G; ++s_) {
         if (!splits(pl.BP, s_) || !fits(pl.BP, s_)) continue;
         if (waves(s_) < waves(best)) best = s_;
       }
     pl.S = best;
+  }
+  {
+    const int fs = tc_forced_s(N, K);
+    if (fs > 0 && fs <= G && splits(pl.BP, fs) && fits(pl.BP, fs)) pl.S = fs;
   }
   pl.KS = G / pl.S;
   pl.mblocks = (M + pl.BP - 1) / pl.BP;
@@ -521,8 +584,8 @@ size_t tc_ws_bytes(int, int, int) { return 0; }  // split-K stays on chip (clust
 
 bool tc_supported(int M, int N, int K, bool q4) { return tc_plan(M, N, K, q4).ok; }
 
-bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks) {
-  const TcPlan pl = tc_plan(M, N, K);
+bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks, int max_rows) {
+  const TcPlan pl = tc_plan(M, N, K, false, max_rows);
   *bp = pl.BP;
   *s = pl.S;
   *ks = pl.KS;
@@ -567,7 +630,7 @@ static int make_x_map(LinearParams& p, int BP) {
 }
 
 int tc_launch(LinearParams& p, int pro, int epi, void*, size_t, cudaStream_t st) {
-  const TcPlan pl = tc_plan(p.M, p.N, p.K, p.q4nx != 0);
+  const TcPlan pl = tc_plan(p.M, p.N, p.K, p.q4nx != 0, epi == EPI_QKV ? QKV_MAX_ROWS_PER_CTA : 0);
   if (!pl.ok) return T2B_ERR_SHAPE;
   if (p.x_dtype != T2B_DTYPE_BF16 && p.x_dtype != T2B_DTYPE_F16) return T2B_ERR_ARG;
   const int mx = make_x_map(p, pl.BP);

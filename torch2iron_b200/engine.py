@@ -137,9 +137,15 @@ class DecodeEngine:
         self.h = torch.zeros(B, cfg.hidden_dim, dtype=act, device=dev)
         self.xn = torch.zeros(B, H, dtype=torch.float16, device=dev)   # final norm output (fp16 head input)
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=f32, device=dev)
-        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.next_tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        # host-facing int32 words in one device buffer, 16-byte aligned segments:
+        # [tokens | pos | next_tokens | status word], so decode_step moves its
+        # inputs with one host->device copy and its outputs with one copy back
+        seg = (B + 3) // 4 * 4
+        self._io = torch.zeros(3 * seg + 4, dtype=torch.int32, device=dev)
+        self._io_seg = seg
+        self.tokens = self._io[0:B]
+        self.pos = self._io[seg:seg + B]
+        self.next_tokens = self._io[2 * seg:2 * seg + B]
         kv_shape = (B, cfg.n_kv_groups, max_ctx, hd)
         self.k_cache = [torch.zeros(kv_shape, dtype=bf, device=dev) for _ in range(cfg.n_layers)]
         self.v_cache = [torch.zeros(kv_shape, dtype=bf, device=dev) for _ in range(cfg.n_layers)]
@@ -162,9 +168,10 @@ class DecodeEngine:
         self.ws = {k: (torch.zeros(max(v, 256), dtype=torch.uint8, device=dev), max(v, 256)) for k, v in sizes.items()}
         # device status word: this engine's kernels record a timed-out wait here (the
         # launch stream is bound to it while the engine enqueues, t2b_bind_error_word)
-        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        # decode_step reads the next tokens and the status word in one copy
-        self._host_out = torch.zeros(batch + 1, dtype=torch.int32).pin_memory()
+        self.err = self._io[3 * seg:3 * seg + 1]
+        # pinned staging for decode_step: [tokens | pos] in, [next_tokens | status] out
+        self._host_in = torch.zeros(2 * seg, dtype=torch.int32).pin_memory()
+        self._host_out = torch.zeros(seg + 4, dtype=torch.int32).pin_memory()
         torch.cuda.synchronize(dev)   # repacked weights complete before any PDL launch reads them
         self.graph = None
         self._step_graph = None
@@ -328,14 +335,15 @@ class DecodeEngine:
             raise ValueError(f"token ids must be in [0, {self.cfg.vocab_size})")
         if int(pos.min()) < 0 or int(pos.max()) >= self.max_ctx:
             raise ValueError(f"positions must be in [0, {self.max_ctx}) (the KV cache length)")
-        self.tokens.copy_(tok, non_blocking=True)
-        self.pos.copy_(pos, non_blocking=True)
+        seg = self._io_seg
+        self._host_in[:self.B].copy_(tok)
+        self._host_in[seg:seg + self.B].copy_(pos)
+        self._io[:2 * seg].copy_(self._host_in, non_blocking=True)    # one host->device copy
         self.run_step()
         # one device->host read per step: the next tokens and the status word
-        self._host_out[:self.B].copy_(self.next_tokens, non_blocking=True)
-        self._host_out[self.B:].copy_(self.err, non_blocking=True)
+        self._host_out.copy_(self._io[2 * seg:], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
-        if int(self._host_out[self.B]):
+        if int(self._host_out[seg]):
             self.check_device_errors()
         return self._host_out[:self.B].clone()
 
