@@ -48,6 +48,9 @@ def attention_call(q, kc, vc, pos, n_heads, n_kv, hd, max_ctx, fn="t2b_decode_at
     (16, 16, 8, 128, 256, [130 + 7 * i for i in range(16)]),
     (8, 4, 1, 128, 1024, "ragged"),       # Qwen3-8B tensor-parallel shard: 4 q heads on 1 kv head
     (2, 8, 1, 128, 256, [255, 31]),       # 8 q heads per kv head
+    # long streams: the 2-stage ring, 3 CTAs per SM
+    (64, 16, 4, 128, 4160, "ragged"),     # Qwen3-8B tensor-parallel rank at TP2, context up to 4096
+    (32, 16, 8, 128, 2048, [2047] * 32),  # equal long units cut between CTAs
 ])
 def test_decode_attention_vs_oracle(B, nq, nkv, hd, ctx, positions):
     g = torch.Generator().manual_seed(407895018 + B + ctx)

@@ -81,19 +81,19 @@ struct AttnParams {
                                // dependency wait (the preceding kernel writes only q and key pos[m])
 };
 
-template <int HD>
+template <int HD, int ST>
 struct AtGeom {
   static constexpr int HALVES = HD / 64;                 // 128-byte swizzle spans per key row
-  static constexpr int STAGES = HD >= 128 ? 3 : 4;
+  static constexpr int STAGES = ST;
   static constexpr int HALF_BYTES = AT_TILE * 128;       // 64 keys x 64 dims
   static constexpr int KV_BYTES = HALVES * HALF_BYTES;   // K (or V) of one tile
   static constexpr int STAGE_BYTES = 2 * KV_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
 };
 
-template <int HD, int QPG>
+template <int HD, int QPG, int ST>
 struct AttnAux {
-  static constexpr int STAGES = AtGeom<HD>::STAGES;
+  static constexpr int STAGES = ST;
   float qb[STAGES][QPG * HD];          // q heads of a unit (fp32, or bf16 in the first half), copied with the unit's first tile
   __nv_bfloat16 msk[STAGES][AT_TILE];
   float ow[AT_WARPS][QPG][HD];         // per-warp (o, max, sum) at a unit's end
@@ -108,9 +108,9 @@ struct AttnAux {
   uint64_t bar[STAGES];
 };
 
-template <int HD, int QPG>
+template <int HD, int QPG, int ST>
 constexpr size_t attn_smem_bytes() {
-  return 1024 + AtGeom<HD>::RING_BYTES + sizeof(AttnAux<HD, QPG>);
+  return 1024 + AtGeom<HD, ST>::RING_BYTES + sizeof(AttnAux<HD, QPG, ST>);
 }
 
 struct TileRef {
@@ -187,10 +187,10 @@ struct SplitUnit {
   int m, h, t0, c1, c2;
 };
 
-template <int HD, int QPG>
+template <int HD, int QPG, int ST>
 __global__ void __launch_bounds__(AT_THREADS) decode_attention_kernel(const __grid_constant__ AttnParams P) {
-  using G = AtGeom<HD>;
-  using Aux = AttnAux<HD, QPG>;
+  using G = AtGeom<HD, ST>;
+  using Aux = AttnAux<HD, QPG, ST>;
   constexpr int STAGES = G::STAGES;
   constexpr int NT16 = HD / 16;  // k-steps of K.q^T, and 16-dim m-tiles of O^T
   constexpr int REC = HD + 2;
@@ -681,10 +681,10 @@ static int make_kv_maps(AttnParams& P, const void* k, const void* v, int hd, lon
 
 // One wave: as many CTAs as are resident at once (capped by the tile count
 // and the workspace bound).
-template <int HD, int QPG>
+template <int HD, int QPG, int ST>
 static int attn_launch_t(AttnParams& P, int max_grid, cudaStream_t st) {
-  auto kern = decode_attention_kernel<HD, QPG>;
-  const size_t smem = attn_smem_bytes<HD, QPG>();
+  auto kern = decode_attention_kernel<HD, QPG, ST>;
+  const size_t smem = attn_smem_bytes<HD, QPG, ST>();
   if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, AT_THREADS, smem) != cudaSuccess || per_sm < 1)
@@ -698,6 +698,18 @@ static int attn_launch_t(AttnParams& P, int max_grid, cudaStream_t st) {
     if (cap > 0) grid = std::min(grid, cap);
   }
   return launch_pdl(kern, dim3(grid), dim3(AT_THREADS), smem, st, P);
+}
+
+// Ring depth of the head_dim-128 kernel.  3 stages of 32 KB (2 CTAs per SM)
+// while a CTA streams few tiles: at short contexts the loads issued before
+// the dependency wait and whole units per CTA decide the time (Qwen3-0.6B,
+// 64 rows, context 190: 16.7 us against 21.5 us with 2 stages).  2 stages
+// (3 CTAs, 12 warps per SM) for long streams, where the tile math -- two
+// score and two P.V MMAs per 16-key slice -- needs the extra warps to keep
+// pace with the copies (Qwen3-8B, 64 rows, context 4096: 181 us against 334
+// us, 5.9 TB/s).  max_keys (the cache length) stands in for the context.
+static int attn_stages_hd128(int rows, int n_kv, int max_keys) {
+  return max_tiles(rows, n_kv, max_keys) >= 12LL * 2 * sm_count() ? 2 : 3;
 }
 
 // max_keys: upper bound on keys per row (sizes the grid and the workspace).
@@ -715,10 +727,12 @@ int attention_launch(AttnParams& P, int rows, int head_dim, int max_keys, void* 
   P.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + part);
   P.rows = rows;
   P.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
-#define T2B_ACASE(hd, qpg_) \
-  if (head_dim == hd && qpg == qpg_) return attn_launch_t<hd, qpg_>(P, grid, st);
-  T2B_ACASE(128, 1) T2B_ACASE(128, 2) T2B_ACASE(128, 4) T2B_ACASE(128, 8)
-  T2B_ACASE(64, 1) T2B_ACASE(64, 2) T2B_ACASE(64, 4) T2B_ACASE(64, 8)
+  const int st128 = attn_stages_hd128(rows, P.n_kv, max_keys);
+#define T2B_ACASE(hd, qpg_, st_) \
+  if (head_dim == hd && qpg == qpg_ && (hd == 64 || st128 == st_)) return attn_launch_t<hd, qpg_, st_>(P, grid, st);
+  T2B_ACASE(128, 1, 3) T2B_ACASE(128, 2, 3) T2B_ACASE(128, 4, 3) T2B_ACASE(128, 8, 3)
+  T2B_ACASE(128, 1, 2) T2B_ACASE(128, 2, 2) T2B_ACASE(128, 4, 2) T2B_ACASE(128, 8, 2)
+  T2B_ACASE(64, 1, 4) T2B_ACASE(64, 2, 4) T2B_ACASE(64, 4, 4) T2B_ACASE(64, 8, 4)
 #undef T2B_ACASE
   return T2B_ERR_SHAPE;
 }
