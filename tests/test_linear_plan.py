@@ -44,8 +44,8 @@ def test_plans_cover_k_and_split_the_batch_tile_evenly(cfg, tp):
             st, (path, rows, groups, ks) = _plan(m, n, k, qkv)
             assert st == _lib.T2B_OK, (name, m, n, k)
             assert groups * ks * 128 == k, (name, m, n, k, rows, groups, ks)
-            if path == 2:
-                assert m >= 257 and rows == 128 and ks == 1
+            if path == 2:   # prefill chunks, or decode batches on linears too wide for one tcgen05 wave
+                assert rows == 128 and ks == 1 and (m >= 257 or (m >= 16 and not qkv))
             elif path == 1:
                 assert rows in (16, 32, 64, 128, 256) and 1 <= ks <= 8 and rows % ks == 0, (name, m, n, k, rows, ks)
             else:
@@ -64,6 +64,18 @@ def test_qkv_plan_caps_rows_per_cta():
     assert _plan(64, 4096, 1024) == (_lib.T2B_OK, (1, 64, 4, 2))
     for m in (1, 8):   # the CUDA-core path is the same plan
         assert _plan(m, 4096, 1024, qkv=True) == _plan(m, 4096, 1024)
+
+
+def test_wide_decode_linears_take_the_large_m_kernel():
+    """Qwen3-8B gate/up (N 24576) and down (K 12288) at 64 rows: the tcgen05 decode grid
+    would run 1536 / 1024 CTAs of one weight-tile slice each; the persistent large-M kernel
+    streams whole tiles instead.  o_proj (256 CTAs) stays on the decode kernel, and the fused
+    qkv (fp32 q) never moves."""
+    assert _plan(64, 24576, 4096)[1][0] == 2
+    assert _plan(64, 4096, 12288)[1][0] == 2
+    assert _plan(64, 4096, 4096)[1][0] == 1
+    assert _plan(64, 24576, 4096, qkv=True)[1][0] == 1
+    assert _plan(8, 24576, 4096)[1][0] == 1    # fewer than 16 rows stay on the decode kernel
 
 
 def test_plan_rejects_bad_shapes():

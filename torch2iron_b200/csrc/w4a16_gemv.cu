@@ -363,6 +363,7 @@ int tc_launch(LinearParams& p, int pro, int epi, void* ws, size_t ws_bytes, cuda
 size_t tc_ws_bytes(int M, int N, int K);
 bool tc_supported(int M, int N, int K, bool q4);
 bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks, int max_rows);
+long tc_grid_ctas(int M, int N, int K, bool q4);
 
 // Rows at or above this count take the tcgen05 path (env T2B_TC_MIN_M overrides).
 static int tc_min_m() {
@@ -384,6 +385,24 @@ static bool half_act(int x_dtype) { return x_dtype == T2B_DTYPE_BF16 || x_dtype 
 
 static bool use_prefill(int M, int wfmt, int x_dtype) {
   return tiled_wfmt(wfmt) && half_act(x_dtype) && M >= prefill_min_m();
+}
+
+// A decode batch on a linear so wide that the tcgen05 decode grid runs more
+// than two waves of CTAs (each CTA holds one weight tile's k-slice and runs
+// once): the large-M kernel's persistent CTAs stream whole weight tiles
+// instead (Qwen3-8B at 64 rows: gate/up 115 -> 51 us, down 118 -> 71 us; the
+// tensor-parallel rank at TP2: gate/up 60 -> 29 us, down 43 -> 39 us).  Not
+// for the qkv epilogue, whose fp32 q output the large-M kernel does not
+// write.  Env T2B_WIDE_MIN_CTAS sets the threshold (experiments; a negative
+// value turns the rule off).
+static bool use_prefill_wide(int M, int N, int K, int wfmt, int x_dtype, int epi) {
+  if (epi == EPI_QKV || M < 16 || !tiled_wfmt(wfmt) || !half_act(x_dtype)) return false;
+  long min_ctas = 2L * 148;
+  if (const char* e = getenv("T2B_WIDE_MIN_CTAS")) {
+    if (*e) min_ctas = atol(e);
+  }
+  if (min_ctas < 0) return false;
+  return tc_grid_ctas(M, N, K, wfmt == T2B_WFMT_Q4NX) > min_ctas;
 }
 
 static bool use_tc(int M, int N, int K, int wfmt, int x_dtype) {
@@ -419,6 +438,7 @@ int linear_launch(LinearParams& p, int pro, int epi, int wfmt, void* ws, size_t 
   if (p.N % TILE_N || p.K % 256) return T2B_ERR_SHAPE;
   p.G = p.K / GROUP;
   if (use_prefill(p.M, wfmt, p.x_dtype)) return prefill_launch(p, pro, epi, st);
+  if (use_prefill_wide(p.M, p.N, p.K, wfmt, p.x_dtype, epi)) return prefill_launch(p, pro, epi, st);
   if (use_tc(p.M, p.N, p.K, wfmt, p.x_dtype)) return tc_launch(p, pro, epi, ws, ws_bytes, st);
   return gemv_launch(p, pro, epi, wfmt, ws, ws_bytes, st);
 }
@@ -448,7 +468,8 @@ static int linear_plan(int M, int N, int K, int max_rows, int* path, int* rows_p
                        int* ksplit) {
   if (!path || !rows_per_cta || !groups_per_cta || !ksplit) return T2B_ERR_ARG;
   if (M < 1 || N <= 0 || K <= 0 || N % TILE_N || K % 256) return T2B_ERR_SHAPE;
-  if (use_prefill(M, T2B_WFMT_T2B, T2B_DTYPE_BF16)) {   // one weight tile x 128 rows per work unit, all of K
+  if (use_prefill(M, T2B_WFMT_T2B, T2B_DTYPE_BF16) ||   // one weight tile x 128 rows per work unit, all of K
+      (max_rows == 0 && use_prefill_wide(M, N, K, T2B_WFMT_T2B, T2B_DTYPE_BF16, EPI_STORE))) {
     *path = 2;
     *rows_per_cta = 128;
     *groups_per_cta = K / GROUP;

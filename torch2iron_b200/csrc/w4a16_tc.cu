@@ -584,6 +584,12 @@ size_t tc_ws_bytes(int, int, int) { return 0; }  // split-K stays on chip (clust
 
 bool tc_supported(int M, int N, int K, bool q4) { return tc_plan(M, N, K, q4).ok; }
 
+// CTAs of the tcgen05 decode grid for this shape (0 when the path cannot take it).
+long tc_grid_ctas(int M, int N, int K, bool q4) {
+  const TcPlan pl = tc_plan(M, N, K, q4);
+  return pl.ok ? (long)(N / TILE_N) * pl.KS * pl.mblocks : 0;
+}
+
 bool tc_plan_info(int M, int N, int K, int* bp, int* s, int* ks, int max_rows) {
   const TcPlan pl = tc_plan(M, N, K, false, max_rows);
   *bp = pl.BP;
