@@ -229,10 +229,10 @@ def run_reference(args, cfg):
 # ---------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode_attention_kernel<128, 2> launch
-# captured with ncu on this workload (64 rows x 8 kv heads, ctx 133: 144 keys loaded per unit).
-NCU_ATTN = {"dram_bytes": 38_076_672 + 4_096, "units": 64 * 8, "keys_loaded": 144, "head_dim": 128,
-            "source": "ncu capture, profiles/decode_attention_qwen3_0.6b_bs64_ctx133.md, scaled by keys loaded"}
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_attention_kernel<128, 2, 3> launch
+# captured with ncu on this workload (64 rows x 8 kv heads, ctx 182: 192 keys loaded per unit).
+NCU_ATTN = {"dram_bytes": 50_922_496 + 78_336, "units": 64 * 8, "keys_loaded": 192, "head_dim": 128,
+            "source": "ncu capture, profiles/decode_attention_qwen3_0.6b_bs64_ctx182.md, scaled by keys loaded"}
 
 
 def gemv_batch1(eng, peak, n_streams: int = 1):
@@ -586,11 +586,17 @@ def run_t2b(args, cfg):
         kv_tok = 2 * cfg.n_kv_groups * cfg.head_dim * 2
         l0 = eng.layers[0]
         kernel_bytes = {
-            "decode_attention": B * ctx0 * kv_tok + 2 * B * cfg.q_dim * 2,
-            "qkv_norm_rope_kvwrite": l0.qkv.nbytes_algorithmic + B * cfg.emb_dim * 4 + B * (cfg.q_dim + 2 * cfg.kv_dim) * 2,
-            "oproj_residual": l0.o_proj.nbytes_algorithmic + B * cfg.q_dim * 2 + 2 * B * cfg.emb_dim * 4,
-            "upgate_swiglu": l0.gate_up.nbytes_algorithmic + B * cfg.emb_dim * 4 + B * cfg.hidden_dim * 2,
-            "down_residual": l0.down.nbytes_algorithmic + B * cfg.hidden_dim * 2 + 2 * B * cfg.emb_dim * 4,
+            # K+V of the attended keys, fp32 q in, fp16 output
+            "decode_attention": B * ctx0 * kv_tok + B * cfg.q_dim * (4 + 2),
+            # weights, fp16 norm input in, fp32 q and bf16 k / v out
+            "qkv_norm_rope_kvwrite": l0.qkv.nbytes_algorithmic + B * cfg.emb_dim * 2
+                                     + B * (cfg.q_dim * 4 + 2 * cfg.kv_dim * 2),
+            # weights, fp16 input, fp32 residual read and written, fp16 next-norm input out
+            "oproj_residual": l0.o_proj.nbytes_algorithmic + B * cfg.q_dim * 2 + 2 * B * cfg.emb_dim * 4
+                              + B * cfg.emb_dim * 2,
+            "upgate_swiglu": l0.gate_up.nbytes_algorithmic + B * cfg.emb_dim * 2 + B * cfg.hidden_dim * 2,
+            "down_residual": l0.down.nbytes_algorithmic + B * cfg.hidden_dim * 2 + 2 * B * cfg.emb_dim * 4
+                             + B * cfg.emb_dim * 2,
             "lm_head_argmax": eng.lm_head.numel() * 2 + B * cfg.emb_dim * 2 + B * 4,
         }
         dur_ms = prof[dom][0]
@@ -606,7 +612,7 @@ def run_t2b(args, cfg):
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int4-weights/bf16-activations/fp32-accumulate",
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4-weights/fp16-activations/fp32-accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random prompt ids)",
             "config": arm_config(args, world),
             "hbm": {"algorithmic_bytes_per_step": int(avg_bytes),
@@ -814,7 +820,7 @@ def run_tp(args, cfg):
         dist.barrier()
         dist.destroy_process_group()
     if line is not None:
-        line.update(higher_is_better=True, vs_baseline=None, dtype="int4-weights/bf16-activations/fp32-accumulate",
+        line.update(higher_is_better=True, vs_baseline=None, dtype="int4-weights/fp16-activations/fp32-accumulate",
                     data="synthetic (seeded N(0,0.02) weights, N(0,1) bf16 KV pre-fill, uniform-random token ids)")
         print(json.dumps(line), flush=True)
         if line["device_status"]:

@@ -232,7 +232,7 @@ T2B_DEV float4 ld_dsmem_f4(uint32_t addr) {
 #ifdef T2B_TRACE
 namespace t2b {
 struct TraceRec {
-  unsigned long long t[8];
+  unsigned long long t[12];
   int tag, bx, by, bz, nblocks, key, pad0, pad1;
 };
 constexpr int TRACE_CAP = 1 << 15;
@@ -242,7 +242,7 @@ static __device__ TraceRec g_trace[TRACE_CAP];
 static __device__ unsigned int g_trace_n;
 }  // namespace t2b
 // Defines the unit's read-back entry point: copies up to max_records records
-// (96 bytes each) to host `dst`, returns the count, resets if `reset`.
+// (128 bytes each) to host `dst`, returns the count, resets if `reset`.
 #define T2B_TRACE_DUMP_FN(fname)                                                                          \
   extern "C" __attribute__((visibility("default"))) int fname(void* dst, int max_records, int reset) {    \
     unsigned int n = 0;                                                                                   \
@@ -269,12 +269,15 @@ static __device__ unsigned int g_trace_n;
     r_.bz = blockIdx.z;                                                                          \
     r_.nblocks = gridDim.x * gridDim.y * gridDim.z;                                              \
     r_.key = (keyv);                                                                             \
-    for (int i_ = 0; i_ < 8; ++i_) r_.t[i_] = 0;                                                 \
+    for (int i_ = 0; i_ < 12; ++i_) r_.t[i_] = 0;                                                \
     r_.t[0] = t2b::globaltimer_ns();                                                             \
   }
 #define T2B_TRACE_MARK(phase) \
   if (threadIdx.x == 0) t2b::g_trace[t2b_trace_slot].t[(phase)] = t2b::globaltimer_ns();
+// Stamp from whichever thread executes it (the caller picks one thread).
+#define T2B_TRACE_STAMP(phase) t2b::g_trace[t2b_trace_slot].t[(phase)] = t2b::globaltimer_ns();
 #else
+#define T2B_TRACE_STAMP(phase)
 #define T2B_TRACE_BEGIN(tagv, keyv)
 #define T2B_TRACE_MARK(phase)
 #define T2B_TRACE_DUMP_FN(fname)

@@ -314,6 +314,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
         for (int atom = 0; atom < 2; ++atom)
           tma_load_2d(xs + gl * L.x_group + atom * (BP * 128), &p.xmap, (g0 + gl) * GROUP + atom * 64, m0, x_full);
       bool ok = mbar_wait_bounded(x_full, 0, p.err);
+      T2B_TRACE_STAMP(8);   // activations in shared memory
       for (int gl = 0; ok && gl < S; ++gl) {
         const int stage = gl % NA;
         if (!mbar_wait_bounded(&a_full[stage], (gl / NA) & 1, p.err)) {
@@ -331,6 +332,7 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
       }
       if (!ok) *abort_flag = 1;
       mma_commit(acc_full);
+      T2B_TRACE_STAMP(9);   // every MMA issued
     }
     __syncwarp();
   } else {
@@ -342,7 +344,9 @@ __global__ void __launch_bounds__(256, 2) w4a16_tc_kernel(const __grid_constant_
         const int m = m0 + b;
         rowscale[b] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;   // model.py:179-180
       }
+    if (threadIdx.x == 160) T2B_TRACE_STAMP(10);   // row scales written
     stage_epilogue_inputs<EPI>(p, sm + L.off_ep, L.ep_rows, tile, mrow0, rows, threadIdx.x - 160, 96);
+    if (threadIdx.x == 160) T2B_TRACE_STAMP(11);   // this thread's epilogue inputs staged
   }
   __syncthreads();  // row scales and staged inputs visible
 
