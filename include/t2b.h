@@ -336,6 +336,28 @@ T2B_API int t2b_residual_norm_input(const void* y, int y_dtype, float* x_resid, 
                                     const uint16_t* next_norm_w, uint16_t* xw_out, int M, int H, void* stream);
 
 /*
+ * The same residual step fused with the tensor-parallel all-reduce it
+ * follows, over peer memory (NVLink), in place of an NCCL all-reduce and
+ * t2b_residual_norm_input.  partials[q] (q < world) is rank q's partial
+ * buffer [M][H] (y_dtype bf16 or fp32) as this process maps it (a peer
+ * pointer for q != rank); flags[q] is rank q's array of `world` int32 flag
+ * words, zeroed before the first call; state is this rank's
+ * t2b_tp_allreduce_state_bytes() of zeroed device memory.  Each rank signals
+ * its partial complete in every peer's flag words, waits (at most 0.5 s,
+ * then T2B_ERR_TIMEOUT in the stream's status word) for every peer's signal
+ * of the same call, and sums the partials in rank order in fp32, so every
+ * rank computes the same residual.  Every rank must make the same sequence
+ * of calls; a partial buffer may be rewritten two calls later at the
+ * earliest (alternate two buffers).  No counterpart in the reference (its NPU
+ * path runs on one device).
+ */
+T2B_API size_t t2b_tp_allreduce_state_bytes(void);
+T2B_API int t2b_tp_allreduce_residual_norm_input(const void* const* partials, int y_dtype, int32_t* const* flags,
+                                                 int32_t* state, int rank, int world, float* x_resid,
+                                                 float* ssq_out, const uint16_t* next_w, void* xw_out, int M, int H,
+                                                 void* stream);
+
+/*
  * Greedy lm_head: idx[m] = argmax_v (xn[m] . lm_head[v]) over V rows of a bf16
  * [V][H] table (tied embedding or untied head), fp32 accumulation; ties to
  * the lowest index (torch.argmax).  max_logit [M] (may be NULL) receives the

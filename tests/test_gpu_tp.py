@@ -1,6 +1,7 @@
-"""Tensor-parallel decode on 2 GPUs (NCCL) against the single-GPU engine on the
-same model: same greedy tokens and residual stream after a prefill.  Skipped
-when fewer than 2 GPUs are visible."""
+"""Tensor-parallel decode on 2 GPUs against the single-GPU engine on the same
+model: same greedy tokens and residual stream after a prefill, with the
+partials summed by the peer-memory kernel (t2b_tp_allreduce_residual_norm_input)
+or by NCCL.  Skipped when fewer than 2 GPUs are visible."""
 
 import os
 import socket
@@ -23,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, batch, partial, out_q):
+def _rank(rank, world, port, batch, partial, collective, out_q):
     import torch.distributed as dist
     from torch2iron_b200 import synth
     from torch2iron_b200.engine import DecodeEngine
@@ -37,7 +38,7 @@ def _rank(rank, world, port, batch, partial, out_q):
         res = {}
         for mode in ("eager", "graph"):
             eng = TPDecodeEngine(CFG, model, batch=batch, max_ctx=64, tp=world, rank=rank, use_graph=mode == "graph",
-                                 partial_dtype=getattr(torch, partial))
+                                 partial_dtype=getattr(torch, partial), collective=collective)
             eng.prefill(prompts)
             toks = [eng.next_tokens.cpu().clone()]
             for _ in range(3):
@@ -60,16 +61,18 @@ def _rank(rank, world, port, batch, partial, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("batch,partial", [(1, "bfloat16"), (5, "bfloat16"), (5, "float32")])
-def test_tp2_engine_matches_single_gpu(batch, partial):
+@pytest.mark.parametrize("batch,partial,collective", [(1, "bfloat16", "p2p"), (5, "bfloat16", "p2p"),
+                                                      (5, "float32", "p2p"), (5, "bfloat16", "nccl")])
+def test_tp2_engine_matches_single_gpu(batch, partial, collective):
     """bf16 row-parallel partials (the default, half the all-reduce bytes) and
-    fp32 ones both hold the single-GPU engine's tokens and residual stream."""
+    fp32 ones both hold the single-GPU engine's tokens and residual stream,
+    summed over peer memory (the default) or by an NCCL all-reduce."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, partial, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, partial, collective, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))

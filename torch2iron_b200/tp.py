@@ -20,10 +20,16 @@ decoder layer (``model.py:240-327``):
 Every split falls on a 128-wide quantization group (``H/tp``, ``I/tp`` and
 the head blocks are multiples of 128), so no scale or zero point is split.
 The residual stream, embedding and norms are replicated.  The two row-parallel
-partials per layer meet in an NCCL all-reduce on the decode stream (bf16
-partials by default, ``[B, H]`` = 512 KiB at 64 rows of Qwen3-8B; fp32 on
-request), followed by ``t2b_residual_norm_input``, which adds the sum into the
-fp32 residual stream.
+partials per layer (bf16 by default, ``[B, H]`` = 512 KiB at 64 rows of
+Qwen3-8B; fp32 on request) are summed across ranks and added into the fp32
+residual stream by one of:
+
+* ``collective="p2p"``: ``t2b_tp_allreduce_residual_norm_input``, one
+  kernel that signals and reads the peers' partials over NVLink (peer-mapped
+  buffers from ``torch.distributed._symmetric_memory``) and does the residual
+  step; o_proj and down write alternate partial buffers;
+* ``collective="nccl"`` (default): an NCCL all-reduce on the decode stream followed by
+  ``t2b_residual_norm_input``.
 """
 
 from __future__ import annotations
@@ -121,7 +127,8 @@ class TPDecodeEngine:
     """
 
     def __init__(self, cfg, model: dict, batch: int, max_ctx: int, tp: int, rank: int, group=None,
-                 device="cuda", use_graph: bool = False, partial_dtype: torch.dtype = torch.bfloat16):
+                 device="cuda", use_graph: bool = False, partial_dtype: torch.dtype = torch.bfloat16,
+                 collective: str = "nccl"):
         import torch.distributed as dist
         from . import _lib
         from . import weights as W
@@ -134,6 +141,9 @@ class TPDecodeEngine:
         if partial_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("the row-parallel partials are bf16 or fp32")
         self.partial_dtype = partial_dtype
+        if collective not in ("p2p", "nccl"):
+            raise ValueError("collective is 'p2p' or 'nccl'")
+        self.collective = collective
         if max_ctx % 64:
             raise ValueError("max_ctx must be a multiple of 64")
         dev, lc = self.device, self.lcfg
@@ -158,7 +168,10 @@ class TPDecodeEngine:
         B, H, hd = batch, cfg.emb_dim, cfg.head_dim
         f32, bf = torch.float32, torch.bfloat16
         self.x = torch.zeros(B, H, dtype=f32, device=dev)
-        self.y = torch.zeros(B, H, dtype=partial_dtype, device=dev)   # row-parallel partial, all-reduced in place
+        if collective == "p2p":
+            self._setup_p2p(B, H, partial_dtype)
+        else:   # one partial, all-reduced in place
+            self.y_bufs = [torch.zeros(B, H, dtype=partial_dtype, device=dev)] * 2
         act = _lib.ACT                                            # fp16 linear inputs (t2b.h)
         self.xw = torch.zeros(B, H, dtype=act, device=dev)
         self.ssq_a = torch.zeros(B, dtype=f32, device=dev)
@@ -201,12 +214,52 @@ class TPDecodeEngine:
     def next_norm_weight(self, li: int) -> torch.Tensor:
         return self.layers[li + 1].input_layernorm if li + 1 < len(self.layers) else self.final_norm
 
-    def _allreduce_residual(self, ssq_out, next_w):
+    def _setup_p2p(self, B, H, dtype) -> None:
+        """Peer-mapped partial buffers (two: o_proj and down alternate) and flag words."""
+        import ctypes as C
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+        group = self.group if self.group is not None else self.dist.group.WORLD
+        name = group.group_name
+        if hasattr(symm_mem, "enable_symm_mem_for_group"):
+            try:
+                symm_mem.enable_symm_mem_for_group(name)
+            except Exception:   # already enabled, or not needed by this torch version
+                pass
+        dev, tp = self.device, self.tp
+        self.y_bufs, ptrs = [], []
+        for _ in range(2):
+            t = symm_mem.empty((B, H), dtype=dtype, device=dev)
+            t.zero_()
+            hdl = symm_mem.rendezvous(t, name)
+            self.y_bufs.append(t)
+            ptrs.append((C.c_void_p * tp)(*[int(q) for q in hdl.buffer_ptrs]))
+            self._p2p_keep = getattr(self, "_p2p_keep", []) + [hdl]
+        flags = symm_mem.empty((tp,), dtype=torch.int32, device=dev)
+        flags.zero_()
+        fh = symm_mem.rendezvous(flags, name)
+        flag_ptrs = (C.c_void_p * tp)(*[int(q) for q in fh.buffer_ptrs])
+        self._p2p = {"parts": [C.addressof(a) for a in ptrs], "flags": C.addressof(flag_ptrs),
+                     "keep": [ptrs, flag_ptrs, flags, fh],
+                     "state": torch.zeros(max(_lib.load().t2b_tp_allreduce_state_bytes(), 16) // 4,
+                                          dtype=torch.int32, device=dev)}
+        torch.cuda.synchronize(dev)
+        self.dist.barrier(group=group)   # every rank's flags are zero before anyone signals
+
+    def _allreduce_residual(self, which, ssq_out, next_w):
         lib, p = self._lib, self._lib.ptr
-        self.dist.all_reduce(self.y, group=self.group)
+        if self.collective == "p2p":
+            q = self._p2p
+            lib.check("t2b_tp_allreduce_residual_norm_input", lib.lib().t2b_tp_allreduce_residual_norm_input(
+                q["parts"][which], lib.DTYPE[self.partial_dtype], q["flags"], p(q["state"]), self.rank, self.tp,
+                p(self.x), p(ssq_out), p(next_w), p(self.xw), self.B, self.cfg.emb_dim, lib.stream()))
+            return
+        self.dist.all_reduce(self.y_bufs[which], group=self.group)
         lib.check("t2b_residual_norm_input", lib.lib().t2b_residual_norm_input(
-            p(self.y), lib.DTYPE[self.partial_dtype], p(self.x), p(ssq_out), p(next_w), p(self.xw), self.B,
-            self.cfg.emb_dim, lib.stream()))
+            p(self.y_bufs[which]), lib.DTYPE[self.partial_dtype], p(self.x), p(ssq_out), p(next_w), p(self.xw),
+            self.B, self.cfg.emb_dim, lib.stream()))
 
     def enqueue_layer(self, li: int) -> None:
         cfg, lc, B = self.cfg, self.lcfg, self.B
@@ -223,16 +276,16 @@ class TPDecodeEngine:
             lib.DTYPE[lib.ACT], B,
             nq, nkv, hd, self.max_ctx, *self._ws("attn"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-            p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[lib.ACT], p(self.y),
+            p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[lib.ACT], p(self.y_bufs[0]),
             lib.DTYPE[self.partial_dtype], B, H, lc.q_dim, 128, *self._ws("o"), st))
-        self._allreduce_residual(self.ssq_b, lw.post_attention_layernorm)
+        self._allreduce_residual(0, self.ssq_b, lw.post_attention_layernorm)
         lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
             p(lw.gate_up.qw), p(lw.gate_up.meta), lw.gate_up.fmt, p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
             p(self.ssq_a), B, H, lc.hidden_dim, *self._ws("ug"), st))
         lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-            p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[lib.ACT], p(self.y),
+            p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[lib.ACT], p(self.y_bufs[1]),
             lib.DTYPE[self.partial_dtype], B, H, lc.hidden_dim, 128, *self._ws("down"), st))
-        self._allreduce_residual(self.ssq_a, self.next_norm_weight(li))
+        self._allreduce_residual(1, self.ssq_a, self.next_norm_weight(li))
 
     def enqueue_step(self) -> None:
         with self._lib.status_word(self.err, self._lib.stream()):
