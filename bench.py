@@ -61,6 +61,9 @@ def parse():
                          "the batch is then the global batch")
     ap.add_argument("--ctx", type=int, default=4096, help="--tp: KV cache pre-filled to this many positions")
     ap.add_argument("--tp-eager", action="store_true", help="--tp: launch every step eagerly (no CUDA graph)")
+    ap.add_argument("--tp-collective", default="nccl", choices=["nccl", "p2p"],
+                    help="tensor parallel: sum the row-parallel partials by NCCL all-reduce, or by the "
+                         "peer-memory kernel fused with the residual step")
     ap.add_argument("--prefill-only", action="store_true",
                     help="one GPU: time the chunked prefill of --batch x --prompt tokens only (profiling case)")
     return ap.parse_args()
@@ -724,7 +727,8 @@ def tp_measure(args, cfg, world, rank, local, batch, ctx) -> dict | None:
     B, C = batch, ctx
     max_ctx = ((C + args.warmup + args.steps + 1 + 63) // 64) * 64
     model = synth.random_model(cfg, seed=args.seed, device="cuda")
-    eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank, use_graph=not args.tp_eager)
+    eng = TPDecodeEngine(cfg, model, batch=B, max_ctx=max_ctx, tp=world, rank=rank, use_graph=not args.tp_eager,
+                         collective=args.tp_collective)
     del model
     torch.cuda.empty_cache()
     g = torch.Generator(device="cuda").manual_seed(args.seed * 1000 + 7 + rank)
@@ -789,6 +793,8 @@ def tp_measure(args, cfg, world, rank, local, batch, ctx) -> dict | None:
             "gpu_launches": eng.kernels_per_step() * steps,
             "collectives_per_step": 2 * cfg.n_layers + 2,
             "allreduce_dtype": str(eng.partial_dtype).replace("torch.", ""),
+            "allreduce": {"nccl": "NCCL all-reduce + t2b_residual_norm_input",
+                          "p2p": "t2b_tp_allreduce_residual_norm_input (peer-memory loads over NVLink)"}[eng.collective],
             "device_status": status,
             "clocks": clocks.summary(),
         }
