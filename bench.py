@@ -235,6 +235,7 @@ def run_reference(args, cfg):
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_attention_kernel<128, 2, 3> launch
 # captured with ncu on this workload (64 rows x 8 kv heads, ctx 182: 192 keys loaded per unit).
 NCU_ATTN = {"dram_bytes": 50_922_496 + 78_336, "units": 64 * 8, "keys_loaded": 192, "head_dim": 128,
+            "cold_us": 20.80, "cold_ctx": 182,
             "source": "ncu capture, profiles/decode_attention_qwen3_0.6b_bs64_ctx182.md, scaled by keys loaded"}
 
 
@@ -630,6 +631,11 @@ def run_t2b(args, cfg):
                          "timing": "per launch in a CUDA graph of the op over all layers in turn (different "
                                    "weights and KV caches each launch; PDL-chained as in the step), 5 replays, "
                                    "CUDA events on the capture stream",
+                         "ncu_cold_launch": ({"us": NCU_ATTN["cold_us"], "ctx": NCU_ATTN["cold_ctx"],
+                                              "frac": round(kernel_bytes[dom] / (NCU_ATTN["cold_us"] * 1e-6) / 1e9 / peak, 4),
+                                              "note": "the same launch in the decode step under ncu: cold cache, "
+                                                      "serialised, no overlap with the qkv kernel"}
+                                             if traffic is not None else None),
                          "kernel_avg_us": {k: round(v[0] * 1000, 2) for k, v in prof.items()},
                          "kernel_eager_us": {k: round(v[0] * 1000, 2) for k, v in eager.items()}},
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * B * 4,
