@@ -6,7 +6,9 @@ bf16 embedding/lm_head, random N(0,0.02) weights quantized int4 g128
 per GPU, greedy decode.  The prompt is prefilled (untimed), ``--warmup``
 decode steps run untimed, then ``--steps`` decode steps are timed.  One step
 = one new token for every row.  Multi-GPU (torchrun): data parallel, every
-rank decodes its own 64 rows (weak scaling, no collective on the data path).
+rank decodes its own 64 rows (weak scaling, no collective on the data path);
+the N>1 line also carries configuration 4 (Qwen3-8B, 64 rows, ctx 4096)
+tensor parallel over the same ranks under ``tp``.
 
 Prints one JSON line on rank 0.  ``--impl reference`` times the reference
 algorithm on the host CPU instead (the oracle restatement of

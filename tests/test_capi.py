@@ -130,3 +130,33 @@ def test_status_word_bindings_are_per_stream_and_per_thread():
     assert word_for(s1) == wd
     assert lib.t2b_set_error_word(None) == 0
     assert word_for(s1) is None
+
+
+def test_tp_allreduce_rejects_bad_arguments_on_the_host():
+    """The peer-memory all-reduce checks its arguments before anything touches a device."""
+    import ctypes as C
+
+    import torch
+    L = _lib.load()
+    buf = (C.c_uint8 * 4096)()
+    base = (C.addressof(buf) + 255) & ~255           # 16-byte aligned host stand-ins (never dereferenced)
+    parts = (C.c_void_p * 2)(base, base + 1024)
+    flags = (C.c_void_p * 2)(base + 2048, base + 2048 + 16)
+    st = base + 3072
+    f = L.t2b_tp_allreduce_residual_norm_input
+    BF16, F16 = _lib.DTYPE[torch.bfloat16], _lib.DTYPE[torch.float16]
+    ERR_SHAPE, ERR_ALIGN, ERR_ARG = 1, 2, 6                  # t2b.h status codes
+
+    def call(world=2, rank=0, dtype=BF16, M=4, H=64, parts_=parts, x=base + 512, w=None, xw=None):
+        return f(C.addressof(parts_), dtype, C.addressof(flags), st, rank, world, x, None, w, xw, M, H, None)
+
+    assert call(world=0) == ERR_ARG
+    assert call(world=9) == ERR_ARG
+    assert call(rank=2) == ERR_ARG
+    assert call(dtype=F16) == ERR_ARG
+    assert call(w=base + 16) == ERR_ARG            # norm weight without an output (or the reverse)
+    assert call(H=60) == ERR_SHAPE
+    assert call(M=0) == ERR_SHAPE
+    assert call(parts_=(C.c_void_p * 2)(base + 4, base + 1024)) == ERR_ALIGN
+    assert call(x=base + 4) == ERR_ALIGN
+    assert L.t2b_tp_allreduce_state_bytes() >= 8
