@@ -63,7 +63,7 @@ def parse():
                          "the batch is then the global batch")
     ap.add_argument("--ctx", type=int, default=4096, help="--tp: KV cache pre-filled to this many positions")
     ap.add_argument("--tp-eager", action="store_true", help="--tp: launch every step eagerly (no CUDA graph)")
-    ap.add_argument("--tp-collective", default="nccl", choices=["nccl", "p2p"],
+    ap.add_argument("--tp-collective", default="p2p", choices=["nccl", "p2p"],
                     help="tensor parallel: sum the row-parallel partials by NCCL all-reduce, or by the "
                          "peer-memory kernel fused with the residual step")
     ap.add_argument("--prefill-only", action="store_true",

@@ -24,11 +24,11 @@ partials per layer (bf16 by default, ``[B, H]`` = 512 KiB at 64 rows of
 Qwen3-8B; fp32 on request) are summed across ranks and added into the fp32
 residual stream by one of:
 
-* ``collective="p2p"``: ``t2b_tp_allreduce_residual_norm_input``, one
+* ``collective="p2p"`` (default): ``t2b_tp_allreduce_residual_norm_input``, one
   kernel that signals and reads the peers' partials over NVLink (peer-mapped
   buffers from ``torch.distributed._symmetric_memory``) and does the residual
   step; o_proj and down write alternate partial buffers;
-* ``collective="nccl"`` (default): an NCCL all-reduce on the decode stream followed by
+* ``collective="nccl"``: an NCCL all-reduce on the decode stream followed by
   ``t2b_residual_norm_input``.
 """
 
@@ -128,7 +128,7 @@ class TPDecodeEngine:
 
     def __init__(self, cfg, model: dict, batch: int, max_ctx: int, tp: int, rank: int, group=None,
                  device="cuda", use_graph: bool = False, partial_dtype: torch.dtype = torch.bfloat16,
-                 collective: str = "nccl"):
+                 collective: str = "p2p"):
         import torch.distributed as dist
         from . import _lib
         from . import weights as W
