@@ -153,6 +153,26 @@ def test_shape_errors_raise():
         gemm(dw, torch.zeros(1, 256, dtype=torch.bfloat16, device="cuda"))
 
 
+@pytest.mark.parametrize("M", [16, 64])
+def test_wide_decode_linear_takes_the_large_m_kernel(M):
+    """A decode batch on a linear whose tcgen05 grid would run more than two waves (the
+    Qwen3-8B gate/up shape of a TP2 rank) goes to the persistent large-M kernel by
+    default, and matches the oracle there."""
+    import ctypes as C
+    N, K = 12288, 4096
+    plan = [C.c_int() for _ in range(4)]
+    _lib.load().t2b_linear_plan(M, N, K, *[C.byref(v) for v in plan])
+    assert plan[0].value == 2
+    g = torch.Generator().manual_seed(M + 12288)
+    lin = synth.random_linear(N, K, g)
+    dw = W.from_autogptq(lin)
+    torch.cuda.synchronize()
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    ref = oracle.GroupedW4A16Linear(lin.qweight, lin.qzeros, lin.scales)(x.float())
+    assert rel_err(gemm(dw, x.cuda(), torch.float32), ref) <= 1e-2
+    assert rel_err(gemm(dw, x.cuda(), torch.bfloat16), ref) <= 1e-2
+
+
 @pytest.mark.parametrize("M", [1, 5, 128, 130])
 @pytest.mark.parametrize("N,K", [(1024, 3072), (384, 256), (256, 12288)])
 def test_large_m_kernel_forced(monkeypatch, M, N, K):
