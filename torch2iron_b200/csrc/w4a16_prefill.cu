@@ -4,7 +4,7 @@
 // Work unit: one 128-row weight tile (n) x one block of BM = 128 activation
 // rows (m), over all K.  Persistent CTAs (one per SM) walk the units with the
 // weight tile fastest, so the CTAs running at once share an activation block.
-// Warp roles (480 threads), each a pipeline stage joined by mbarriers:
+// Warp roles (608 threads), each a pipeline stage joined by mbarriers:
 //   * warp 14, weights: one bulk copy per group of the tile's raw int4 block
 //     (8 KB) and meta (512 B) into a ring of NR shared-memory stages
 //     (constant data: this runs ahead of the dependency wait);
@@ -18,10 +18,12 @@
 //   * warp 13, MMA: 8 tcgen05.mma (M 128, N BM, K 16, A from TMEM) per group
 //     into one of two fp32 TMEM accumulators, freeing A and X stages by
 //     tcgen05.commit;
-//   * warps 8-11, epilogue: drain the other accumulator (times the RMSNorm row
-//     scale) into shared memory and run the decode path's fused epilogue
-//     (linear_common.cuh) on the [BM][128] tile, while the MMAs of the next
-//     unit run.
+//   * warps 8-11 and 15-18, epilogue: drain the other accumulator (times the
+//     RMSNorm row scale) into shared memory -- each group of four warps half
+//     of the tile's activation rows -- and run the decode path's fused
+//     epilogue (linear_common.cuh) on the [BM][128] tile with all eight,
+//     while the MMAs of the next unit run (the epilogue bounded this kernel
+//     with four warps).
 // A weight tile is dequantised once per activation block (M/BM times in all).
 // Every mbarrier wait is time-bounded; a role that gives up records
 // T2B_ERR_TIMEOUT and raises the CTA's abort flag, the others stop at their
@@ -42,8 +44,8 @@ constexpr int PF_NX = 3;                 // activation stages
 constexpr int PF_NA = 4;                 // TMEM A stages (64 columns each)
 constexpr int PF_NR = 4;                 // raw weight stages
 constexpr int PF_RAW = BLOCK_BYTES + Q4NX_META_WORDS * 4;   // int4 block + meta of one (tile, group), either format
-constexpr int PF_GT = 480;               // threads: 8 producer, 4 epilogue, TMA, MMA, weight warps
-constexpr int PF_EPI_T0 = 256;           // first epilogue thread
+constexpr int PF_GT = 608;               // threads: 8 producer, 8 epilogue, TMA, MMA, weight warps
+constexpr int PF_EPI = 256;              // epilogue threads: warps 8-11 and 15-18
 constexpr uint32_t PF_TMEM_COLS = 512;   // accumulators [0, 2*BM), A stages from column 2*BM
 constexpr uint32_t PF_A0 = 2 * PF_BM;
 
@@ -74,8 +76,8 @@ struct PfLayout {
 #define PF_PUT(slot, v)
 #endif
 
-// Named barrier among the four epilogue warps (id 1; 0 is __syncthreads).
-T2B_DEV void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier among the eight epilogue warps (id 1; 0 is __syncthreads).
+T2B_DEV void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // Epilogues for a [BM][128] tile with many rows.  Same arithmetic as the
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[i], 8);  // one arrival per epilogue warp
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -413,20 +415,23 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       PF_PUT(3, we);
     }
   } else {
-    // ---- epilogue warps 8-11: drain accumulator j&1, fused epilogue on the tile ----
-    const int t = threadIdx.x - PF_EPI_T0;              // 0..127
-    const int q4 = warp & 3;                            // TMEM lane quarter
+    // ---- epilogue warps 8-11 and 15-18: drain accumulator j&1 (group 0 takes the
+    //      first 64 activation rows of the tile, group 1 the last 64), then the
+    //      fused epilogue on the tile with all 256 threads ----
+    const int grp = warp >= 15 ? 1 : 0;
+    const int q4 = warp & 3;                            // TMEM lane quarter (a warp reaches lanes 32*(warp%4)..)
+    const int t = grp * 128 + q4 * 32 + lane;           // 0..255
     const int r = q4 * 32 + lane;                       // weight row
     const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
     grid_dep_wait();   // row sums, residual rows, positions come from earlier kernels
-    maybe_clear_ssq(p, blockIdx.x == 0, t, 128);
+    maybe_clear_ssq(p, blockIdx.x == 0, t, PF_EPI);
     long long wf = 0;
     (void)wf;
     for (int j = 0; j < my_units; ++j) {
       const int buf = j & 1;
       const int u = unit_of(j);
       const int tile = u % n_tiles, m0 = (u / n_tiles) * PF_BM;
-      if (PRO == PRO_RMSNORM) {
+      if (PRO == PRO_RMSNORM && t < PF_BM) {
         const int m = m0 + t;
         rowscale[t] = (m < p.M) ? rsqrtf(p.ssq[m] / (float)p.K + p.eps) : 0.f;   // model.py:179-180
       }
@@ -442,7 +447,7 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < PF_BM; c0 += 32) {
+      for (int c0 = grp * (PF_BM / 2); c0 < (grp + 1) * (PF_BM / 2); c0 += 32) {
         uint32_t v[32];
         tmem_ld32(lane_base + (uint32_t)(buf * PF_BM + c0), v);
         tmem_ld_wait();
@@ -459,12 +464,12 @@ __global__ void __launch_bounds__(PF_GT, 1) w4a16_prefill_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&acc_empty[buf]);   // the MMAs of unit j+2 may overwrite it
       epi_sync();                                    // the whole tile is in shared memory
       if (EPI == EPI_QKV) {
-        if (p.head_dim == 128) pf_qkv_epilogue<128, 4>(p, tile_acc, tile, m0, PF_BM, t, 128);
-        else pf_qkv_epilogue<64, 4>(p, tile_acc, tile, m0, PF_BM, t, 128);
+        if (p.head_dim == 128) pf_qkv_epilogue<128, 4>(p, tile_acc, tile, m0, PF_BM, t, PF_EPI);
+        else pf_qkv_epilogue<64, 4>(p, tile_acc, tile, m0, PF_BM, t, PF_EPI);
       } else if (EPI == EPI_RESIDUAL) {
-        pf_residual_epilogue<8>(p, tile_acc, tile, m0, PF_BM, t, 128);
+        pf_residual_epilogue<8>(p, tile_acc, tile, m0, PF_BM, t, PF_EPI);
       } else {
-        tile_epilogue<EPI>(p, tile_acc, scratch, tile, m0, PF_BM, EpiCache{}, t, 128);
+        tile_epilogue<EPI>(p, tile_acc, scratch, tile, m0, PF_BM, EpiCache{}, t, PF_EPI);
       }
     }
     if (t == 0) PF_PUT(6, wf);
