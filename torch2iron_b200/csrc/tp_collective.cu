@@ -28,7 +28,7 @@
 namespace t2b {
 
 constexpr int TPAR_MAX_WORLD = 8;
-constexpr int TPAR_THREADS = 256;
+constexpr int TPAR_THREADS = 512;   // one 8-element chunk per thread for H = 4096
 
 struct TpArParams {
   const void* part[TPAR_MAX_WORLD];  // every rank's partial [M][H] (peer-mapped; this rank's at [rank])
@@ -49,8 +49,8 @@ T2B_DEV int ld_acquire_sys(const int* p) {
   return v;
 }
 
-T2B_DEV void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+T2B_DEV void st_relaxed_sys(int* p, int v) {
+  asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // 16 bytes of a peer's partial, not cached on this GPU (the buffer is rewritten every other call)
@@ -62,27 +62,40 @@ T2B_DEV uint4 ld_peer16(const void* p) {
   return v;
 }
 
-// Eight partial values starting at element o: 8 bf16 (16 bytes) or 8 fp32 (two 16-byte loads).
-T2B_DEV void add_partial8(const TpArParams& P, int q, size_t o, float* a) {
+// Eight partial values starting at element o from every rank, summed in rank
+// order.  All ranks' loads are issued before the first add: each is an
+// NVLink round trip, and issued one after another they would add up.
+T2B_DEV void sum_partials8(const TpArParams& P, size_t o, float* a) {
+  uint4 r[TPAR_MAX_WORLD][2];
   if (P.ybf16) {
-    const uint4 r = ld_peer16(static_cast<const __nv_bfloat16*>(P.part[q]) + o);
-    const uint32_t u[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      a[2 * j] += __uint_as_float(u[j] << 16);
-      a[2 * j + 1] += __uint_as_float(u[j] & 0xffff0000u);
+    for (int q = 0; q < TPAR_MAX_WORLD; ++q)
+      if (q < P.world) r[q][0] = ld_peer16(static_cast<const __nv_bfloat16*>(P.part[q]) + o);
+#pragma unroll
+    for (int q = 0; q < TPAR_MAX_WORLD; ++q) {
+      if (q >= P.world) break;
+      const uint32_t u[4] = {r[q][0].x, r[q][0].y, r[q][0].z, r[q][0].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        a[2 * j] += __uint_as_float(u[j] << 16);
+        a[2 * j + 1] += __uint_as_float(u[j] & 0xffff0000u);
+      }
     }
   } else {
-    const float* f = static_cast<const float*>(P.part[q]) + o;
-    const uint4 r0 = ld_peer16(f), r1 = ld_peer16(f + 4);
-    a[0] += __uint_as_float(r0.x);
-    a[1] += __uint_as_float(r0.y);
-    a[2] += __uint_as_float(r0.z);
-    a[3] += __uint_as_float(r0.w);
-    a[4] += __uint_as_float(r1.x);
-    a[5] += __uint_as_float(r1.y);
-    a[6] += __uint_as_float(r1.z);
-    a[7] += __uint_as_float(r1.w);
+#pragma unroll
+    for (int q = 0; q < TPAR_MAX_WORLD; ++q)
+      if (q < P.world) {
+        const float* f = static_cast<const float*>(P.part[q]) + o;
+        r[q][0] = ld_peer16(f);
+        r[q][1] = ld_peer16(f + 4);
+      }
+#pragma unroll
+    for (int q = 0; q < TPAR_MAX_WORLD; ++q) {
+      if (q >= P.world) break;
+      const uint32_t u[8] = {r[q][0].x, r[q][0].y, r[q][0].z, r[q][0].w, r[q][1].x, r[q][1].y, r[q][1].z, r[q][1].w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] += __uint_as_float(u[j]);
+    }
   }
 }
 
@@ -93,13 +106,16 @@ __global__ void __launch_bounds__(TPAR_THREADS) tp_allreduce_residual_kernel(con
   __shared__ int s_call, s_ok;
   __shared__ float part_sq[TPAR_THREADS / 32];
   const int m = blockIdx.x;
+  const int call = *reinterpret_cast<volatile int*>(&P.state[0]) + 1;
+  if (m == 0 && threadIdx.x < P.world) {
+    // lane q signals rank q (this one included) that this rank's partial of `call`
+    // is complete: a system-scope fence orders the partial before the flag, and the
+    // stores to the peers go out in parallel, not one release after another
+    __threadfence_system();
+    st_relaxed_sys(P.flags[threadIdx.x] + P.rank, call);
+  }
   if (threadIdx.x == 0) {
-    const int call = *reinterpret_cast<volatile int*>(&P.state[0]) + 1;
     s_call = call;
-    if (m == 0) {  // signal every rank (this one included) that this rank's partial of `call` is complete
-      __threadfence_system();
-      for (int q = 0; q < P.world; ++q) st_release_sys(P.flags[q] + P.rank, call);
-    }
     bool ok = true;
     const uint64_t t0 = globaltimer_ns();
     for (int q = 0; q < P.world && ok; ++q)
@@ -118,7 +134,7 @@ __global__ void __launch_bounds__(TPAR_THREADS) tp_allreduce_residual_kernel(con
     for (int i = threadIdx.x * 8; i < P.H; i += TPAR_THREADS * 8) {
       const size_t o = (size_t)m * P.H + i;
       float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int q = 0; q < P.world; ++q) add_partial8(P, q, o, a);   // rank order on every rank
+      sum_partials8(P, o, a);   // rank order on every rank
       float4* xp = reinterpret_cast<float4*>(P.x + o);
       const float4 x0 = xp[0], x1 = xp[1];
       const float v[8] = {x0.x + a[0], x0.y + a[1], x0.z + a[2], x0.w + a[3],
