@@ -223,11 +223,14 @@ class TPDecodeEngine:
         from . import _lib
         group = self.group if self.group is not None else self.dist.group.WORLD
         name = group.group_name
-        if hasattr(symm_mem, "enable_symm_mem_for_group"):
-            try:
-                symm_mem.enable_symm_mem_for_group(name)
-            except Exception:   # already enabled, or not needed by this torch version
-                pass
+        if hasattr(symm_mem, "enable_symm_mem_for_group"):   # needed by older torch versions only
+            import warnings
+            with warnings.catch_warnings():
+                warnings.simplefilter("ignore")
+                try:
+                    symm_mem.enable_symm_mem_for_group(name)
+                except Exception:   # already enabled, or not needed by this torch version
+                    pass
         dev, tp = self.device, self.tp
         self.y_bufs, ptrs = [], []
         for _ in range(2):
