@@ -373,6 +373,26 @@ T2B_API int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* lm_head, int 
                                int32_t* idx, float* max_logit, float* logits, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/*
+ * The same greedy head on a tensor-parallel vocabulary slice (table rows are
+ * vocabulary entries vocab_off .. vocab_off + V_local - 1), with the pick
+ * merged over the ranks inside the kernel: its last CTA writes this rank's
+ * best (logit, index) key of every row into every rank's gather buffer
+ * (gather[q] is rank q's [world][M] uint64 buffer, peer-mapped), signals
+ * through flags[q] (rank q's [world] int32 words, zeroed before the first
+ * call) and, once every rank signalled the call (at most 0.5 s, then
+ * T2B_ERR_TIMEOUT in the stream's status word), writes idx [M] = the
+ * vocabulary index of the largest logit of the whole row (ties to the lowest
+ * index).  state: this rank's call counter, one zeroed int32.  Every rank
+ * makes the same sequence of calls.  Replaces a local argmax, two
+ * all-gathers and a host-side merge; no counterpart in the reference (its
+ * head runs on one device).
+ */
+T2B_API int t2b_lm_head_argmax_tp(const uint16_t* xn, const uint16_t* lm_head_slice, int dtype, int M, int H,
+                                  int V_local, int vocab_off, void* const* gather, int32_t* const* flags,
+                                  int32_t* state, int rank, int world, int32_t* idx, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 T2B_API size_t t2b_argmax_workspace_bytes(int M, int V);
 T2B_API int t2b_argmax_rows(const void* logits, int dtype, int M, int V, int ld, int32_t* idx, void* workspace,
                     size_t workspace_bytes, void* stream);

@@ -34,6 +34,7 @@ namespace t2b {
 constexpr int LM_THREADS = 192;
 constexpr int LM_ROWS = 128;   // vocab rows per tile (MMA M)
 constexpr int LM_KB = 64;      // k per TMA box / pipeline stage
+constexpr int LM_MAX_WORLD = 8;
 
 struct LmParams {
   CUtensorMap emap;   // E [V][H] bf16, box 64 k x 128 rows
@@ -46,6 +47,14 @@ struct LmParams {
   unsigned long long* keys;  // [M], zero between calls
   int* cnt;           // ticket, zero between calls
   int* err;
+  // tensor-parallel vocabulary slice (t2b_lm_head_argmax_tp): row v of this
+  // table is vocabulary entry vocab_off + v, and the last CTA merges the
+  // greedy pick over the ranks (tp_world > 0)
+  int vocab_off;
+  int tp_world, tp_rank;
+  unsigned long long* gather[LM_MAX_WORLD];  // every rank's [world][M] key buffer (peer-mapped)
+  int* flags[LM_MAX_WORLD];                  // every rank's [world] flag words (peer-mapped)
+  int* tp_state;                             // this rank's call counter
 };
 
 template <int BP>
@@ -76,7 +85,7 @@ T2B_DEV unsigned long long shfl_xor_u64(unsigned long long x, int m) {
   return ((unsigned long long)hi << 32) | lo;
 }
 
-template <int BP>
+template <int BP, bool TP>
 __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __grid_constant__ LmParams p) {
   using G = LmGeom<BP>;
   constexpr int STG = G::STAGES;
@@ -220,7 +229,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __g
           const bool use = live && e < BP;
           const float val = __uint_as_float(v[e < BP ? e : 0]);
           if (p.logits && use && col < p.M) p.logits[(size_t)col * p.V + row] = val;
-          c[e] = use ? lm_key(val, row) : 0ull;
+          c[e] = use ? lm_key(val, TP ? row + p.vocab_off : row) : 0ull;
         }
         // transpose-reduce: after the step with mask s, lane keeps the half of its
         // columns selected by its bit s, maxed with the partner's copy of that half
@@ -266,6 +275,62 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __g
   }
   __syncthreads();
   if (!*last_flag) return;
+  if constexpr (TP) {
+    // Tensor parallel: this rank's best key of every row goes to every rank's
+    // gather buffer (slot [tp_rank][m]); after a system-scope fence one lane
+    // per rank stores this call's number into that rank's flag word; then,
+    // once every rank has signalled the call (time bounded), the largest key
+    // over the ranks is the greedy pick of the whole vocabulary row (ties to
+    // the lowest vocabulary index, as torch.argmax over the full row).
+    volatile int* ok_flag = last_flag + 1;
+    const int call = *reinterpret_cast<volatile int*>(p.tp_state) + 1;
+    for (int m = tid; m < p.M; m += LM_THREADS) {
+      const unsigned long long k = atomicExch(p.keys + m, 0ull);
+      for (int q = 0; q < p.tp_world; ++q)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.gather[q] + (size_t)p.tp_rank * p.M + m), "l"(k)
+                     : "memory");
+    }
+    __syncthreads();
+    if (tid < p.tp_world) {
+      __threadfence_system();
+      asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(p.flags[tid] + p.tp_rank), "r"(call) : "memory");
+    }
+    if (tid == 0) {
+      bool ok = true;
+      const uint64_t t0 = globaltimer_ns();
+      for (int q = 0; q < p.tp_world && ok; ++q)
+        for (;;) {
+          int f;
+          asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(f) : "l"(p.flags[p.tp_rank] + q) : "memory");
+          if (f >= call) break;
+          if (globaltimer_ns() - t0 > 500000000ull) {   // 0.5 s: a rank never signalled
+            if (p.err) atomicCAS(p.err, 0, T2B_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+        }
+      *ok_flag = ok;
+    }
+    __syncthreads();
+    if (*ok_flag)
+      for (int m = tid; m < p.M; m += LM_THREADS) {
+        unsigned long long best = 0ull;
+        for (int q = 0; q < p.tp_world; ++q) {
+          unsigned long long k;
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(p.gather[p.tp_rank] + (size_t)q * p.M + m)
+                       : "memory");
+          best = k > best ? k : best;
+        }
+        p.idx[m] = best ? (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull)) : 0;
+        if (p.vals) p.vals[m] = lm_key_value(best);
+      }
+    __syncthreads();
+    if (tid == 0) {
+      atomicExch(p.cnt, 0);
+      *reinterpret_cast<volatile int*>(p.tp_state) = call;
+    }
+    return;
+  }
   for (int m = tid; m < p.M; m += LM_THREADS) {
     const unsigned long long k = atomicExch(p.keys + m, 0ull);
     p.idx[m] = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
@@ -284,9 +349,9 @@ static int lm_bp(int M) {
 
 size_t lm_head_workspace_bytes(int M) { return (((size_t)M * 8 + 255) & ~size_t(255)) + 256; }
 
-template <int BP>
+template <int BP, bool TP>
 static int lm_launch_t(LmParams& p, cudaStream_t st) {
-  auto kern = lm_head_argmax_kernel<BP>;
+  auto kern = lm_head_argmax_kernel<BP, TP>;
   const size_t smem = LmGeom<BP>::SMEM;
   if (allow_smem(kern, smem) != T2B_OK) return T2B_ERR_LAUNCH;
   int dev = 0, sms = 148;
@@ -310,8 +375,15 @@ static int encode_2d(CUtensorMap* m, const void* base, int inner, int outer, int
   return r == CUDA_SUCCESS ? T2B_OK : T2B_ERR_ARG;
 }
 
+struct LmTp {
+  int vocab_off, world, rank;
+  unsigned long long* const* gather;
+  int* const* flags;
+  int* state;
+};
+
 int lm_head_argmax(const uint16_t* xn, const uint16_t* lm, int dtype, int M, int H, int V, int32_t* idx,
-                   float* vals, float* logits, void* ws, size_t ws_bytes, cudaStream_t st) {
+                   float* vals, float* logits, void* ws, size_t ws_bytes, cudaStream_t st, const LmTp* tp = nullptr) {
   if (M < 1 || M > 256 || H < LM_KB || H % LM_KB || V < 1) return T2B_ERR_SHAPE;
   if (dtype != T2B_DTYPE_BF16 && dtype != T2B_DTYPE_F16) return T2B_ERR_ARG;
   if (ws_bytes < lm_head_workspace_bytes(M) || !ws) return T2B_ERR_WORKSPACE;
@@ -331,11 +403,28 @@ int lm_head_argmax(const uint16_t* xn, const uint16_t* lm, int dtype, int M, int
   p.keys = reinterpret_cast<unsigned long long*>(ws);
   p.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * 8 + 255) & ~size_t(255)));
   p.err = error_word(st);
-  if (bp == 16) return lm_launch_t<16>(p, st);
-  if (bp == 32) return lm_launch_t<32>(p, st);
-  if (bp == 64) return lm_launch_t<64>(p, st);
-  if (bp == 128) return lm_launch_t<128>(p, st);
-  return lm_launch_t<256>(p, st);
+  if (tp) {
+    p.vocab_off = tp->vocab_off;
+    p.tp_world = tp->world;
+    p.tp_rank = tp->rank;
+    p.tp_state = tp->state;
+    for (int q = 0; q < tp->world; ++q) {
+      p.gather[q] = tp->gather[q];
+      p.flags[q] = tp->flags[q];
+    }
+  }
+  if (tp) {   // the tensor-parallel merge is its own instantiation: the one-GPU kernel is unchanged
+    if (bp == 16) return lm_launch_t<16, true>(p, st);
+    if (bp == 32) return lm_launch_t<32, true>(p, st);
+    if (bp == 64) return lm_launch_t<64, true>(p, st);
+    if (bp == 128) return lm_launch_t<128, true>(p, st);
+    return lm_launch_t<256, true>(p, st);
+  }
+  if (bp == 16) return lm_launch_t<16, false>(p, st);
+  if (bp == 32) return lm_launch_t<32, false>(p, st);
+  if (bp == 64) return lm_launch_t<64, false>(p, st);
+  if (bp == 128) return lm_launch_t<128, false>(p, st);
+  return lm_launch_t<256, false>(p, st);
 }
 
 }  // namespace t2b
@@ -354,4 +443,23 @@ extern "C" int t2b_lm_head_argmax(const uint16_t* xn, const uint16_t* lm_head, i
   if ((reinterpret_cast<uintptr_t>(xn) | reinterpret_cast<uintptr_t>(lm_head)) & 15) return T2B_ERR_ALIGN;
   return lm_head_argmax(xn, lm_head, dtype, M, H, V, idx, max_logit, logits, ws, ws_bytes,
                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int t2b_lm_head_argmax_tp(const uint16_t* xn, const uint16_t* lm_head_slice, int dtype, int M, int H,
+                                     int V_local, int vocab_off, void* const* gather, int32_t* const* flags,
+                                     int32_t* state, int rank, int world, int32_t* idx, void* ws, size_t ws_bytes,
+                                     void* stream) {
+  if (!xn || !lm_head_slice || !idx || !gather || !flags || !state) return T2B_ERR_ARG;
+  if (world < 1 || world > LM_MAX_WORLD || rank < 0 || rank >= world || vocab_off < 0) return T2B_ERR_ARG;
+  if ((long long)vocab_off + V_local > 0x7FFFFFFFLL) return T2B_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(xn) | reinterpret_cast<uintptr_t>(lm_head_slice)) & 15) return T2B_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(state) & 3) return T2B_ERR_ALIGN;
+  for (int q = 0; q < world; ++q) {
+    if (!gather[q] || !flags[q]) return T2B_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(gather[q]) & 7) || (reinterpret_cast<uintptr_t>(flags[q]) & 3))
+      return T2B_ERR_ALIGN;
+  }
+  const LmTp tp{vocab_off, world, rank, reinterpret_cast<unsigned long long* const*>(gather), flags, state};
+  return lm_head_argmax(xn, lm_head_slice, dtype, M, H, V_local, idx, nullptr, nullptr, ws, ws_bytes,
+                        reinterpret_cast<cudaStream_t>(stream), &tp);
 }

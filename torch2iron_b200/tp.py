@@ -30,6 +30,10 @@ residual stream by one of:
   step; o_proj and down write alternate partial buffers;
 * ``collective="nccl"``: an NCCL all-reduce on the decode stream followed by
   ``t2b_residual_norm_input``.
+
+With ``collective="p2p"`` the greedy head also merges its pick over the ranks
+inside its kernel (``t2b_lm_head_argmax_tp``); with ``"nccl"`` the local
+(max, index) pairs are all-gathered and merged by ``merge_argmax``.
 """
 
 from __future__ import annotations
@@ -244,8 +248,19 @@ class TPDecodeEngine:
         flags.zero_()
         fh = symm_mem.rendezvous(flags, name)
         flag_ptrs = (C.c_void_p * tp)(*[int(q) for q in fh.buffer_ptrs])
+        # the greedy head: every rank's [tp][B] best-key buffer and its own flag words
+        gather = symm_mem.empty((tp * B,), dtype=torch.int64, device=dev)
+        gather.zero_()
+        gh = symm_mem.rendezvous(gather, name)
+        hflags = symm_mem.empty((tp,), dtype=torch.int32, device=dev)
+        hflags.zero_()
+        hh = symm_mem.rendezvous(hflags, name)
+        gather_ptrs = (C.c_void_p * tp)(*[int(q) for q in gh.buffer_ptrs])
+        hflag_ptrs = (C.c_void_p * tp)(*[int(q) for q in hh.buffer_ptrs])
         self._p2p = {"parts": [C.addressof(a) for a in ptrs], "flags": C.addressof(flag_ptrs),
-                     "keep": [ptrs, flag_ptrs, flags, fh],
+                     "gather": C.addressof(gather_ptrs), "head_flags": C.addressof(hflag_ptrs),
+                     "head_state": torch.zeros(4, dtype=torch.int32, device=dev),
+                     "keep": [ptrs, flag_ptrs, flags, fh, gather, gh, hflags, hh, gather_ptrs, hflag_ptrs],
                      "state": torch.zeros(max(_lib.load().t2b_tp_allreduce_state_bytes(), 16) // 4,
                                           dtype=torch.int32, device=dev)}
         torch.cuda.synchronize(dev)
@@ -306,6 +321,12 @@ class TPDecodeEngine:
         f16 = lib.DTYPE[torch.float16]
         lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
                                                            cfg.rms_norm_eps, p(self.xn), f16, B, cfg.emb_dim, st))
+        if self.collective == "p2p":   # the pick merged over the ranks inside the head kernel
+            q = self._p2p
+            lib.check("t2b_lm_head_argmax_tp", L.t2b_lm_head_argmax_tp(
+                p(self.xn), p(self.lm_head), f16, B, cfg.emb_dim, self.v_local, self.rank * self.v_local, q["gather"],
+                q["head_flags"], p(q["head_state"]), self.rank, self.tp, p(self.next_tokens), *self._ws("lm"), st))
+            return
         lib.check("t2b_lm_head_argmax", L.t2b_lm_head_argmax(
             p(self.xn), p(self.lm_head), f16, B, cfg.emb_dim, self.v_local, p(self.local_idx), p(self.local_max),
             None, *self._ws("lm"), st))
