@@ -799,7 +799,9 @@ def tp_measure(args, cfg, world, rank, local, batch, ctx) -> dict | None:
             "hbm": {"algorithmic_bytes_per_step_per_gpu": int(gpu_bytes), "achieved_gbs_per_gpu": round(per_gpu_gbs, 1),
                     "frac_of_peak": round(per_gpu_gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_kind},
             "gpu_launches": eng.kernels_per_step() * steps,
-            "collectives_per_step": 2 * cfg.n_layers + 2,
+            "collectives_per_step": ({"peer_memory_allreduce_residual": 2 * cfg.n_layers, "head_argmax_merge": 1,
+                                      "nccl": 0} if eng.collective == "p2p" else
+                                     {"nccl_allreduce": 2 * cfg.n_layers, "nccl_allgather": 2}),
             "allreduce_dtype": str(eng.partial_dtype).replace("torch.", ""),
             "allreduce": {"nccl": "NCCL all-reduce + t2b_residual_norm_input",
                           "p2p": "t2b_tp_allreduce_residual_norm_input (peer-memory loads over NVLink)"}[eng.collective],
