@@ -16,7 +16,9 @@ from torch2iron_b200.config import QuantizedQwenConfig
 from torch2iron_b200.modules import AutoGPTQWeights, PackedW4A16Linear, QuantizedQwenLayer, T2BTensorWeights
 
 PACKED = os.path.join(os.path.dirname(__file__), "golden", "packed_tiny")
-REF_SRC = "/root/reference/src"
+# the reference checkout beside this repository, when present (env T2B_REFERENCE_SRC overrides)
+REF_SRC = os.environ.get("T2B_REFERENCE_SRC") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference", "src")
 
 
 def test_packed_linear_validates_like_a_constructor_and_refuses_cpu():
