@@ -31,6 +31,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -171,10 +172,12 @@ class DecodeEngine:
         self.err = self._io[3 * seg:3 * seg + 1]
         # pinned staging for decode_step: [tokens | pos] in, [next_tokens | status] out
         self._host_in = torch.zeros(2 * seg, dtype=torch.int32).pin_memory()
+        self._host_in_np = self._host_in.numpy()
         self._host_out = torch.zeros(seg + 4, dtype=torch.int32).pin_memory()
         torch.cuda.synchronize(dev)   # repacked weights complete before any PDL launch reads them
         self.graph = None
         self._step_graph = None
+        self._io_graph = None
 
     # -- byte accounting (algorithmic, for the roofline) ---------------------
     def weight_bytes(self) -> int:
@@ -296,6 +299,15 @@ class DecodeEngine:
             self.enqueue_step()
             self.tokens.copy_(self.next_tokens)
             self.pos.add_(1)
+        # decode_step's graph: the host->device copy of the pinned tokens and
+        # positions, the step, and the device->host copy of the next tokens and
+        # the status word, so one replay and one synchronisation serve a call
+        seg = self._io_seg
+        self._io_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._io_graph):
+            self._io[:2 * seg].copy_(self._host_in, non_blocking=True)
+            self.enqueue_step()
+            self._host_out.copy_(self._io[2 * seg:], non_blocking=True)
 
     def run_step(self) -> None:
         """One step from the device-resident tokens / pos (outputs ``next_tokens``, ``logits``)."""
@@ -327,25 +339,34 @@ class DecodeEngine:
     # -- host-facing API (the reference runner's decode_step, qwen_npu.py:166-236) --
     def decode_step(self, tokens, positions) -> torch.Tensor:
         """tokens / positions: host sequences of length B -> next greedy tokens (host int32 [B])."""
-        tok = torch.as_tensor(tokens, dtype=torch.int32)
-        pos = torch.as_tensor(positions, dtype=torch.int32)
-        if tok.shape != (self.B,) or pos.shape != (self.B,):
-            raise ValueError(f"decode_step takes {self.B} tokens and {self.B} positions")
-        if int(tok.min()) < 0 or int(tok.max()) >= self.cfg.vocab_size:
+        B, seg = self.B, self._io_seg
+        hin = self._host_in_np                    # the pinned staging buffer, as numpy
+        try:
+            tok = np.asarray(tokens).reshape(-1)
+            pos = np.asarray(positions).reshape(-1)
+        except (TypeError, ValueError) as e:
+            raise ValueError(f"decode_step takes {B} tokens and {B} positions") from e
+        if tok.shape != (B,) or pos.shape != (B,):
+            raise ValueError(f"decode_step takes {B} tokens and {B} positions")
+        if tok.min() < 0 or tok.max() >= self.cfg.vocab_size:
             raise ValueError(f"token ids must be in [0, {self.cfg.vocab_size})")
-        if int(pos.min()) < 0 or int(pos.max()) >= self.max_ctx:
+        if pos.min() < 0 or pos.max() >= self.max_ctx:
             raise ValueError(f"positions must be in [0, {self.max_ctx}) (the KV cache length)")
-        seg = self._io_seg
-        self._host_in[:self.B].copy_(tok)
-        self._host_in[seg:seg + self.B].copy_(pos)
-        self._io[:2 * seg].copy_(self._host_in, non_blocking=True)    # one host->device copy
-        self.run_step()
-        # one device->host read per step: the next tokens and the status word
-        self._host_out.copy_(self._io[2 * seg:], non_blocking=True)
+        hin[:B] = tok
+        hin[seg:seg + B] = pos
+        if self.use_graph:
+            if self.graph is None:
+                self.capture()
+            self._io_graph.replay()              # copy in, step, copy out
+        else:
+            self._io[:2 * seg].copy_(self._host_in, non_blocking=True)    # one host->device copy
+            self.run_step()
+            # one device->host read per step: the next tokens and the status word
+            self._host_out.copy_(self._io[2 * seg:], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         if int(self._host_out[seg]):
             self.check_device_errors()
-        return self._host_out[:self.B].clone()
+        return self._host_out[:B].clone()
 
     # -- chunked prefill (prefill_runtime.py:95-164, for B sequences at once) --
     PREFILL_ROWS = 8192      # prompt tokens (all sequences) per chunk by default
@@ -510,3 +531,4 @@ class DecodeEngine:
         """Drop the captured graphs (the engine's buffers stay usable for eager steps)."""
         self.graph = None
         self._step_graph = None
+        self._io_graph = None
