@@ -160,3 +160,27 @@ def test_tp_allreduce_rejects_bad_arguments_on_the_host():
     assert call(parts_=(C.c_void_p * 2)(base + 4, base + 1024)) == ERR_ALIGN
     assert call(x=base + 4) == ERR_ALIGN
     assert L.t2b_tp_allreduce_state_bytes() >= 8
+
+
+def test_tp_head_rejects_bad_arguments_on_the_host():
+    """The tensor-parallel greedy head checks its arguments before anything touches a device."""
+    import ctypes as C
+    L = _lib.load()
+    buf = (C.c_uint8 * 8192)()
+    base = (C.addressof(buf) + 255) & ~255           # 16-byte aligned host stand-ins (never dereferenced)
+    gather = (C.c_void_p * 2)(base, base + 1024)
+    flags = (C.c_void_p * 2)(base + 2048, base + 2048 + 16)
+    f = L.t2b_lm_head_argmax_tp
+    ERR_SHAPE, ERR_ALIGN, ERR_ARG = 1, 2, 6                  # t2b.h status codes
+
+    def call(world=2, rank=0, off=0, V=1024, xn=base + 4096, gather_=gather):
+        return f(xn, base + 6144, 0, 4, 64, V, off, C.addressof(gather_), C.addressof(flags), base + 3072, rank, world,
+                 base + 3584, base + 7168, 512, None)
+
+    assert call(world=0) == ERR_ARG
+    assert call(world=9) == ERR_ARG
+    assert call(rank=2) == ERR_ARG
+    assert call(off=-1) == ERR_ARG
+    assert call(off=0x7FFFFFF0, V=1024) == ERR_SHAPE
+    assert call(xn=base + 4100) == ERR_ALIGN
+    assert call(gather_=(C.c_void_p * 2)(base + 4, base + 1024)) == ERR_ALIGN
