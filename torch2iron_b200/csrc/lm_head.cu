@@ -329,14 +329,14 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const __g
       atomicExch(p.cnt, 0);
       *reinterpret_cast<volatile int*>(p.tp_state) = call;
     }
-    return;
+  } else {
+    for (int m = tid; m < p.M; m += LM_THREADS) {
+      const unsigned long long k = atomicExch(p.keys + m, 0ull);
+      p.idx[m] = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+      if (p.vals) p.vals[m] = lm_key_value(k);
+    }
+    if (tid == 0) atomicExch(p.cnt, 0);
   }
-  for (int m = tid; m < p.M; m += LM_THREADS) {
-    const unsigned long long k = atomicExch(p.keys + m, 0ull);
-    p.idx[m] = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
-    if (p.vals) p.vals[m] = lm_key_value(k);
-  }
-  if (tid == 0) atomicExch(p.cnt, 0);
 }
 
 // ---------------------------------------------------------------------------
