@@ -63,9 +63,10 @@ def parse():
                          "the batch is then the global batch")
     ap.add_argument("--ctx", type=int, default=4096, help="--tp: KV cache pre-filled to this many positions")
     ap.add_argument("--tp-eager", action="store_true", help="--tp: launch every step eagerly (no CUDA graph)")
-    ap.add_argument("--tp-collective", default="p2p", choices=["nccl", "p2p"],
+    ap.add_argument("--tp-collective", default="p2p", choices=["nccl", "p2p", "push"],
                     help="tensor parallel: sum the row-parallel partials by NCCL all-reduce, or by the "
-                         "peer-memory kernel fused with the residual step")
+                         "peer-memory kernel fused with the residual step (p2p: it loads the peers' partials; "
+                         "push: each GEMM epilogue stores its partial into every rank's memory)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="one GPU: time the chunked prefill of --batch x --prompt tokens only (profiling case)")
     return ap.parse_args()
@@ -800,11 +801,13 @@ def tp_measure(args, cfg, world, rank, local, batch, ctx) -> dict | None:
                     "frac_of_peak": round(per_gpu_gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_kind},
             "gpu_launches": eng.kernels_per_step() * steps,
             "collectives_per_step": ({"peer_memory_allreduce_residual": 2 * cfg.n_layers, "head_argmax_merge": 1,
-                                      "nccl": 0} if eng.collective == "p2p" else
+                                      "nccl": 0} if eng.collective in ("p2p", "push") else
                                      {"nccl_allreduce": 2 * cfg.n_layers, "nccl_allgather": 2}),
             "allreduce_dtype": str(eng.partial_dtype).replace("torch.", ""),
             "allreduce": {"nccl": "NCCL all-reduce + t2b_residual_norm_input",
-                          "p2p": "t2b_tp_allreduce_residual_norm_input (peer-memory loads over NVLink)"}[eng.collective],
+                          "p2p": "t2b_tp_allreduce_residual_norm_input (peer-memory loads over NVLink)",
+                          "push": "t2b_w4a16_gemm_push (epilogue stores over NVLink) + "
+                                  "t2b_tp_allreduce_residual_norm_input (local loads)"}[eng.collective],
             "device_status": status,
             "clocks": clocks.summary(),
         }

@@ -140,6 +140,18 @@ T2B_API int t2b_repack_autogptq(const int32_t* qweight, const int32_t* qzeros, c
  * kernel.cc:29-133) and the W4A16GEMM family (w4a16_gemm/op.py:22-399).
  */
 T2B_API size_t t2b_w4a16_gemm_workspace_bytes(int M, int N, int K);
+/*
+ * The same GEMM for a tensor-parallel row-parallel linear whose partial is
+ * pushed where it is summed: y [M][N] (bf16 or fp32) is written to `y` and,
+ * bit for bit, to each of n_peers (<= 7) buffers y_peers[q] of the same
+ * layout -- other ranks' memory, peer-mapped -- from the GEMM's epilogue, so
+ * the transfer over NVLink overlaps the other tiles' work.  y and the peers
+ * 16-byte aligned.  No counterpart in the reference (its NPU path runs on one
+ * device).
+ */
+T2B_API int t2b_w4a16_gemm_push(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype,
+                                void* y, int y_dtype, void* const* y_peers, int n_peers, int M, int N, int K,
+                                int group_size, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * The launch plan every W4A16 linear of shape [M,N,K] takes (host only, no

@@ -184,3 +184,31 @@ def test_tp_head_rejects_bad_arguments_on_the_host():
     assert call(off=0x7FFFFFF0, V=1024) == ERR_SHAPE
     assert call(xn=base + 4100) == ERR_ALIGN
     assert call(gather_=(C.c_void_p * 2)(base + 4, base + 1024)) == ERR_ALIGN
+
+
+def test_gemm_push_rejects_bad_arguments_on_the_host():
+    """The row-parallel GEMM that pushes its partial into peer buffers checks the
+    peers, the output type and the alignment before it launches anything."""
+    import ctypes as C
+
+    import torch
+    L = _lib.load()
+    buf = (C.c_uint8 * 8192)()
+    base = (C.addressof(buf) + 255) & ~255           # 16-byte aligned host stand-ins (never dereferenced)
+    f = L.t2b_w4a16_gemm_push
+    BF16, F16, F32 = (_lib.DTYPE[t] for t in (torch.bfloat16, torch.float16, torch.float32))
+    ERR_SHAPE, ERR_ALIGN, ERR_ARG = 1, 2, 6                  # t2b.h status codes
+    good = (C.c_void_p * 7)(*[base + 4096 + 256 * i for i in range(7)])
+
+    def call(peers=good, n=1, y=base + 2048, y_dtype=BF16, N=128, K=256):
+        return f(base, base + 1024, _lib.WFMT_T2B, base + 1536, F16, y, y_dtype, C.addressof(peers) if peers else None,
+                 n, 4, N, K, 128, None, 0, None)
+
+    assert call(n=8) == ERR_ARG
+    assert call(n=-1) == ERR_ARG
+    assert call(peers=None) == ERR_ARG
+    assert call(y_dtype=F16) == ERR_ARG
+    assert call(N=96) == ERR_SHAPE
+    assert call(y=base + 2052, y_dtype=F32) == ERR_ALIGN
+    assert call(peers=(C.c_void_p * 2)(base + 4096, base + 4100), n=2) == ERR_ALIGN
+    assert call(peers=(C.c_void_p * 2)(base + 4096, None), n=2) == ERR_ARG

@@ -153,3 +153,21 @@ def test_tp2_attention_partials_over_gloo():
     for r in range(2):
         got = torch.from_numpy(res[r])
         assert (got - ref).abs().max().item() <= 1e-4 * ref.abs().max().item()
+
+
+def test_push_slots_pair_every_writer_with_its_reader():
+    """Push collective addressing: what rank r writes into rank q's buffer is
+    exactly the slot rank q reads as rank r's partial, for every pair."""
+    world, slot = 8, 64 * 4096 * 2
+    bases = [0x7F0000000000 + (q << 32) for q in range(world)]
+    table = [TP.push_slots(bases, r, slot) for r in range(world)]
+    for r in range(world):
+        reads, pushes = table[r]
+        assert len(reads) == world and len(pushes) == world - 1
+        assert reads[r] == bases[r] + r * slot                 # its own slot, written locally
+        peers = [q for q in range(world) if q != r]
+        for q, addr in zip(peers, pushes):
+            assert addr == table[q][0][r]                     # rank q reads it as rank r's partial
+    assert TP.push_slots(bases[:1], 0, slot) == ([bases[0]], [])
+    with pytest.raises(ValueError):
+        TP.push_slots(bases, world, slot)

@@ -38,6 +38,7 @@ SIGNATURES = {
     "t2b_linear_plan": (I, [I, I, I, P, P, P, P]),
     "t2b_linear_plan_qkv": (I, [I, I, I, P, P, P, P]),
     "t2b_tp_allreduce_state_bytes": (Z, []),
+    "t2b_w4a16_gemm_push": (I, [P, P, I, P, I, P, I, P, I, I, I, I, I, P, Z, P]),
     "t2b_lm_head_argmax_tp": (I, [P, P, I, I, I, I, I, P, P, P, I, I, P, P, Z, P]),
     "t2b_tp_allreduce_residual_norm_input": (I, [P, I, P, P, I, I, P, P, P, P, I, I, P]),
     "t2b_w4a16_gemm": (I, [P, P, I, P, I, P, I, I, I, I, I, P, Z, P]),

@@ -63,6 +63,10 @@ struct LinearParams {
   int n_heads, n_kv, head_dim, max_ctx;
   int* err;
   int q4nx;               // 1: Q4NX meta (bf16 scale | bf16 zero per 32-k piece), 0: T2B (per 128-k group)
+  // EPI_STORE: the same output also stored into these buffers (tensor-parallel
+  // partials pushed into the peers' memory; same layout as y)
+  void* y_peer[7];
+  int n_y_peer;
 };
 
 T2B_DEV size_t qw_block_offset(int nt, int g, int G) { return ((size_t)nt * G + g) * BLOCK_BYTES; }
@@ -271,9 +275,29 @@ T2B_DEV void tile_epilogue(const LinearParams& p, const float* tile_acc, float* 
   const int lane = t & 31;
   const int row0 = tile * TILE_N;
   if (EPI == EPI_STORE) {
-    for (int idx = t; idx < MB * TILE_N; idx += NT) {
-      const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
-      if (m < p.M) store_act(p.y, p.y_dtype, (size_t)m * p.y_ld + row0 + lr, tile_acc[idx]);
+    if (p.n_y_peer) {
+      // tensor-parallel push: the tile into this rank's buffer and every peer's,
+      // four outputs per store and the same bits everywhere (bf16 or fp32)
+      for (int idx = t * 4; idx < MB * TILE_N; idx += NT * 4) {
+        const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
+        if (m >= p.M) continue;
+        const float4 v = *reinterpret_cast<const float4*>(tile_acc + idx);
+        const size_t o = (size_t)m * p.y_ld + row0 + lr;
+        if (p.y_dtype == T2B_DTYPE_F32) {
+          *reinterpret_cast<float4*>(static_cast<float*>(p.y) + o) = v;
+          for (int q = 0; q < p.n_y_peer; ++q) *reinterpret_cast<float4*>(static_cast<float*>(p.y_peer[q]) + o) = v;
+        } else {
+          const uint2 w = pack_bf16x4(v.x, v.y, v.z, v.w);
+          *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.y) + o) = w;
+          for (int q = 0; q < p.n_y_peer; ++q)
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.y_peer[q]) + o) = w;
+        }
+      }
+    } else {
+      for (int idx = t; idx < MB * TILE_N; idx += NT) {
+        const int b = idx / TILE_N, lr = idx - b * TILE_N, m = m0 + b;
+        if (m < p.M) store_act(p.y, p.y_dtype, (size_t)m * p.y_ld + row0 + lr, tile_acc[idx]);
+      }
     }
   } else if (EPI == EPI_RESIDUAL) {
     // x += y ; sum of squares for the next RMSNorm ; bf16(x * w_next) for its GEMM.

@@ -560,6 +560,24 @@ extern "C" int t2b_w4a16_gemm(const void* weight, const uint32_t* meta, int wfmt
   return gemm_launch(p, wfmt, ws, ws_bytes, S_(stream));
 }
 
+extern "C" int t2b_w4a16_gemm_push(const void* weight, const uint32_t* meta, int wfmt, const void* x, int x_dtype,
+                                   void* y, int y_dtype, void* const* y_peers, int n_peers, int M, int N, int K,
+                                   int group_size, void* ws, size_t ws_bytes, void* stream) {
+  LinearParams p;
+  const int r = gemm_params(weight, meta, wfmt, x, x_dtype, y, y_dtype, M, N, K, group_size, &p);
+  if (r != T2B_OK) return r;
+  if (n_peers < 0 || n_peers > 7 || (n_peers > 0 && !y_peers)) return T2B_ERR_ARG;
+  if (y_dtype != T2B_DTYPE_BF16 && y_dtype != T2B_DTYPE_F32) return T2B_ERR_ARG;
+  if (!al(y, 16)) return T2B_ERR_ALIGN;
+  for (int q = 0; q < n_peers; ++q) {
+    if (!y_peers[q]) return T2B_ERR_ARG;
+    if (!al(y_peers[q], 16)) return T2B_ERR_ALIGN;
+    p.y_peer[q] = y_peers[q];
+  }
+  p.n_y_peer = n_peers;
+  return gemm_launch(p, wfmt, ws, ws_bytes, S_(stream));
+}
+
 extern "C" size_t t2b_qkv_workspace_bytes(int M, int H, int n_heads, int n_kv, int head_dim) {
   if (M < 1 || H < 256 || n_kv < 1) return 0;
   return linear_workspace_bytes(M, (n_heads + 2 * n_kv) * head_dim, H);

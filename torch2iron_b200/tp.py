@@ -118,6 +118,22 @@ def merge_argmax(vals: torch.Tensor, idx: torch.Tensor, v_per_rank: int) -> torc
 # ---------------------------------------------------------------------------
 # the engine (one rank)
 # ---------------------------------------------------------------------------
+def push_slots(bases: list[int], rank: int, slot_bytes: int) -> tuple[list[int], list[int]]:
+    """Addresses of the push collective's receive buffer, one [world][slot]
+    buffer per rank (``bases``: its address as every rank maps it).
+
+    Returns (reads, pushes): ``reads[q]`` is slot q of this rank's own buffer,
+    where rank q's partial lands (read locally by the all-reduce kernel);
+    ``pushes`` lists, for every other rank q in rank order, slot ``rank`` of
+    rank q's buffer (written over NVLink by this rank's GEMM epilogue)."""
+    world = len(bases)
+    if not 0 <= rank < world or slot_bytes <= 0:
+        raise ValueError("rank outside the group or empty slot")
+    reads = [bases[rank] + q * slot_bytes for q in range(world)]
+    pushes = [bases[q] + rank * slot_bytes for q in range(world) if q != rank]
+    return reads, pushes
+
+
 class TPDecodeEngine:
     """Greedy batch decoder for one tensor-parallel rank.
 
@@ -145,8 +161,8 @@ class TPDecodeEngine:
         if partial_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("the row-parallel partials are bf16 or fp32")
         self.partial_dtype = partial_dtype
-        if collective not in ("p2p", "nccl"):
-            raise ValueError("collective is 'p2p' or 'nccl'")
+        if collective not in ("push", "p2p", "nccl"):
+            raise ValueError("collective is 'push', 'p2p' or 'nccl'")
         self.collective = collective
         if max_ctx % 64:
             raise ValueError("max_ctx must be a multiple of 64")
@@ -172,7 +188,7 @@ class TPDecodeEngine:
         B, H, hd = batch, cfg.emb_dim, cfg.head_dim
         f32, bf = torch.float32, torch.bfloat16
         self.x = torch.zeros(B, H, dtype=f32, device=dev)
-        if collective == "p2p":
+        if collective in ("push", "p2p"):
             self._setup_p2p(B, H, partial_dtype)
         else:   # one partial, all-reduced in place
             self.y_bufs = [torch.zeros(B, H, dtype=partial_dtype, device=dev)] * 2
@@ -236,14 +252,25 @@ class TPDecodeEngine:
                 except Exception:   # already enabled, or not needed by this torch version
                     pass
         dev, tp = self.device, self.tp
-        self.y_bufs, ptrs = [], []
+        esize = torch.tensor([], dtype=dtype).element_size()
+        self.y_bufs, ptrs, self._push = [], [], []
         for _ in range(2):
-            t = symm_mem.empty((B, H), dtype=dtype, device=dev)
-            t.zero_()
-            hdl = symm_mem.rendezvous(t, name)
-            self.y_bufs.append(t)
-            ptrs.append((C.c_void_p * tp)(*[int(q) for q in hdl.buffer_ptrs]))
-            self._p2p_keep = getattr(self, "_p2p_keep", []) + [hdl]
+            if self.collective == "push":
+                # [tp][B][H]: slot q holds rank q's partial, written by rank q's GEMM epilogue
+                t = symm_mem.empty((tp, B, H), dtype=dtype, device=dev)
+                t.zero_()
+                hdl = symm_mem.rendezvous(t, name)
+                reads, pushes = push_slots([int(q) for q in hdl.buffer_ptrs], self.rank, B * H * esize)
+                self.y_bufs.append(t[self.rank])                              # this rank's own slot
+                ptrs.append((C.c_void_p * tp)(*reads))
+                self._push.append((C.c_void_p * max(tp - 1, 1))(*pushes))
+            else:
+                t = symm_mem.empty((B, H), dtype=dtype, device=dev)
+                t.zero_()
+                hdl = symm_mem.rendezvous(t, name)
+                self.y_bufs.append(t)
+                ptrs.append((C.c_void_p * tp)(*[int(q) for q in hdl.buffer_ptrs]))
+            self._p2p_keep = getattr(self, "_p2p_keep", []) + [hdl, t]
         flags = symm_mem.empty((tp,), dtype=torch.int32, device=dev)
         flags.zero_()
         fh = symm_mem.rendezvous(flags, name)
@@ -266,9 +293,25 @@ class TPDecodeEngine:
         torch.cuda.synchronize(dev)
         self.dist.barrier(group=group)   # every rank's flags are zero before anyone signals
 
+    def _row_parallel(self, which, lw_lin, x, K, st) -> None:
+        """A row-parallel linear (o_proj / down) writing its partial into buffer ``which``."""
+        lib, L, p = self._lib, self._lib.lib(), self._lib.ptr
+        H = self.cfg.emb_dim
+        ws = self._ws("o" if which == 0 else "down")
+        if self.collective == "push":   # partial pushed into every rank's buffer from the GEMM epilogue
+            import ctypes as C
+            peers = self._push[which]
+            lib.check("t2b_w4a16_gemm_push", L.t2b_w4a16_gemm_push(
+                p(lw_lin.qw), p(lw_lin.meta), lib.WFMT_T2B, p(x), lib.DTYPE[lib.ACT], p(self.y_bufs[which]),
+                lib.DTYPE[self.partial_dtype], C.addressof(peers), self.tp - 1, self.B, H, K, 128, *ws, st))
+            return
+        lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
+            p(lw_lin.qw), p(lw_lin.meta), lib.WFMT_T2B, p(x), lib.DTYPE[lib.ACT], p(self.y_bufs[which]),
+            lib.DTYPE[self.partial_dtype], self.B, H, K, 128, *ws, st))
+
     def _allreduce_residual(self, which, ssq_out, next_w):
         lib, p = self._lib, self._lib.ptr
-        if self.collective == "p2p":
+        if self.collective in ("push", "p2p"):
             q = self._p2p
             lib.check("t2b_tp_allreduce_residual_norm_input", lib.lib().t2b_tp_allreduce_residual_norm_input(
                 q["parts"][which], lib.DTYPE[self.partial_dtype], q["flags"], p(q["state"]), self.rank, self.tp,
@@ -293,16 +336,12 @@ class TPDecodeEngine:
             p(self.q), lib.DTYPE[lib.QDT], p(self.k_cache[li]), p(self.v_cache[li]), p(self.pos), p(self.attn),
             lib.DTYPE[lib.ACT], B,
             nq, nkv, hd, self.max_ctx, *self._ws("attn"), st))
-        lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-            p(lw.o_proj.qw), p(lw.o_proj.meta), lib.WFMT_T2B, p(self.attn), lib.DTYPE[lib.ACT], p(self.y_bufs[0]),
-            lib.DTYPE[self.partial_dtype], B, H, lc.q_dim, 128, *self._ws("o"), st))
+        self._row_parallel(0, lw.o_proj, self.attn, lc.q_dim, st)
         self._allreduce_residual(0, self.ssq_b, lw.post_attention_layernorm)
         lib.check("t2b_upgate_swiglu", L.t2b_upgate_swiglu(
             p(lw.gate_up.qw), p(lw.gate_up.meta), lw.gate_up.fmt, p(self.xw), p(self.ssq_b), cfg.rms_norm_eps, p(self.h),
             p(self.ssq_a), B, H, lc.hidden_dim, *self._ws("ug"), st))
-        lib.check("t2b_w4a16_gemm", L.t2b_w4a16_gemm(
-            p(lw.down.qw), p(lw.down.meta), lib.WFMT_T2B, p(self.h), lib.DTYPE[lib.ACT], p(self.y_bufs[1]),
-            lib.DTYPE[self.partial_dtype], B, H, lc.hidden_dim, 128, *self._ws("down"), st))
+        self._row_parallel(1, lw.down, self.h, lc.hidden_dim, st)
         self._allreduce_residual(1, self.ssq_a, self.next_norm_weight(li))
 
     def enqueue_step(self) -> None:
@@ -321,7 +360,7 @@ class TPDecodeEngine:
         f16 = lib.DTYPE[torch.float16]
         lib.check("t2b_rms_norm_rows", L.t2b_rms_norm_rows(p(self.x), p(self.ssq_a), p(self.final_norm),
                                                            cfg.rms_norm_eps, p(self.xn), f16, B, cfg.emb_dim, st))
-        if self.collective == "p2p":   # the pick merged over the ranks inside the head kernel
+        if self.collective in ("push", "p2p"):   # the pick merged over the ranks inside the head kernel
             q = self._p2p
             lib.check("t2b_lm_head_argmax_tp", L.t2b_lm_head_argmax_tp(
                 p(self.xn), p(self.lm_head), f16, B, cfg.emb_dim, self.v_local, self.rank * self.v_local, q["gather"],
