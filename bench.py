@@ -63,10 +63,11 @@ def parse():
                          "the batch is then the global batch")
     ap.add_argument("--ctx", type=int, default=4096, help="--tp: KV cache pre-filled to this many positions")
     ap.add_argument("--tp-eager", action="store_true", help="--tp: launch every step eagerly (no CUDA graph)")
-    ap.add_argument("--tp-collective", default="p2p", choices=["nccl", "p2p", "push"],
+    ap.add_argument("--tp-collective", default="auto", choices=["auto", "nccl", "p2p", "push"],
                     help="tensor parallel: sum the row-parallel partials by NCCL all-reduce, or by the "
                          "peer-memory kernel fused with the residual step (p2p: it loads the peers' partials; "
-                         "push: each GEMM epilogue stores its partial into every rank's memory)")
+                         "push: each GEMM epilogue stores its partial into every rank's memory; auto: push "
+                         "up to 4 ranks, p2p above)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="one GPU: time the chunked prefill of --batch x --prompt tokens only (profiling case)")
     return ap.parse_args()
