@@ -63,7 +63,8 @@ def _rank(rank, world, port, batch, partial, collective, out_q):
 
 @pytest.mark.parametrize("batch,partial,collective", [(1, "bfloat16", "p2p"), (5, "bfloat16", "p2p"),
                                                       (5, "float32", "p2p"), (5, "bfloat16", "nccl"),
-                                                      (5, "bfloat16", "push"), (3, "float32", "push")])
+                                                      (1, "bfloat16", "push"), (5, "bfloat16", "push"),
+                                                      (3, "float32", "push")])
 def test_tp2_engine_matches_single_gpu(batch, partial, collective):
     """bf16 row-parallel partials (the default, half the all-reduce bytes) and
     fp32 ones both hold the single-GPU engine's tokens and residual stream,
